@@ -1,0 +1,146 @@
+/*
+ * stew_nf4.h -- C ABI of the B200 (sm_100a) NF4 hot path.
+ *
+ * Every entry point takes raw device pointers, sizes and a CUDA stream handle
+ * (cudaStream_t passed as void*; NULL = legacy default stream), enqueues its
+ * kernels on that stream and returns a status code (NF4B_OK == 0).  None of
+ * them synchronises the stream or allocates device memory; the caller owns
+ * every buffer.  Inputs outside the supported envelope return
+ * NF4B_ERR_UNSUPPORTED without launching anything, so a caller can route them
+ * to another implementation (the reference does the same: nf4.py:61-70 guard,
+ * nf4.py:112 fallback).
+ *
+ * The functions mirror the reference's Python interface (evilandangry/stew,
+ * solution/nf4.py) as follows:
+ *   nf4b_dequant          <- dequantize_nf4(A, st)             nf4.py:73-92
+ *                            (the launch of _nf4_unpack,       nf4.py:30-50)
+ *   nf4b_dequant_batched  <- 196 x dequantize_nf4 per step     tools/bench_nf4.py:47
+ *   nf4b_linear_fwd       <- patched MatMul4Bit.forward        nf4.py:142-159
+ *                            (unpack + F.linear, nf4.py:148-152) fused, plus the
+ *                            peft lora.Linear q/v term y += (x A^T) B^T * s
+ *   nf4b_linear_bwd_dx    <- bitsandbytes MatMul4Bit.backward grad_A = dY . W
+ *                            on the re-dequantised weight      nf4.py:102-112, :131-133
+ *                            plus the LoRA input-gradient term
+ *   nf4b_lora_grads       <- peft LoRA weight grads (autograd through lora_A/lora_B)
+ */
+#ifndef STEW_NF4_H
+#define STEW_NF4_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum nf4b_status {
+  NF4B_OK = 0,
+  NF4B_ERR_INVALID_ARG = 1,  /* NULL pointer, negative or inconsistent size */
+  NF4B_ERR_UNSUPPORTED = 2,  /* outside the envelope (blocksize, dtype, shape); nothing launched */
+  NF4B_ERR_ALIGNMENT = 3,    /* a pointer or row stride the kernel needs aligned is not */
+  NF4B_ERR_CUDA = 4,         /* a CUDA runtime call or a launch failed */
+  NF4B_ERR_DEVICE = 5        /* current device is not an sm_100 part */
+};
+
+enum nf4b_dtype { NF4B_F16 = 0, NF4B_F32 = 1 };
+
+/* The fields of a bitsandbytes QuantState the unpack reads (nf4.py:61-70, :80-91).
+ * Nested (double-quantized) state:
+ *   scale[r] = code2[absmax8[r]] * absmax2[r / blocksize2] + offset[0]
+ * Plain state:
+ *   scale[r] = absmax32[r]
+ * value = code[nibble] * scale[r], fp32, rounded once to the output dtype.  */
+typedef struct nf4b_qstate {
+  const uint8_t* absmax8;   /* nested: 8-bit absmax codes, one per block      */
+  const float* absmax32;    /* plain: fp32 absmax, one per block             */
+  const float* code2;       /* nested: 256-entry fp32 second-level code      */
+  const float* absmax2;     /* nested: fp32, one per blocksize2 blocks       */
+  const float* offset;      /* nested: one fp32 on the device (QuantState.offset) */
+  const float* code;        /* 16-entry fp32 NF4 code                        */
+  int32_t blocksize;        /* 32, 64, 128 or 256                            */
+  int32_t blocksize2;       /* nested: 256                                   */
+  int32_t nested;           /* 1 = nested (double-quantized), 0 = plain      */
+  int32_t reserved;
+} nf4b_qstate;
+
+/* Unpack one packed NF4 tensor of `numel` values (numel/2 bytes, high nibble
+ * first) into `out` (fp16 or fp32, numel values, row-major).
+ * Replaces dequantize_nf4 (nf4.py:73-92).  */
+int nf4b_dequant(const uint8_t* packed, const nf4b_qstate* qs, void* out, int32_t out_dtype,
+                 int64_t numel, void* stream);
+
+/* One unpack job of a batched sweep.  */
+typedef struct nf4b_dequant_job {
+  const uint8_t* packed;
+  void* out;
+  nf4b_qstate qs;
+  int64_t numel;
+  int32_t out_dtype;
+  int32_t reserved;
+} nf4b_dequant_job;
+
+/* Size in bytes of the device-side plan nf4b_dequant_batched needs for n_jobs jobs.  */
+int64_t nf4b_dequant_plan_bytes(int32_t n_jobs);
+
+/* Build the device-side plan of a batched sweep: validates `jobs` (host array),
+ * copies them and a CTA->job table into `plan_dev` (nf4b_dequant_plan_bytes(n_jobs)
+ * bytes of 16-byte aligned device memory owned by the caller) with one
+ * cudaMemcpyAsync on `stream`, and returns the launch size in *n_ctas.
+ * The plan stays valid while the buffers it names do.  */
+int nf4b_dequant_plan(const nf4b_dequant_job* jobs, int32_t n_jobs, void* plan_dev,
+                      int64_t* n_ctas, void* stream);
+
+/* Unpack every job of a plan in ONE launch (replaces a loop of dequantize_nf4
+ * calls, e.g. the 196 per-step unpacks of tools/bench_nf4.py:47).  */
+int nf4b_dequant_batched(const void* plan_dev, int32_t n_jobs, int64_t n_ctas, void* stream);
+
+/* LoRA adapter operands of a fused linear (peft lora.Linear, r = rank).
+ * A is [rank, in] fp16 (lora_A.weight), B is [out, rank] fp16 (lora_B.weight),
+ * scale = lora_alpha / r.  */
+typedef struct nf4b_lora {
+  const void* a;            /* fp16 [rank, in]                                */
+  const void* b;            /* fp16 [out, rank]                               */
+  float scale;
+  int32_t rank;             /* 16                                             */
+  void* xa;                 /* fwd: optional fp16 [n, rank] output of x A^T (saved for the backward) */
+} nf4b_lora;
+
+/* Y[n, out] = X[n, in] . W^T (+ bias) (+ (X A^T) B^T * scale), W the NF4 weight
+ * [out, in] unpacked on the fly; fp16 in, fp32 accumulate, fp16 out.
+ * Replaces the patched MatMul4Bit.forward (nf4.py:142-159).  */
+int nf4b_linear_fwd(const void* x, const uint8_t* packed, const nf4b_qstate* qs,
+                    const void* bias, const nf4b_lora* lora, void* y,
+                    int64_t n, int64_t in_features, int64_t out_features, void* stream);
+
+/* dX[n, in] = dY[n, out] . W (+ scale * (dY B) A), W re-unpacked on the fly.
+ * Replaces bitsandbytes MatMul4Bit.backward's grad_A (nf4.py:131-133).
+ * `dyb` (fp16 [n, rank]) receives dY . B when lora is given (needed by nf4b_lora_grads).  */
+int nf4b_linear_bwd_dx(const void* dy, const uint8_t* packed, const nf4b_qstate* qs,
+                       const nf4b_lora* lora, void* dyb, void* dx,
+                       int64_t n, int64_t in_features, int64_t out_features, void* stream);
+
+/* LoRA weight gradients (fp32 out, overwritten):
+ *   dA[rank, in]  = scale * (dY B)^T X
+ *   dB[out, rank] = scale * dY^T (X A^T)
+ * x fp16 [n, in], dy fp16 [n, out], xa fp16 [n, rank], dyb fp16 [n, rank].
+ * `work` is caller-provided fp32 scratch of nf4b_lora_grads_work_bytes() bytes.  */
+int64_t nf4b_lora_grads_work_bytes(int64_t n, int64_t in_features, int64_t out_features, int32_t rank);
+int nf4b_lora_grads(const void* x, const void* dy, const void* xa, const void* dyb, float scale,
+                    float* da, float* db, void* work, int64_t n, int64_t in_features,
+                    int64_t out_features, int32_t rank, void* stream);
+
+/* Reads (and with reset != 0 clears) the device-side flag the fused GEMMs set
+ * when a pipeline wait ran out of time (the kernel then ends early instead of
+ * hanging).  0 = no timeout since the last reset.  Synchronous.  */
+int nf4b_gemm_error_flag(int* value, int reset);
+
+/* Human-readable name of a status code.  */
+const char* nf4b_status_string(int status);
+
+/* Library build tag (for logs).  */
+const char* nf4b_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* STEW_NF4_H */

@@ -1,0 +1,122 @@
+"""ctypes binding of libstew_nf4.so (the C ABI declared in include/stew_nf4.h).
+
+The library is built in-tree by stew_b200.build (nvcc, sm_100a).  Loading fails
+loudly when it is missing: there is no CPU or Triton fallback behind this API.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+from . import build as _build
+
+NF4B_OK = 0
+NF4B_ERR_INVALID_ARG = 1
+NF4B_ERR_UNSUPPORTED = 2
+NF4B_ERR_ALIGNMENT = 3
+NF4B_ERR_CUDA = 4
+NF4B_ERR_DEVICE = 5
+NF4B_F16 = 0
+NF4B_F32 = 1
+
+c_void_p = ctypes.c_void_p
+c_int32 = ctypes.c_int32
+c_int64 = ctypes.c_int64
+c_float = ctypes.c_float
+
+
+class QStateC(ctypes.Structure):
+    """nf4b_qstate."""
+    _fields_ = [("absmax8", c_void_p), ("absmax32", c_void_p), ("code2", c_void_p),
+                ("absmax2", c_void_p), ("offset", c_void_p), ("code", c_void_p),
+                ("blocksize", c_int32), ("blocksize2", c_int32), ("nested", c_int32),
+                ("reserved", c_int32)]
+
+
+class DequantJobC(ctypes.Structure):
+    """nf4b_dequant_job."""
+    _fields_ = [("packed", c_void_p), ("out", c_void_p), ("qs", QStateC), ("numel", c_int64),
+                ("out_dtype", c_int32), ("reserved", c_int32)]
+
+
+class LoraC(ctypes.Structure):
+    """nf4b_lora."""
+    _fields_ = [("a", c_void_p), ("b", c_void_p), ("scale", c_float), ("rank", c_int32),
+                ("xa", c_void_p)]
+
+
+# name -> (restype, argtypes); every symbol include/stew_nf4.h declares
+SIGNATURES = {
+    "nf4b_dequant": (c_int32, [c_void_p, ctypes.POINTER(QStateC), c_void_p, c_int32, c_int64, c_void_p]),
+    "nf4b_dequant_plan_bytes": (c_int64, [c_int32]),
+    "nf4b_dequant_plan": (c_int32, [ctypes.POINTER(DequantJobC), c_int32, c_void_p,
+                                    ctypes.POINTER(c_int64), c_void_p]),
+    "nf4b_dequant_batched": (c_int32, [c_void_p, c_int32, c_int64, c_void_p]),
+    "nf4b_linear_fwd": (c_int32, [c_void_p, c_void_p, ctypes.POINTER(QStateC), c_void_p,
+                                  ctypes.POINTER(LoraC), c_void_p, c_int64, c_int64, c_int64, c_void_p]),
+    "nf4b_linear_bwd_dx": (c_int32, [c_void_p, c_void_p, ctypes.POINTER(QStateC),
+                                     ctypes.POINTER(LoraC), c_void_p, c_void_p, c_int64, c_int64,
+                                     c_int64, c_void_p]),
+    "nf4b_lora_grads_work_bytes": (c_int64, [c_int64, c_int64, c_int64, c_int32]),
+    "nf4b_lora_grads": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p,
+                                  c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int32, c_void_p]),
+    "nf4b_gemm_error_flag": (c_int32, [ctypes.POINTER(c_int32), c_int32]),
+    "nf4b_status_string": (ctypes.c_char_p, [c_int32]),
+    "nf4b_version": (ctypes.c_char_p, []),
+}
+
+_LIB = None
+_LOCK = threading.Lock()
+
+
+class NF4Error(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+    def __init__(self, status: int, what: str):
+        self.status = status
+        msg = lib().nf4b_status_string(status).decode() if _LIB is not None else str(status)
+        super().__init__(f"{what}: status {status} ({msg})")
+
+
+class NF4Unsupported(NF4Error):
+    """The input is outside the kernel envelope; nothing was launched."""
+
+
+def lib_path() -> str:
+    return _build.LIB
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library; raises if it has not been built."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    with _LOCK:
+        if _LIB is None:
+            path = lib_path()
+            if not os.path.exists(path):
+                raise RuntimeError(
+                    f"stew_b200 CUDA library not built ({path} missing): run "
+                    "`python -m stew_b200.build` (or __graft_entry__.build())")
+            handle = ctypes.CDLL(path)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.restype = res
+                fn.argtypes = args
+            _LIB = handle
+    return _LIB
+
+
+def check(status: int, what: str) -> None:
+    if status == NF4B_OK:
+        return
+    if status == NF4B_ERR_UNSUPPORTED:
+        raise NF4Unsupported(status, what)
+    raise NF4Error(status, what)
+
+
+def gemm_error_flag(reset: bool = True) -> int:
+    v = c_int32(0)
+    check(lib().nf4b_gemm_error_flag(ctypes.byref(v), 1 if reset else 0), "nf4b_gemm_error_flag")
+    return int(v.value)

@@ -1,0 +1,614 @@
+// Fused NF4 dequant + GEMM on the 5th-gen tensor cores (tcgen05, TMEM, TMA).
+//
+// Forward  (patched MatMul4Bit.forward, solution/nf4.py:142-159 = unpack + F.linear):
+//     Y[n, out]  = X[n, in] . W[out, in]^T (+ bias) (+ (X A^T) (s B)^T)
+// Backward (bitsandbytes MatMul4Bit.backward grad_A on the re-unpacked weight):
+//     dX[n, in]  = dY[n, out] . W[out, in] (+ (dY B) (s A))
+//
+// Both are computed transposed on the tensor core ("swap AB"): the MMA's M side
+// is the weight (128 rows = out features forward, in features backward) and its
+// N side is up to 256 tokens, so a decoded 128 x 64 weight tile feeds 128x256x64
+// MACs and the fp32 accumulator (128 lanes x <=256 columns) uses half of TMEM.
+//   D[m, t] (TMEM) = sum_k Wtile[m, k] . Act[t, k]
+//
+// One CTA computes one 128 x 256 output tile; 6 warps:
+//   warp 0    TMA producer: activation tile [256 tok x 64] fp16 (128B swizzle) and
+//             the packed weight tile (4 KB) per stage, one mbarrier per stage.
+//   warp 1    TMEM allocator + single-thread tcgen05.mma issuer.
+//   warps 2-5 decode the packed tile in registers (nf4_decode.cuh) straight into
+//             the 128B-swizzled fp16 operand layout the MMA reads (K-major forward,
+//             MN-major backward), then drain TMEM in the epilogue.
+// LoRA is one extra K=16 MMA ("slab") into the same accumulator: the rank-16
+// token activations (X A^T or dY B, computed by lora.cu) against the scaled
+// adapter weight, so the adapter adds no pass over the output.
+//
+// Every pipeline wait is bounded (~2 s); on expiry the CTA raises an abort flag,
+// records the failure in g_gemm_error, and winds down without hanging the GPU.
+#include <mutex>
+
+#include "common.cuh"
+#include "nf4_decode.cuh"
+
+namespace nf4b {
+
+constexpr int G_M = 128;       // MMA M: weight rows per tile
+constexpr int G_NMAX = 256;    // MMA N: tokens per tile
+constexpr int G_K = 64;        // K per pipeline stage (one 128-byte swizzle row of fp16)
+constexpr int G_STAGES = 4;
+constexpr int G_DQ_WARPS = 4;
+constexpr int G_THREADS = 64 + 32 * G_DQ_WARPS;
+constexpr int G_TMEM_COLS = 256;
+
+constexpr int SM_X_BYTES = G_NMAX * 128;   // activation stage
+constexpr int SM_A_BYTES = G_M * 128;      // decoded weight stage
+constexpr int SM_P_BYTES = 4096;           // packed weight stage (128 x 32 B or 64 x 64 B)
+constexpr int SM_LA_BYTES = G_M * 32;      // LoRA slab, weight side [128][16] fp16
+constexpr int SM_LB_BYTES = G_NMAX * 32;   // LoRA slab, token side [256][16] fp16
+constexpr int SM_X = 0;
+constexpr int SM_A = SM_X + G_STAGES * SM_X_BYTES;
+constexpr int SM_P = SM_A + G_STAGES * SM_A_BYTES;
+constexpr int SM_LA = SM_P + G_STAGES * SM_P_BYTES;
+constexpr int SM_LB = SM_LA + SM_LA_BYTES;
+constexpr int SM_CODE = SM_LB + SM_LB_BYTES;
+constexpr int SM_BAR = SM_CODE + 64;
+constexpr int G_NUM_BARS = 3 * G_STAGES + 2;
+constexpr int SM_MISC = SM_BAR + G_NUM_BARS * 8;
+constexpr int SM_TOTAL = SM_MISC + 16;
+constexpr int SM_ALLOC = SM_TOTAL + 1024;  // slack to align the base to 1024 B
+static_assert(SM_ALLOC <= 232448, "shared memory budget");
+
+struct GemmArgs {
+  const uint8_t* absmax8;
+  const float* absmax32;
+  const float* code2;
+  const float* absmax2;
+  const float* offset;
+  const float* code;
+  const __half* bias;     // forward only, [out] or null
+  const __half* lora_w;   // forward: lora B [out, 16]; backward: lora A [16, in]
+  const __half* lora_t;   // forward: X A^T [n, 16];   backward: dY B [n, 16]
+  float lora_scale;
+  int32_t has_lora;
+  __half* out;            // forward: Y [n, out]; backward: dX [n, in]
+  int64_t n;
+  int64_t in_f;
+  int64_t out_f;
+  int32_t log2_bs;
+  int32_t nested;
+};
+
+__device__ int g_gemm_error;
+
+constexpr long long kWaitLimitCycles = 4000000000ll;  // ~2 s at 1.9 GHz
+
+__device__ __forceinline__ bool pipe_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      *abort_flag = 1;
+      atomicExch(&g_gemm_error, 1);
+      return false;
+    }
+  }
+  return true;
+}
+
+// Time-bounded wait that ignores the abort flag (used to drain in-flight copies).
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitLimitCycles) {
+      atomicExch(&g_gemm_error, 2);
+      return;
+    }
+  }
+}
+
+// SWIZZLE_NONE K-major descriptor: 8-row x 16-byte core matrices; K-adjacent core
+// matrices `lbo` apart, 8-row groups `sbo` apart.
+__device__ __forceinline__ uint64_t smem_desc_nosw(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr >> 4) & 0x3FFF);
+  d |= uint64_t((lbo >> 4) & 0x3FFF) << 16;
+  d |= uint64_t((sbo >> 4) & 0x3FFF) << 32;
+  d |= uint64_t(1) << 46;
+  return d;
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+// Byte offset of LoRA slab element row `r`, 16-byte chunk `kc` (0/1): [r/8][kc][r%8][16 B].
+__device__ __forceinline__ uint32_t slab_off(int r, int kc) {
+  return uint32_t((r >> 3) * 256 + kc * 128 + (r & 7) * 16);
+}
+
+__device__ __forceinline__ uint4 scale_pack8(uint4 v, float s) {
+  const __half2* h = reinterpret_cast<const __half2*>(&v);
+  uint4 o;
+  uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    op[i] = pack_half2(f.x * s, f.y * s);
+  }
+  return o;
+}
+
+struct ScaleSrc {
+  uint32_t q;   // nested: 8-bit code (or two of them for 32-value blocks)
+  float a;      // nested: second-level absmax; plain: absmax
+  float a_hi;   // plain, 32-value blocks: absmax of the second block
+};
+
+template <bool BS32>
+__device__ __forceinline__ ScaleSrc load_scale_src(const GemmArgs& g, int64_t blk, bool valid) {
+  ScaleSrc s{0u, 0.f, 0.f};
+  if (!valid) return s;
+  if (g.nested) {
+    s.q = __ldg(g.absmax8 + blk);
+    if (BS32) s.q |= uint32_t(__ldg(g.absmax8 + blk + 1)) << 8;
+    s.a = __ldg(g.absmax2 + (blk >> 8));
+    if (BS32) s.a_hi = __ldg(g.absmax2 + ((blk + 1) >> 8));
+  } else {
+    s.a = __ldg(g.absmax32 + blk);
+    if (BS32) s.a_hi = __ldg(g.absmax32 + blk + 1);
+  }
+  return s;
+}
+
+// scale = code2[q] * absmax2 + offset, two separate roundings (nf4.py:39).
+__device__ __forceinline__ float nested_scale(const GemmArgs& g, uint32_t q, float a2, float off) {
+  return __fadd_rn(__fmul_rn(__ldg(g.code2 + q), a2), off);
+}
+
+template <bool BWD, bool BS32>
+__global__ void __launch_bounds__(G_THREADS, 1)
+    nf4_gemm_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_w,
+                    const GemmArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  const uint32_t sbase = smem_u32(smem);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SM_BAR);
+  uint64_t* afull = full + G_STAGES;
+  uint64_t* empty = afull + G_STAGES;
+  uint64_t* lora_bar = empty + G_STAGES;
+  uint64_t* accf = lora_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SM_MISC + 4);
+  float* s_code = reinterpret_cast<float*>(smem + SM_CODE);
+
+  const int64_t m0 = int64_t(blockIdx.x) * G_M;
+  const int64_t t0 = int64_t(blockIdx.y) * G_NMAX;
+  const int tn_real = int(min64(G_NMAX, g.n - t0));
+  const int tn = (tn_real + 15) & ~15;
+  const int64_t kdim = BWD ? g.out_f : g.in_f;
+  const int nk = int(kdim / G_K);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < G_STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&afull[i], G_DQ_WARPS);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(lora_bar, G_DQ_WARPS);
+    mbar_init(accf, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tma_desc(&tm_act);
+    prefetch_tma_desc(&tm_w);
+  }
+  if (threadIdx.x < 16) s_code[threadIdx.x] = __ldg(g.code + threadIdx.x);
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, G_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int k = 0; k < nk; ++k) {
+        const int s = k % G_STAGES;
+        const uint32_t ph = (k / G_STAGES) & 1;
+        if (!pipe_wait(&empty[s], ph ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&full[s], SM_X_BYTES + SM_P_BYTES);
+        tma_load_2d(smem + SM_X + s * SM_X_BYTES, &tm_act, &full[s], k * G_K, int(t0));
+        if (!BWD)
+          tma_load_2d(smem + SM_P + s * SM_P_BYTES, &tm_w, &full[s], k * (G_K / 2), int(m0));
+        else
+          tma_load_2d(smem + SM_P + s * SM_P_BYTES, &tm_w, &full[s], int(m0 / 2), k * G_K);
+        issued = k + 1;
+      }
+      // no bulk copy may still be landing in this CTA's shared memory at exit
+      for (int k = (issued > G_STAGES ? issued - G_STAGES : 0); k < issued; ++k)
+        drain_wait(&full[k % G_STAGES], (k / G_STAGES) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(G_M, tn, BWD, false);
+      const uint32_t idesc_slab = idesc_f16(G_M, tn, false, false);
+      bool acc = false;
+      bool ok = true;
+      if (g.has_lora) {
+        ok = pipe_wait(lora_bar, 0, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          umma_f16(tmem_base, smem_desc_nosw(sbase + SM_LA, 128, 256),
+                   smem_desc_nosw(sbase + SM_LB, 128, 256), idesc_slab, 0u);
+          acc = true;
+        }
+      }
+      for (int k = 0; ok && k < nk; ++k) {
+        const int s = k % G_STAGES;
+        const uint32_t ph = (k / G_STAGES) & 1;
+        if (!pipe_wait(&full[s], ph, abort_flag) || !pipe_wait(&afull[s], ph, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t a_base = sbase + SM_A + s * SM_A_BYTES;
+        const uint32_t x_base = sbase + SM_X + s * SM_X_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < G_K / 16; ++kk) {
+          // K-major 128B swizzle: advance 32 B per 16 K; MN-major: two 8-row atoms.
+          const uint64_t ad = BWD ? smem_desc_sw128(a_base + kk * 2048, 8192, 1024)
+                                  : smem_desc_sw128(a_base + kk * 32, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(x_base + kk * 32, 16, 1024);
+          umma_f16(tmem_base, ad, bd, idesc, (acc || kk > 0) ? 1u : 0u);
+        }
+        acc = true;
+        umma_commit(&empty[s]);
+      }
+      umma_commit(accf);
+    }
+  } else {
+    // ------------------------------------------------- decode + epilogue warps
+    const int d = threadIdx.x - 64;  // 0..127
+    float code[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) code[i] = s_code[i];
+    const float off = g.nested ? __ldg(g.offset) : 0.f;
+
+    if (g.has_lora) {
+      const uint32_t la = sbase + SM_LA;
+      const uint32_t lb = sbase + SM_LB;
+      if (!BWD) {
+        const int64_t o = m0 + d;  // s * B[o, 0:16]
+        uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0;
+        if (o < g.out_f) {
+          const uint4* src = reinterpret_cast<const uint4*>(g.lora_w + o * 16);
+          v0 = scale_pack8(__ldg(src), g.lora_scale);
+          v1 = scale_pack8(__ldg(src + 1), g.lora_scale);
+        }
+        st_shared_v4(la + slab_off(d, 0), v0);
+        st_shared_v4(la + slab_off(d, 1), v1);
+      } else {
+        const int64_t i = m0 + d;  // s * A[0:16, i]
+        float v[16];
+#pragma unroll
+        for (int r = 0; r < 16; ++r)
+          v[r] = (i < g.in_f) ? __half2float(g.lora_w[int64_t(r) * g.in_f + i]) * g.lora_scale : 0.f;
+        st_shared_v4(la + slab_off(d, 0),
+                     make_uint4(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]),
+                                pack_half2(v[4], v[5]), pack_half2(v[6], v[7])));
+        st_shared_v4(la + slab_off(d, 1),
+                     make_uint4(pack_half2(v[8], v[9]), pack_half2(v[10], v[11]),
+                                pack_half2(v[12], v[13]), pack_half2(v[14], v[15])));
+      }
+      // token side: 256 rows x 2 chunks of 16 B
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c = d + 128 * j;
+        const int t = c >> 1, kc = c & 1;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (t < tn_real)
+          v = __ldg(reinterpret_cast<const uint4*>(g.lora_t + (t0 + t) * 16 + kc * 8));
+        st_shared_v4(lb + slab_off(t, kc), v);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(lora_bar);
+    }
+
+    // Per-thread geometry of the decoded tile.
+    //  forward : thread d owns weight row o = m0 + d; K-major row d of the tile.
+    //  backward: thread d owns weight row k*64 + (d & 63), tile columns (d >> 6) * 64 .. +64;
+    //            MN-major: 64-wide M chunk (d >> 6), K row (d & 63).
+    const int r = BWD ? (d & 63) : d;
+    const int j = BWD ? (d >> 6) : 0;
+    const uint32_t p_off = BWD ? uint32_t(r * 64 + j * 32) : uint32_t(d * 32);
+    const uint32_t a_off = uint32_t(j * 8192 + (r >> 3) * 1024 + (r & 7) * 128);
+    const uint32_t key = uint32_t(r & 7);
+    const int64_t col = BWD ? (m0 + 64 * j) : 0;
+    const bool lane_valid = BWD ? (col < g.in_f) : (m0 + d < g.out_f);
+    auto block_of = [&](int k) -> int64_t {
+      const int64_t row = BWD ? int64_t(k) * G_K + r : m0 + d;
+      const int64_t c = BWD ? col : int64_t(k) * G_K;
+      return (row * g.in_f + c) >> g.log2_bs;
+    };
+
+    ScaleSrc cur = load_scale_src<BS32>(g, lane_valid ? block_of(0) : 0, lane_valid && nk > 0);
+    for (int k = 0; k < nk; ++k) {
+      const int s = k % G_STAGES;
+      const uint32_t ph = (k / G_STAGES) & 1;
+      ScaleSrc nxt{0u, 0.f, 0.f};
+      if (k + 1 < nk) nxt = load_scale_src<BS32>(g, lane_valid ? block_of(k + 1) : 0, lane_valid);
+      float sc0, sc1;
+      if (g.nested) {
+        sc0 = lane_valid ? nested_scale(g, cur.q & 0xFFu, cur.a, off) : 0.f;
+        sc1 = (BS32 && lane_valid) ? nested_scale(g, (cur.q >> 8) & 0xFFu, cur.a_hi, off) : sc0;
+      } else {
+        sc0 = cur.a;
+        sc1 = BS32 ? cur.a_hi : cur.a;
+      }
+      const Nf4Table t0tab = make_table(code, sc0);
+      Nf4Table t1tab = t0tab;
+      if (BS32) t1tab = make_table(code, sc1);
+
+      if (!pipe_wait(&full[s], ph, abort_flag)) break;
+      const uint32_t pbase = sbase + SM_P + s * SM_P_BYTES + p_off;
+      const uint4 w0 = ld_shared_v4(pbase);
+      const uint4 w1 = ld_shared_v4(pbase + 16);
+      const uint32_t abase = sbase + SM_A + s * SM_A_BYTES + a_off;
+      const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = decode_word_f16((BS32 && c >= 4) ? t1tab : t0tab, w[c]);
+        st_shared_v4(abase + ((uint32_t(c) ^ key) << 4), v);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&afull[s]);
+      cur = nxt;
+    }
+
+    // ------------------------------------------------------------- epilogue
+    const bool ok = pipe_wait(accf, 0, abort_flag);
+    __syncwarp();  // tcgen05.ld is warp-collective
+    tc_fence_after();
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int64_t row = m0 + 32 * q + lane;
+    const int64_t ld_out = BWD ? g.in_f : g.out_f;
+    const bool row_ok = ok && row < ld_out;
+    const float bias_v = (!BWD && g.bias != nullptr && row_ok) ? __half2float(g.bias[row]) : 0.f;
+    __half* outp = g.out + t0 * ld_out + row;
+    for (int c0 = 0; c0 < tn; c0 += 32) {
+      uint32_t acc[32];
+      tmem_ld_32x32b_x32(tmem_base + (uint32_t(32 * q) << 16) + uint32_t(c0), acc);
+      tmem_ld_wait();
+      if (row_ok) {
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          if (c0 + jj < tn_real)
+            outp[int64_t(c0 + jj) * ld_out] = __float2half_rn(__uint_as_float(acc[jj]) + bias_v);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, G_TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+static int make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                        uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                        CUtensorMapSwizzle sw) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return NF4B_ERR_CUDA;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NF4B_OK : NF4B_ERR_CUDA;
+}
+
+template <bool BWD, bool BS32>
+static int set_smem_attr() {
+  static std::mutex mu;
+  static bool done[64] = {false};
+  int dev = 0;
+  NF4B_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return NF4B_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!done[dev]) {
+    NF4B_CUDA_TRY(cudaFuncSetAttribute(nf4_gemm_kernel<BWD, BS32>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SM_ALLOC));
+    done[dev] = true;
+  }
+  return NF4B_OK;
+}
+
+template <bool BWD, bool BS32>
+static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const GemmArgs& g, dim3 grid,
+                       cudaStream_t s) {
+  int st = set_smem_attr<BWD, BS32>();
+  if (st != NF4B_OK) return st;
+  nf4_gemm_kernel<BWD, BS32><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw, g);
+  return launch_status();
+}
+
+// Validates the shared part of the forward/backward arguments.
+static int gemm_common_checks(const void* act, const uint8_t* packed, const nf4b_qstate* qs,
+                              const void* out, int64_t n, int64_t in_f, int64_t out_f,
+                              int32_t* log2_bs) {
+  NF4B_RETURN_IF(!act || !packed || !qs || !out || !qs->code, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(n < 0 || in_f <= 0 || out_f <= 0, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(in_f % G_K != 0 || out_f % G_K != 0, NF4B_ERR_UNSUPPORTED);
+  NF4B_RETURN_IF(in_f > (1 << 24) || out_f > (1 << 24) || n > (int64_t(1) << 31),
+                 NF4B_ERR_UNSUPPORTED);
+  const int lb = ilog2_exact(qs->blocksize);
+  NF4B_RETURN_IF(lb < 5 || lb > 8, NF4B_ERR_UNSUPPORTED);
+  if (qs->nested) {
+    NF4B_RETURN_IF(!qs->absmax8 || !qs->code2 || !qs->absmax2 || !qs->offset, NF4B_ERR_INVALID_ARG);
+    NF4B_RETURN_IF(qs->blocksize2 != 256, NF4B_ERR_UNSUPPORTED);
+  } else {
+    NF4B_RETURN_IF(!qs->absmax32, NF4B_ERR_INVALID_ARG);
+  }
+  NF4B_RETURN_IF(!aligned(act, 16) || !aligned(packed, 16) || !aligned(out, 2),
+                 NF4B_ERR_ALIGNMENT);
+  *log2_bs = lb;
+  return NF4B_OK;
+}
+
+static void fill_qstate_args(GemmArgs* g, const nf4b_qstate* qs, int32_t log2_bs) {
+  g->absmax8 = qs->absmax8;
+  g->absmax32 = qs->absmax32;
+  g->code2 = qs->code2;
+  g->absmax2 = qs->absmax2;
+  g->offset = qs->offset;
+  g->code = qs->code;
+  g->log2_bs = log2_bs;
+  g->nested = qs->nested ? 1 : 0;
+}
+
+int lora_project16(const void* act, const void* w, int64_t w_stride_r, int64_t w_stride_k,
+                   void* out, int64_t n, int64_t kdim, cudaStream_t s);  // lora.cu
+
+}  // namespace nf4b
+
+using namespace nf4b;
+
+extern "C" int nf4b_linear_fwd(const void* x, const uint8_t* packed, const nf4b_qstate* qs,
+                               const void* bias, const nf4b_lora* lora, void* y, int64_t n,
+                               int64_t in_features, int64_t out_features, void* stream) {
+  int32_t lb = 0;
+  int st = gemm_common_checks(x, packed, qs, y, n, in_features, out_features, &lb);
+  if (st != NF4B_OK) return st;
+  if (lora) {
+    NF4B_RETURN_IF(lora->rank != 16, NF4B_ERR_UNSUPPORTED);
+    NF4B_RETURN_IF(!lora->a || !lora->b || !lora->xa, NF4B_ERR_INVALID_ARG);
+    NF4B_RETURN_IF(!aligned(lora->a, 16) || !aligned(lora->b, 16) || !aligned(lora->xa, 16),
+                   NF4B_ERR_ALIGNMENT);
+  }
+  if (n == 0) return NF4B_OK;
+  st = check_device();
+  if (st != NF4B_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUtensorMap ta, tw;
+  st = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, uint64_t(in_features), uint64_t(n),
+                    uint64_t(in_features) * 2, G_K, G_NMAX, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != NF4B_OK) return st;
+  st = make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, uint64_t(in_features / 2),
+                    uint64_t(out_features), uint64_t(in_features / 2), G_K / 2, G_M,
+                    CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (st != NF4B_OK) return st;
+  GemmArgs g{};
+  fill_qstate_args(&g, qs, lb);
+  g.bias = static_cast<const __half*>(bias);
+  g.out = static_cast<__half*>(y);
+  g.n = n;
+  g.in_f = in_features;
+  g.out_f = out_features;
+  if (lora) {
+    st = lora_project16(x, lora->a, in_features, 1, lora->xa, n, in_features, s);
+    if (st != NF4B_OK) return st;
+    g.has_lora = 1;
+    g.lora_w = static_cast<const __half*>(lora->b);
+    g.lora_t = static_cast<const __half*>(lora->xa);
+    g.lora_scale = lora->scale;
+  }
+  dim3 grid(unsigned((out_features + G_M - 1) / G_M), unsigned((n + G_NMAX - 1) / G_NMAX));
+  NF4B_RETURN_IF(grid.y > 65535u, NF4B_ERR_UNSUPPORTED);
+  return lb == 5 ? launch_gemm<false, true>(ta, tw, g, grid, s)
+                 : launch_gemm<false, false>(ta, tw, g, grid, s);
+}
+
+extern "C" int nf4b_linear_bwd_dx(const void* dy, const uint8_t* packed, const nf4b_qstate* qs,
+                                  const nf4b_lora* lora, void* dyb, void* dx, int64_t n,
+                                  int64_t in_features, int64_t out_features, void* stream) {
+  int32_t lb = 0;
+  int st = gemm_common_checks(dy, packed, qs, dx, n, in_features, out_features, &lb);
+  if (st != NF4B_OK) return st;
+  if (lora) {
+    NF4B_RETURN_IF(lora->rank != 16, NF4B_ERR_UNSUPPORTED);
+    NF4B_RETURN_IF(!lora->a || !lora->b || !dyb, NF4B_ERR_INVALID_ARG);
+    NF4B_RETURN_IF(!aligned(lora->a, 16) || !aligned(lora->b, 16) || !aligned(dyb, 16),
+                   NF4B_ERR_ALIGNMENT);
+  }
+  if (n == 0) return NF4B_OK;
+  st = check_device();
+  if (st != NF4B_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUtensorMap ta, tw;
+  st = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, dy, uint64_t(out_features), uint64_t(n),
+                    uint64_t(out_features) * 2, G_K, G_NMAX, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != NF4B_OK) return st;
+  st = make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, uint64_t(in_features / 2),
+                    uint64_t(out_features), uint64_t(in_features / 2), G_M / 2, G_K,
+                    CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (st != NF4B_OK) return st;
+  GemmArgs g{};
+  fill_qstate_args(&g, qs, lb);
+  g.out = static_cast<__half*>(dx);
+  g.n = n;
+  g.in_f = in_features;
+  g.out_f = out_features;
+  if (lora) {
+    // dY B: B is [out, 16] row-major -> element (r, k=o) at o*16 + r
+    st = lora_project16(dy, lora->b, 1, 16, dyb, n, out_features, s);
+    if (st != NF4B_OK) return st;
+    g.has_lora = 1;
+    g.lora_w = static_cast<const __half*>(lora->a);
+    g.lora_t = static_cast<const __half*>(dyb);
+    g.lora_scale = lora->scale;
+  }
+  dim3 grid(unsigned((in_features + G_M - 1) / G_M), unsigned((n + G_NMAX - 1) / G_NMAX));
+  NF4B_RETURN_IF(grid.y > 65535u, NF4B_ERR_UNSUPPORTED);
+  return lb == 5 ? launch_gemm<true, true>(ta, tw, g, grid, s)
+                 : launch_gemm<true, false>(ta, tw, g, grid, s);
+}
+
+extern "C" int nf4b_gemm_error_flag(int* value, int reset) {
+  NF4B_RETURN_IF(value == nullptr, NF4B_ERR_INVALID_ARG);
+  NF4B_CUDA_TRY(cudaMemcpyFromSymbol(value, g_gemm_error, sizeof(int)));
+  if (reset) {
+    const int zero = 0;
+    NF4B_CUDA_TRY(cudaMemcpyToSymbol(g_gemm_error, &zero, sizeof(int)));
+  }
+  return NF4B_OK;
+}

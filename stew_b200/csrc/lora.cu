@@ -1,0 +1,228 @@
+// LoRA (rank 16) side kernels of the q/v adapter (peft lora.Linear,
+// y = base(x) + lora_B(lora_A(x)) * scaling; the reference keeps peft's module and
+// only touches its input cast, solution/rmsnorm.py:137-150).
+//
+//  lora_project16   out[t, r] = sum_k act[t, k] * W[r, k]       (X A^T forward, dY B backward)
+//                   fp32 accumulate, fp16 result (what peft's fp16 autocast linear yields).
+//                   HBM-bound on `act`: one warp per token row, the 16 x K weight slice
+//                   staged in shared memory, a transposing butterfly reduces the 16 sums.
+//  lora_outer16     G[r, c] = sum_t P[t, r] * Q[t, c]            (the two weight gradients)
+//                   split over tokens; partial sums go to caller-provided scratch and a
+//                   second kernel adds them up and applies the scale.
+#include "common.cuh"
+
+namespace nf4b {
+
+constexpr int LP_THREADS = 256;
+constexpr int LP_TOK_PER_WARP = 4;
+constexpr int LP_TOK_PER_CTA = (LP_THREADS / 32) * LP_TOK_PER_WARP;  // 32
+constexpr int LP_KCHUNK = 1024;                                      // 32 KB of fp16 weights
+
+__global__ void __launch_bounds__(LP_THREADS)
+    lora_project16_kernel(const __half* __restrict__ act, const __half* __restrict__ w, int64_t sr,
+                          int64_t sk, __half* __restrict__ out, int64_t n, int64_t kdim) {
+  __shared__ __align__(16) __half ws[LP_KCHUNK * 16];  // [k][r]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t tbase = int64_t(blockIdx.x) * LP_TOK_PER_CTA + warp * LP_TOK_PER_WARP;
+  float acc[LP_TOK_PER_WARP][16];
+#pragma unroll
+  for (int i = 0; i < LP_TOK_PER_WARP; ++i)
+#pragma unroll
+    for (int r = 0; r < 16; ++r) acc[i][r] = 0.f;
+
+  for (int64_t kc = 0; kc < kdim; kc += LP_KCHUNK) {
+    const int klen = int(min64(LP_KCHUNK, kdim - kc));
+    __syncthreads();
+    for (int e = threadIdx.x; e < klen * 16; e += LP_THREADS) {
+      // element (k, r) with r fastest in smem; read k-fastest when sk == 1 for coalescing
+      int k, r;
+      if (sk == 1) { r = e / klen; k = e - r * klen; } else { k = e >> 4; r = e & 15; }
+      ws[k * 16 + r] = w[int64_t(r) * sr + (kc + k) * sk];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < LP_TOK_PER_WARP; ++i) {
+      const int64_t t = tbase + i;
+      if (t >= n) break;
+      const __half* arow = act + t * kdim + kc;
+      for (int k8 = lane * 8; k8 < klen; k8 += 256) {
+        const uint4 av = __ldg(reinterpret_cast<const uint4*>(arow + k8));
+        const __half* ah = reinterpret_cast<const __half*>(&av);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float a = __half2float(ah[q]);
+          const uint4* wr = reinterpret_cast<const uint4*>(ws + (k8 + q) * 16);
+          const uint4 w0 = wr[0], w1 = wr[1];
+          const __half2* h0 = reinterpret_cast<const __half2*>(&w0);
+          const __half2* h1 = reinterpret_cast<const __half2*>(&w1);
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const float2 f0 = __half22float2(h0[p]);
+            const float2 f1 = __half22float2(h1[p]);
+            acc[i][2 * p] = fmaf(a, f0.x, acc[i][2 * p]);
+            acc[i][2 * p + 1] = fmaf(a, f0.y, acc[i][2 * p + 1]);
+            acc[i][8 + 2 * p] = fmaf(a, f1.x, acc[i][8 + 2 * p]);
+            acc[i][8 + 2 * p + 1] = fmaf(a, f1.y, acc[i][8 + 2 * p + 1]);
+          }
+        }
+      }
+    }
+  }
+  // Transposing butterfly: after it, lanes 2r and 2r+1 hold the full sum for r.
+#pragma unroll
+  for (int i = 0; i < LP_TOK_PER_WARP; ++i) {
+    float* v = acc[i];
+#pragma unroll
+    for (int off = 16, cnt = 8; off >= 2; off >>= 1, cnt >>= 1) {
+      const bool upper = (lane & off) != 0;
+#pragma unroll
+      for (int q = 0; q < cnt; ++q) {
+        const float send = upper ? v[q] : v[q + cnt];
+        const float keep = upper ? v[q + cnt] : v[q];
+        v[q] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+      }
+    }
+    v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+    const int64_t t = tbase + i;
+    if (t < n && (lane & 1) == 0) out[t * 16 + (lane >> 1)] = __float2half_rn(v[0]);
+  }
+}
+
+int lora_project16(const void* act, const void* w, int64_t w_stride_r, int64_t w_stride_k,
+                   void* out, int64_t n, int64_t kdim, cudaStream_t s) {
+  NF4B_RETURN_IF(kdim % 8 != 0, NF4B_ERR_UNSUPPORTED);
+  NF4B_RETURN_IF(!aligned(act, 16), NF4B_ERR_ALIGNMENT);
+  if (n == 0) return NF4B_OK;
+  const int64_t ctas = (n + LP_TOK_PER_CTA - 1) / LP_TOK_PER_CTA;
+  NF4B_RETURN_IF(ctas > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
+  lora_project16_kernel<<<unsigned(ctas), LP_THREADS, 0, s>>>(
+      static_cast<const __half*>(act), static_cast<const __half*>(w), w_stride_r, w_stride_k,
+      static_cast<__half*>(out), n, kdim);
+  return launch_status();
+}
+
+// ---------------------------------------------------------------- weight grads
+constexpr int LO_THREADS = 128;
+constexpr int LO_COLS = 2 * LO_THREADS;  // 256 columns per CTA
+constexpr int LO_TSTAGE = 64;            // token rows of P staged per pass
+constexpr int LO_TARGET_CTAS = 2 * 148;  // two waves' worth of CTAs on a 148-SM B200
+
+static int64_t outer_splits(int64_t n, int64_t cols) {
+  const int64_t col_ctas = (cols + LO_COLS - 1) / LO_COLS;
+  int64_t s = (LO_TARGET_CTAS + col_ctas - 1) / col_ctas;
+  const int64_t max_s = (n + LO_TSTAGE - 1) / LO_TSTAGE;
+  if (s > max_s) s = max_s;
+  return s < 1 ? 1 : s;
+}
+
+// partial[split][r][c] = sum over this split's tokens of P[t, r] * Q[t, c]
+__global__ void __launch_bounds__(LO_THREADS)
+    lora_outer16_kernel(const __half* __restrict__ P, const __half* __restrict__ Q, int64_t n,
+                        int64_t cols, int64_t tok_per_split, float* __restrict__ partial) {
+  __shared__ __align__(16) float ps[LO_TSTAGE * 16];
+  const int64_t c = int64_t(blockIdx.x) * LO_COLS + 2 * threadIdx.x;
+  const int64_t tb = int64_t(blockIdx.y) * tok_per_split;
+  const int64_t te = min64(n, tb + tok_per_split);
+  float acc[16][2];
+#pragma unroll
+  for (int r = 0; r < 16; ++r) acc[r][0] = acc[r][1] = 0.f;
+  const bool cok = c < cols;  // cols is even
+  for (int64_t ts = tb; ts < te; ts += LO_TSTAGE) {
+    const int tl = int(min64(LO_TSTAGE, te - ts));
+    __syncthreads();
+    for (int e = threadIdx.x; e < tl * 16; e += LO_THREADS) ps[e] = __half2float(P[ts * 16 + e]);
+    __syncthreads();
+    if (cok) {
+      for (int t = 0; t < tl; ++t) {
+        const float2 q = __half22float2(*reinterpret_cast<const __half2*>(Q + (ts + t) * cols + c));
+        const float4* pr = reinterpret_cast<const float4*>(ps + t * 16);
+#pragma unroll
+        for (int v4 = 0; v4 < 4; ++v4) {
+          const float4 p = pr[v4];
+          acc[4 * v4 + 0][0] = fmaf(p.x, q.x, acc[4 * v4 + 0][0]);
+          acc[4 * v4 + 0][1] = fmaf(p.x, q.y, acc[4 * v4 + 0][1]);
+          acc[4 * v4 + 1][0] = fmaf(p.y, q.x, acc[4 * v4 + 1][0]);
+          acc[4 * v4 + 1][1] = fmaf(p.y, q.y, acc[4 * v4 + 1][1]);
+          acc[4 * v4 + 2][0] = fmaf(p.z, q.x, acc[4 * v4 + 2][0]);
+          acc[4 * v4 + 2][1] = fmaf(p.z, q.y, acc[4 * v4 + 2][1]);
+          acc[4 * v4 + 3][0] = fmaf(p.w, q.x, acc[4 * v4 + 3][0]);
+          acc[4 * v4 + 3][1] = fmaf(p.w, q.y, acc[4 * v4 + 3][1]);
+        }
+      }
+    }
+  }
+  if (cok) {
+    float* dst = partial + int64_t(blockIdx.y) * 16 * cols + c;
+#pragma unroll
+    for (int r = 0; r < 16; ++r)
+      *reinterpret_cast<float2*>(dst + int64_t(r) * cols) = make_float2(acc[r][0], acc[r][1]);
+  }
+}
+
+// out = scale * sum_s partial[s]; transpose_out: out[c][r] (dB [out, 16]) else out[r][c] (dA).
+__global__ void lora_reduce_kernel(const float* __restrict__ partial, int64_t splits, int64_t cols,
+                                   float scale, int transpose_out, float* __restrict__ out) {
+  const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;  // index into [16][cols]
+  if (e >= 16 * cols) return;
+  float sum = 0.f;
+  for (int64_t s = 0; s < splits; ++s) sum += partial[s * 16 * cols + e];
+  const int64_t r = e / cols, c = e - r * cols;
+  if (transpose_out)
+    out[c * 16 + r] = sum * scale;
+  else
+    out[e] = sum * scale;
+}
+
+static int outer_and_reduce(const __half* P, const __half* Q, int64_t n, int64_t cols, float scale,
+                            int transpose_out, float* out, float* work, cudaStream_t s) {
+  const int64_t splits = outer_splits(n, cols);
+  const int64_t tps = (n + splits - 1) / splits;
+  dim3 grid(unsigned((cols + LO_COLS - 1) / LO_COLS), unsigned(splits));
+  lora_outer16_kernel<<<grid, LO_THREADS, 0, s>>>(P, Q, n, cols, tps, work);
+  int st = launch_status();
+  if (st != NF4B_OK) return st;
+  const int64_t total = 16 * cols;
+  lora_reduce_kernel<<<unsigned((total + 255) / 256), 256, 0, s>>>(work, splits, cols, scale,
+                                                                  transpose_out, out);
+  return launch_status();
+}
+
+}  // namespace nf4b
+
+using namespace nf4b;
+
+extern "C" int64_t nf4b_lora_grads_work_bytes(int64_t n, int64_t in_features, int64_t out_features,
+                                              int32_t rank) {
+  if (n < 0 || in_features <= 0 || out_features <= 0 || rank != 16) return -1;
+  const int64_t a = outer_splits(n, in_features) * 16 * in_features;
+  const int64_t b = outer_splits(n, out_features) * 16 * out_features;
+  return (a > b ? a : b) * int64_t(sizeof(float));
+}
+
+extern "C" int nf4b_lora_grads(const void* x, const void* dy, const void* xa, const void* dyb,
+                               float scale, float* da, float* db, void* work, int64_t n,
+                               int64_t in_features, int64_t out_features, int32_t rank,
+                               void* stream) {
+  NF4B_RETURN_IF(!x || !dy || !xa || !dyb || !da || !db || !work, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(n < 0 || in_features <= 0 || out_features <= 0, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(rank != 16, NF4B_ERR_UNSUPPORTED);
+  NF4B_RETURN_IF(in_features % 2 != 0 || out_features % 2 != 0, NF4B_ERR_UNSUPPORTED);
+  NF4B_RETURN_IF(!aligned(x, 4) || !aligned(dy, 4) || !aligned(xa, 16) || !aligned(dyb, 16) ||
+                     !aligned(work, 8),
+                 NF4B_ERR_ALIGNMENT);
+  int st = check_device();
+  if (st != NF4B_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n == 0) {
+    NF4B_CUDA_TRY(cudaMemsetAsync(da, 0, size_t(16 * in_features) * sizeof(float), s));
+    NF4B_CUDA_TRY(cudaMemsetAsync(db, 0, size_t(16 * out_features) * sizeof(float), s));
+    return NF4B_OK;
+  }
+  // dA[r, i] = s * sum_t dyb[t, r] x[t, i]
+  st = outer_and_reduce(static_cast<const __half*>(dyb), static_cast<const __half*>(x), n,
+                        in_features, scale, 0, da, static_cast<float*>(work), s);
+  if (st != NF4B_OK) return st;
+  // dB[o, r] = s * sum_t dy[t, o] xa[t, r]  (computed as G[r, o], written transposed)
+  return outer_and_reduce(static_cast<const __half*>(xa), static_cast<const __half*>(dy), n,
+                          out_features, scale, 1, db, static_cast<float*>(work), s);
+}

@@ -1,0 +1,196 @@
+"""NF4 base weight + rank-16 LoRA adapter as one fused autograd op.
+
+peft's lora.Linear computes y = base(x) + lora_B(lora_A(dropout(x))) * scaling; on the
+q/v projections of the reference run the base layer is a bitsandbytes Linear4bit NF4
+(r = 16, lora_alpha = 32 -> scaling 2; the reference only touches peft's input cast,
+solution/rmsnorm.py:137-150, and its dropout modules, solution/unpad.py:77-138).
+
+Here the whole thing is three launches forward (x A^T, then one tensor-core GEMM that
+unpacks W and adds the adapter as an extra K=16 slab) and four backward (dY B, the
+fused dX GEMM with the adapter slab, and the two weight-gradient reductions).
+Dropout must be 0 (the configuration this path serves); other adapters use peft's own path.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .nf4 import _qstate, _stream, _supported, linear_backward_dx, linear_forward
+
+LORA_RANK = 16
+
+
+def _lora_c(a16, b16, scale, xa=None) -> _lib.LoraC:
+    c = _lib.LoraC()
+    c.a = a16.data_ptr()
+    c.b = b16.data_ptr()
+    c.scale = float(scale)
+    c.rank = LORA_RANK
+    c.xa = None if xa is None else xa.data_ptr()
+    return c
+
+
+def _fusable(x, st, lora_a, lora_b) -> bool:
+    out_f, in_f = int(st.shape[0]), int(st.shape[1])
+    return (x.dtype == torch.float16 and in_f % 64 == 0 and out_f % 64 == 0
+            and lora_a.shape == (LORA_RANK, in_f) and lora_b.shape == (out_f, LORA_RANK))
+
+
+class NF4LoraFunction(torch.autograd.Function):
+    """y = x W^T (+ bias) + (x A^T) B^T * scaling, W the NF4 weight (packed, st)."""
+
+    @staticmethod
+    def forward(ctx, x, packed, st, bias, lora_a, lora_b, scaling):
+        out_f, in_f = int(st.shape[0]), int(st.shape[1])
+        a16 = lora_a.to(torch.float16).contiguous()
+        b16 = lora_b.to(torch.float16).contiguous()
+        x2 = x.reshape(-1, in_f).contiguous()
+        n = x2.shape[0]
+        Bv = packed.view(-1, 1)
+        y = torch.empty(n, out_f, dtype=torch.float16, device=x.device)
+        xa = torch.empty(n, LORA_RANK, dtype=torch.float16, device=x.device)
+        with torch.cuda.device(x.device):
+            qs = _qstate(st, x.device)
+            lc = _lora_c(a16, b16, scaling, xa)
+            b = None if bias is None else bias.to(torch.float16).contiguous()
+            _lib.check(_lib.lib().nf4b_linear_fwd(
+                x2.data_ptr(), Bv.data_ptr(), ctypes.byref(qs), None if b is None else b.data_ptr(),
+                ctypes.byref(lc), y.data_ptr(), n, in_f, out_f, _stream(x.device)), "nf4b_linear_fwd")
+        ctx.save_for_backward(x2, xa, a16, b16)
+        ctx.st, ctx.Bv, ctx.scaling = st, Bv, float(scaling)
+        ctx.x_shape = x.shape
+        ctx.has_bias = bias is not None
+        ctx.param_dtypes = (lora_a.dtype, lora_b.dtype, None if bias is None else bias.dtype)
+        return y.reshape(*x.shape[:-1], out_f)
+
+    @staticmethod
+    def backward(ctx, grad_y):
+        x2, xa, a16, b16 = ctx.saved_tensors
+        st = ctx.st
+        out_f, in_f = int(st.shape[0]), int(st.shape[1])
+        dy = grad_y.reshape(-1, out_f).to(torch.float16).contiguous()
+        n = dy.shape[0]
+        dev = dy.device
+        need_x, need_a, need_b = ctx.needs_input_grad[0], ctx.needs_input_grad[4], ctx.needs_input_grad[5]
+        dx = da = db = dbias = None
+        dyb = torch.empty(n, LORA_RANK, dtype=torch.float16, device=dev)
+        with torch.cuda.device(dev):
+            qs = _qstate(st, dev)
+            lc = _lora_c(a16, b16, ctx.scaling)
+            L = _lib.lib()
+            dxt = torch.empty(n, in_f, dtype=torch.float16, device=dev)
+            _lib.check(L.nf4b_linear_bwd_dx(dy.data_ptr(), ctx.Bv.data_ptr(), ctypes.byref(qs),
+                                            ctypes.byref(lc), dyb.data_ptr(), dxt.data_ptr(), n, in_f,
+                                            out_f, _stream(dev)), "nf4b_linear_bwd_dx")
+            if need_x:
+                dx = dxt.reshape(ctx.x_shape)
+            if need_a or need_b:
+                da32 = torch.empty(LORA_RANK, in_f, dtype=torch.float32, device=dev)
+                db32 = torch.empty(out_f, LORA_RANK, dtype=torch.float32, device=dev)
+                wb = int(L.nf4b_lora_grads_work_bytes(n, in_f, out_f, LORA_RANK))
+                work = torch.empty(max(wb, 16) // 4 + 4, dtype=torch.float32, device=dev)
+                _lib.check(L.nf4b_lora_grads(x2.data_ptr(), dy.data_ptr(), xa.data_ptr(), dyb.data_ptr(),
+                                             ctx.scaling, da32.data_ptr(), db32.data_ptr(),
+                                             work.data_ptr(), n, in_f, out_f, LORA_RANK, _stream(dev)),
+                           "nf4b_lora_grads")
+                da = da32.to(ctx.param_dtypes[0]) if need_a else None
+                db = db32.to(ctx.param_dtypes[1]) if need_b else None
+        if ctx.has_bias and ctx.needs_input_grad[3]:
+            dbias = dy.float().sum(0).to(ctx.param_dtypes[2])
+        return dx, None, None, dbias, da, db, None
+
+
+def nf4_lora_linear(x, packed, st, lora_a, lora_b, scaling, bias=None):
+    """Functional entry: fused when the envelope allows, else base + adapter composed
+    from the fused base GEMM and plain torch for the adapter."""
+    if _supported(packed, st) and _fusable(x, st, lora_a, lora_b):
+        return NF4LoraFunction.apply(x, packed, st, bias, lora_a, lora_b, scaling)
+    from .nf4 import matmul_4bit
+    y = matmul_4bit(x, packed.t(), st, bias=bias)
+    return y + (x @ lora_a.to(x.dtype).t()) @ lora_b.to(x.dtype).t() * scaling
+
+
+class NF4LoraLinear(torch.nn.Module):
+    """A frozen NF4 Linear with a trainable rank-16 LoRA adapter (peft layout:
+    lora_A.weight [16, in], lora_B.weight [out, 16], scaling = alpha / r)."""
+
+    def __init__(self, packed, quant_state, lora_alpha: float = 32.0, bias=None,
+                 lora_init: str = "kaiming", device=None):
+        super().__init__()
+        out_f, in_f = int(quant_state.shape[0]), int(quant_state.shape[1])
+        self.register_buffer("packed", packed)
+        self.quant_state = quant_state
+        self.bias = bias
+        self.scaling = lora_alpha / LORA_RANK
+        dev = device or packed.device
+        self.lora_A = torch.nn.Parameter(torch.empty(LORA_RANK, in_f, dtype=torch.float32, device=dev))
+        self.lora_B = torch.nn.Parameter(torch.zeros(out_f, LORA_RANK, dtype=torch.float32, device=dev))
+        torch.nn.init.kaiming_uniform_(self.lora_A, a=5 ** 0.5)
+        self.in_features, self.out_features = in_f, out_f
+
+    def forward(self, x):
+        return nf4_lora_linear(x, self.packed, self.quant_state, self.lora_A, self.lora_B,
+                               self.scaling, self.bias)
+
+
+class NF4Linear(torch.nn.Module):
+    """A frozen NF4 Linear without adapter (bitsandbytes Linear4bit.forward contract)."""
+
+    def __init__(self, packed, quant_state, bias=None):
+        super().__init__()
+        self.register_buffer("packed", packed)
+        self.quant_state = quant_state
+        self.bias = bias
+        self.out_features, self.in_features = int(quant_state.shape[0]), int(quant_state.shape[1])
+
+    def forward(self, x):
+        from .nf4 import matmul_4bit
+        return matmul_4bit(x, self.packed.t(), self.quant_state, bias=self.bias)
+
+
+def patch_peft_lora():
+    """Route peft lora.Linear.forward through the fused op for adapters it fits: base layer a
+    bitsandbytes Linear4bit NF4, one active adapter of rank 16, dropout 0 (or identity),
+    not merged.  Everything else keeps peft's forward."""
+    from peft.tuners.lora import layer as L
+
+    cls = L.Linear
+    orig = cls.forward
+    if getattr(orig, "_stew_b200", False):
+        return
+
+    def forward(self, x, *args, **kwargs):
+        try:
+            base = self.get_base_layer()
+            names = list(self.active_adapters)
+        except Exception:  # noqa: BLE001
+            return orig(self, x, *args, **kwargs)
+        if (not args and not kwargs and len(names) == 1 and not getattr(self, "merged", False)
+                and not getattr(self, "disable_adapters", False)):
+            name = names[0]
+            w = getattr(base, "weight", None)
+            st = getattr(w, "quant_state", None)
+            drop = self.lora_dropout[name] if name in self.lora_dropout else None
+            p = getattr(drop, "p", 0.0)
+            if (st is not None and self.r.get(name) == LORA_RANK and p == 0.0
+                    and x.is_cuda and _supported(w, st) and x.dtype == torch.float16):
+                la = self.lora_A[name].weight
+                lb = self.lora_B[name].weight
+                if _fusable(x, st, la, lb):
+                    return NF4LoraFunction.apply(x, w.t(), st, getattr(base, "bias", None), la, lb,
+                                                 self.scaling[name])
+        return orig(self, x, *args, **kwargs)
+
+    forward._stew_b200 = True
+    cls.forward = forward
+
+
+def linear_forward_unfused(x, packed, st, bias=None):
+    """The base layer alone (fused unpack + GEMM)."""
+    return linear_forward(x, packed.view(-1, 1), st, bias)
+
+
+def linear_backward_unfused(dy, packed, st):
+    return linear_backward_dx(dy, packed.view(-1, 1), st)

@@ -1,0 +1,112 @@
+"""CPU: the oracle is pinned to the reference kernel's golden vectors, and the product's
+tables and quantizer agree with the oracle bit for bit."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import nf4_oracle as O
+from tests.helpers import case_inputs, golden, sha
+
+
+def _cases():
+    meta, _ = golden()
+    return meta["cases"]
+
+
+@pytest.mark.parametrize("case", _cases(), ids=lambda c: c["name"])
+def test_oracle_matches_reference_kernel_golden(case):
+    """Oracle restatement of nf4.py:30-50 == reference `_nf4_unpack` (interpreted) outputs."""
+    _, arrays = golden()
+    packed, st = case_inputs(case, arrays)
+    out = O.dequant_nf4(packed, st)
+    assert out.dtype == (np.float16 if case["dtype"] == "float16" else np.float32)
+    assert out.shape == tuple(case["shape"])
+    if case["full"]:
+        ref = arrays[f"{case['name']}/out"]
+        view = np.uint16 if case["dtype"] == "float16" else np.uint32
+        assert np.array_equal(out.view(view), ref.view(view))
+    assert sha(out) == case["sha_out"]
+
+
+def test_golden_covers_reference_test_matrix():
+    """Shapes/blocksizes/nesting of test_nf4_unpack.py:9-14 (plus 32/256 and fp32 out)."""
+    cases = _cases()
+    shapes = {tuple(c["shape"]) for c in cases}
+    assert {(100, 64), (256, 1536), (1536, 1536)} <= shapes
+    assert {c["blocksize"] for c in cases} == {32, 64, 128, 256}
+    assert {c["nested"] for c in cases} == {True, False}
+    assert {c["dtype"] for c in cases} == {"float16", "float32"}
+
+
+def test_nf4_table_matches_paper_construction():
+    assert np.abs(O.nf4_construction() - O.nf4_codebook()).max() < 2e-7
+    t = O.nf4_codebook()
+    assert t[0] == -1.0 and t[7] == 0.0 and t[15] == 1.0 and np.all(np.diff(t) > 0)
+
+
+def test_dynamic_map_properties():
+    m = O.dynamic_map_signed()
+    assert m.shape == (256,) and m.dtype == np.float32
+    assert np.all(np.diff(m) > 0)
+    assert m.max() == 1.0 and 0.0 in m
+    assert np.isclose(m.min(), -0.99296875)
+
+
+def test_product_tables_equal_oracle():
+    from stew_b200 import codebooks
+    assert np.array_equal(codebooks.nf4_table().numpy(), O.nf4_codebook())
+    assert np.array_equal(codebooks.dynamic8_signed().numpy(), O.dynamic_map_signed())
+
+
+@pytest.mark.parametrize("nested", [True, False])
+@pytest.mark.parametrize("shape,bs", [((100, 64), 64), ((64, 512), 32), ((256, 1536), 128),
+                                      ((48, 512), 256)])
+def test_product_quantizer_equals_oracle(nested, shape, bs):
+    """stew_b200.quantize_4bit (torch ops) == oracle.quantize_nf4 (numpy), bit for bit."""
+    from stew_b200 import quantize_4bit
+    rng = np.random.default_rng(7)
+    w = (rng.standard_normal(shape, dtype=np.float32) * 0.02).astype(np.float16)
+    w[0, :4] = 0  # an all-zero run inside a block
+    p_o, s_o = O.quantize_nf4(w, blocksize=bs, nested=nested)
+    p_t, s_t = quantize_4bit(torch.from_numpy(w), blocksize=bs, compress_statistics=nested)
+    assert np.array_equal(p_t.numpy(), p_o)
+    if nested:
+        assert np.array_equal(s_t.absmax.numpy(), s_o.absmax)
+        assert np.array_equal(s_t.state2.absmax.numpy(), s_o.state2.absmax)
+        assert np.float32(s_t.offset.item()) == np.float32(s_o.offset)
+    else:
+        assert np.array_equal(s_t.absmax.numpy(), s_o.absmax)
+
+
+def test_quantize_roundtrip_error_is_bounded():
+    """Decode(quantize(w)) stays within half the widest NF4 gap of each block's absmax."""
+    rng = np.random.default_rng(3)
+    w = (rng.standard_normal((64, 256), dtype=np.float32) * 0.02).astype(np.float16)
+    packed, st = O.quantize_nf4(w, blocksize=64, nested=False)
+    out = O.dequant_nf4(packed, st).astype(np.float32)
+    gap = np.diff(O.nf4_codebook()).max() / 2
+    err = np.abs(out - w.astype(np.float32)).reshape(-1, 64)
+    assert np.all(err <= gap * st.absmax[:, None] * (1 + 1e-3) + 1e-3 * np.abs(w).max())
+
+
+def test_linear_refs_are_consistent():
+    """linear_bwd_ref is the adjoint of linear_fwd_ref (LoRA included)."""
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((5, 64))
+    w = rng.standard_normal((32, 64)).astype(np.float16)
+    a = rng.standard_normal((16, 64))
+    b = rng.standard_normal((32, 16))
+    dy = rng.standard_normal((5, 32))
+    y = O.linear_fwd_ref(x, w, lora_a=a, lora_b=b, scaling=2.0)
+    dx, da, db = O.linear_bwd_ref(dy, w, x=x, lora_a=a, lora_b=b, scaling=2.0)
+    eps = 1e-6
+    # <dy, dY/dx . h> == <dx, h>
+    h = rng.standard_normal(x.shape)
+    y2 = O.linear_fwd_ref(x + eps * h, w, lora_a=a, lora_b=b, scaling=2.0)
+    assert np.isclose(((y2 - y) / eps * dy).sum(), (dx * h).sum(), rtol=1e-5)
+    ha = rng.standard_normal(a.shape)
+    y3 = O.linear_fwd_ref(x, w, lora_a=a + eps * ha, lora_b=b, scaling=2.0)
+    assert np.isclose(((y3 - y) / eps * dy).sum(), (da * ha).sum(), rtol=1e-5)
+    hb = rng.standard_normal(b.shape)
+    y4 = O.linear_fwd_ref(x, w, lora_a=a, lora_b=b + eps * hb, scaling=2.0)
+    assert np.isclose(((y4 - y) / eps * dy).sum(), (db * hb).sum(), rtol=1e-5)
