@@ -133,6 +133,10 @@ int nf4b_lora_grads(const void* x, const void* dy, const void* xa, const void* d
  * hanging).  0 = no timeout since the last reset.  Synchronous.  */
 int nf4b_gemm_error_flag(int* value, int reset);
 
+/* The CUDA error behind the last NF4B_ERR_CUDA returned on the calling host
+ * thread ("<call>: <cudaErrorName> (<description>)"), or "" if none.  */
+const char* nf4b_last_error(void);
+
 /* Human-readable name of a status code.  */
 const char* nf4b_status_string(int status);
 

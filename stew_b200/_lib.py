@@ -63,6 +63,7 @@ SIGNATURES = {
                                   c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int32, c_void_p]),
     "nf4b_gemm_error_flag": (c_int32, [ctypes.POINTER(c_int32), c_int32]),
     "nf4b_status_string": (ctypes.c_char_p, [c_int32]),
+    "nf4b_last_error": (ctypes.c_char_p, []),
     "nf4b_version": (ctypes.c_char_p, []),
 }
 
@@ -76,6 +77,8 @@ class NF4Error(RuntimeError):
     def __init__(self, status: int, what: str):
         self.status = status
         msg = lib().nf4b_status_string(status).decode() if _LIB is not None else str(status)
+        if status == NF4B_ERR_CUDA and _LIB is not None:
+            msg += "; " + _LIB.nf4b_last_error().decode()
         super().__init__(f"{what}: status {status} ({msg})")
 
 

@@ -1,5 +1,22 @@
-// Status strings and build tag of the C ABI.
+// Status strings, error detail and build tag of the C ABI.
+#include <stdio.h>
+
 #include "common.cuh"
+
+namespace nf4b {
+
+static thread_local char g_last_error[256] = "";
+
+void record_cuda_error(const char* where, cudaError_t e) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%s)", where, cudaGetErrorName(e),
+           cudaGetErrorString(e));
+}
+
+void record_driver_error(const char* where, int cu_result) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s: CUresult %d", where, cu_result);
+}
+
+}  // namespace nf4b
 
 extern "C" const char* nf4b_status_string(int status) {
   switch (status) {
@@ -12,5 +29,7 @@ extern "C" const char* nf4b_status_string(int status) {
     default: return "unknown status";
   }
 }
+
+extern "C" const char* nf4b_last_error(void) { return nf4b::g_last_error; }
 
 extern "C" const char* nf4b_version(void) { return "stew_nf4 sm_100a 0.1"; }

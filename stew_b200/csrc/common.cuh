@@ -14,17 +14,27 @@
     if (cond) return (code);       \
   } while (0)
 
-#define NF4B_CUDA_TRY(expr)                         \
-  do {                                              \
-    cudaError_t _e = (expr);                        \
-    if (_e != cudaSuccess) return NF4B_ERR_CUDA;    \
+#define NF4B_CUDA_TRY(expr)                                  \
+  do {                                                       \
+    cudaError_t _e = (expr);                                 \
+    if (_e != cudaSuccess) {                                 \
+      ::nf4b::record_cuda_error(#expr, _e);                  \
+      return NF4B_ERR_CUDA;                                  \
+    }                                                        \
   } while (0)
 
 namespace nf4b {
 
-inline int launch_status() {
+// Remembers (per host thread) which CUDA call failed and why; read through
+// nf4b_last_error().
+void record_cuda_error(const char* where, cudaError_t e);
+void record_driver_error(const char* where, int cu_result);
+
+inline int launch_status(const char* where = "kernel launch") {
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? NF4B_OK : NF4B_ERR_CUDA;
+  if (e == cudaSuccess) return NF4B_OK;
+  record_cuda_error(where, e);
+  return NF4B_ERR_CUDA;
 }
 
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }

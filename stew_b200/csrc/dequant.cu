@@ -206,15 +206,20 @@ static int make_params(const uint8_t* packed, const nf4b_qstate* qs, void* out, 
   return NF4B_OK;
 }
 
+// Resolves the calling thread's device (the context current on the thread, as the
+// caller's framework left it), makes sure that device's primary context is bound to
+// this thread -- a thread can reach us with no current context (e.g. a worker thread
+// whose framework-level device guard was a no-op), and driver-API calls such as the
+// tensor-map encoder need one -- and checks for an sm_100 part.  Cached per thread.
 int check_device() {
   static thread_local int cached_dev = -1;
   static thread_local int cached_ok = 0;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return NF4B_ERR_CUDA;
+  NF4B_CUDA_TRY(cudaGetDevice(&dev));
   if (dev != cached_dev) {
+    NF4B_CUDA_TRY(cudaSetDevice(dev));
     int major = 0;
-    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
-      return NF4B_ERR_CUDA;
+    NF4B_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
     cached_dev = dev;
     cached_ok = (major == 10);
   }

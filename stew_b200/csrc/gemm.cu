@@ -436,7 +436,10 @@ static int make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base
                         uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
                         CUtensorMapSwizzle sw) {
   EncodeTiledFn enc = encode_fn();
-  if (!enc) return NF4B_ERR_CUDA;
+  if (!enc) {
+    record_driver_error("cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)", -1);
+    return NF4B_ERR_CUDA;
+  }
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {row_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
@@ -444,7 +447,11 @@ static int make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base
   CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? NF4B_OK : NF4B_ERR_CUDA;
+  if (r != CUDA_SUCCESS) {
+    record_driver_error("cuTensorMapEncodeTiled", int(r));
+    return NF4B_ERR_CUDA;
+  }
+  return NF4B_OK;
 }
 
 template <bool BWD, bool BS32>
@@ -469,7 +476,7 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const GemmA
   int st = set_smem_attr<BWD, BS32>();
   if (st != NF4B_OK) return st;
   nf4_gemm_kernel<BWD, BS32><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw, g);
-  return launch_status();
+  return launch_status(BWD ? "nf4_gemm_kernel<bwd> launch" : "nf4_gemm_kernel<fwd> launch");
 }
 
 // Validates the shared part of the forward/backward arguments.
