@@ -128,6 +128,22 @@ int nf4b_lora_grads(const void* x, const void* dy, const void* xa, const void* d
                     float* da, float* db, void* work, int64_t n, int64_t in_features,
                     int64_t out_features, int32_t rank, void* stream);
 
+/* nf4b_lora_grads without the `work` argument, for callers that cannot call
+ * cudaMalloc on this path (inside a framework that already holds the device's memory
+ * in its own pool, or in a loop where allocating is not allowed).  It allocates
+ * nothing: its split-token partial sums live in a fixed device array of
+ * NF4B_NOALLOC_SCRATCH_BYTES inside the library, present on every GPU that loads the
+ * library until the process exits.  Problems whose partial sums need more
+ * (nf4b_lora_grads_work_bytes() > NF4B_NOALLOC_SCRATCH_BYTES) return
+ * NF4B_ERR_UNSUPPORTED with a message in nf4b_last_error().  All calls share the
+ * array, so calls that overlap on the GPU race; each call writes all it reads.  The
+ * first call on a device looks up the array's device address; make that first call
+ * before any stream capture.  No counterpart in the reference.  */
+#define NF4B_NOALLOC_SCRATCH_BYTES (8 << 20)
+int nf4b_lora_grads_noalloc(const void* x, const void* dy, const void* xa, const void* dyb,
+                            float scale, float* da, float* db, int64_t n, int64_t in_features,
+                            int64_t out_features, int32_t rank, void* stream);
+
 /* Reads (and with reset != 0 clears) the device-side flag the fused GEMMs set
  * when a pipeline wait ran out of time (the kernel then ends early instead of
  * hanging).  0 = no timeout since the last reset.  Synchronous.  */

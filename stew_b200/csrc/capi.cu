@@ -16,6 +16,8 @@ void record_driver_error(const char* where, int cu_result) {
   snprintf(g_last_error, sizeof(g_last_error), "%s: CUresult %d", where, cu_result);
 }
 
+void record_message(const char* msg) { snprintf(g_last_error, sizeof(g_last_error), "%s", msg); }
+
 }  // namespace nf4b
 
 extern "C" const char* nf4b_status_string(int status) {

@@ -9,6 +9,8 @@
 //  lora_outer16     G[r, c] = sum_t P[t, r] * Q[t, c]            (the two weight gradients)
 //                   split over tokens; partial sums go to caller-provided scratch and a
 //                   second kernel adds them up and applies the scale.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace nf4b {
@@ -225,4 +227,74 @@ extern "C" int nf4b_lora_grads(const void* x, const void* dy, const void* xa, co
   // dB[o, r] = s * sum_t dy[t, o] xa[t, r]  (computed as G[r, o], written transposed)
   return outer_and_reduce(static_cast<const __half*>(xa), static_cast<const __half*>(dy), n,
                           out_features, scale, 1, db, static_cast<float*>(work), s);
+}
+
+// ------------------------------------------------- entry point without allocation
+// For callers that cannot call cudaMalloc on this path -- code running inside a framework that
+// has already reserved the device's memory for its own pool (an allocation behind its back can
+// fail or break its accounting), or a latency-critical loop where allocating is not allowed --
+// nf4b_lora_grads_noalloc keeps its split-token partial sums in this fixed file-scope device
+// array instead of a caller-provided buffer.  Every GPU that loads the library holds these
+// NF4B_NOALLOC_SCRATCH_BYTES until the process exits.  All calls share it: calls that overlap on
+// the GPU (other streams, other host threads) race on it.  Each call writes every partial sum it
+// later reads, so nothing has to start at zero and no clearing is needed.
+namespace nf4b {
+
+static __device__ __align__(256) float g_lora_noalloc_scratch[NF4B_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+void record_message(const char* msg);  // capi.cu
+
+// Device address of the scratch array for the calling thread's current device.  Host code must
+// not hand the symbol itself to a kernel (on the host it names a host-side stand-in), so the
+// address is looked up once per device, with that device current, and cached.
+static int noalloc_scratch(float** out) {
+  static std::mutex mu;
+  static float* addr[64] = {nullptr};
+  int dev = 0;
+  NF4B_CUDA_TRY(cudaGetDevice(&dev));
+  NF4B_RETURN_IF(dev < 0 || dev >= 64, NF4B_ERR_DEVICE);
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    NF4B_CUDA_TRY(cudaGetSymbolAddress(&p, g_lora_noalloc_scratch));
+    addr[dev] = static_cast<float*>(p);
+  }
+  *out = addr[dev];
+  return NF4B_OK;
+}
+
+}  // namespace nf4b
+
+extern "C" int nf4b_lora_grads_noalloc(const void* x, const void* dy, const void* xa,
+                                       const void* dyb, float scale, float* da, float* db,
+                                       int64_t n, int64_t in_features, int64_t out_features,
+                                       int32_t rank, void* stream) {
+  NF4B_RETURN_IF(!x || !dy || !xa || !dyb || !da || !db, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(n < 0 || in_features <= 0 || out_features <= 0, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(rank != 16, NF4B_ERR_UNSUPPORTED);
+  NF4B_RETURN_IF(in_features % 2 != 0 || out_features % 2 != 0, NF4B_ERR_UNSUPPORTED);
+  NF4B_RETURN_IF(!aligned(x, 4) || !aligned(dy, 4) || !aligned(xa, 16) || !aligned(dyb, 16),
+                 NF4B_ERR_ALIGNMENT);
+  const int64_t need = nf4b_lora_grads_work_bytes(n, in_features, out_features, rank);
+  if (need > int64_t(NF4B_NOALLOC_SCRATCH_BYTES)) {
+    record_message("nf4b_lora_grads_noalloc: the split-token partial sums need more than "
+                   "NF4B_NOALLOC_SCRATCH_BYTES; use nf4b_lora_grads with a caller buffer");
+    return NF4B_ERR_UNSUPPORTED;
+  }
+  int st = check_device();
+  if (st != NF4B_OK) return st;
+  float* work = nullptr;
+  st = noalloc_scratch(&work);
+  if (st != NF4B_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n == 0) {
+    NF4B_CUDA_TRY(cudaMemsetAsync(da, 0, size_t(16 * in_features) * sizeof(float), s));
+    NF4B_CUDA_TRY(cudaMemsetAsync(db, 0, size_t(16 * out_features) * sizeof(float), s));
+    return NF4B_OK;
+  }
+  st = outer_and_reduce(static_cast<const __half*>(dyb), static_cast<const __half*>(x), n,
+                        in_features, scale, 0, da, work, s);
+  if (st != NF4B_OK) return st;
+  return outer_and_reduce(static_cast<const __half*>(xa), static_cast<const __half*>(dy), n,
+                          out_features, scale, 1, db, work, s);
 }
