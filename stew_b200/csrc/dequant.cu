@@ -8,7 +8,7 @@
 // fp32 math with one rounding per operation (explicit __fmul_rn / __fadd_rn, so
 // no FMA contraction can change a bit), one rounding to the output dtype.
 //
-// Work split (HBM-bound: 0.5 B in + 2 B out per value, ~1/64 B of scales):
+// General path (fp32 out, unaligned buffers, numel not a multiple of 64), HBM-bound:
 //   one CTA = one chunk of 1024 packed 32-bit words (8192 values); thread t of
 //   the CTA owns words t, t+256, t+512, t+768, so every warp-wide load reads
 //   128 contiguous bytes and every warp-wide fp16 store writes 512 contiguous
@@ -17,12 +17,13 @@
 //   The 16-entry code sits in shared memory (16 distinct words in 16 banks: a
 //   warp's lookups never conflict); the 256-entry second-level code is read
 //   through the read-only cache.
-// The batched variant runs many tensors in one launch: a device-side plan maps
-// each CTA to (job, chunk).
+// The main fp16 path is the chunk kernel further down; its batched variant runs many
+// tensors in one launch from a device-side plan.
 #include <mutex>
 #include <vector>
 
 #include "common.cuh"
+#include "nf4_decode.cuh"
 
 namespace nf4b {
 
@@ -150,28 +151,133 @@ __global__ void __launch_bounds__(DQ_THREADS) nf4_dequant_kernel(const DqParams 
   dequant_chunk<ALIGNED>(p, blockIdx.x, s_code);
 }
 
-// Batched plan layout in device memory:
-//   DqParams params[n_jobs]; int64_t cta_start[n_jobs + 1]
-__global__ void __launch_bounds__(DQ_THREADS)
-    nf4_dequant_batched_kernel(const DqParams* __restrict__ params,
-                               const int64_t* __restrict__ cta_start, int32_t n_jobs) {
-  __shared__ float s_code[16];
-  __shared__ int s_job;
-  const int64_t cta = blockIdx.x;
-  if (threadIdx.x == 0) {
-    int lo = 0, hi = n_jobs - 1;  // last job whose start <= cta
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (__ldg(cta_start + mid) <= cta) lo = mid; else hi = mid - 1;
-    }
-    s_job = lo;
+// ---------------------------------------------------------------- chunk kernel
+// Main path (fp16 out, 16-byte aligned buffers, numel a multiple of 64): one lane owns one
+// 64-value chunk (32 packed bytes, one scale for blocksize >= 64, two for 32), builds the
+// block's 16-entry fp16 table in registers (nf4_decode.cuh: T[i] = fp16(code[i] * scale),
+// bit-identical to the reference's per-value multiply-then-round) and decodes 8 words with
+// byte permutes.  The warp's 32 chunks (4 KB of fp16) go through a per-warp shared buffer,
+// written with the 16-byte slot XOR-swizzled by (lane & 7) and read back transposed, so both
+// sides are bank-conflict free and every global store instruction writes 512 contiguous
+// bytes.  Persistent grid: warps stride over 32-chunk iterations; in the batched kernel a
+// warp's iterations ascend, so its job index only moves forward.
+constexpr int DQ2_THREADS = 256;
+constexpr int DQ2_WARPS = DQ2_THREADS / 32;
+constexpr int DQ2_CHUNKS_PER_ITER = 32;  // one per lane
+constexpr int DQ2_CTAS_PER_SM = 3;       // persistent grid: 24 resident warps per SM
+
+__device__ __forceinline__ void load_code16(const float* code, float (&c)[16]) {
+  const float4* c4 = reinterpret_cast<const float4*>(code);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 v = __ldg(c4 + i);
+    c[4 * i] = v.x; c[4 * i + 1] = v.y; c[4 * i + 2] = v.z; c[4 * i + 3] = v.w;
   }
-  __syncthreads();
-  const int job = s_job;
-  const DqParams& p = params[job];
-  if (threadIdx.x < 16) s_code[threadIdx.x] = __ldg(p.code + threadIdx.x);
-  __syncthreads();
-  dequant_chunk<true>(p, cta - __ldg(cta_start + job), s_code);
+}
+
+// One warp iteration: chunks [iter*32, iter*32+32) of job p.
+__device__ __forceinline__ void dequant_iter_v2(const DqParams& p, int64_t nchunks, int64_t iter,
+                                                const float (&code)[16], uint8_t* wbuf) {
+  const int lane = threadIdx.x & 31;
+  const int64_t ch = iter * DQ2_CHUNKS_PER_ITER + lane;
+  const bool valid = ch < nchunks;
+  uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
+  float s0 = 0.f, s1 = 0.f;
+  if (valid) {
+    const uint4* src = reinterpret_cast<const uint4*>(p.packed + ch * 32);
+    w0 = __ldg(src);
+    w1 = __ldg(src + 1);
+    if (p.log2_bs >= 6) {
+      const int64_t blk = (ch << 6) >> p.log2_bs;
+      s0 = s1 = block_scale(p, blk);
+    } else {  // 32-value blocks: two per chunk
+      s0 = block_scale(p, 2 * ch);
+      s1 = block_scale(p, 2 * ch + 1);
+    }
+  }
+  const Nf4Table t0 = make_table(code, s0);
+  const Nf4Table t1 = (p.log2_bs >= 6) ? t0 : make_table(code, s1);
+  const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  const uint32_t row = smem_u32(wbuf) + uint32_t(lane) * 128u;
+  const uint32_t key = uint32_t(lane & 7);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint4 v = decode_word_f16(j < 4 ? t0 : t1, w[j]);
+    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(row + ((uint32_t(j) ^ key) << 4)),
+                 "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+  }
+  __syncwarp();
+  uint8_t* out = static_cast<uint8_t*>(p.out) + iter * (DQ2_CHUNKS_PER_ITER * 128);
+  const int c = lane & 7;
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const int b = 4 * r + (lane >> 3);  // chunk of this 16-byte piece
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(smem_u32(wbuf) + uint32_t(b) * 128u + ((uint32_t(c) ^ uint32_t(b & 7)) << 4)));
+    if (iter * DQ2_CHUNKS_PER_ITER + b < nchunks) st_cs_u128(out + r * 512 + lane * 16, v);
+  }
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(DQ2_THREADS, DQ2_CTAS_PER_SM) nf4_dequant_chunk_kernel(const DqParams p) {
+  __shared__ __align__(128) uint8_t stage[DQ2_WARPS][4096];
+  const int warp = threadIdx.x >> 5;
+  float code[16];
+  load_code16(p.code, code);
+  const int64_t nchunks = p.nwords >> 3;
+  const int64_t iters = (nchunks + DQ2_CHUNKS_PER_ITER - 1) / DQ2_CHUNKS_PER_ITER;
+  for (int64_t it = int64_t(blockIdx.x) * DQ2_WARPS + warp; it < iters;
+       it += int64_t(gridDim.x) * DQ2_WARPS)
+    dequant_iter_v2(p, nchunks, it, code, stage[warp]);
+}
+
+// Batched plan in device memory: DqParams params[n_jobs]; int64_t iter_start[n_jobs + 1]
+// (prefix sums of 32-chunk iterations).
+__global__ void __launch_bounds__(DQ2_THREADS, DQ2_CTAS_PER_SM)
+    nf4_dequant_batched_kernel(const DqParams* __restrict__ params,
+                               const int64_t* __restrict__ iter_start, int32_t n_jobs) {
+  __shared__ __align__(128) uint8_t stage[DQ2_WARPS][4096];
+  const int warp = threadIdx.x >> 5;
+  const int64_t total = __ldg(iter_start + n_jobs);
+  int job = -1;
+  int64_t job_lo = 0, job_hi = 0, nchunks = 0;
+  DqParams p;
+  float code[16];
+  for (int64_t it = int64_t(blockIdx.x) * DQ2_WARPS + warp; it < total;
+       it += int64_t(gridDim.x) * DQ2_WARPS) {
+    if (it >= job_hi) {  // warp-uniform: advance to the job holding iteration `it`
+      do {
+        ++job;
+        job_lo = __ldg(iter_start + job);
+        job_hi = __ldg(iter_start + job + 1);
+      } while (it >= job_hi && job + 1 < n_jobs);
+      p = params[job];
+      nchunks = p.nwords >> 3;
+      load_code16(p.code, code);
+    }
+    dequant_iter_v2(p, nchunks, it - job_lo, code, stage[warp]);
+  }
+}
+
+static int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = v > 0 ? v : 148;
+  }
+  return cached[dev];
+}
+
+// Chunk-kernel eligibility: fp16 out, whole 64-value chunks, 16-byte aligned buffers.
+static bool chunk_path_ok(const DqParams& p) {
+  return !p.f32out && (p.nwords % 8) == 0 && aligned(p.packed, 16) && aligned(p.out, 16) &&
+         aligned(p.code, 16);
 }
 
 // ------------------------------------------------------------------- host side
@@ -238,10 +344,17 @@ extern "C" int nf4b_dequant(const uint8_t* packed, const nf4b_qstate* qs, void* 
   if (numel == 0) return NF4B_OK;
   st = check_device();
   if (st != NF4B_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (chunk_path_ok(p)) {
+    const int64_t iters = (p.nwords / 8 + DQ2_CHUNKS_PER_ITER - 1) / DQ2_CHUNKS_PER_ITER;
+    const int64_t want = (iters + DQ2_WARPS - 1) / DQ2_WARPS;
+    const int64_t cap = int64_t(sm_count()) * DQ2_CTAS_PER_SM;
+    nf4_dequant_chunk_kernel<<<unsigned(want < cap ? want : cap), DQ2_THREADS, 0, s>>>(p);
+    return launch_status("nf4_dequant_chunk_kernel launch");
+  }
   const int64_t ctas = (p.nwords + DQ_WORDS_PER_CTA - 1) / DQ_WORDS_PER_CTA;
   NF4B_RETURN_IF(ctas > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
   const bool al = aligned(packed, 4) && aligned(out, 16);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (al)
     nf4_dequant_kernel<true><<<unsigned(ctas), DQ_THREADS, 0, s>>>(p);
   else
@@ -267,14 +380,16 @@ extern "C" int nf4b_dequant_plan(const nf4b_dequant_job* jobs, int32_t n_jobs, v
     int st = make_params(jobs[i].packed, &jobs[i].qs, jobs[i].out, jobs[i].out_dtype,
                          jobs[i].numel, &params[i]);
     if (st != NF4B_OK) return st;
-    // the batched kernel has only the vectorised path
-    NF4B_RETURN_IF(!aligned(jobs[i].packed, 4) || !aligned(jobs[i].out, 16), NF4B_ERR_ALIGNMENT);
+    // the batched kernel has only the chunk path: fp16 out, 64-value chunks, aligned buffers
+    NF4B_RETURN_IF(params[i].f32out || params[i].nwords % 8 != 0, NF4B_ERR_UNSUPPORTED);
+    NF4B_RETURN_IF(!chunk_path_ok(params[i]), NF4B_ERR_ALIGNMENT);
     starts[i] = total;
-    total += (params[i].nwords + DQ_WORDS_PER_CTA - 1) / DQ_WORDS_PER_CTA;
+    total += (params[i].nwords / 8 + DQ2_CHUNKS_PER_ITER - 1) / DQ2_CHUNKS_PER_ITER;
   }
   starts[n_jobs] = total;
-  NF4B_RETURN_IF(total > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
-  *n_ctas = total;
+  const int64_t want = (total + DQ2_WARPS - 1) / DQ2_WARPS;
+  const int64_t cap = int64_t(sm_count()) * DQ2_CTAS_PER_SM;
+  *n_ctas = want < cap ? want : cap;
   // A copy from pageable host memory returns once the source has been staged,
   // so the local buffer may be released right after.
   NF4B_CUDA_TRY(cudaMemcpyAsync(plan_dev, host.data(), host.size(), cudaMemcpyHostToDevice,
@@ -292,7 +407,7 @@ extern "C" int nf4b_dequant_batched(const void* plan_dev, int32_t n_jobs, int64_
   const DqParams* params = static_cast<const DqParams*>(plan_dev);
   const int64_t* starts = reinterpret_cast<const int64_t*>(
       static_cast<const uint8_t*>(plan_dev) + size_t(n_jobs) * sizeof(DqParams));
-  nf4_dequant_batched_kernel<<<unsigned(n_ctas), DQ_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+  nf4_dequant_batched_kernel<<<unsigned(n_ctas), DQ2_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
       params, starts, n_jobs);
-  return launch_status();
+  return launch_status("nf4_dequant_batched_kernel launch");
 }

@@ -35,7 +35,7 @@ constexpr int G_M = 128;       // MMA M: weight rows per tile
 constexpr int G_NMAX = 256;    // MMA N: tokens per tile
 constexpr int G_K = 64;        // K per pipeline stage (one 128-byte swizzle row of fp16)
 constexpr int G_STAGES = 4;
-constexpr int G_DQ_WARPS = 4;
+constexpr int G_DQ_WARPS = 8;
 constexpr int G_THREADS = 64 + 32 * G_DQ_WARPS;
 constexpr int G_TMEM_COLS = 256;
 
@@ -148,23 +148,18 @@ __device__ __forceinline__ uint4 scale_pack8(uint4 v, float s) {
 }
 
 struct ScaleSrc {
-  uint32_t q;   // nested: 8-bit code (or two of them for 32-value blocks)
+  uint32_t q;   // nested: 8-bit code
   float a;      // nested: second-level absmax; plain: absmax
-  float a_hi;   // plain, 32-value blocks: absmax of the second block
 };
 
-template <bool BS32>
 __device__ __forceinline__ ScaleSrc load_scale_src(const GemmArgs& g, int64_t blk, bool valid) {
-  ScaleSrc s{0u, 0.f, 0.f};
+  ScaleSrc s{0u, 0.f};
   if (!valid) return s;
   if (g.nested) {
     s.q = __ldg(g.absmax8 + blk);
-    if (BS32) s.q |= uint32_t(__ldg(g.absmax8 + blk + 1)) << 8;
     s.a = __ldg(g.absmax2 + (blk >> 8));
-    if (BS32) s.a_hi = __ldg(g.absmax2 + ((blk + 1) >> 8));
   } else {
     s.a = __ldg(g.absmax32 + blk);
-    if (BS32) s.a_hi = __ldg(g.absmax32 + blk + 1);
   }
   return s;
 }
@@ -174,7 +169,7 @@ __device__ __forceinline__ float nested_scale(const GemmArgs& g, uint32_t q, flo
   return __fadd_rn(__fmul_rn(__ldg(g.code2 + q), a2), off);
 }
 
-template <bool BWD, bool BS32>
+template <bool BWD>
 __global__ void __launch_bounds__(G_THREADS, 1)
     nf4_gemm_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_w,
                     const GemmArgs g) {
@@ -282,7 +277,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     }
   } else {
     // ------------------------------------------------- decode + epilogue warps
-    const int d = threadIdx.x - 64;  // 0..127
+    const int d = threadIdx.x - 64;  // 0..255
     float code[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) code[i] = s_code[i];
@@ -291,7 +286,9 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     if (g.has_lora) {
       const uint32_t la = sbase + SM_LA;
       const uint32_t lb = sbase + SM_LB;
-      if (!BWD) {
+      if (d >= G_M) {
+        // weight side has 128 rows: threads 128..255 only fill the token side
+      } else if (!BWD) {
         const int64_t o = m0 + d;  // s * B[o, 0:16]
         uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0;
         if (o < g.out_f) {
@@ -316,8 +313,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       }
       // token side: 256 rows x 2 chunks of 16 B
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int c = d + 128 * j;
+      for (int j = 0; j < 2; ++j) {
+        const int c = d + 256 * j;
         const int t = c >> 1, kc = c & 1;
         uint4 v = make_uint4(0, 0, 0, 0);
         if (t < tn_real)
@@ -329,51 +326,43 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       if (lane == 0) mbar_arrive(lora_bar);
     }
 
-    // Per-thread geometry of the decoded tile.
-    //  forward : thread d owns weight row o = m0 + d; K-major row d of the tile.
-    //  backward: thread d owns weight row k*64 + (d & 63), tile columns (d >> 6) * 64 .. +64;
-    //            MN-major: 64-wide M chunk (d >> 6), K row (d & 63).
-    const int r = BWD ? (d & 63) : d;
-    const int j = BWD ? (d >> 6) : 0;
-    const uint32_t p_off = BWD ? uint32_t(r * 64 + j * 32) : uint32_t(d * 32);
+    // Per-thread geometry of the decoded tile: 256 threads, 4 packed words (32 values,
+    // always inside one quantization block, so one scale) per thread and stage.
+    //  forward : row d >> 1 of the K-major tile (weight row m0 + (d >> 1)), K half d & 1.
+    //  backward: weight row k*64 + (d & 63) = K row of the MN-major tile; tile columns
+    //            64*(q >> 1) + 32*(q & 1) .. +32 with q = d >> 6 (64-wide M chunk q >> 1).
+    const int r = BWD ? (d & 63) : (d >> 1);
+    const int q = BWD ? (d >> 6) : (d & 1);
+    const int j = BWD ? (q >> 1) : 0;    // 64-wide M chunk (backward)
+    const int hh = BWD ? (q & 1) : q;    // which 4 of the 8 16-byte slots of the row
+    const uint32_t p_off = BWD ? uint32_t(r * 64 + q * 16) : uint32_t(r * 32 + q * 16);
     const uint32_t a_off = uint32_t(j * 8192 + (r >> 3) * 1024 + (r & 7) * 128);
     const uint32_t key = uint32_t(r & 7);
-    const int64_t col = BWD ? (m0 + 64 * j) : 0;
-    const bool lane_valid = BWD ? (col < g.in_f) : (m0 + d < g.out_f);
+    const int64_t col = BWD ? (m0 + 64 * j + 32 * hh) : 0;
+    const bool lane_valid = BWD ? (col < g.in_f) : (m0 + r < g.out_f);
     auto block_of = [&](int k) -> int64_t {
-      const int64_t row = BWD ? int64_t(k) * G_K + r : m0 + d;
-      const int64_t c = BWD ? col : int64_t(k) * G_K;
+      const int64_t row = BWD ? int64_t(k) * G_K + r : m0 + r;
+      const int64_t c = BWD ? col : int64_t(k) * G_K + 32 * hh;
       return (row * g.in_f + c) >> g.log2_bs;
     };
 
-    ScaleSrc cur = load_scale_src<BS32>(g, lane_valid ? block_of(0) : 0, lane_valid && nk > 0);
+    ScaleSrc cur = load_scale_src(g, lane_valid ? block_of(0) : 0, lane_valid && nk > 0);
     for (int k = 0; k < nk; ++k) {
       const int s = k % G_STAGES;
       const uint32_t ph = (k / G_STAGES) & 1;
-      ScaleSrc nxt{0u, 0.f, 0.f};
-      if (k + 1 < nk) nxt = load_scale_src<BS32>(g, lane_valid ? block_of(k + 1) : 0, lane_valid);
-      float sc0, sc1;
-      if (g.nested) {
-        sc0 = lane_valid ? nested_scale(g, cur.q & 0xFFu, cur.a, off) : 0.f;
-        sc1 = (BS32 && lane_valid) ? nested_scale(g, (cur.q >> 8) & 0xFFu, cur.a_hi, off) : sc0;
-      } else {
-        sc0 = cur.a;
-        sc1 = BS32 ? cur.a_hi : cur.a;
-      }
-      const Nf4Table t0tab = make_table(code, sc0);
-      Nf4Table t1tab = t0tab;
-      if (BS32) t1tab = make_table(code, sc1);
+      ScaleSrc nxt{0u, 0.f};
+      if (k + 1 < nk) nxt = load_scale_src(g, lane_valid ? block_of(k + 1) : 0, lane_valid);
+      const float sc = g.nested ? (lane_valid ? nested_scale(g, cur.q, cur.a, off) : 0.f) : cur.a;
+      const Nf4Table tab = make_table(code, sc);
 
       if (!pipe_wait(&full[s], ph, abort_flag)) break;
-      const uint32_t pbase = sbase + SM_P + s * SM_P_BYTES + p_off;
-      const uint4 w0 = ld_shared_v4(pbase);
-      const uint4 w1 = ld_shared_v4(pbase + 16);
+      const uint4 wv = ld_shared_v4(sbase + SM_P + s * SM_P_BYTES + p_off);
       const uint32_t abase = sbase + SM_A + s * SM_A_BYTES + a_off;
-      const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 v = decode_word_f16((BS32 && c >= 4) ? t1tab : t0tab, w[c]);
-        st_shared_v4(abase + ((uint32_t(c) ^ key) << 4), v);
+      for (int c = 0; c < 4; ++c) {
+        const uint4 v = decode_word_f16(tab, w[c]);
+        st_shared_v4(abase + ((uint32_t(4 * hh + c) ^ key) << 4), v);
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -385,15 +374,18 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     const bool ok = pipe_wait(accf, 0, abort_flag);
     __syncwarp();  // tcgen05.ld is warp-collective
     tc_fence_after();
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int64_t row = m0 + 32 * q + lane;
+    // Warp w may only read TMEM lanes 32*(w%4)..+31; the two groups of four warps
+    // (2-5 and 6-9) take alternate 32-column chunks of the accumulator.
+    const int lq = warp & 3;
+    const int grp = (warp - 2) >> 2;
+    const int64_t row = m0 + 32 * lq + lane;
     const int64_t ld_out = BWD ? g.in_f : g.out_f;
     const bool row_ok = ok && row < ld_out;
     const float bias_v = (!BWD && g.bias != nullptr && row_ok) ? __half2float(g.bias[row]) : 0.f;
     __half* outp = g.out + t0 * ld_out + row;
-    for (int c0 = 0; c0 < tn; c0 += 32) {
+    for (int c0 = 32 * grp; c0 < tn; c0 += 64) {
       uint32_t acc[32];
-      tmem_ld_32x32b_x32(tmem_base + (uint32_t(32 * q) << 16) + uint32_t(c0), acc);
+      tmem_ld_32x32b_x32(tmem_base + (uint32_t(32 * lq) << 16) + uint32_t(c0), acc);
       tmem_ld_wait();
       if (row_ok) {
 #pragma unroll
@@ -454,7 +446,7 @@ static int make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base
   return NF4B_OK;
 }
 
-template <bool BWD, bool BS32>
+template <bool BWD>
 static int set_smem_attr() {
   static std::mutex mu;
   static bool done[64] = {false};
@@ -463,19 +455,19 @@ static int set_smem_attr() {
   if (dev < 0 || dev >= 64) return NF4B_ERR_DEVICE;
   std::lock_guard<std::mutex> lock(mu);
   if (!done[dev]) {
-    NF4B_CUDA_TRY(cudaFuncSetAttribute(nf4_gemm_kernel<BWD, BS32>,
+    NF4B_CUDA_TRY(cudaFuncSetAttribute(nf4_gemm_kernel<BWD>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, SM_ALLOC));
     done[dev] = true;
   }
   return NF4B_OK;
 }
 
-template <bool BWD, bool BS32>
+template <bool BWD>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const GemmArgs& g, dim3 grid,
                        cudaStream_t s) {
-  int st = set_smem_attr<BWD, BS32>();
+  int st = set_smem_attr<BWD>();
   if (st != NF4B_OK) return st;
-  nf4_gemm_kernel<BWD, BS32><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw, g);
+  nf4_gemm_kernel<BWD><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw, g);
   return launch_status(BWD ? "nf4_gemm_kernel<bwd> launch" : "nf4_gemm_kernel<fwd> launch");
 }
 
@@ -561,8 +553,7 @@ extern "C" int nf4b_linear_fwd(const void* x, const uint8_t* packed, const nf4b_
   }
   dim3 grid(unsigned((out_features + G_M - 1) / G_M), unsigned((n + G_NMAX - 1) / G_NMAX));
   NF4B_RETURN_IF(grid.y > 65535u, NF4B_ERR_UNSUPPORTED);
-  return lb == 5 ? launch_gemm<false, true>(ta, tw, g, grid, s)
-                 : launch_gemm<false, false>(ta, tw, g, grid, s);
+  return launch_gemm<false>(ta, tw, g, grid, s);
 }
 
 extern "C" int nf4b_linear_bwd_dx(const void* dy, const uint8_t* packed, const nf4b_qstate* qs,
@@ -606,8 +597,7 @@ extern "C" int nf4b_linear_bwd_dx(const void* dy, const uint8_t* packed, const n
   }
   dim3 grid(unsigned((in_features + G_M - 1) / G_M), unsigned((n + G_NMAX - 1) / G_NMAX));
   NF4B_RETURN_IF(grid.y > 65535u, NF4B_ERR_UNSUPPORTED);
-  return lb == 5 ? launch_gemm<true, true>(ta, tw, g, grid, s)
-                 : launch_gemm<true, false>(ta, tw, g, grid, s);
+  return launch_gemm<true>(ta, tw, g, grid, s);
 }
 
 extern "C" int nf4b_gemm_error_flag(int* value, int reset) {
