@@ -5,22 +5,23 @@
 // Backward (bitsandbytes MatMul4Bit.backward grad_A on the re-unpacked weight):
 //     dX[n, in]  = dY[n, out] . W[out, in] (+ (dY B) (s A))
 //
-// Both are computed transposed on the tensor core ("swap AB"): the MMA's M side
-// is the weight (128 rows = out features forward, in features backward) and its
-// N side is up to 256 tokens, so a decoded 128 x 64 weight tile feeds 128x256x64
-// MACs and the fp32 accumulator (128 lanes x <=256 columns) uses half of TMEM.
-//   D[m, t] (TMEM) = sum_k Wtile[m, k] . Act[t, k]
+// Both are computed transposed on the tensor core ("swap AB"): the MMA's M side is
+// the weight (128 rows = out features forward, in features backward) and its N side
+// is up to 256 tokens, so a decoded 128 x 64 weight tile feeds 128x256x64 MACs.
+//   D[m, t] (TMEM, fp32) = sum_k Wtile[m, k] . Act[t, k]
 //
-// One CTA computes one 128 x 256 output tile; 6 warps:
-//   warp 0    TMA producer: activation tile [256 tok x 64] fp16 (128B swizzle) and
-//             the packed weight tile (4 KB) per stage, one mbarrier per stage.
-//   warp 1    TMEM allocator + single-thread tcgen05.mma issuer.
-//   warps 2-5 decode the packed tile in registers (nf4_decode.cuh) straight into
-//             the 128B-swizzled fp16 operand layout the MMA reads (K-major forward,
-//             MN-major backward), then drain TMEM in the epilogue.
-// LoRA is one extra K=16 MMA ("slab") into the same accumulator: the rank-16
-// token activations (X A^T or dY B, computed by lora.cu) against the scaled
-// adapter weight, so the adapter adds no pass over the output.
+// Persistent, warp-specialised: one CTA per SM walks output tiles (128 weight rows x
+// 256 tokens) with stride gridDim.x; the 4-stage shared-memory ring and the stage
+// counters run on across tiles, and the two 256-column accumulators in TMEM alternate
+// between tiles, so a tile's epilogue overlaps the next tile's main loop.
+//   warp 0      TMA producer: activation tile [256 tok x 64] fp16 (128B swizzle) and
+//               the packed weight tile (4 KB) per stage.
+//   warp 1      TMEM allocation (512 columns) + single-thread tcgen05.mma issuer.
+//   warps 2-9   decode the packed tile in registers (nf4_decode.cuh) straight into the
+//               128B-swizzled fp16 operand layout (K-major forward, MN-major backward).
+//   warps 10-13 epilogue: tcgen05.ld of the finished accumulator -> fp16 -> global.
+// LoRA is one extra K=16 MMA ("slab") into the tile's accumulator: the rank-16 token
+// activations (X A^T or dY B, from lora.cu) against the scaled adapter weight.
 //
 // Every pipeline wait is bounded (~2 s); on expiry the CTA raises an abort flag,
 // records the failure in g_gemm_error, and winds down without hanging the GPU.
@@ -36,8 +37,12 @@ constexpr int G_NMAX = 256;    // MMA N: tokens per tile
 constexpr int G_K = 64;        // K per pipeline stage (one 128-byte swizzle row of fp16)
 constexpr int G_STAGES = 4;
 constexpr int G_DQ_WARPS = 8;
-constexpr int G_THREADS = 64 + 32 * G_DQ_WARPS;
-constexpr int G_TMEM_COLS = 256;
+constexpr int G_EPI_WARPS = 8;
+constexpr int G_DQ_WARP0 = 2;
+constexpr int G_EPI_WARP0 = G_DQ_WARP0 + G_DQ_WARPS;  // 10
+constexpr int G_THREADS = 32 * (G_EPI_WARP0 + G_EPI_WARPS);
+constexpr int G_ACC_COLS = 256;                        // one accumulator
+constexpr int G_TMEM_COLS = 2 * G_ACC_COLS;            // double-buffered
 
 constexpr int SM_X_BYTES = G_NMAX * 128;   // activation stage
 constexpr int SM_A_BYTES = G_M * 128;      // decoded weight stage
@@ -51,7 +56,8 @@ constexpr int SM_LA = SM_P + G_STAGES * SM_P_BYTES;
 constexpr int SM_LB = SM_LA + SM_LA_BYTES;
 constexpr int SM_CODE = SM_LB + SM_LB_BYTES;
 constexpr int SM_BAR = SM_CODE + 64;
-constexpr int G_NUM_BARS = 3 * G_STAGES + 2;
+// full[S], afull[S], empty[S], acc_full[2], acc_empty[2], lora_full, lora_empty, mma_done
+constexpr int G_NUM_BARS = 3 * G_STAGES + 7;
 constexpr int SM_MISC = SM_BAR + G_NUM_BARS * 8;
 constexpr int SM_TOTAL = SM_MISC + 16;
 constexpr int SM_ALLOC = SM_TOTAL + 1024;  // slack to align the base to 1024 B
@@ -75,6 +81,8 @@ struct GemmArgs {
   int64_t out_f;
   int32_t log2_bs;
   int32_t nested;
+  int32_t m_tiles;        // 128-row weight tiles
+  int32_t n_tiles;        // 256-token tiles
 };
 
 __device__ int g_gemm_error;
@@ -84,7 +92,7 @@ constexpr long long kWaitLimitCycles = 4000000000ll;  // ~2 s at 1.9 GHz
 __device__ __forceinline__ bool pipe_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
     if (*abort_flag) return false;
     if (clock64() - t0 > kWaitLimitCycles) {
       *abort_flag = 1;
@@ -95,10 +103,10 @@ __device__ __forceinline__ bool pipe_wait(uint64_t* bar, uint32_t parity, volati
   return true;
 }
 
-// Time-bounded wait that ignores the abort flag (used to drain in-flight copies).
+// Time-bounded wait that ignores the abort flag (used to drain in-flight work).
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
     if (clock64() - t0 > kWaitLimitCycles) {
       atomicExch(&g_gemm_error, 2);
       return;
@@ -169,6 +177,24 @@ __device__ __forceinline__ float nested_scale(const GemmArgs& g, uint32_t q, flo
   return __fadd_rn(__fmul_rn(__ldg(g.code2 + q), a2), off);
 }
 
+struct TileCoord {
+  int64_t m0;   // first weight row (forward: out feature; backward: in feature)
+  int64_t t0;   // first token
+  int tn_real;  // tokens in this tile
+  int tn;       // MMA N (tn_real rounded up to 16)
+};
+
+__device__ __forceinline__ TileCoord tile_coord(const GemmArgs& g, int tile) {
+  TileCoord c;
+  const int mt = tile / g.n_tiles;
+  const int nt = tile - mt * g.n_tiles;
+  c.m0 = int64_t(mt) * G_M;
+  c.t0 = int64_t(nt) * G_NMAX;
+  c.tn_real = int(min64(G_NMAX, g.n - c.t0));
+  c.tn = (c.tn_real + 15) & ~15;
+  return c;
+}
+
 template <bool BWD>
 __global__ void __launch_bounds__(G_THREADS, 1)
     nf4_gemm_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_w,
@@ -183,16 +209,16 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + SM_BAR);
   uint64_t* afull = full + G_STAGES;
   uint64_t* empty = afull + G_STAGES;
-  uint64_t* lora_bar = empty + G_STAGES;
-  uint64_t* accf = lora_bar + 1;
+  uint64_t* acc_full = empty + G_STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;     // [2]
+  uint64_t* lora_full = acc_empty + 2;
+  uint64_t* lora_empty = lora_full + 1;
+  uint64_t* mma_done = lora_empty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SM_MISC + 4);
   float* s_code = reinterpret_cast<float*>(smem + SM_CODE);
 
-  const int64_t m0 = int64_t(blockIdx.x) * G_M;
-  const int64_t t0 = int64_t(blockIdx.y) * G_NMAX;
-  const int tn_real = int(min64(G_NMAX, g.n - t0));
-  const int tn = (tn_real + 15) & ~15;
+  const int ntiles = g.m_tiles * g.n_tiles;
   const int64_t kdim = BWD ? g.out_f : g.in_f;
   const int nk = int(kdim / G_K);
 
@@ -202,8 +228,13 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       mbar_init(&afull[i], G_DQ_WARPS);
       mbar_init(&empty[i], 1);
     }
-    mbar_init(lora_bar, G_DQ_WARPS);
-    mbar_init(accf, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], G_EPI_WARPS);
+    }
+    mbar_init(lora_full, G_DQ_WARPS);
+    mbar_init(lora_empty, 1);
+    mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tma_desc(&tm_act);
@@ -222,109 +253,85 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      int issued = 0;
-      for (int k = 0; k < nk; ++k) {
-        const int s = k % G_STAGES;
-        const uint32_t ph = (k / G_STAGES) & 1;
-        if (!pipe_wait(&empty[s], ph ^ 1, abort_flag)) break;
-        mbar_arrive_expect_tx(&full[s], SM_X_BYTES + SM_P_BYTES);
-        tma_load_2d(smem + SM_X + s * SM_X_BYTES, &tm_act, &full[s], k * G_K, int(t0));
-        if (!BWD)
-          tma_load_2d(smem + SM_P + s * SM_P_BYTES, &tm_w, &full[s], k * (G_K / 2), int(m0));
-        else
-          tma_load_2d(smem + SM_P + s * SM_P_BYTES, &tm_w, &full[s], int(m0 / 2), k * G_K);
-        issued = k + 1;
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+        const TileCoord tc = tile_coord(g, tile);
+        for (int k = 0; k < nk; ++k, ++it) {
+          const int s = it % G_STAGES;
+          const uint32_t ph = (it / G_STAGES) & 1;
+          if (!pipe_wait(&empty[s], ph ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], SM_X_BYTES + SM_P_BYTES);
+          tma_load_2d(smem + SM_X + s * SM_X_BYTES, &tm_act, &full[s], k * G_K, int(tc.t0));
+          if (!BWD)
+            tma_load_2d(smem + SM_P + s * SM_P_BYTES, &tm_w, &full[s], k * (G_K / 2), int(tc.m0));
+          else
+            tma_load_2d(smem + SM_P + s * SM_P_BYTES, &tm_w, &full[s], int(tc.m0 / 2), k * G_K);
+        }
       }
       // no bulk copy may still be landing in this CTA's shared memory at exit
-      for (int k = (issued > G_STAGES ? issued - G_STAGES : 0); k < issued; ++k)
-        drain_wait(&full[k % G_STAGES], (k / G_STAGES) & 1);
+      for (uint32_t j = (it > G_STAGES ? it - G_STAGES : 0); j < it; ++j)
+        drain_wait(&full[j % G_STAGES], (j / G_STAGES) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(G_M, tn, BWD, false);
-      const uint32_t idesc_slab = idesc_f16(G_M, tn, false, false);
-      bool acc = false;
+      uint32_t it = 0, lt = 0;
       bool ok = true;
-      if (g.has_lora) {
-        ok = pipe_wait(lora_bar, 0, abort_flag);
-        if (ok) {
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++lt) {
+        const TileCoord tc = tile_coord(g, tile);
+        const uint32_t b = lt & 1;
+        const uint32_t use = lt >> 1;
+        const uint32_t d_tmem = tmem_base + b * G_ACC_COLS;
+        const uint32_t idesc = idesc_f16(G_M, tc.tn, BWD, false);
+        if (!pipe_wait(&acc_empty[b], (use & 1) ^ 1, abort_flag)) break;
+        tc_fence_after();
+        bool acc = false;
+        if (g.has_lora) {
+          if (!pipe_wait(lora_full, lt & 1, abort_flag)) break;
           tc_fence_after();
-          umma_f16(tmem_base, smem_desc_nosw(sbase + SM_LA, 128, 256),
-                   smem_desc_nosw(sbase + SM_LB, 128, 256), idesc_slab, 0u);
+          umma_f16(d_tmem, smem_desc_nosw(sbase + SM_LA, 128, 256),
+                   smem_desc_nosw(sbase + SM_LB, 128, 256), idesc_f16(G_M, tc.tn, false, false), 0u);
+          umma_commit(lora_empty);
           acc = true;
         }
-      }
-      for (int k = 0; ok && k < nk; ++k) {
-        const int s = k % G_STAGES;
-        const uint32_t ph = (k / G_STAGES) & 1;
-        if (!pipe_wait(&full[s], ph, abort_flag) || !pipe_wait(&afull[s], ph, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t a_base = sbase + SM_A + s * SM_A_BYTES;
-        const uint32_t x_base = sbase + SM_X + s * SM_X_BYTES;
+        for (int k = 0; k < nk; ++k, ++it) {
+          const int s = it % G_STAGES;
+          const uint32_t ph = (it / G_STAGES) & 1;
+          if (!pipe_wait(&full[s], ph, abort_flag) || !pipe_wait(&afull[s], ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = sbase + SM_A + s * SM_A_BYTES;
+          const uint32_t x_base = sbase + SM_X + s * SM_X_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < G_K / 16; ++kk) {
-          // K-major 128B swizzle: advance 32 B per 16 K; MN-major: two 8-row atoms.
-          const uint64_t ad = BWD ? smem_desc_sw128(a_base + kk * 2048, 8192, 1024)
-                                  : smem_desc_sw128(a_base + kk * 32, 16, 1024);
-          const uint64_t bd = smem_desc_sw128(x_base + kk * 32, 16, 1024);
-          umma_f16(tmem_base, ad, bd, idesc, (acc || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < G_K / 16; ++kk) {
+            // K-major 128B swizzle: advance 32 B per 16 K; MN-major: two 8-row atoms.
+            const uint64_t ad = BWD ? smem_desc_sw128(a_base + kk * 2048, 8192, 1024)
+                                    : smem_desc_sw128(a_base + kk * 32, 16, 1024);
+            const uint64_t bd = smem_desc_sw128(x_base + kk * 32, 16, 1024);
+            umma_f16(d_tmem, ad, bd, idesc, (acc || kk > 0) ? 1u : 0u);
+          }
+          acc = true;
+          umma_commit(&empty[s]);
         }
-        acc = true;
-        umma_commit(&empty[s]);
+        umma_commit(&acc_full[b]);
       }
-      umma_commit(accf);
+      // every MMA must be complete before TMEM is released
+      umma_commit(mma_done);
+      drain_wait(mma_done, 0);
     }
-  } else {
-    // ------------------------------------------------- decode + epilogue warps
-    const int d = threadIdx.x - 64;  // 0..255
+  } else if (warp < G_EPI_WARP0) {
+    // ------------------------------------------------------------ decode warps
+    const int d = threadIdx.x - 32 * G_DQ_WARP0;  // 0..255
     float code[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) code[i] = s_code[i];
     const float off = g.nested ? __ldg(g.offset) : 0.f;
-
-    if (g.has_lora) {
-      const uint32_t la = sbase + SM_LA;
-      const uint32_t lb = sbase + SM_LB;
-      if (d >= G_M) {
-        // weight side has 128 rows: threads 128..255 only fill the token side
-      } else if (!BWD) {
-        const int64_t o = m0 + d;  // s * B[o, 0:16]
-        uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0;
-        if (o < g.out_f) {
-          const uint4* src = reinterpret_cast<const uint4*>(g.lora_w + o * 16);
-          v0 = scale_pack8(__ldg(src), g.lora_scale);
-          v1 = scale_pack8(__ldg(src + 1), g.lora_scale);
-        }
-        st_shared_v4(la + slab_off(d, 0), v0);
-        st_shared_v4(la + slab_off(d, 1), v1);
-      } else {
-        const int64_t i = m0 + d;  // s * A[0:16, i]
-        float v[16];
-#pragma unroll
-        for (int r = 0; r < 16; ++r)
-          v[r] = (i < g.in_f) ? __half2float(g.lora_w[int64_t(r) * g.in_f + i]) * g.lora_scale : 0.f;
-        st_shared_v4(la + slab_off(d, 0),
-                     make_uint4(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]),
-                                pack_half2(v[4], v[5]), pack_half2(v[6], v[7])));
-        st_shared_v4(la + slab_off(d, 1),
-                     make_uint4(pack_half2(v[8], v[9]), pack_half2(v[10], v[11]),
-                                pack_half2(v[12], v[13]), pack_half2(v[14], v[15])));
-      }
-      // token side: 256 rows x 2 chunks of 16 B
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int c = d + 256 * j;
-        const int t = c >> 1, kc = c & 1;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (t < tn_real)
-          v = __ldg(reinterpret_cast<const uint4*>(g.lora_t + (t0 + t) * 16 + kc * 8));
-        st_shared_v4(lb + slab_off(t, kc), v);
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(lora_bar);
-    }
 
     // Per-thread geometry of the decoded tile: 256 threads, 4 packed words (32 values,
     // always inside one quantization block, so one scale) per thread and stage.
@@ -333,67 +340,140 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     //            64*(q >> 1) + 32*(q & 1) .. +32 with q = d >> 6 (64-wide M chunk q >> 1).
     const int r = BWD ? (d & 63) : (d >> 1);
     const int q = BWD ? (d >> 6) : (d & 1);
-    const int j = BWD ? (q >> 1) : 0;    // 64-wide M chunk (backward)
-    const int hh = BWD ? (q & 1) : q;    // which 4 of the 8 16-byte slots of the row
+    const int j = BWD ? (q >> 1) : 0;  // 64-wide M chunk (backward)
+    const int hh = BWD ? (q & 1) : q;  // which 4 of the 8 16-byte slots of the row
     const uint32_t p_off = BWD ? uint32_t(r * 64 + q * 16) : uint32_t(r * 32 + q * 16);
     const uint32_t a_off = uint32_t(j * 8192 + (r >> 3) * 1024 + (r & 7) * 128);
     const uint32_t key = uint32_t(r & 7);
-    const int64_t col = BWD ? (m0 + 64 * j + 32 * hh) : 0;
-    const bool lane_valid = BWD ? (col < g.in_f) : (m0 + r < g.out_f);
-    auto block_of = [&](int k) -> int64_t {
-      const int64_t row = BWD ? int64_t(k) * G_K + r : m0 + r;
-      const int64_t c = BWD ? col : int64_t(k) * G_K + 32 * hh;
-      return (row * g.in_f + c) >> g.log2_bs;
-    };
 
-    ScaleSrc cur = load_scale_src(g, lane_valid ? block_of(0) : 0, lane_valid && nk > 0);
-    for (int k = 0; k < nk; ++k) {
-      const int s = k % G_STAGES;
-      const uint32_t ph = (k / G_STAGES) & 1;
-      ScaleSrc nxt{0u, 0.f};
-      if (k + 1 < nk) nxt = load_scale_src(g, lane_valid ? block_of(k + 1) : 0, lane_valid);
-      const float sc = g.nested ? (lane_valid ? nested_scale(g, cur.q, cur.a, off) : 0.f) : cur.a;
-      const Nf4Table tab = make_table(code, sc);
-
-      if (!pipe_wait(&full[s], ph, abort_flag)) break;
-      const uint4 wv = ld_shared_v4(sbase + SM_P + s * SM_P_BYTES + p_off);
-      const uint32_t abase = sbase + SM_A + s * SM_A_BYTES + a_off;
-      const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t it = 0, lt = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++lt) {
+      const TileCoord tc = tile_coord(g, tile);
+      if (g.has_lora) {
+        if (!pipe_wait(lora_empty, (lt & 1) ^ 1, abort_flag)) break;
+        const uint32_t la = sbase + SM_LA;
+        const uint32_t lb = sbase + SM_LB;
+        if (d < G_M) {
+          if (!BWD) {
+            const int64_t o = tc.m0 + d;  // s * B[o, 0:16]
+            uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0;
+            if (o < g.out_f) {
+              const uint4* src = reinterpret_cast<const uint4*>(g.lora_w + o * 16);
+              v0 = scale_pack8(__ldg(src), g.lora_scale);
+              v1 = scale_pack8(__ldg(src + 1), g.lora_scale);
+            }
+            st_shared_v4(la + slab_off(d, 0), v0);
+            st_shared_v4(la + slab_off(d, 1), v1);
+          } else {
+            const int64_t i = tc.m0 + d;  // s * A[0:16, i]
+            float v[16];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint4 v = decode_word_f16(tab, w[c]);
-        st_shared_v4(abase + ((uint32_t(4 * hh + c) ^ key) << 4), v);
+            for (int rr = 0; rr < 16; ++rr)
+              v[rr] = (i < g.in_f) ? __half2float(g.lora_w[int64_t(rr) * g.in_f + i]) * g.lora_scale
+                                   : 0.f;
+            st_shared_v4(la + slab_off(d, 0),
+                         make_uint4(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]),
+                                    pack_half2(v[4], v[5]), pack_half2(v[6], v[7])));
+            st_shared_v4(la + slab_off(d, 1),
+                         make_uint4(pack_half2(v[8], v[9]), pack_half2(v[10], v[11]),
+                                    pack_half2(v[12], v[13]), pack_half2(v[14], v[15])));
+          }
+        }
+        // token side: 256 rows x 2 chunks of 16 B
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int c = d + 256 * jj;
+          const int t = c >> 1, kc = c & 1;
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (t < tc.tn_real)
+            v = __ldg(reinterpret_cast<const uint4*>(g.lora_t + (tc.t0 + t) * 16 + kc * 8));
+          st_shared_v4(lb + slab_off(t, kc), v);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(lora_full);
       }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&afull[s]);
-      cur = nxt;
-    }
 
-    // ------------------------------------------------------------- epilogue
-    const bool ok = pipe_wait(accf, 0, abort_flag);
-    __syncwarp();  // tcgen05.ld is warp-collective
-    tc_fence_after();
-    // Warp w may only read TMEM lanes 32*(w%4)..+31; the two groups of four warps
-    // (2-5 and 6-9) take alternate 32-column chunks of the accumulator.
-    const int lq = warp & 3;
-    const int grp = (warp - 2) >> 2;
-    const int64_t row = m0 + 32 * lq + lane;
-    const int64_t ld_out = BWD ? g.in_f : g.out_f;
-    const bool row_ok = ok && row < ld_out;
-    const float bias_v = (!BWD && g.bias != nullptr && row_ok) ? __half2float(g.bias[row]) : 0.f;
-    __half* outp = g.out + t0 * ld_out + row;
-    for (int c0 = 32 * grp; c0 < tn; c0 += 64) {
-      uint32_t acc[32];
-      tmem_ld_32x32b_x32(tmem_base + (uint32_t(32 * lq) << 16) + uint32_t(c0), acc);
-      tmem_ld_wait();
-      if (row_ok) {
+      const int64_t col = BWD ? (tc.m0 + 64 * j + 32 * hh) : 0;
+      const bool lane_valid = BWD ? (col < g.in_f) : (tc.m0 + r < g.out_f);
+      auto block_of = [&](int k) -> int64_t {
+        const int64_t row = BWD ? int64_t(k) * G_K + r : tc.m0 + r;
+        const int64_t c = BWD ? col : int64_t(k) * G_K + 32 * hh;
+        return (row * g.in_f + c) >> g.log2_bs;
+      };
+      ScaleSrc cur = load_scale_src(g, lane_valid ? block_of(0) : 0, lane_valid && nk > 0);
+      for (int k = 0; k < nk; ++k, ++it) {
+        const int s = it % G_STAGES;
+        const uint32_t ph = (it / G_STAGES) & 1;
+        ScaleSrc nxt{0u, 0.f};
+        if (k + 1 < nk) nxt = load_scale_src(g, lane_valid ? block_of(k + 1) : 0, lane_valid);
+        const float sc = g.nested ? (lane_valid ? nested_scale(g, cur.q, cur.a, off) : 0.f) : cur.a;
+        const Nf4Table tab = make_table(code, sc);
+
+        if (!pipe_wait(&full[s], ph, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint4 wv = ld_shared_v4(sbase + SM_P + s * SM_P_BYTES + p_off);
+        const uint32_t abase = sbase + SM_A + s * SM_A_BYTES + a_off;
+        const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          if (c0 + jj < tn_real)
-            outp[int64_t(c0 + jj) * ld_out] = __float2half_rn(__uint_as_float(acc[jj]) + bias_v);
+        for (int c = 0; c < 4; ++c) {
+          const uint4 v = decode_word_f16(tab, w[c]);
+          st_shared_v4(abase + ((uint32_t(4 * hh + c) ^ key) << 4), v);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[s]);
+        cur = nxt;
+      }
+    }
+  } else {
+    // --------------------------------------------------------------- epilogue
+    // Warp w may only read TMEM lanes 32*(w%4)..+31 (the tile's weight rows); the two
+    // groups of four warps take alternate 32-column chunks.  Lanes 2i and 2i+1 hold
+    // adjacent weight rows, i.e. adjacent output columns, so one shuffle per pair of
+    // tokens lets each lane store a 4-byte half2: the even lane writes token j, the odd
+    // lane token j+1.
+    const int lq = warp & 3;
+    const int grp = (warp - G_EPI_WARP0) >> 2;
+    const bool odd = (lane & 1) != 0;
+    const int64_t ld_out = BWD ? g.in_f : g.out_f;
+    uint32_t lt = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++lt) {
+      const TileCoord tc = tile_coord(g, tile);
+      const uint32_t b = lt & 1;
+      const uint32_t use = lt >> 1;
+      // warp-uniform: tcgen05.ld below is warp-collective
+      const bool ok = __all_sync(0xffffffffu, pipe_wait(&acc_full[b], use & 1, abort_flag));
+      tc_fence_after();
+      if (!ok) break;
+      const int64_t row = tc.m0 + 32 * lq + lane;
+      const bool row_ok = row < ld_out;  // ld_out is a multiple of 64: pairs are all in or out
+      const float bias_v = (!BWD && g.bias != nullptr && row_ok) ? __half2float(g.bias[row]) : 0.f;
+      // the even lane of a pair writes columns (row, row+1) of token j; the odd lane the
+      // same two columns of token j+1
+      uint32_t* outp = reinterpret_cast<uint32_t*>(g.out + tc.t0 * ld_out + (row & ~int64_t(1)));
+      const uint32_t taddr = tmem_base + (uint32_t(32 * lq) << 16) + b * G_ACC_COLS;
+      for (int c0 = 32 * grp; c0 < tc.tn; c0 += 64) {
+        uint32_t acc[32];
+        tmem_ld_32x32b_x32(taddr + uint32_t(c0), acc);
+        tmem_ld_wait();
+#pragma unroll
+        for (int jj = 0; jj < 32; jj += 2) {
+          const float v0 = __uint_as_float(acc[jj]) + bias_v;      // token c0+jj
+          const float v1 = __uint_as_float(acc[jj + 1]) + bias_v;  // token c0+jj+1
+          // even lane sends its token-(j+1) value, odd lane its token-j value
+          const float other = __shfl_xor_sync(0xffffffffu, odd ? v0 : v1, 1);
+          const int tok = c0 + jj + (odd ? 1 : 0);
+          const uint32_t h = odd ? pack_half2(other, v1) : pack_half2(v0, other);
+          if (row_ok && tok < tc.tn_real) outp[(int64_t(tok) * ld_out) >> 1] = h;
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
   }
 
@@ -446,6 +526,18 @@ static int make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base
   return NF4B_OK;
 }
 
+static int sm_count_cached() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = v > 0 ? v : 148;
+  }
+  return cached[dev];
+}
+
 template <bool BWD>
 static int set_smem_attr() {
   static std::mutex mu;
@@ -462,11 +554,20 @@ static int set_smem_attr() {
   return NF4B_OK;
 }
 
+// One persistent CTA per SM (at most one per tile).
 template <bool BWD>
-static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const GemmArgs& g, dim3 grid,
+static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, GemmArgs g, int64_t m_rows,
                        cudaStream_t s) {
   int st = set_smem_attr<BWD>();
   if (st != NF4B_OK) return st;
+  const int64_t m_tiles = (m_rows + G_M - 1) / G_M;
+  const int64_t n_tiles = (g.n + G_NMAX - 1) / G_NMAX;
+  NF4B_RETURN_IF(m_tiles * n_tiles > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
+  g.m_tiles = int32_t(m_tiles);
+  g.n_tiles = int32_t(n_tiles);
+  const int64_t tiles = m_tiles * n_tiles;
+  const int64_t sms = sm_count_cached();
+  const unsigned grid = unsigned(tiles < sms ? tiles : sms);
   nf4_gemm_kernel<BWD><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw, g);
   return launch_status(BWD ? "nf4_gemm_kernel<bwd> launch" : "nf4_gemm_kernel<fwd> launch");
 }
@@ -488,7 +589,7 @@ static int gemm_common_checks(const void* act, const uint8_t* packed, const nf4b
   } else {
     NF4B_RETURN_IF(!qs->absmax32, NF4B_ERR_INVALID_ARG);
   }
-  NF4B_RETURN_IF(!aligned(act, 16) || !aligned(packed, 16) || !aligned(out, 2),
+  NF4B_RETURN_IF(!aligned(act, 16) || !aligned(packed, 16) || !aligned(out, 4),
                  NF4B_ERR_ALIGNMENT);
   *log2_bs = lb;
   return NF4B_OK;
@@ -551,9 +652,7 @@ extern "C" int nf4b_linear_fwd(const void* x, const uint8_t* packed, const nf4b_
     g.lora_t = static_cast<const __half*>(lora->xa);
     g.lora_scale = lora->scale;
   }
-  dim3 grid(unsigned((out_features + G_M - 1) / G_M), unsigned((n + G_NMAX - 1) / G_NMAX));
-  NF4B_RETURN_IF(grid.y > 65535u, NF4B_ERR_UNSUPPORTED);
-  return launch_gemm<false>(ta, tw, g, grid, s);
+  return launch_gemm<false>(ta, tw, g, out_features, s);
 }
 
 extern "C" int nf4b_linear_bwd_dx(const void* dy, const uint8_t* packed, const nf4b_qstate* qs,
@@ -595,9 +694,7 @@ extern "C" int nf4b_linear_bwd_dx(const void* dy, const uint8_t* packed, const n
     g.lora_t = static_cast<const __half*>(dyb);
     g.lora_scale = lora->scale;
   }
-  dim3 grid(unsigned((in_features + G_M - 1) / G_M), unsigned((n + G_NMAX - 1) / G_NMAX));
-  NF4B_RETURN_IF(grid.y > 65535u, NF4B_ERR_UNSUPPORTED);
-  return launch_gemm<true>(ta, tw, g, grid, s);
+  return launch_gemm<true>(ta, tw, g, in_features, s);
 }
 
 extern "C" int nf4b_gemm_error_flag(int* value, int reset) {
