@@ -54,8 +54,9 @@ constexpr int SM_A = SM_X + G_STAGES * SM_X_BYTES;
 constexpr int SM_P = SM_A + G_STAGES * SM_A_BYTES;
 constexpr int SM_LA = SM_P + G_STAGES * SM_P_BYTES;
 constexpr int SM_LB = SM_LA + SM_LA_BYTES;
-constexpr int SM_CODE = SM_LB + SM_LB_BYTES;
-constexpr int SM_BAR = SM_CODE + 64;
+constexpr int SM_CODE = SM_LB + SM_LB_BYTES;   // 16 fp32 NF4 code
+constexpr int SM_CODE2 = SM_CODE + 64;         // 256 fp32 second-level code
+constexpr int SM_BAR = SM_CODE2 + 1024;
 // full[S], afull[S], empty[S], acc_full[2], acc_empty[2], lora_full, lora_empty, mma_done
 constexpr int G_NUM_BARS = 3 * G_STAGES + 7;
 constexpr int SM_MISC = SM_BAR + G_NUM_BARS * 8;
@@ -172,11 +173,6 @@ __device__ __forceinline__ ScaleSrc load_scale_src(const GemmArgs& g, int64_t bl
   return s;
 }
 
-// scale = code2[q] * absmax2 + offset, two separate roundings (nf4.py:39).
-__device__ __forceinline__ float nested_scale(const GemmArgs& g, uint32_t q, float a2, float off) {
-  return __fadd_rn(__fmul_rn(__ldg(g.code2 + q), a2), off);
-}
-
 struct TileCoord {
   int64_t m0;   // first weight row (forward: out feature; backward: in feature)
   int64_t t0;   // first token
@@ -217,6 +213,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SM_MISC + 4);
   float* s_code = reinterpret_cast<float*>(smem + SM_CODE);
+  float* s_code2 = reinterpret_cast<float*>(smem + SM_CODE2);
 
   const int ntiles = g.m_tiles * g.n_tiles;
   const int64_t kdim = BWD ? g.out_f : g.in_f;
@@ -241,6 +238,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     prefetch_tma_desc(&tm_w);
   }
   if (threadIdx.x < 16) s_code[threadIdx.x] = __ldg(g.code + threadIdx.x);
+  if (g.nested && threadIdx.x < 256) s_code2[threadIdx.x] = __ldg(g.code2 + threadIdx.x);
   if (warp == 1) {
     tmem_alloc(tmem_slot, G_TMEM_COLS);
     tmem_relinquish();
@@ -342,7 +340,11 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     const int q = BWD ? (d >> 6) : (d & 1);
     const int j = BWD ? (q >> 1) : 0;  // 64-wide M chunk (backward)
     const int hh = BWD ? (q & 1) : q;  // which 4 of the 8 16-byte slots of the row
-    const uint32_t p_off = BWD ? uint32_t(r * 64 + q * 16) : uint32_t(r * 32 + q * 16);
+    // Packed tile: forward rows of 32 B (unswizzled, already conflict-free); backward rows
+    // of 64 B loaded with the 64B swizzle (16-byte chunk c of row r at c ^ ((r >> 1) & 3)),
+    // so a warp's 8-row phase reads 8 different bank groups.
+    const uint32_t p_off = BWD ? uint32_t(r * 64 + ((q ^ ((r >> 1) & 3)) * 16))
+                               : uint32_t(r * 32 + q * 16);
     const uint32_t a_off = uint32_t(j * 8192 + (r >> 3) * 1024 + (r & 7) * 128);
     const uint32_t key = uint32_t(r & 7);
 
@@ -397,19 +399,28 @@ __global__ void __launch_bounds__(G_THREADS, 1)
 
       const int64_t col = BWD ? (tc.m0 + 64 * j + 32 * hh) : 0;
       const bool lane_valid = BWD ? (col < g.in_f) : (tc.m0 + r < g.out_f);
-      auto block_of = [&](int k) -> int64_t {
-        const int64_t row = BWD ? int64_t(k) * G_K + r : tc.m0 + r;
-        const int64_t c = BWD ? col : int64_t(k) * G_K + 32 * hh;
-        return (row * g.in_f + c) >> g.log2_bs;
+      // Element offset (row * in + column) of this thread's first value at stage k, and
+      // its quantization block; stages step by 64 columns forward, 64 rows backward.
+      const int64_t e_step = BWD ? int64_t(G_K) * g.in_f : int64_t(G_K);
+      int64_t e_pos = BWD ? int64_t(r) * g.in_f + col : (tc.m0 + r) * g.in_f + 32 * hh;
+      auto scale_of = [&](const ScaleSrc& s) -> float {
+        if (!lane_valid) return 0.f;
+        return g.nested ? __fadd_rn(__fmul_rn(s_code2[s.q], s.a), off) : s.a;
       };
-      ScaleSrc cur = load_scale_src(g, lane_valid ? block_of(0) : 0, lane_valid && nk > 0);
+      // Scale pipeline: the stage's scale is ready before its data arrives, the next
+      // stage's is computed while this one decodes, and the raw absmax of the stage
+      // after that is in flight.
+      float sc = scale_of(load_scale_src(g, e_pos >> g.log2_bs, lane_valid && nk > 0));
+      e_pos += e_step;
+      ScaleSrc raw1 = load_scale_src(g, e_pos >> g.log2_bs, lane_valid && nk > 1);
+      e_pos += e_step;
       for (int k = 0; k < nk; ++k, ++it) {
         const int s = it % G_STAGES;
         const uint32_t ph = (it / G_STAGES) & 1;
-        ScaleSrc nxt{0u, 0.f};
-        if (k + 1 < nk) nxt = load_scale_src(g, lane_valid ? block_of(k + 1) : 0, lane_valid);
-        const float sc = g.nested ? (lane_valid ? nested_scale(g, cur.q, cur.a, off) : 0.f) : cur.a;
         const Nf4Table tab = make_table(code, sc);
+        const ScaleSrc raw2 = load_scale_src(g, e_pos >> g.log2_bs, lane_valid && k + 2 < nk);
+        e_pos += e_step;
+        const float sc1 = scale_of(raw1);
 
         if (!pipe_wait(&full[s], ph, abort_flag)) {
           ok = false;
@@ -426,7 +437,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&afull[s]);
-        cur = nxt;
+        sc = sc1;
+        raw1 = raw2;
       }
     }
   } else {
@@ -677,7 +689,7 @@ extern "C" int nf4b_linear_bwd_dx(const void* dy, const uint8_t* packed, const n
   if (st != NF4B_OK) return st;
   st = make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, uint64_t(in_features / 2),
                     uint64_t(out_features), uint64_t(in_features / 2), G_M / 2, G_K,
-                    CU_TENSOR_MAP_SWIZZLE_NONE);
+                    CU_TENSOR_MAP_SWIZZLE_64B);
   if (st != NF4B_OK) return st;
   GemmArgs g{};
   fill_qstate_args(&g, qs, lb);
