@@ -335,6 +335,8 @@ def main():
     ap.add_argument("--gemm-n", type=str, default="1170,2048,8192")
     ap.add_argument("--gemm-steps", type=int, default=5)
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--step-steps", type=int, default=5)
+    ap.add_argument("--no-step", action="store_true")
     ap.add_argument("--no-gemm", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -380,6 +382,30 @@ def main():
             res["launches_per_pass"] = gp.run(fwd=True, bwd=True, lora=True)
             gemm["passes"][str(n)] = res
             del gp
+        torch.cuda.synchronize()
+
+    # ---- the full QLoRA step (28 layers, packed rows, LoRA-grad all-reduce across ranks)
+    step = None
+    if not args.no_step and args.layers == 28:
+        from stew_b200.qlora_step import QLoRATrainer, QwenConfig, QwenQLoRA, step_flops, synthetic_batch
+        model = QwenQLoRA(QwenConfig(), device="cuda", seed=0, weights=weights)
+        trainer = QLoRATrainer(model)
+        tokens, lengths = synthetic_batch(seed=1000 + rank)
+        real = torch.tensor([float(lengths.sum())], device="cuda")
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(real)
+        t = _timed(world, lambda: trainer.step(tokens, lengths), args.step_steps, 2) / args.step_steps
+        fl = step_flops(model.cfg, int(lengths.sum()))
+        step = {"workload": "Qwen2.5-1.5B QLoRA step: 28 layers, NF4 projections, LoRA r=16 on q/v, "
+                            "4 right-padded rows x 512 per rank (~57% real tokens, packed), fwd+bwd, "
+                            "LoRA-grad all-reduce, AdamW",
+                "ms_per_step": round(t, 3), "tokens_per_s": round(real.item() / (t * 1e-3), 1),
+                "real_tokens_per_step_all_ranks": int(real.item()),
+                "allreduce_bytes": trainer.lora_grad_bytes(),
+                "nf4_gemm_tflops_in_step_rank0": round(fl["nf4_gemm"] / (t * 1e-3) / 1e12, 1),
+                "scaling": "weak (each rank its own 4 rows)"}
+        del trainer, model
         torch.cuda.synchronize()
     clk = clocks.stop()
 
@@ -433,6 +459,7 @@ def main():
                          "traffic": traffic,
                          "units_per_launch": "196 matrices, 1,310,195,712 weights x 2.5159 B"},
             "gemm": gemm,
+            "qlora_step": step,
             "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clk,

@@ -1,0 +1,64 @@
+"""Data parallelism of the QLoRA step: one process per GPU, each with a full replica of the
+packed NF4 weights and the LoRA adapters, each running its own batch of packed token rows.
+The only exchange is ONE all-reduce per step of a flat fp32 buffer holding every LoRA
+gradient plus the rank's labelled-token count, after which the gradients are divided by the
+global count -- the loss normalisation of the reference's head loss (sum of per-token CE
+over the batch divided by the number of labelled tokens, solution/head_loss.py:164-169),
+taken over all ranks' batches.
+
+With a process group of size 1 (or no group) the same code runs without communication, so a
+G-rank step equals a 1-rank step over the concatenated batches.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def _world(group) -> int:
+    if not (dist.is_available() and dist.is_initialized()):
+        return 1
+    return dist.get_world_size(group)
+
+
+def flatten_grads(params, extra: float) -> torch.Tensor:
+    """One fp32 buffer: every parameter's gradient (zeros where it has none), then `extra`."""
+    parts = []
+    dev = None
+    for p in params:
+        dev = p.device
+        g = p.grad if p.grad is not None else torch.zeros_like(p)
+        parts.append(g.reshape(-1).float())
+    parts.append(torch.tensor([float(extra)], dtype=torch.float32, device=dev))
+    return torch.cat(parts)
+
+
+def unflatten_into_grads(params, flat: torch.Tensor) -> None:
+    off = 0
+    for p in params:
+        n = p.numel()
+        g = flat[off:off + n].view_as(p).to(p.dtype)
+        if p.grad is None:
+            p.grad = g.clone()
+        else:
+            p.grad.copy_(g)
+        off += n
+
+
+def allreduce_lora_grads(params, local_labels: float, group=None) -> float:
+    """Sum the LoRA gradients and the labelled-token counts over the ranks in one
+    all-reduce, then divide the gradients by the global count.  The gradients on entry
+    are of the rank's summed (not averaged) loss.  Returns the global count."""
+    params = list(params)
+    flat = flatten_grads(params, local_labels)
+    if _world(group) > 1:
+        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+    total = float(flat[-1].item())
+    if total <= 0:
+        total = 1.0
+    unflatten_into_grads(params, flat[:-1] / total)
+    return total
+
+
+def lora_grad_bytes(params) -> int:
+    return 4 * (sum(p.numel() for p in params) + 1)

@@ -1,0 +1,180 @@
+"""The full QLoRA training step the NF4 path serves: Qwen2.5-1.5B (28 layers, hidden 1536,
+SwiGLU MLP 8960, 12 query / 2 key-value heads of dim 128, RMSNorm, RoPE theta 1e6, vocabulary
+151936, tied fp16 embedding / LM head) with every projection an NF4 weight and a rank-16
+LoRA adapter on q and v, run on packed token rows.
+
+Scope: the reference patches this model (transformers' Qwen2 under peft/bitsandbytes) and runs
+it on packed real tokens (solution/unpad.py:278-345).  Here only the NF4 projections and the
+LoRA adapters are this library's kernels (fused unpack + tcgen05 GEMMs, forward and backward);
+RMSNorm, RoPE, attention, SwiGLU and the LM-head loss are plain torch operations, because they
+are not on the NF4 path.  Weights are random (seeded) and NF4-quantized on the GPU: no
+checkpoint is used.
+
+`train_step` = forward on the packed rows, backward (LoRA grads only: base weights, norms and
+embedding are frozen), one all-reduce of the LoRA grads across data-parallel ranks
+(stew_b200.dp), AdamW on the adapters.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from . import dp
+from .lora import LORA_RANK, NF4Linear, NF4LoraLinear
+from .sweep import QWEN_PROJ, qwen_model_weights
+
+
+@dataclass
+class QwenConfig:
+    layers: int = 28
+    hidden: int = 1536
+    intermediate: int = 8960
+    heads: int = 12
+    kv_heads: int = 2
+    head_dim: int = 128
+    vocab: int = 151936
+    rope_theta: float = 1e6
+    rms_eps: float = 1e-6
+    lora_alpha: float = 32.0
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w).to(torch.float16)
+
+
+def rope_tables(positions: torch.Tensor, head_dim: int, theta: float):
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, device=positions.device, dtype=torch.float32) / head_dim))
+    ang = positions.float()[:, None] * inv[None, :]
+    emb = torch.cat([ang, ang], dim=-1)
+    return emb.cos(), emb.sin()
+
+
+def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """x [N, heads, d]; rotate-half convention of Qwen2."""
+    xf = x.float()
+    d = xf.shape[-1] // 2
+    rot = torch.cat([-xf[..., d:], xf[..., :d]], dim=-1)
+    return (xf * cos[:, None, :] + rot * sin[:, None, :]).to(x.dtype)
+
+
+class Layer(torch.nn.Module):
+    def __init__(self, cfg: QwenConfig, weights, device):
+        super().__init__()
+        self.cfg = cfg
+        mods = {}
+        for (name, _), (packed, st) in zip(QWEN_PROJ, weights):
+            if name in ("q", "v"):
+                m = NF4LoraLinear(packed, st, lora_alpha=cfg.lora_alpha, device=device)
+                torch.nn.init.normal_(m.lora_B, std=0.01)
+            else:
+                m = NF4Linear(packed, st)
+            mods[name] = m
+        self.proj = torch.nn.ModuleDict(mods)
+        self.register_buffer("ln1", torch.ones(cfg.hidden, device=device))
+        self.register_buffer("ln2", torch.ones(cfg.hidden, device=device))
+
+    def forward(self, x, cos, sin, mask):
+        c, p = self.cfg, self.proj
+        n = x.shape[0]
+        h = rms_norm(x, self.ln1, c.rms_eps)
+        q = apply_rope(p["q"](h).view(n, c.heads, c.head_dim), cos, sin)
+        k = apply_rope(p["k"](h).view(n, c.kv_heads, c.head_dim), cos, sin)
+        v = p["v"](h).view(n, c.kv_heads, c.head_dim)
+        # packed rows: block-diagonal causal mask over the N real tokens
+        a = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
+                                           v.transpose(0, 1)[None], attn_mask=mask, enable_gqa=True)
+        x = x + p["o"](a[0].transpose(0, 1).reshape(n, c.heads * c.head_dim))
+        h = rms_norm(x, self.ln2, c.rms_eps)
+        m = F.silu(p["gate"](h).float()).to(torch.float16) * p["up"](h)
+        return x + p["down"](m)
+
+
+class QwenQLoRA(torch.nn.Module):
+    def __init__(self, cfg: QwenConfig = QwenConfig(), device="cuda", seed: int = 0, weights=None):
+        super().__init__()
+        self.cfg = cfg
+        ws = weights if weights is not None else qwen_model_weights(layers=cfg.layers, device=device,
+                                                                     seed=seed)
+        g = torch.Generator(device=device).manual_seed(seed + 7)
+        self.register_buffer("embed", (torch.randn(cfg.vocab, cfg.hidden, generator=g, device=device)
+                                       * 0.02).to(torch.float16))
+        torch.manual_seed(seed)
+        self.layers = torch.nn.ModuleList(
+            [Layer(cfg, ws[7 * i:7 * i + 7], device) for i in range(cfg.layers)])
+        self.register_buffer("ln_f", torch.ones(cfg.hidden, device=device))
+
+    def lora_parameters(self):
+        return [p for p in self.parameters() if p.requires_grad]
+
+    def forward(self, tokens: torch.Tensor, lengths: torch.Tensor):
+        """tokens [B, T] right-padded, lengths [B].  Returns (sum of next-token CE over the
+        labelled tokens, number of labelled tokens)."""
+        B, T = tokens.shape
+        dev = tokens.device
+        lens = lengths.tolist()
+        keep = torch.arange(T, device=dev)[None, :] < lengths[:, None]
+        ids = tokens[keep]                                    # packed real tokens [N]
+        positions = torch.cat([torch.arange(L, device=dev) for L in lens])
+        seg = torch.cat([torch.full((L,), i, device=dev) for i, L in enumerate(lens)])
+        mask = (seg[:, None] == seg[None, :]) & (positions[None, :] <= positions[:, None])
+        cos, sin = rope_tables(positions, self.cfg.head_dim, self.cfg.rope_theta)
+        x = self.embed[ids]
+        for layer in self.layers:
+            x = layer(x, cos, sin, mask)
+        h = rms_norm(x, self.ln_f, self.cfg.rms_eps)
+        # next-token labels inside each row; a row's last token has none
+        nxt = torch.roll(ids, -1)
+        has = torch.roll(seg, -1) == seg
+        has[-1] = False
+        logits = h[has] @ self.embed.t()
+        loss_sum = F.cross_entropy(logits.float(), nxt[has], reduction="sum")
+        return loss_sum, int(has.sum().item())
+
+
+def synthetic_batch(batch: int = 4, seq: int = 512, vocab: int = 151936, mean_frac: float = 0.57,
+                    seed: int = 0, device="cuda"):
+    """4 right-padded rows of 512 with uniform-random real lengths averaging 57% of the row
+    (about 1170 real tokens), token ids uniform over the vocabulary."""
+    g = torch.Generator().manual_seed(seed)
+    lo, hi = int(seq * (2 * mean_frac - 1.0)), seq
+    lengths = torch.randint(lo, hi + 1, (batch,), generator=g)
+    tokens = torch.randint(0, vocab, (batch, seq), generator=g)
+    tokens[torch.arange(seq)[None, :] >= lengths[:, None]] = 0
+    return tokens.to(device), lengths.to(device)
+
+
+class QLoRATrainer:
+    """One QLoRA step per call: forward, backward, LoRA-grad all-reduce, AdamW."""
+
+    def __init__(self, model: QwenQLoRA, lr: float = 2e-4, group=None):
+        self.model = model
+        self.params = model.lora_parameters()
+        self.opt = torch.optim.AdamW(self.params, lr=lr, weight_decay=0.0)
+        self.group = group
+
+    def step(self, tokens, lengths):
+        loss_sum, n_lab = self.model(tokens, lengths)
+        loss_sum.backward()
+        total = dp.allreduce_lora_grads(self.params, n_lab, self.group)
+        self.opt.step()
+        self.opt.zero_grad(set_to_none=True)
+        return float(loss_sum.detach()) / max(n_lab, 1), n_lab, total
+
+    def lora_grad_bytes(self) -> int:
+        return dp.lora_grad_bytes(self.params)
+
+
+def step_flops(cfg: QwenConfig, n_tokens: int) -> dict:
+    """Algorithmic FLOPs of the NF4 projections in one step (forward + input-gradient
+    backward) plus the LoRA terms on q/v."""
+    nf4 = 0
+    lora = 0
+    for name, (out_f, in_f) in QWEN_PROJ:
+        nf4 += 2 * 2 * n_tokens * in_f * out_f  # forward + backward dX
+        if name in ("q", "v"):
+            lora += 6 * n_tokens * LORA_RANK * (in_f + out_f)
+    return {"nf4_gemm": nf4 * cfg.layers, "lora": lora * cfg.layers}

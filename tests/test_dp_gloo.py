@@ -1,0 +1,115 @@
+"""CPU, 2 gloo ranks: the data-parallel LoRA-gradient exchange of the QLoRA step
+(stew_b200.dp) -- G ranks x their own rows give the same normalised gradients as one rank
+over all rows; and a rank that fails before the all-reduce makes the other rank's
+collective end with an error within the process-group timeout instead of hanging."""
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from stew_b200 import dp
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+class TinyLoRA(torch.nn.Module):
+    """A frozen base projection with a rank-4 adapter and a per-token CE head: enough
+    structure for summed-loss / global-count normalisation to matter."""
+
+    def __init__(self):
+        super().__init__()
+        g = torch.Generator().manual_seed(0)
+        self.register_buffer("w", torch.randn(24, 16, generator=g) * 0.2)
+        self.a = torch.nn.Parameter(torch.randn(4, 16, generator=g) * 0.3)
+        self.b = torch.nn.Parameter(torch.randn(24, 4, generator=g) * 0.3)
+
+    def forward(self, x, labels):
+        y = x @ self.w.t() + (x @ self.a.t()) @ self.b.t() * 2.0
+        keep = labels >= 0
+        return torch.nn.functional.cross_entropy(y[keep], labels[keep], reduction="sum"), int(keep.sum())
+
+
+def _rows(seed):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(13 + seed, 16, generator=g)
+    labels = torch.randint(0, 24, (13 + seed,), generator=g)
+    labels[::5] = -100
+    return x, labels
+
+
+def _worker(rank, world, port, q, fail_rank):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    try:
+        if rank == fail_rank:
+            raise RuntimeError("injected failure before the all-reduce")
+        m = TinyLoRA()
+        loss, n = m(*_rows(rank))
+        loss.backward()
+        total = dp.allreduce_lora_grads([m.a, m.b], n)
+        q.put((rank, "ok", total, m.a.grad.clone(), m.b.grad.clone()))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, "error", repr(e), None, None))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:  # noqa: BLE001
+            pass
+
+
+def _run(world, fail_rank=-1):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, fail_rank)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    for _ in range(world):
+        r, status, a, ga, gb = q.get(timeout=120)
+        out[r] = (status, a, ga, gb)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    return out
+
+
+def test_two_ranks_equal_one_rank_over_all_rows():
+    out = _run(2)
+    m = TinyLoRA()
+    loss0, n0 = m(*_rows(0))
+    loss1, n1 = m(*_rows(1))
+    ((loss0 + loss1) / (n0 + n1)).backward()
+    for r in (0, 1):
+        status, total, ga, gb = out[r]
+        assert status == "ok"
+        assert total == n0 + n1
+        torch.testing.assert_close(ga, m.a.grad, rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(gb, m.b.grad, rtol=1e-5, atol=1e-6)
+
+
+def test_single_process_needs_no_group():
+    m = TinyLoRA()
+    loss, n = m(*_rows(3))
+    loss.backward()
+    ga = m.a.grad.clone()
+    total = dp.allreduce_lora_grads([m.a, m.b], n)
+    assert total == n
+    torch.testing.assert_close(m.a.grad, ga / n)
+
+
+@pytest.mark.timeout(180)
+def test_failed_rank_ends_peer_collective_with_error():
+    out = _run(2, fail_rank=1)
+    assert out[1][0] == "error" and "injected failure" in out[1][1]
+    assert out[0][0] == "error", "the surviving rank must not hang or succeed"
