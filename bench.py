@@ -325,6 +325,27 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def profile_case():
+    """Launches, in order: nf4_dequant_batched_kernel (2 layers = 14 matrices, 235.7 MB of
+    algorithmic traffic, larger than L2), nf4_gemm_kernel<fwd> and nf4_gemm_kernel<bwd> on the
+    gate projection (8960 x 1536) at N = 2048 tokens."""
+    import torch
+    from stew_b200.nf4 import linear_backward_dx, linear_forward
+    from stew_b200.sweep import DequantSweep, qwen_model_weights
+    ws = qwen_model_weights(layers=2, device="cuda", seed=0)
+    sweep = DequantSweep(ws)
+    torch.cuda.synchronize()
+    sweep.run()
+    q, st = ws[4]
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(2048, 1536, generator=g, device="cuda").half()
+    dy = (torch.randn(2048, 8960, generator=g, device="cuda") * 0.01).half()
+    linear_forward(x, q.view(-1, 1), st)
+    linear_backward_dx(dy, q.view(-1, 1), st)
+    torch.cuda.synchronize()
+    print("profile case done")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -340,10 +361,15 @@ def main():
     ap.add_argument("--no-gemm", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile-case", action="store_true",
+                    help="small single-GPU case for ncu captures: one 2-layer unpack sweep, then one "
+                         "fused forward and one fused backward GEMM of the gate projection at N=2048")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile_case:
+        return profile_case()
 
     import torch
     world, rank, local = _dist()
