@@ -4,8 +4,7 @@
 //
 //  lora_project16   out[t, r] = sum_k act[t, k] * W[r, k]       (X A^T forward, dY B backward)
 //                   fp32 accumulate, fp16 result (what peft's fp16 autocast linear yields).
-//                   HBM-bound on `act`: one warp per token row, the 16 x K weight slice
-//                   staged in shared memory, a transposing butterfly reduces the 16 sums.
+//                   HBM-bound on `act`; mma.sync tiles of 16 tokens, K split over 8 warps.
 //  lora_outer16     G[r, c] = sum_t P[t, r] * Q[t, c]            (the two weight gradients)
 //                   split over tokens; partial sums go to caller-provided scratch and a
 //                   second kernel adds them up and applies the scale.
@@ -15,92 +14,84 @@
 
 namespace nf4b {
 
+// Rank-16 projection on the tensor cores (mma.sync m16n8k16, fp16 in, fp32 accumulate): a
+// CTA of 8 warps owns 16 tokens, each warp one eighth of K; the eight partial 16x16 tiles are
+// summed through shared memory.  Streams `act` once (HBM-bound); W (16 x K) stays in L2.
 constexpr int LP_THREADS = 256;
-constexpr int LP_TOK_PER_WARP = 4;
-constexpr int LP_TOK_PER_CTA = (LP_THREADS / 32) * LP_TOK_PER_WARP;  // 32
-constexpr int LP_KCHUNK = 1024;                                      // 32 KB of fp16 weights
+constexpr int LP_WARPS = LP_THREADS / 32;
+constexpr int LP_TOK = 16;
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// W(r, k) and W(r, k+1) as one half2 (k in the low half); k is even.
+__device__ __forceinline__ uint32_t ld_w_pair(const __half* w, int64_t sr, int64_t sk, int r,
+                                              int64_t k) {
+  if (sk == 1) return __ldg(reinterpret_cast<const unsigned int*>(w + r * sr + k));
+  const uint32_t lo = __ldg(reinterpret_cast<const unsigned short*>(w + r * sr + k * sk));
+  const uint32_t hi = __ldg(reinterpret_cast<const unsigned short*>(w + r * sr + (k + 1) * sk));
+  return lo | (hi << 16);
+}
 
 __global__ void __launch_bounds__(LP_THREADS)
     lora_project16_kernel(const __half* __restrict__ act, const __half* __restrict__ w, int64_t sr,
                           int64_t sk, __half* __restrict__ out, int64_t n, int64_t kdim) {
-  __shared__ __align__(16) __half ws[LP_KCHUNK * 16];  // [k][r]
+  __shared__ float red[LP_WARPS][LP_TOK][17];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t tbase = int64_t(blockIdx.x) * LP_TOK_PER_CTA + warp * LP_TOK_PER_WARP;
-  float acc[LP_TOK_PER_WARP][16];
-#pragma unroll
-  for (int i = 0; i < LP_TOK_PER_WARP; ++i)
-#pragma unroll
-    for (int r = 0; r < 16; ++r) acc[i][r] = 0.f;
-
-  for (int64_t kc = 0; kc < kdim; kc += LP_KCHUNK) {
-    const int klen = int(min64(LP_KCHUNK, kdim - kc));
-    __syncthreads();
-    for (int e = threadIdx.x; e < klen * 16; e += LP_THREADS) {
-      // element (k, r) with r fastest in smem; read k-fastest when sk == 1 for coalescing
-      int k, r;
-      if (sk == 1) { r = e / klen; k = e - r * klen; } else { k = e >> 4; r = e & 15; }
-      ws[k * 16 + r] = w[int64_t(r) * sr + (kc + k) * sk];
-    }
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < LP_TOK_PER_WARP; ++i) {
-      const int64_t t = tbase + i;
-      if (t >= n) break;
-      const __half* arow = act + t * kdim + kc;
-      for (int k8 = lane * 8; k8 < klen; k8 += 256) {
-        const uint4 av = __ldg(reinterpret_cast<const uint4*>(arow + k8));
-        const __half* ah = reinterpret_cast<const __half*>(&av);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float a = __half2float(ah[q]);
-          const uint4* wr = reinterpret_cast<const uint4*>(ws + (k8 + q) * 16);
-          const uint4 w0 = wr[0], w1 = wr[1];
-          const __half2* h0 = reinterpret_cast<const __half2*>(&w0);
-          const __half2* h1 = reinterpret_cast<const __half2*>(&w1);
-#pragma unroll
-          for (int p = 0; p < 4; ++p) {
-            const float2 f0 = __half22float2(h0[p]);
-            const float2 f1 = __half22float2(h1[p]);
-            acc[i][2 * p] = fmaf(a, f0.x, acc[i][2 * p]);
-            acc[i][2 * p + 1] = fmaf(a, f0.y, acc[i][2 * p + 1]);
-            acc[i][8 + 2 * p] = fmaf(a, f1.x, acc[i][8 + 2 * p]);
-            acc[i][8 + 2 * p + 1] = fmaf(a, f1.y, acc[i][8 + 2 * p + 1]);
-          }
-        }
-      }
-    }
+  const int g = lane >> 2, c = lane & 3;  // mma fragment coordinates
+  const int64_t t0 = int64_t(blockIdx.x) * LP_TOK;
+  const int64_t ksteps = kdim / 16;
+  const int64_t per = (ksteps + LP_WARPS - 1) / LP_WARPS;
+  const int64_t kb = warp * per;
+  const int64_t ke = min64(ksteps, kb + per);
+  const bool v0 = t0 + g < n, v1 = t0 + g + 8 < n;
+  const unsigned int* x0 = reinterpret_cast<const unsigned int*>(act + (t0 + g) * kdim);
+  const unsigned int* x1 = reinterpret_cast<const unsigned int*>(act + (t0 + g + 8) * kdim);
+  float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+  for (int64_t ks = kb; ks < ke; ++ks) {
+    const int64_t k = ks * 16 + 2 * c;
+    uint32_t a[4];
+    a[0] = v0 ? __ldg(x0 + (k >> 1)) : 0u;      // rows g / g+8, k..k+1
+    a[1] = v1 ? __ldg(x1 + (k >> 1)) : 0u;
+    a[2] = v0 ? __ldg(x0 + (k >> 1) + 4) : 0u;  // k+8..k+9
+    a[3] = v1 ? __ldg(x1 + (k >> 1) + 4) : 0u;
+    mma16816(d0, a, ld_w_pair(w, sr, sk, g, k), ld_w_pair(w, sr, sk, g, k + 8));
+    mma16816(d1, a, ld_w_pair(w, sr, sk, 8 + g, k), ld_w_pair(w, sr, sk, 8 + g, k + 8));
   }
-  // Transposing butterfly: after it, lanes 2r and 2r+1 hold the full sum for r.
+  red[warp][g][2 * c] = d0[0];
+  red[warp][g][2 * c + 1] = d0[1];
+  red[warp][g + 8][2 * c] = d0[2];
+  red[warp][g + 8][2 * c + 1] = d0[3];
+  red[warp][g][8 + 2 * c] = d1[0];
+  red[warp][g][8 + 2 * c + 1] = d1[1];
+  red[warp][g + 8][8 + 2 * c] = d1[2];
+  red[warp][g + 8][8 + 2 * c + 1] = d1[3];
+  __syncthreads();
+  const int t = threadIdx.x >> 4, r = threadIdx.x & 15;
+  float sum = 0.f;
 #pragma unroll
-  for (int i = 0; i < LP_TOK_PER_WARP; ++i) {
-    float* v = acc[i];
-#pragma unroll
-    for (int off = 16, cnt = 8; off >= 2; off >>= 1, cnt >>= 1) {
-      const bool upper = (lane & off) != 0;
-#pragma unroll
-      for (int q = 0; q < cnt; ++q) {
-        const float send = upper ? v[q] : v[q + cnt];
-        const float keep = upper ? v[q + cnt] : v[q];
-        v[q] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-      }
-    }
-    v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
-    const int64_t t = tbase + i;
-    if (t < n && (lane & 1) == 0) out[t * 16 + (lane >> 1)] = __float2half_rn(v[0]);
-  }
+  for (int ww = 0; ww < LP_WARPS; ++ww) sum += red[ww][t][r];
+  if (t0 + t < n) out[(t0 + t) * 16 + r] = __float2half_rn(sum);
 }
 
 int lora_project16(const void* act, const void* w, int64_t w_stride_r, int64_t w_stride_k,
                    void* out, int64_t n, int64_t kdim, cudaStream_t s) {
-  NF4B_RETURN_IF(kdim % 8 != 0, NF4B_ERR_UNSUPPORTED);
-  NF4B_RETURN_IF(!aligned(act, 16), NF4B_ERR_ALIGNMENT);
+  NF4B_RETURN_IF(kdim % 16 != 0, NF4B_ERR_UNSUPPORTED);
+  NF4B_RETURN_IF(!aligned(act, 16) || !aligned(w, 4), NF4B_ERR_ALIGNMENT);
   if (n == 0) return NF4B_OK;
-  const int64_t ctas = (n + LP_TOK_PER_CTA - 1) / LP_TOK_PER_CTA;
+  const int64_t ctas = (n + LP_TOK - 1) / LP_TOK;
   NF4B_RETURN_IF(ctas > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
   lora_project16_kernel<<<unsigned(ctas), LP_THREADS, 0, s>>>(
       static_cast<const __half*>(act), static_cast<const __half*>(w), w_stride_r, w_stride_k,
       static_cast<__half*>(out), n, kdim);
-  return launch_status();
+  return launch_status("lora_project16_kernel launch");
 }
 
 // ---------------------------------------------------------------- weight grads
@@ -135,20 +126,31 @@ __global__ void __launch_bounds__(LO_THREADS)
     for (int e = threadIdx.x; e < tl * 16; e += LO_THREADS) ps[e] = __half2float(P[ts * 16 + e]);
     __syncthreads();
     if (cok) {
-      for (int t = 0; t < tl; ++t) {
-        const float2 q = __half22float2(*reinterpret_cast<const __half2*>(Q + (ts + t) * cols + c));
-        const float4* pr = reinterpret_cast<const float4*>(ps + t * 16);
+      // eight tokens' loads in flight before their multiply-adds
+      constexpr int U = 8;
+      int t = 0;
+      for (; t < tl; t += U) {
+        float2 q[U];
 #pragma unroll
-        for (int v4 = 0; v4 < 4; ++v4) {
-          const float4 p = pr[v4];
-          acc[4 * v4 + 0][0] = fmaf(p.x, q.x, acc[4 * v4 + 0][0]);
-          acc[4 * v4 + 0][1] = fmaf(p.x, q.y, acc[4 * v4 + 0][1]);
-          acc[4 * v4 + 1][0] = fmaf(p.y, q.x, acc[4 * v4 + 1][0]);
-          acc[4 * v4 + 1][1] = fmaf(p.y, q.y, acc[4 * v4 + 1][1]);
-          acc[4 * v4 + 2][0] = fmaf(p.z, q.x, acc[4 * v4 + 2][0]);
-          acc[4 * v4 + 2][1] = fmaf(p.z, q.y, acc[4 * v4 + 2][1]);
-          acc[4 * v4 + 3][0] = fmaf(p.w, q.x, acc[4 * v4 + 3][0]);
-          acc[4 * v4 + 3][1] = fmaf(p.w, q.y, acc[4 * v4 + 3][1]);
+        for (int u = 0; u < U; ++u)
+          q[u] = (t + u < tl) ? __half22float2(*reinterpret_cast<const __half2*>(Q + (ts + t + u) * cols + c))
+                              : make_float2(0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          if (t + u >= tl) break;  // rows past the staged ones hold stale values
+          const float4* pr = reinterpret_cast<const float4*>(ps + (t + u) * 16);
+#pragma unroll
+          for (int v4 = 0; v4 < 4; ++v4) {
+            const float4 p = pr[v4];
+            acc[4 * v4 + 0][0] = fmaf(p.x, q[u].x, acc[4 * v4 + 0][0]);
+            acc[4 * v4 + 0][1] = fmaf(p.x, q[u].y, acc[4 * v4 + 0][1]);
+            acc[4 * v4 + 1][0] = fmaf(p.y, q[u].x, acc[4 * v4 + 1][0]);
+            acc[4 * v4 + 1][1] = fmaf(p.y, q[u].y, acc[4 * v4 + 1][1]);
+            acc[4 * v4 + 2][0] = fmaf(p.z, q[u].x, acc[4 * v4 + 2][0]);
+            acc[4 * v4 + 2][1] = fmaf(p.z, q[u].y, acc[4 * v4 + 2][1]);
+            acc[4 * v4 + 3][0] = fmaf(p.w, q[u].x, acc[4 * v4 + 3][0]);
+            acc[4 * v4 + 3][1] = fmaf(p.w, q[u].y, acc[4 * v4 + 3][1]);
+          }
         }
       }
     }
