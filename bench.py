@@ -215,6 +215,10 @@ class GemmPass:
                 self.items.append((li, name, out_f, in_f, q, qs, lc))
         wb = max(int(self.L.nf4b_lora_grads_work_bytes(n, in_f, out_f, 16)) for _, out_f, in_f in QWEN_PROJ)
         self.work = torch.empty(wb // 4 + 4, device=dev, dtype=torch.float32)
+        # split-K workspace (zeroed once; every call leaves its counters zero)
+        self.ws_bytes = max(int(self.L.nf4b_linear_work_bytes(n, in_f, out_f, bwd))
+                            for _, out_f, in_f in QWEN_PROJ for bwd in (0, 1))
+        self.ws = torch.zeros(max(self.ws_bytes, 256), device=dev, dtype=torch.uint8)
 
     def flops(self, fwd=True, bwd=True, lora=True):
         f = 0
@@ -234,18 +238,20 @@ class GemmPass:
         for li, name, out_f, in_f, q, qs, lc in self.items:
             use = lora and lc is not None
             if fwd:
-                st = self.L.nf4b_linear_fwd(self.x[in_f].data_ptr(), q.data_ptr(), ct.byref(qs), None,
-                                            ct.byref(lc) if use else None, self.y[out_f].data_ptr(),
-                                            self.n, in_f, out_f, stream)
+                st = self.L.nf4b_linear_fwd_ws(self.x[in_f].data_ptr(), q.data_ptr(), ct.byref(qs), None,
+                                               ct.byref(lc) if use else None, self.y[out_f].data_ptr(),
+                                               self.n, in_f, out_f, self.ws.data_ptr(), self.ws.numel(),
+                                               stream)
                 assert st == 0, st
                 launches += 2 if use else 1
             if bwd:
                 if use:
                     a, b, xa, dyb, da, db, _ = self.lora[(li, name)]
-                st = self.L.nf4b_linear_bwd_dx(self.dy[out_f].data_ptr(), q.data_ptr(), ct.byref(qs),
-                                               ct.byref(lc) if use else None,
-                                               dyb.data_ptr() if use else None,
-                                               self.dx[in_f].data_ptr(), self.n, in_f, out_f, stream)
+                st = self.L.nf4b_linear_bwd_dx_ws(self.dy[out_f].data_ptr(), q.data_ptr(), ct.byref(qs),
+                                                  ct.byref(lc) if use else None,
+                                                  dyb.data_ptr() if use else None,
+                                                  self.dx[in_f].data_ptr(), self.n, in_f, out_f,
+                                                  self.ws.data_ptr(), self.ws.numel(), stream)
                 assert st == 0, st
                 launches += 2 if use else 1
                 if use:

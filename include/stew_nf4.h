@@ -118,6 +118,32 @@ int nf4b_linear_bwd_dx(const void* dy, const uint8_t* packed, const nf4b_qstate*
                        const nf4b_lora* lora, void* dyb, void* dx,
                        int64_t n, int64_t in_features, int64_t out_features, void* stream);
 
+/* Split-K variants of the two above.  When a launch has fewer output tiles (128 weight
+ * rows x 256 tokens) than the GPU has SMs, the K reduction of each tile is split over
+ * several CTAs; the last CTA of a tile to finish adds the others' fp32 partials, so the
+ * result differs from the unsplit call only in fp32 summation order.  Same arguments
+ * as nf4b_linear_fwd / nf4b_linear_bwd_dx plus a caller-owned workspace:
+ *   work        device buffer, 256-byte aligned, of at least
+ *               nf4b_linear_work_bytes(n, in, out, backward) bytes (0 = no split for
+ *               this shape on the current device: any pointer, or NULL, will do);
+ *               its leading counter words must be zero before the first call and every
+ *               successful call leaves them zero, so allocate it zeroed once and reuse it.
+ *               Calls that may run concurrently (different streams) need distinct
+ *               workspaces.  work == NULL runs unsplit.
+ *   work_bytes  size of `work`; smaller than required -> NF4B_ERR_INVALID_ARG.
+ * No counterpart in the reference, whose forward and backward are one cuBLAS GEMM each
+ * (F.linear, nf4.py:152; bitsandbytes MatMul4Bit.backward).  */
+int64_t nf4b_linear_work_bytes(int64_t n, int64_t in_features, int64_t out_features,
+                               int32_t backward);
+int nf4b_linear_fwd_ws(const void* x, const uint8_t* packed, const nf4b_qstate* qs,
+                       const void* bias, const nf4b_lora* lora, void* y,
+                       int64_t n, int64_t in_features, int64_t out_features,
+                       void* work, int64_t work_bytes, void* stream);
+int nf4b_linear_bwd_dx_ws(const void* dy, const uint8_t* packed, const nf4b_qstate* qs,
+                          const nf4b_lora* lora, void* dyb, void* dx,
+                          int64_t n, int64_t in_features, int64_t out_features,
+                          void* work, int64_t work_bytes, void* stream);
+
 /* LoRA weight gradients (fp32 out, overwritten):
  *   dA[rank, in]  = scale * (dY B)^T X
  *   dB[out, rank] = scale * dY^T (X A^T)

@@ -58,6 +58,13 @@ SIGNATURES = {
     "nf4b_linear_bwd_dx": (c_int32, [c_void_p, c_void_p, ctypes.POINTER(QStateC),
                                      ctypes.POINTER(LoraC), c_void_p, c_void_p, c_int64, c_int64,
                                      c_int64, c_void_p]),
+    "nf4b_linear_work_bytes": (c_int64, [c_int64, c_int64, c_int64, c_int32]),
+    "nf4b_linear_fwd_ws": (c_int32, [c_void_p, c_void_p, ctypes.POINTER(QStateC), c_void_p,
+                                     ctypes.POINTER(LoraC), c_void_p, c_int64, c_int64, c_int64,
+                                     c_void_p, c_int64, c_void_p]),
+    "nf4b_linear_bwd_dx_ws": (c_int32, [c_void_p, c_void_p, ctypes.POINTER(QStateC),
+                                        ctypes.POINTER(LoraC), c_void_p, c_void_p, c_int64, c_int64,
+                                        c_int64, c_void_p, c_int64, c_void_p]),
     "nf4b_lora_grads_work_bytes": (c_int64, [c_int64, c_int64, c_int64, c_int32]),
     "nf4b_lora_grads": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p,
                                   c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int32, c_void_p]),

@@ -64,6 +64,13 @@ constexpr int SM_TOTAL = SM_MISC + 16;
 constexpr int SM_ALLOC = SM_TOTAL + 1024;  // slack to align the base to 1024 B
 static_assert(SM_ALLOC <= 232448, "shared memory budget");
 
+// Split-K workspace: a fixed counter region (arrivals at [0, G_SPLIT_MAX_TILES), finished
+// partials at [G_SPLIT_MAX_TILES, 2 * G_SPLIT_MAX_TILES)), then the fp32 partial tiles.  The
+// region does not depend on the launch's shape, so one zeroed workspace serves any sequence
+// of calls on a stream.
+constexpr int G_SPLIT_MAX_TILES = 512;
+constexpr int64_t G_SPLIT_CNT_BYTES = 2 * G_SPLIT_MAX_TILES * 4;
+
 struct GemmArgs {
   const uint8_t* absmax8;
   const float* absmax32;
@@ -84,6 +91,10 @@ struct GemmArgs {
   int32_t nested;
   int32_t m_tiles;        // 128-row weight tiles
   int32_t n_tiles;        // 256-token tiles
+  int32_t splits;         // K ranges per tile (split-K); 1 = none
+  int32_t nk;             // K stages of the whole reduction
+  float* ws_part;         // split-K: fp32 partial tiles [tiles][splits-1][128][256]
+  int32_t* ws_cnt;        // split-K: per-tile counters [2][G_SPLIT_MAX_TILES], zero between launches
 };
 
 __device__ int g_gemm_error;
@@ -191,7 +202,60 @@ __device__ __forceinline__ TileCoord tile_coord(const GemmArgs& g, int tile) {
   return c;
 }
 
-template <bool BWD>
+// Work unit of the persistent loop: one K range of one output tile.  The units of a tile
+// are consecutive, so its K ranges run at the same time on neighbouring CTAs.
+struct WorkUnit {
+  TileCoord tc;
+  int tile;
+  int split;
+  int kb, ke;   // stage range [kb, ke)
+};
+
+__device__ __forceinline__ WorkUnit work_unit(const GemmArgs& g, int u) {
+  WorkUnit w;
+  w.tile = u / g.splits;
+  w.split = u - w.tile * g.splits;
+  w.tc = tile_coord(g, w.tile);
+  w.kb = int((int64_t(w.split) * g.nk) / g.splits);
+  w.ke = int((int64_t(w.split + 1) * g.nk) / g.splits);
+  return w;
+}
+
+// Named barrier 1 over the epilogue warps only.
+__device__ __forceinline__ void epi_bar_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(G_EPI_WARPS * 32) : "memory");
+}
+// Same barrier, returning the AND of `v` over the epilogue threads.
+__device__ __forceinline__ bool epi_bar_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(uint32_t(v)), "n"(G_EPI_WARPS * 32)
+      : "memory");
+  return r != 0;
+}
+
+// Bounded wait until *p == want (acquire at GPU scope); false on timeout.
+__device__ __forceinline__ bool wait_count(const int32_t* p, int want) {
+  const long long t0 = clock64();
+  for (;;) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    if (v == want) return true;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      atomicExch(&g_gemm_error, 3);
+      return false;
+    }
+    __nanosleep(64);
+  }
+}
+
+// SPLIT: compiled with the split-K epilogue (launches with g.splits > 1).
+template <bool BWD, bool SPLIT>
 __global__ void __launch_bounds__(G_THREADS, 1)
     nf4_gemm_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_w,
                     const GemmArgs g) {
@@ -215,9 +279,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   float* s_code = reinterpret_cast<float*>(smem + SM_CODE);
   float* s_code2 = reinterpret_cast<float*>(smem + SM_CODE2);
 
-  const int ntiles = g.m_tiles * g.n_tiles;
-  const int64_t kdim = BWD ? g.out_f : g.in_f;
-  const int nk = int(kdim / G_K);
+  const int nunits = g.m_tiles * g.n_tiles * g.splits;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < G_STAGES; ++i) {
@@ -253,9 +315,10 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-        const TileCoord tc = tile_coord(g, tile);
-        for (int k = 0; k < nk; ++k, ++it) {
+      for (int u = blockIdx.x; ok && u < nunits; u += gridDim.x) {
+        const WorkUnit wu = work_unit(g, u);
+        const TileCoord& tc = wu.tc;
+        for (int k = wu.kb; k < wu.ke; ++k, ++it) {
           const int s = it % G_STAGES;
           const uint32_t ph = (it / G_STAGES) & 1;
           if (!pipe_wait(&empty[s], ph ^ 1, abort_flag)) {
@@ -277,10 +340,11 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      uint32_t it = 0, lt = 0;
+      uint32_t it = 0, lt = 0, lc = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++lt) {
-        const TileCoord tc = tile_coord(g, tile);
+      for (int u = blockIdx.x; ok && u < nunits; u += gridDim.x, ++lt) {
+        const WorkUnit wu = work_unit(g, u);
+        const TileCoord& tc = wu.tc;
         const uint32_t b = lt & 1;
         const uint32_t use = lt >> 1;
         const uint32_t d_tmem = tmem_base + b * G_ACC_COLS;
@@ -288,15 +352,16 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         if (!pipe_wait(&acc_empty[b], (use & 1) ^ 1, abort_flag)) break;
         tc_fence_after();
         bool acc = false;
-        if (g.has_lora) {
-          if (!pipe_wait(lora_full, lt & 1, abort_flag)) break;
+        if (g.has_lora && wu.split == 0) {  // the LoRA term belongs to the first K range
+          if (!pipe_wait(lora_full, lc & 1, abort_flag)) break;
+          ++lc;
           tc_fence_after();
           umma_f16(d_tmem, smem_desc_nosw(sbase + SM_LA, 128, 256),
                    smem_desc_nosw(sbase + SM_LB, 128, 256), idesc_f16(G_M, tc.tn, false, false), 0u);
           umma_commit(lora_empty);
           acc = true;
         }
-        for (int k = 0; k < nk; ++k, ++it) {
+        for (int k = wu.kb; k < wu.ke; ++k, ++it) {
           const int s = it % G_STAGES;
           const uint32_t ph = (it / G_STAGES) & 1;
           if (!pipe_wait(&full[s], ph, abort_flag) || !pipe_wait(&afull[s], ph, abort_flag)) {
@@ -348,12 +413,14 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     const uint32_t a_off = uint32_t(j * 8192 + (r >> 3) * 1024 + (r & 7) * 128);
     const uint32_t key = uint32_t(r & 7);
 
-    uint32_t it = 0, lt = 0;
+    uint32_t it = 0, lc = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++lt) {
-      const TileCoord tc = tile_coord(g, tile);
-      if (g.has_lora) {
-        if (!pipe_wait(lora_empty, (lt & 1) ^ 1, abort_flag)) break;
+    for (int u = blockIdx.x; ok && u < nunits; u += gridDim.x) {
+      const WorkUnit wu = work_unit(g, u);
+      const TileCoord& tc = wu.tc;
+      if (g.has_lora && wu.split == 0) {
+        if (!pipe_wait(lora_empty, (lc & 1) ^ 1, abort_flag)) break;
+        ++lc;
         const uint32_t la = sbase + SM_LA;
         const uint32_t lb = sbase + SM_LB;
         if (d < G_M) {
@@ -401,8 +468,10 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       const bool lane_valid = BWD ? (col < g.in_f) : (tc.m0 + r < g.out_f);
       // Element offset (row * in + column) of this thread's first value at stage k, and
       // its quantization block; stages step by 64 columns forward, 64 rows backward.
+      const int nk = wu.ke - wu.kb;
       const int64_t e_step = BWD ? int64_t(G_K) * g.in_f : int64_t(G_K);
       int64_t e_pos = BWD ? int64_t(r) * g.in_f + col : (tc.m0 + r) * g.in_f + 32 * hh;
+      e_pos += int64_t(wu.kb) * e_step;
       auto scale_of = [&](const ScaleSrc& s) -> float {
         if (!lane_valid) return 0.f;
         return g.nested ? __fadd_rn(__fmul_rn(s_code2[s.q], s.a), off) : s.a;
@@ -452,35 +521,85 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     const int grp = (warp - G_EPI_WARP0) >> 2;
     const bool odd = (lane & 1) != 0;
     const int64_t ld_out = BWD ? g.in_f : g.out_f;
+    constexpr bool split = SPLIT;
+    const int nparts = SPLIT ? g.splits - 1 : 0;
+    const bool leader = threadIdx.x == 32 * G_EPI_WARP0;
+    volatile int* s_ticket = reinterpret_cast<volatile int*>(smem + SM_MISC + 8);  // [2]
     uint32_t lt = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++lt) {
-      const TileCoord tc = tile_coord(g, tile);
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++lt) {
+      const WorkUnit wu = work_unit(g, u);
+      const TileCoord& tc = wu.tc;
       const uint32_t b = lt & 1;
       const uint32_t use = lt >> 1;
-      // warp-uniform: tcgen05.ld below is warp-collective
-      const bool ok = __all_sync(0xffffffffu, pipe_wait(&acc_full[b], use & 1, abort_flag));
+      // uniform over the warp (tcgen05.ld is warp-collective) and, for split-K, over all
+      // epilogue warps (they meet at named barriers below)
+      bool ok = pipe_wait(&acc_full[b], use & 1, abort_flag);
+      ok = split ? epi_bar_and(ok) : __all_sync(0xffffffffu, ok);
       tc_fence_after();
       if (!ok) break;
-      const int64_t row = tc.m0 + 32 * lq + lane;
+      const int prow = 32 * lq + lane;  // accumulator row = TMEM lane
+      const int64_t row = tc.m0 + prow;
       const bool row_ok = row < ld_out;  // ld_out is a multiple of 64: pairs are all in or out
-      const float bias_v = (!BWD && g.bias != nullptr && row_ok) ? __half2float(g.bias[row]) : 0.f;
-      // the even lane of a pair writes columns (row, row+1) of token j; the odd lane the
-      // same two columns of token j+1
-      uint32_t* outp = reinterpret_cast<uint32_t*>(g.out + tc.t0 * ld_out + (row & ~int64_t(1)));
       const uint32_t taddr = tmem_base + (uint32_t(32 * lq) << 16) + b * G_ACC_COLS;
-      for (int c0 = 32 * grp; c0 < tc.tn; c0 += 64) {
-        uint32_t acc[32];
-        tmem_ld_32x32b_x32(taddr + uint32_t(c0), acc);
-        tmem_ld_wait();
+      // Split-K: every K range of a tile takes a ticket; all but the last write their fp32
+      // partial to the workspace, the last adds those partials to its own accumulator and
+      // writes the output.  The last one only waits for ranges that already hold tickets,
+      // i.e. are past their main loops, so the wait cannot depend on unscheduled work.
+      int ticket = nparts;
+      if (split) {
+        if (leader) s_ticket[lt & 1] = atomicAdd(g.ws_cnt + wu.tile, 1);
+        epi_bar_sync();
+        ticket = s_ticket[lt & 1];
+      }
+      // partial tiles are column-major [256 tokens][128 rows]: for one token the 32 lanes
+      // of a warp (32 consecutive rows) touch one 128-byte line
+      const float* part0 = g.ws_part + int64_t(wu.tile) * nparts * (G_M * G_ACC_COLS) + prow;
+      if (ticket < nparts) {
+        float* dst = const_cast<float*>(part0) + int64_t(ticket) * (G_M * G_ACC_COLS);
+        for (int c0 = 32 * grp; c0 < tc.tn; c0 += 64) {
+          uint32_t acc[32];
+          tmem_ld_32x32b_x32(taddr + uint32_t(c0), acc);
+          tmem_ld_wait();
 #pragma unroll
-        for (int jj = 0; jj < 32; jj += 2) {
-          const float v0 = __uint_as_float(acc[jj]) + bias_v;      // token c0+jj
-          const float v1 = __uint_as_float(acc[jj + 1]) + bias_v;  // token c0+jj+1
-          // even lane sends its token-(j+1) value, odd lane its token-j value
-          const float other = __shfl_xor_sync(0xffffffffu, odd ? v0 : v1, 1);
-          const int tok = c0 + jj + (odd ? 1 : 0);
-          const uint32_t h = odd ? pack_half2(other, v1) : pack_half2(v0, other);
-          if (row_ok && tok < tc.tn_real) outp[(int64_t(tok) * ld_out) >> 1] = h;
+          for (int j = 0; j < 32; ++j) __stcg(dst + (c0 + j) * G_M, __uint_as_float(acc[j]));
+        }
+        __threadfence();
+        epi_bar_sync();
+        if (leader) atomicAdd(g.ws_cnt + G_SPLIT_MAX_TILES + wu.tile, 1);
+      } else {
+        if (split) {
+          if (leader) {
+            if (!wait_count(g.ws_cnt + G_SPLIT_MAX_TILES + wu.tile, nparts)) *abort_flag = 1;
+            g.ws_cnt[wu.tile] = 0;  // every range of the tile has arrived: reset for reuse
+            g.ws_cnt[G_SPLIT_MAX_TILES + wu.tile] = 0;
+            __threadfence();
+          }
+          epi_bar_sync();
+        }
+        const float bias_v = (!BWD && g.bias != nullptr && row_ok) ? __half2float(g.bias[row]) : 0.f;
+        // the even lane of a pair writes columns (row, row+1) of token j; the odd lane the
+        // same two columns of token j+1
+        uint32_t* outp = reinterpret_cast<uint32_t*>(g.out + tc.t0 * ld_out + (row & ~int64_t(1)));
+        for (int c0 = 32 * grp; c0 < tc.tn; c0 += 64) {
+          uint32_t acc[32];
+          tmem_ld_32x32b_x32(taddr + uint32_t(c0), acc);
+          tmem_ld_wait();
+          for (int p = 0; p < nparts; ++p) {
+            const float* src = part0 + int64_t(p) * (G_M * G_ACC_COLS) + c0 * G_M;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              acc[j] = __float_as_uint(__uint_as_float(acc[j]) + __ldcg(src + j * G_M));
+          }
+#pragma unroll
+          for (int jj = 0; jj < 32; jj += 2) {
+            const float v0 = __uint_as_float(acc[jj]) + bias_v;      // token c0+jj
+            const float v1 = __uint_as_float(acc[jj + 1]) + bias_v;  // token c0+jj+1
+            // even lane sends its token-(j+1) value, odd lane its token-j value
+            const float other = __shfl_xor_sync(0xffffffffu, odd ? v0 : v1, 1);
+            const int tok = c0 + jj + (odd ? 1 : 0);
+            const uint32_t h = odd ? pack_half2(other, v1) : pack_half2(v0, other);
+            if (row_ok && tok < tc.tn_real) outp[(int64_t(tok) * ld_out) >> 1] = h;
+          }
         }
       }
       tc_fence_before();
@@ -550,7 +669,7 @@ static int sm_count_cached() {
   return cached[dev];
 }
 
-template <bool BWD>
+template <bool BWD, bool SPLIT>
 static int set_smem_attr() {
   static std::mutex mu;
   static bool done[64] = {false};
@@ -559,28 +678,83 @@ static int set_smem_attr() {
   if (dev < 0 || dev >= 64) return NF4B_ERR_DEVICE;
   std::lock_guard<std::mutex> lock(mu);
   if (!done[dev]) {
-    NF4B_CUDA_TRY(cudaFuncSetAttribute(nf4_gemm_kernel<BWD>,
+    NF4B_CUDA_TRY(cudaFuncSetAttribute(nf4_gemm_kernel<BWD, SPLIT>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, SM_ALLOC));
     done[dev] = true;
   }
   return NF4B_OK;
 }
 
-// One persistent CTA per SM (at most one per tile).
+// Tiling of one launch: 128-row weight tiles x 256-token tiles, each tile's K stages
+// split into `splits` ranges when there are fewer tiles than SMs.
+struct GemmPlan {
+  int64_t m_tiles, n_tiles, tiles;
+  int32_t nk;
+  int32_t splits;
+};
+
+constexpr int G_MAX_SPLITS = 8;
+
+// Split-K choice from a cost model in stage-times (~0.7 us) of the busiest SM: a unit costs
+// its stages plus ~3 stages of pipeline fill and drain; a split tile adds the round trip
+// of its fp32 partials through L2, measured at ~3 us to write one 128 x 256 partial and
+// ~3 us per partial for the last CTA to read back (4 + 4 per partial, in stage-times).  A
+// split must beat the unsplit launch by 5 % and leave every range at least 2 stages.
+static GemmPlan plan_gemm(int64_t n, int64_t m_rows, int64_t kdim, int64_t sms) {
+  GemmPlan p;
+  p.m_tiles = (m_rows + G_M - 1) / G_M;
+  p.n_tiles = (n + G_NMAX - 1) / G_NMAX;
+  p.tiles = p.m_tiles * p.n_tiles;
+  p.nk = int32_t(kdim / G_K);
+  p.splits = 1;
+  if (p.tiles <= 0 || p.tiles >= sms || p.tiles > G_SPLIT_MAX_TILES) return p;
+  auto cost = [&](int64_t sp) {
+    const int64_t waves = (p.tiles * sp + sms - 1) / sms;
+    const double reduce = sp > 1 ? 4.0 + 4.0 * double(sp - 1) : 0.0;
+    return double(waves) * double((p.nk + sp - 1) / sp + 3) + reduce;
+  };
+  double best = cost(1);
+  for (int sp = 2; sp <= G_MAX_SPLITS && p.nk / sp >= 2; ++sp) {
+    const double c = cost(sp);
+    if (c < 0.95 * best) {
+      best = c;
+      p.splits = sp;
+    }
+  }
+  return p;
+}
+
+static int64_t plan_work_bytes(const GemmPlan& p) {
+  if (p.splits <= 1) return 0;
+  return G_SPLIT_CNT_BYTES + p.tiles * (p.splits - 1) * int64_t(G_M) * G_ACC_COLS * int64_t(sizeof(float));
+}
+
+// One persistent CTA per SM (at most one per work unit).
 template <bool BWD>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, GemmArgs g, int64_t m_rows,
-                       cudaStream_t s) {
-  int st = set_smem_attr<BWD>();
-  if (st != NF4B_OK) return st;
-  const int64_t m_tiles = (m_rows + G_M - 1) / G_M;
-  const int64_t n_tiles = (g.n + G_NMAX - 1) / G_NMAX;
-  NF4B_RETURN_IF(m_tiles * n_tiles > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
-  g.m_tiles = int32_t(m_tiles);
-  g.n_tiles = int32_t(n_tiles);
-  const int64_t tiles = m_tiles * n_tiles;
+                       void* work, int64_t work_bytes, cudaStream_t s) {
   const int64_t sms = sm_count_cached();
-  const unsigned grid = unsigned(tiles < sms ? tiles : sms);
-  nf4_gemm_kernel<BWD><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw, g);
+  GemmPlan p = plan_gemm(g.n, m_rows, BWD ? g.out_f : g.in_f, sms);
+  if (work == nullptr) p.splits = 1;
+  NF4B_RETURN_IF(p.tiles * p.splits > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
+  if (p.splits > 1) {
+    NF4B_RETURN_IF(work_bytes < plan_work_bytes(p), NF4B_ERR_INVALID_ARG);
+    NF4B_RETURN_IF(!aligned(work, 256), NF4B_ERR_ALIGNMENT);
+    g.ws_cnt = static_cast<int32_t*>(work);
+    g.ws_part = reinterpret_cast<float*>(static_cast<uint8_t*>(work) + G_SPLIT_CNT_BYTES);
+  }
+  g.m_tiles = int32_t(p.m_tiles);
+  g.n_tiles = int32_t(p.n_tiles);
+  g.splits = p.splits;
+  g.nk = p.nk;
+  const int64_t units = p.tiles * p.splits;
+  const unsigned grid = unsigned(units < sms ? units : sms);
+  int st = p.splits > 1 ? set_smem_attr<BWD, true>() : set_smem_attr<BWD, false>();
+  if (st != NF4B_OK) return st;
+  if (p.splits > 1)
+    nf4_gemm_kernel<BWD, true><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw, g);
+  else
+    nf4_gemm_kernel<BWD, false><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw, g);
   return launch_status(BWD ? "nf4_gemm_kernel<bwd> launch" : "nf4_gemm_kernel<fwd> launch");
 }
 
@@ -625,9 +799,19 @@ int lora_project16(const void* act, const void* w, int64_t w_stride_r, int64_t w
 
 using namespace nf4b;
 
-extern "C" int nf4b_linear_fwd(const void* x, const uint8_t* packed, const nf4b_qstate* qs,
-                               const void* bias, const nf4b_lora* lora, void* y, int64_t n,
-                               int64_t in_features, int64_t out_features, void* stream) {
+extern "C" int64_t nf4b_linear_work_bytes(int64_t n, int64_t in_features, int64_t out_features,
+                                          int32_t backward) {
+  if (n <= 0 || in_features <= 0 || out_features <= 0) return 0;
+  if (check_device() != NF4B_OK) return -1;
+  const GemmPlan p = plan_gemm(n, backward ? in_features : out_features,
+                               backward ? out_features : in_features, sm_count_cached());
+  return plan_work_bytes(p);
+}
+
+extern "C" int nf4b_linear_fwd_ws(const void* x, const uint8_t* packed, const nf4b_qstate* qs,
+                                  const void* bias, const nf4b_lora* lora, void* y, int64_t n,
+                                  int64_t in_features, int64_t out_features, void* work,
+                                  int64_t work_bytes, void* stream) {
   int32_t lb = 0;
   int st = gemm_common_checks(x, packed, qs, y, n, in_features, out_features, &lb);
   if (st != NF4B_OK) return st;
@@ -664,12 +848,20 @@ extern "C" int nf4b_linear_fwd(const void* x, const uint8_t* packed, const nf4b_
     g.lora_t = static_cast<const __half*>(lora->xa);
     g.lora_scale = lora->scale;
   }
-  return launch_gemm<false>(ta, tw, g, out_features, s);
+  return launch_gemm<false>(ta, tw, g, out_features, work, work_bytes, s);
 }
 
-extern "C" int nf4b_linear_bwd_dx(const void* dy, const uint8_t* packed, const nf4b_qstate* qs,
-                                  const nf4b_lora* lora, void* dyb, void* dx, int64_t n,
-                                  int64_t in_features, int64_t out_features, void* stream) {
+extern "C" int nf4b_linear_fwd(const void* x, const uint8_t* packed, const nf4b_qstate* qs,
+                               const void* bias, const nf4b_lora* lora, void* y, int64_t n,
+                               int64_t in_features, int64_t out_features, void* stream) {
+  return nf4b_linear_fwd_ws(x, packed, qs, bias, lora, y, n, in_features, out_features, nullptr, 0,
+                            stream);
+}
+
+extern "C" int nf4b_linear_bwd_dx_ws(const void* dy, const uint8_t* packed, const nf4b_qstate* qs,
+                                     const nf4b_lora* lora, void* dyb, void* dx, int64_t n,
+                                     int64_t in_features, int64_t out_features, void* work,
+                                     int64_t work_bytes, void* stream) {
   int32_t lb = 0;
   int st = gemm_common_checks(dy, packed, qs, dx, n, in_features, out_features, &lb);
   if (st != NF4B_OK) return st;
@@ -706,7 +898,14 @@ extern "C" int nf4b_linear_bwd_dx(const void* dy, const uint8_t* packed, const n
     g.lora_t = static_cast<const __half*>(dyb);
     g.lora_scale = lora->scale;
   }
-  return launch_gemm<true>(ta, tw, g, in_features, s);
+  return launch_gemm<true>(ta, tw, g, in_features, work, work_bytes, s);
+}
+
+extern "C" int nf4b_linear_bwd_dx(const void* dy, const uint8_t* packed, const nf4b_qstate* qs,
+                                  const nf4b_lora* lora, void* dyb, void* dx, int64_t n,
+                                  int64_t in_features, int64_t out_features, void* stream) {
+  return nf4b_linear_bwd_dx_ws(dy, packed, qs, lora, dyb, dx, n, in_features, out_features, nullptr,
+                               0, stream);
 }
 
 extern "C" int nf4b_gemm_error_flag(int* value, int reset) {

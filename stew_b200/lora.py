@@ -17,7 +17,7 @@ import ctypes
 import torch
 
 from . import _lib
-from .nf4 import _qstate, _stream, _supported, linear_backward_dx, linear_forward
+from .nf4 import _qstate, _stream, _supported, _workspace, linear_backward_dx, linear_forward
 
 LORA_RANK = 16
 
@@ -55,9 +55,11 @@ class NF4LoraFunction(torch.autograd.Function):
             qs = _qstate(st, x.device)
             lc = _lora_c(a16, b16, scaling, xa)
             b = None if bias is None else bias.to(torch.float16).contiguous()
-            _lib.check(_lib.lib().nf4b_linear_fwd(
+            work, wbytes = _workspace(x.device, n, in_f, out_f, False)
+            _lib.check(_lib.lib().nf4b_linear_fwd_ws(
                 x2.data_ptr(), Bv.data_ptr(), ctypes.byref(qs), None if b is None else b.data_ptr(),
-                ctypes.byref(lc), y.data_ptr(), n, in_f, out_f, _stream(x.device)), "nf4b_linear_fwd")
+                ctypes.byref(lc), y.data_ptr(), n, in_f, out_f, work, wbytes, _stream(x.device)),
+                "nf4b_linear_fwd_ws")
         ctx.save_for_backward(x2, xa, a16, b16)
         ctx.st, ctx.Bv, ctx.scaling = st, Bv, float(scaling)
         ctx.x_shape = x.shape
@@ -81,9 +83,10 @@ class NF4LoraFunction(torch.autograd.Function):
             lc = _lora_c(a16, b16, ctx.scaling)
             L = _lib.lib()
             dxt = torch.empty(n, in_f, dtype=torch.float16, device=dev)
-            _lib.check(L.nf4b_linear_bwd_dx(dy.data_ptr(), ctx.Bv.data_ptr(), ctypes.byref(qs),
-                                            ctypes.byref(lc), dyb.data_ptr(), dxt.data_ptr(), n, in_f,
-                                            out_f, _stream(dev)), "nf4b_linear_bwd_dx")
+            work, wbytes = _workspace(dev, n, in_f, out_f, True)
+            _lib.check(L.nf4b_linear_bwd_dx_ws(dy.data_ptr(), ctx.Bv.data_ptr(), ctypes.byref(qs),
+                                               ctypes.byref(lc), dyb.data_ptr(), dxt.data_ptr(), n, in_f,
+                                               out_f, work, wbytes, _stream(dev)), "nf4b_linear_bwd_dx_ws")
             if need_x:
                 dx = dxt.reshape(ctx.x_shape)
             if need_a or need_b:

@@ -117,6 +117,25 @@ def dequantize_nf4(A: torch.Tensor, st) -> torch.Tensor:
     return out
 
 
+_WORK = {}  # (device index, stream handle) -> split-K workspace (uint8, zeroed once)
+
+
+def _workspace(device, n: int, in_f: int, out_f: int, backward: bool):
+    """(pointer, bytes) of the split-K workspace of nf4b_linear_*_ws for the current stream
+    of `device`, or (None, 0) when this shape runs unsplit.  One workspace per stream: its
+    counter words are zero between calls (allocated zeroed, left zero by every call), and
+    calls on one stream never overlap."""
+    need = int(_lib.lib().nf4b_linear_work_bytes(n, in_f, out_f, 1 if backward else 0))
+    if need <= 0:
+        return None, 0
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    buf = _WORK.get(key)
+    if buf is None or buf.numel() < need:
+        buf = torch.zeros(need, dtype=torch.uint8, device=device)
+        _WORK[key] = buf
+    return buf.data_ptr(), buf.numel()
+
+
 def _fused_ok(A: torch.Tensor, out_f: int, in_f: int) -> bool:
     return (A.dtype == torch.float16 and in_f % 64 == 0 and out_f % 64 == 0
             and A.data_ptr() % 16 == 0)
@@ -132,9 +151,11 @@ def linear_forward(A: torch.Tensor, Bv: torch.Tensor, st, bias=None) -> torch.Te
         b = None if bias is None else bias.contiguous()
         with torch.cuda.device(A.device):
             qs = _qstate(st, A.device)
-            _lib.check(_lib.lib().nf4b_linear_fwd(
+            work, wbytes = _workspace(A.device, x.shape[0], in_f, out_f, False)
+            _lib.check(_lib.lib().nf4b_linear_fwd_ws(
                 x.data_ptr(), Bv.data_ptr(), ctypes.byref(qs), None if b is None else b.data_ptr(),
-                None, y.data_ptr(), x.shape[0], in_f, out_f, _stream(A.device)), "nf4b_linear_fwd")
+                None, y.data_ptr(), x.shape[0], in_f, out_f, work, wbytes, _stream(A.device)),
+                "nf4b_linear_fwd_ws")
         return y.reshape(*A.shape[:-1], out_f)
     weight = dequantize_nf4(Bv, st).to(A.dtype)
     return torch.nn.functional.linear(A, weight, bias)
@@ -148,9 +169,10 @@ def linear_backward_dx(grad_output: torch.Tensor, Bv: torch.Tensor, st) -> torch
         dx = torch.empty(dy.shape[0], in_f, dtype=torch.float16, device=dy.device)
         with torch.cuda.device(dy.device):
             qs = _qstate(st, dy.device)
-            _lib.check(_lib.lib().nf4b_linear_bwd_dx(
+            work, wbytes = _workspace(dy.device, dy.shape[0], in_f, out_f, True)
+            _lib.check(_lib.lib().nf4b_linear_bwd_dx_ws(
                 dy.data_ptr(), Bv.data_ptr(), ctypes.byref(qs), None, None, dx.data_ptr(),
-                dy.shape[0], in_f, out_f, _stream(dy.device)), "nf4b_linear_bwd_dx")
+                dy.shape[0], in_f, out_f, work, wbytes, _stream(dy.device)), "nf4b_linear_bwd_dx_ws")
         return dx.reshape(*grad_output.shape[:-1], in_f)
     weight = dequantize_nf4(Bv, st).to(grad_output.dtype)
     return torch.matmul(grad_output, weight)
