@@ -1,0 +1,57 @@
+/*
+ * stew_step.h -- C ABI of the layer kernels around the NF4 projections in the packed-token
+ * QLoRA step (same library and conventions as stew_nf4.h: device pointers, sizes in elements,
+ * `void* stream` = cudaStream_t, int status, no allocation, no host synchronisation).
+ *
+ * They stand in for the reference's Triton kernels of the same Qwen2 layer:
+ *   nf4b_rmsnorm_fwd (delta == NULL) <- solution/rmsnorm.py:19-34  _rms_fwd
+ *   nf4b_rmsnorm_fwd (delta given)   <- solution/rmsnorm.py:152-168 _add_rms_fwd
+ *   nf4b_rmsnorm_bwd (dsum NULL/set) <- solution/rmsnorm.py:36-50 _rms_bwd, :171-190 _add_rms_bwd
+ *   nf4b_rope_qk                     <- solution/rope.py:24-52 rope_kernel (forward, and INVERSE
+ *                                       for the backward) applied to q and k in one launch
+ *   nf4b_swiglu_fwd / _bwd           <- solution/swiglu.py:15-40
+ * Activations are fp16, row-major.
+ */
+#ifndef STEW_STEP_H
+#define STEW_STEP_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* y[r] = fp16(w * fp16(s[r] * rstd[r])), rstd[r] = 1/sqrt(mean(s[r]^2) + eps), where
+ * s = x (delta == NULL) or s = fp16(x + delta), then also written to `sum` (the residual
+ * stream).  x, delta, sum, y: fp16 [rows, hidden]; w: fp32 [hidden]; rstd: fp32 [rows].
+ * hidden must be a multiple of 256 and at most 4096.  */
+int nf4b_rmsnorm_fwd(const void* x, const void* delta, const float* w, float eps, void* sum,
+                     void* y, float* rstd, int64_t rows, int64_t hidden, void* stream);
+
+/* dx = rstd * (w*dy - xn * mean(w*dy*xn)) (+ dsum), xn = x * rstd: the input gradient of
+ * nf4b_rmsnorm_fwd (x = the normalised input s); with the fused add, dsum is the gradient
+ * arriving at `sum`, and dx is the gradient of both x and delta.  */
+int nf4b_rmsnorm_bwd(const void* dy, const void* x, const float* w, const float* rstd,
+                     const void* dsum, void* dx, int64_t rows, int64_t hidden, void* stream);
+
+/* Rotary embedding (rotate-half convention, fp32 math) on q [tokens, q_heads, head_dim] and
+ * k [tokens, k_heads, head_dim] with cos/sin fp32 [tokens, head_dim]:
+ *   out[i] = x[i] cos[i] - x[i+d] sin[i],   out[i+d] = x[i+d] cos[i+d] + x[i] sin[i+d],
+ * d = head_dim/2; inverse != 0 applies the transposed rotation (the backward).
+ * head_dim must be a multiple of 16; either tensor may be skipped with 0 heads.  */
+int nf4b_rope_qk(const void* q, const void* k, const float* cos_t, const float* sin_t, void* q_out,
+                 void* k_out, int64_t tokens, int32_t q_heads, int32_t k_heads, int32_t head_dim,
+                 int32_t inverse, void* stream);
+
+/* m = fp16(fp16(silu(gate)) * up), n elements (a multiple of 8).  */
+int nf4b_swiglu_fwd(const void* gate, const void* up, void* out, int64_t n, void* stream);
+
+/* dgate = fp16(fp16(dout*up) * silu'(gate)), dup = fp16(dout * fp16(silu(gate))).  */
+int nf4b_swiglu_bwd(const void* dout, const void* gate, const void* up, void* dgate, void* dup,
+                    int64_t n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* STEW_STEP_H */

@@ -1,4 +1,5 @@
-"""ctypes binding of libstew_nf4.so (the C ABI declared in include/stew_nf4.h).
+"""ctypes binding of libstew_nf4.so (the C ABI declared in include/stew_nf4.h and
+include/stew_step.h).
 
 The library is built in-tree by stew_b200.build (nvcc, sm_100a).  Loading fails
 loudly when it is missing: there is no CPU or Triton fallback behind this API.
@@ -46,7 +47,7 @@ class LoraC(ctypes.Structure):
                 ("xa", c_void_p)]
 
 
-# name -> (restype, argtypes); every symbol include/stew_nf4.h declares
+# name -> (restype, argtypes); every symbol include/*.h declares
 SIGNATURES = {
     "nf4b_dequant": (c_int32, [c_void_p, ctypes.POINTER(QStateC), c_void_p, c_int32, c_int64, c_void_p]),
     "nf4b_dequant_plan_bytes": (c_int64, [c_int32]),
@@ -66,6 +67,15 @@ SIGNATURES = {
                                         ctypes.POINTER(LoraC), c_void_p, c_void_p, c_int64, c_int64,
                                         c_int64, c_void_p, c_int64, c_void_p]),
     "nf4b_lora_grads_work_bytes": (c_int64, [c_int64, c_int64, c_int64, c_int32]),
+    # layer kernels of the QLoRA step (include/stew_step.h)
+    "nf4b_rmsnorm_fwd": (c_int32, [c_void_p, c_void_p, c_void_p, ctypes.c_float, c_void_p, c_void_p,
+                                   c_void_p, c_int64, c_int64, c_void_p]),
+    "nf4b_rmsnorm_bwd": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                   c_int64, c_int64, c_void_p]),
+    "nf4b_rope_qk": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                               c_int32, c_int32, c_int32, c_int32, c_void_p]),
+    "nf4b_swiglu_fwd": (c_int32, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "nf4b_swiglu_bwd": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "nf4b_lora_grads": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p,
                                   c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int32, c_void_p]),
     "nf4b_lora_grads_noalloc": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p,

@@ -1,0 +1,327 @@
+// Elementwise and row-reduction kernels of the packed-token Qwen2 layer that surrounds the
+// NF4 projections in the QLoRA step: RMSNorm (plain and fused with the residual add), rotary
+// position embedding on q and k, and the SwiGLU product -- forward and backward.
+//
+// They replace the reference's Triton kernels of the same layer (solution/rmsnorm.py:19-50
+// _rms_fwd/_rms_bwd, :152-190 _add_rms_fwd/_add_rms_bwd, solution/rope.py:24-52 rope_kernel,
+// solution/swiglu.py:15-40) with the same rounding points:
+//   RMSNorm      y = fp16(w * fp16(x * r)),  r = rsqrt(mean(x^2) + eps), fp32 math
+//   add+RMSNorm  s = fp16(res + delta), then RMSNorm of s
+//   RoPE         out[i] = x[i] c[i] - x[i+d] s[i],  out[i+d] = x[i+d] c[i+d] + x[i] s[i+d]
+//                (the rotate-half convention of Qwen2); the backward applies the transpose
+//   SwiGLU       m = fp16(fp16(silu(g)) * u)
+// All activations are fp16 row-major; one warp owns one row of a norm (16-byte loads, the
+// row kept in registers between the two passes); the elementwise kernels move 16 bytes per
+// thread and access.
+#include "common.cuh"
+#include "stew_step.h"
+
+namespace nf4b {
+
+constexpr int NORM_WARPS = 8;         // rows per 256-thread CTA
+constexpr int NORM_MAX_CHUNKS = 16;   // 16 x 256 = 4096 features per row at most
+
+__device__ __forceinline__ void h8_to_f(uint4 v, float (&f)[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __half22float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ uint4 f_to_h8(const float (&f)[8]) {
+  uint4 v;
+  uint32_t* p = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) p[i] = pack_half2(f[2 * i], f[2 * i + 1]);
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float round_h(float v) { return __half2float(__float2half_rn(v)); }
+
+// Forward RMSNorm of one row; `delta` (nullable) is added first (fused residual add) and the
+// fp16 sum written to `sum`.
+__global__ void __launch_bounds__(32 * NORM_WARPS)
+    rmsnorm_fwd_kernel(const __half* __restrict__ x, const __half* __restrict__ delta,
+                       const float* __restrict__ w, float eps, __half* __restrict__ sum,
+                       __half* __restrict__ y, float* __restrict__ rstd, int64_t rows, int hidden) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = int64_t(blockIdx.x) * NORM_WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int nc = hidden >> 8;  // 256-value chunks: lane owns values [chunk*256 + lane*8, +8)
+  const __half* xr = x + row * hidden;
+  uint4 v[NORM_MAX_CHUNKS];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NORM_MAX_CHUNKS; ++c) {
+    if (c < nc) {
+      const int off = c * 256 + lane * 8;
+      v[c] = *reinterpret_cast<const uint4*>(xr + off);
+      if (delta != nullptr) {
+        float a[8], b[8];
+        h8_to_f(v[c], a);
+        h8_to_f(*reinterpret_cast<const uint4*>(delta + row * hidden + off), b);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a[i] = __fadd_rn(a[i], b[i]);
+        v[c] = f_to_h8(a);  // the fp16 residual stream
+        *reinterpret_cast<uint4*>(sum + row * hidden + off) = v[c];
+      }
+      float f[8];
+      h8_to_f(v[c], f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / float(hidden) + eps);
+  if (lane == 0) rstd[row] = r;
+#pragma unroll
+  for (int c = 0; c < NORM_MAX_CHUNKS; ++c) {
+    if (c < nc) {
+      const int off = c * 256 + lane * 8;
+      float f[8];
+      h8_to_f(v[c], f);
+      const float4 w0 = *reinterpret_cast<const float4*>(w + off);
+      const float4 w1 = *reinterpret_cast<const float4*>(w + off + 4);
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = __fmul_rn(wv[i], round_h(__fmul_rn(f[i], r)));
+      *reinterpret_cast<uint4*>(y + row * hidden + off) = f_to_h8(f);
+    }
+  }
+}
+
+// Backward: dx = r * (w dy - xn * mean(w dy xn)) (+ dsum), xn = x r.
+__global__ void __launch_bounds__(32 * NORM_WARPS)
+    rmsnorm_bwd_kernel(const __half* __restrict__ dy, const __half* __restrict__ x,
+                       const float* __restrict__ w, const float* __restrict__ rstd,
+                       const __half* __restrict__ dsum, __half* __restrict__ dx, int64_t rows,
+                       int hidden) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = int64_t(blockIdx.x) * NORM_WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int nc = hidden >> 8;
+  const float r = rstd[row];
+  uint4 xv[NORM_MAX_CHUNKS], gv[NORM_MAX_CHUNKS];
+  float dot = 0.f;
+#pragma unroll
+  for (int c = 0; c < NORM_MAX_CHUNKS; ++c) {
+    if (c < nc) {
+      const int off = c * 256 + lane * 8;
+      xv[c] = *reinterpret_cast<const uint4*>(x + row * hidden + off);
+      gv[c] = *reinterpret_cast<const uint4*>(dy + row * hidden + off);
+      float a[8], g[8];
+      h8_to_f(xv[c], a);
+      h8_to_f(gv[c], g);
+      const float4 w0 = *reinterpret_cast<const float4*>(w + off);
+      const float4 w1 = *reinterpret_cast<const float4*>(w + off + 4);
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dot = fmaf(wv[i] * g[i], a[i] * r, dot);
+    }
+  }
+  const float cmean = warp_sum(dot) / float(hidden);
+#pragma unroll
+  for (int c = 0; c < NORM_MAX_CHUNKS; ++c) {
+    if (c < nc) {
+      const int off = c * 256 + lane * 8;
+      float a[8], g[8], o[8];
+      h8_to_f(xv[c], a);
+      h8_to_f(gv[c], g);
+      const float4 w0 = *reinterpret_cast<const float4*>(w + off);
+      const float4 w1 = *reinterpret_cast<const float4*>(w + off + 4);
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      float ds[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (dsum != nullptr) h8_to_f(*reinterpret_cast<const uint4*>(dsum + row * hidden + off), ds);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = r * (wv[i] * g[i] - a[i] * r * cmean) + ds[i];
+      *reinterpret_cast<uint4*>(dx + row * hidden + off) = f_to_h8(o);
+    }
+  }
+}
+
+// RoPE on q [T, hq, D] and k [T, hk, D]: one thread per (token, head, 8 consecutive pairs).
+// inverse = 1 applies the transposed rotation (the backward).
+__global__ void rope_qk_kernel(const __half* __restrict__ q, const __half* __restrict__ k,
+                               const float* __restrict__ cosv, const float* __restrict__ sinv,
+                               __half* __restrict__ qo, __half* __restrict__ ko, int64_t tokens,
+                               int hq, int hk, int head_dim, int inverse) {
+  const int d = head_dim >> 1;
+  const int per_head = d >> 3;  // threads per (token, head)
+  const int64_t per_tok = int64_t(hq + hk) * per_head;
+  const int64_t tid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (tid >= tokens * per_tok) return;
+  const int64_t t = tid / per_tok;
+  const int rem = int(tid - t * per_tok);
+  const int head = rem / per_head;
+  const int i0 = (rem - head * per_head) * 8;
+  const bool isq = head < hq;
+  const __half* src = isq ? q + (t * hq + head) * head_dim : k + (t * hk + (head - hq)) * head_dim;
+  __half* dst = isq ? qo + (t * hq + head) * head_dim : ko + (t * hk + (head - hq)) * head_dim;
+  float a[8], b[8];
+  h8_to_f(*reinterpret_cast<const uint4*>(src + i0), a);      // x[i]
+  h8_to_f(*reinterpret_cast<const uint4*>(src + i0 + d), b);  // x[i+d]
+  const float* cr = cosv + t * head_dim;
+  const float* sr = sinv + t * head_dim;
+  float oa[8], ob[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float c0 = cr[i0 + j], c1 = cr[i0 + d + j];
+    const float s0 = sr[i0 + j], s1 = sr[i0 + d + j];
+    if (!inverse) {
+      oa[j] = __fsub_rn(__fmul_rn(a[j], c0), __fmul_rn(b[j], s0));
+      ob[j] = __fadd_rn(__fmul_rn(b[j], c1), __fmul_rn(a[j], s1));
+    } else {
+      oa[j] = __fadd_rn(__fmul_rn(a[j], c0), __fmul_rn(b[j], s1));
+      ob[j] = __fsub_rn(__fmul_rn(b[j], c1), __fmul_rn(a[j], s0));
+    }
+  }
+  *reinterpret_cast<uint4*>(dst + i0) = f_to_h8(oa);
+  *reinterpret_cast<uint4*>(dst + i0 + d) = f_to_h8(ob);
+}
+
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
+// silu(x) = x / (1 + exp(-x)), IEEE division (the form torch's silu evaluates)
+__device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, __fadd_rn(1.f, expf(-x))); }
+
+// SwiGLU: 8 values per thread.
+__global__ void swiglu_fwd_kernel(const __half* __restrict__ g, const __half* __restrict__ u,
+                                  __half* __restrict__ m, int64_t n8) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  float gf[8], uf[8], o[8];
+  h8_to_f(reinterpret_cast<const uint4*>(g)[i], gf);
+  h8_to_f(reinterpret_cast<const uint4*>(u)[i], uf);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = __fmul_rn(round_h(silu_f(gf[j])), uf[j]);
+  reinterpret_cast<uint4*>(m)[i] = f_to_h8(o);
+}
+
+// dg = fp16(fp16(dm u) * silu'(g)), du = fp16(dm fp16(silu(g))).
+__global__ void swiglu_bwd_kernel(const __half* __restrict__ dm, const __half* __restrict__ g,
+                                  const __half* __restrict__ u, __half* __restrict__ dg,
+                                  __half* __restrict__ du, int64_t n8) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  float df[8], gf[8], uf[8], og[8], ou[8];
+  h8_to_f(reinterpret_cast<const uint4*>(dm)[i], df);
+  h8_to_f(reinterpret_cast<const uint4*>(g)[i], gf);
+  h8_to_f(reinterpret_cast<const uint4*>(u)[i], uf);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float sg = sigmoid_f(gf[j]);
+    const float s16 = round_h(silu_f(gf[j]));
+    ou[j] = __fmul_rn(df[j], s16);
+    const float ds = round_h(__fmul_rn(df[j], uf[j]));
+    og[j] = ds * (sg * (1.f + gf[j] * (1.f - sg)));
+  }
+  reinterpret_cast<uint4*>(dg)[i] = f_to_h8(og);
+  reinterpret_cast<uint4*>(du)[i] = f_to_h8(ou);
+}
+
+static int norm_checks(int64_t rows, int64_t hidden) {
+  NF4B_RETURN_IF(rows < 0 || hidden <= 0, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(hidden % 256 != 0 || hidden > 256 * NORM_MAX_CHUNKS, NF4B_ERR_UNSUPPORTED);
+  return NF4B_OK;
+}
+
+static unsigned norm_grid(int64_t rows) { return unsigned((rows + NORM_WARPS - 1) / NORM_WARPS); }
+
+}  // namespace nf4b
+
+using namespace nf4b;
+
+extern "C" int nf4b_rmsnorm_fwd(const void* x, const void* delta, const float* w, float eps,
+                                void* sum, void* y, float* rstd, int64_t rows, int64_t hidden,
+                                void* stream) {
+  int st = norm_checks(rows, hidden);
+  if (st != NF4B_OK) return st;
+  NF4B_RETURN_IF(!x || !w || !y || !rstd || (delta && !sum), NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(!aligned(x, 16) || !aligned(w, 16) || !aligned(y, 16) ||
+                     (delta && (!aligned(delta, 16) || !aligned(sum, 16))),
+                 NF4B_ERR_ALIGNMENT);
+  if (rows == 0) return NF4B_OK;
+  st = check_device();
+  if (st != NF4B_OK) return st;
+  rmsnorm_fwd_kernel<<<norm_grid(rows), 32 * NORM_WARPS, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(x), static_cast<const __half*>(delta), w, eps,
+      static_cast<__half*>(sum), static_cast<__half*>(y), rstd, rows, int(hidden));
+  return launch_status("rmsnorm_fwd_kernel launch");
+}
+
+extern "C" int nf4b_rmsnorm_bwd(const void* dy, const void* x, const float* w, const float* rstd,
+                                const void* dsum, void* dx, int64_t rows, int64_t hidden,
+                                void* stream) {
+  int st = norm_checks(rows, hidden);
+  if (st != NF4B_OK) return st;
+  NF4B_RETURN_IF(!dy || !x || !w || !rstd || !dx, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(!aligned(dy, 16) || !aligned(x, 16) || !aligned(w, 16) || !aligned(dx, 16) ||
+                     (dsum && !aligned(dsum, 16)),
+                 NF4B_ERR_ALIGNMENT);
+  if (rows == 0) return NF4B_OK;
+  st = check_device();
+  if (st != NF4B_OK) return st;
+  rmsnorm_bwd_kernel<<<norm_grid(rows), 32 * NORM_WARPS, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(dy), static_cast<const __half*>(x), w, rstd,
+      static_cast<const __half*>(dsum), static_cast<__half*>(dx), rows, int(hidden));
+  return launch_status("rmsnorm_bwd_kernel launch");
+}
+
+extern "C" int nf4b_rope_qk(const void* q, const void* k, const float* cos_t, const float* sin_t,
+                            void* q_out, void* k_out, int64_t tokens, int32_t q_heads,
+                            int32_t k_heads, int32_t head_dim, int32_t inverse, void* stream) {
+  NF4B_RETURN_IF(tokens < 0 || q_heads < 0 || k_heads < 0 || head_dim <= 0, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(head_dim % 16 != 0, NF4B_ERR_UNSUPPORTED);
+  NF4B_RETURN_IF((q_heads && (!q || !q_out)) || (k_heads && (!k || !k_out)) || !cos_t || !sin_t,
+                 NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF((q && !aligned(q, 16)) || (k && !aligned(k, 16)) || (q_out && !aligned(q_out, 16)) ||
+                     (k_out && !aligned(k_out, 16)),
+                 NF4B_ERR_ALIGNMENT);
+  const int64_t threads = tokens * (q_heads + k_heads) * (head_dim / 16);
+  if (threads == 0) return NF4B_OK;
+  int st = check_device();
+  if (st != NF4B_OK) return st;
+  rope_qk_kernel<<<unsigned((threads + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(q), static_cast<const __half*>(k), cos_t, sin_t,
+      static_cast<__half*>(q_out), static_cast<__half*>(k_out), tokens, q_heads, k_heads, head_dim,
+      inverse);
+  return launch_status("rope_qk_kernel launch");
+}
+
+extern "C" int nf4b_swiglu_fwd(const void* gate, const void* up, void* out, int64_t n, void* stream) {
+  NF4B_RETURN_IF(n < 0 || (n > 0 && (!gate || !up || !out)), NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(n % 8 != 0, NF4B_ERR_UNSUPPORTED);
+  NF4B_RETURN_IF(!aligned(gate, 16) || !aligned(up, 16) || !aligned(out, 16), NF4B_ERR_ALIGNMENT);
+  if (n == 0) return NF4B_OK;
+  int st = check_device();
+  if (st != NF4B_OK) return st;
+  const int64_t n8 = n / 8;
+  swiglu_fwd_kernel<<<unsigned((n8 + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(gate), static_cast<const __half*>(up), static_cast<__half*>(out), n8);
+  return launch_status("swiglu_fwd_kernel launch");
+}
+
+extern "C" int nf4b_swiglu_bwd(const void* dout, const void* gate, const void* up, void* dgate,
+                               void* dup, int64_t n, void* stream) {
+  NF4B_RETURN_IF(n < 0 || (n > 0 && (!dout || !gate || !up || !dgate || !dup)), NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(n % 8 != 0, NF4B_ERR_UNSUPPORTED);
+  NF4B_RETURN_IF(!aligned(dout, 16) || !aligned(gate, 16) || !aligned(up, 16) || !aligned(dgate, 16) ||
+                     !aligned(dup, 16),
+                 NF4B_ERR_ALIGNMENT);
+  if (n == 0) return NF4B_OK;
+  int st = check_device();
+  if (st != NF4B_OK) return st;
+  const int64_t n8 = n / 8;
+  swiglu_bwd_kernel<<<unsigned((n8 + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(dout), static_cast<const __half*>(gate), static_cast<const __half*>(up),
+      static_cast<__half*>(dgate), static_cast<__half*>(dup), n8);
+  return launch_status("swiglu_bwd_kernel launch");
+}

@@ -4,11 +4,12 @@ SwiGLU MLP 8960, 12 query / 2 key-value heads of dim 128, RMSNorm, RoPE theta 1e
 LoRA adapter on q and v, run on packed token rows.
 
 Scope: the reference patches this model (transformers' Qwen2 under peft/bitsandbytes) and runs
-it on packed real tokens (solution/unpad.py:278-345).  Here only the NF4 projections and the
-LoRA adapters are this library's kernels (fused unpack + tcgen05 GEMMs, forward and backward);
-RMSNorm, RoPE, attention, SwiGLU and the LM-head loss are plain torch operations, because they
-are not on the NF4 path.  Weights are random (seeded) and NF4-quantized on the GPU: no
-checkpoint is used.
+it on packed real tokens (solution/unpad.py:278-345).  The NF4 projections and the LoRA
+adapters are this library's kernels (fused unpack + tcgen05 GEMMs, forward and backward), and
+so are the layer's RMSNorm (fused with the residual add), RoPE and SwiGLU (step_ops, the
+counterparts of solution/rmsnorm.py, rope.py, swiglu.py); attention is torch's variable-length
+flash attention over the packed rows, and the tied LM head + cross-entropy are torch.  Weights
+are random (seeded) and NF4-quantized on the GPU: no checkpoint is used.
 
 `train_step` = forward on the packed rows, backward (LoRA grads only: base weights, norms and
 embedding are frozen), one all-reduce of the LoRA grads across data-parallel ranks
@@ -24,6 +25,7 @@ import torch.nn.functional as F
 
 from . import dp
 from .lora import LORA_RANK, NF4Linear, NF4LoraLinear
+from .step_ops import add_rms_norm, rms_norm, rope_qk, swiglu
 from .sweep import QWEN_PROJ, qwen_model_weights
 
 
@@ -41,11 +43,6 @@ class QwenConfig:
     lora_alpha: float = 32.0
 
 
-def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    xf = x.float()
-    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w).to(torch.float16)
-
-
 def rope_tables(positions: torch.Tensor, head_dim: int, theta: float):
     inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, device=positions.device, dtype=torch.float32) / head_dim))
     ang = positions.float()[:, None] * inv[None, :]
@@ -53,12 +50,15 @@ def rope_tables(positions: torch.Tensor, head_dim: int, theta: float):
     return emb.cos(), emb.sin()
 
 
-def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """x [N, heads, d]; rotate-half convention of Qwen2."""
-    xf = x.float()
-    d = xf.shape[-1] // 2
-    rot = torch.cat([-xf[..., d:], xf[..., :d]], dim=-1)
-    return (xf * cos[:, None, :] + rot * sin[:, None, :]).to(x.dtype)
+def packed_causal_attention(q, k, v, rows):
+    """Causal attention inside each packed row: q [N, H, D], k/v [N, KH, D] (grouped-query
+    heads), rows = (cu_seqlens int32 [B+1], longest row).  The variable-length flash kernel
+    sees only the real tokens, no [N, N] mask."""
+    from torch.nn.attention.varlen import varlen_attn
+    cu, longest = rows
+    r = q.shape[1] // k.shape[1]
+    return varlen_attn(q, k.repeat_interleave(r, 1), v.repeat_interleave(r, 1), cu, cu, longest,
+                       longest, window_size=(-1, 0))
 
 
 class Layer(torch.nn.Module):
@@ -77,20 +77,19 @@ class Layer(torch.nn.Module):
         self.register_buffer("ln1", torch.ones(cfg.hidden, device=device))
         self.register_buffer("ln2", torch.ones(cfg.hidden, device=device))
 
-    def forward(self, x, cos, sin, mask):
+    def attention(self, h, cos, sin, rows):
+        """o(attn(rope(q(h)), rope(k(h)), v(h))) for the normed input h [N, hidden]."""
         c, p = self.cfg, self.proj
-        n = x.shape[0]
-        h = rms_norm(x, self.ln1, c.rms_eps)
-        q = apply_rope(p["q"](h).view(n, c.heads, c.head_dim), cos, sin)
-        k = apply_rope(p["k"](h).view(n, c.kv_heads, c.head_dim), cos, sin)
+        n = h.shape[0]
+        q, k = rope_qk(p["q"](h).view(n, c.heads, c.head_dim), p["k"](h).view(n, c.kv_heads, c.head_dim),
+                       cos, sin)
         v = p["v"](h).view(n, c.kv_heads, c.head_dim)
-        # packed rows: block-diagonal causal mask over the N real tokens
-        a = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
-                                           v.transpose(0, 1)[None], attn_mask=mask, enable_gqa=True)
-        x = x + p["o"](a[0].transpose(0, 1).reshape(n, c.heads * c.head_dim))
-        h = rms_norm(x, self.ln2, c.rms_eps)
-        m = F.silu(p["gate"](h).float()).to(torch.float16) * p["up"](h)
-        return x + p["down"](m)
+        a = packed_causal_attention(q, k, v, rows)
+        return p["o"](a.reshape(n, c.heads * c.head_dim))
+
+    def mlp(self, h):
+        p = self.proj
+        return p["down"](swiglu(p["gate"](h), p["up"](h)))
 
 
 class QwenQLoRA(torch.nn.Module):
@@ -120,12 +119,18 @@ class QwenQLoRA(torch.nn.Module):
         ids = tokens[keep]                                    # packed real tokens [N]
         positions = torch.cat([torch.arange(L, device=dev) for L in lens])
         seg = torch.cat([torch.full((L,), i, device=dev) for i, L in enumerate(lens)])
-        mask = (seg[:, None] == seg[None, :]) & (positions[None, :] <= positions[:, None])
+        cu = torch.zeros(B + 1, dtype=torch.int32, device=dev)
+        cu[1:] = torch.cumsum(lengths.to(torch.int32), 0)
+        rows = (cu, max(lens))
         cos, sin = rope_tables(positions, self.cfg.head_dim, self.cfg.rope_theta)
         x = self.embed[ids]
-        for layer in self.layers:
-            x = layer(x, cos, sin, mask)
-        h = rms_norm(x, self.ln_f, self.cfg.rms_eps)
+        eps = self.cfg.rms_eps
+        h = rms_norm(x, self.layers[0].ln1, eps)
+        for i, layer in enumerate(self.layers):
+            # residual adds fused into the following norm: x += attn; h = norm(x); x += mlp; h = ...
+            x, h = add_rms_norm(x, layer.attention(h, cos, sin, rows), layer.ln2, eps)
+            nxt = self.layers[i + 1].ln1 if i + 1 < len(self.layers) else self.ln_f
+            x, h = add_rms_norm(x, layer.mlp(h), nxt, eps)
         # next-token labels inside each row; a row's last token has none
         nxt = torch.roll(ids, -1)
         has = torch.roll(seg, -1) == seg

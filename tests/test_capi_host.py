@@ -1,4 +1,4 @@
-"""CPU: the C-ABI library loads and exports every symbol include/stew_nf4.h declares;
+"""CPU: the C-ABI library loads and exports every symbol include/*.h declares;
 argument validation happens on the host before any launch; the bitsandbytes patch logic
 (idempotence, alias rebinding, delegation of unsupported inputs) against a stand-in
 bitsandbytes module."""
@@ -15,10 +15,14 @@ from tests.conftest import ROOT
 
 
 def _declared_functions():
-    txt = open(os.path.join(ROOT, "include", "stew_nf4.h")).read()
-    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
-    names = re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(nf4b_\w+)\s*\(", txt, flags=re.M)
-    return sorted(set(names))
+    names = set()
+    inc = os.path.join(ROOT, "include")
+    for h in sorted(os.listdir(inc)):
+        if not h.endswith(".h"):
+            continue
+        txt = re.sub(r"/\*.*?\*/", "", open(os.path.join(inc, h)).read(), flags=re.S)
+        names |= set(re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(nf4b_\w+)\s*\(", txt, flags=re.M))
+    return sorted(names)
 
 
 def test_library_builds_and_exports_all_declared_symbols():

@@ -20,9 +20,25 @@ def _small_model(layers=2, vocab=4096):
     return QwenQLoRA(cfg, device="cuda", seed=3)
 
 
+def rms_norm(x, w, eps):
+    """Qwen2 RMSNorm: fp32 statistics, normalised value rounded to fp16, then the weight."""
+    xf = x.float()
+    xn = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(torch.float16)
+    return (w * xn.float()).to(torch.float16)
+
+
+def apply_rope(x, cos, sin):
+    """x [N, heads, d]; rotate-half convention of Qwen2, fp32 math."""
+    xf = x.float()
+    d = xf.shape[-1] // 2
+    rot = torch.cat([-xf[..., d:], xf[..., :d]], dim=-1)
+    return (xf * cos[:, None, :] + rot * sin[:, None, :]).to(x.dtype)
+
+
 def _ref_loss(model, tokens, lengths):
-    """fp32 reference forward with the oracle-dequantised weights."""
-    from stew_b200.qlora_step import apply_rope, rms_norm, rope_tables
+    """fp32 reference forward with the oracle-dequantised weights: torch attention with a
+    dense block-diagonal causal mask, torch RMSNorm / RoPE / SwiGLU."""
+    from stew_b200.qlora_step import rope_tables
     cfg = model.cfg
     dev = tokens.device
     lens = lengths.tolist()
