@@ -421,7 +421,7 @@ def main():
     if not args.no_step and args.layers == 28:
         from stew_b200.qlora_step import QLoRATrainer, QwenConfig, QwenQLoRA, step_flops, synthetic_batch
         model = QwenQLoRA(QwenConfig(), device="cuda", seed=0, weights=weights)
-        trainer = QLoRATrainer(model)
+        trainer = QLoRATrainer(model, cuda_graph=True)
         tokens, lengths = synthetic_batch(seed=1000 + rank)
         real = torch.tensor([float(lengths.sum())], device="cuda")
         if world > 1:
@@ -431,12 +431,13 @@ def main():
         fl = step_flops(model.cfg, int(lengths.sum()))
         step = {"workload": "Qwen2.5-1.5B QLoRA step: 28 layers, NF4 projections, LoRA r=16 on q/v, "
                             "4 right-padded rows x 512 per rank (~57% real tokens, packed), fwd+bwd, "
-                            "LoRA-grad all-reduce, AdamW",
+                            "LoRA-grad all-reduce, AdamW; the step replayed from one CUDA graph",
                 "ms_per_step": round(t, 3), "tokens_per_s": round(real.item() / (t * 1e-3), 1),
                 "real_tokens_per_step_all_ranks": int(real.item()),
                 "allreduce_bytes": trainer.lora_grad_bytes(),
                 "nf4_gemm_tflops_in_step_rank0": round(fl["nf4_gemm"] / (t * 1e-3) / 1e12, 1),
                 "scaling": "weak (each rank its own 4 rows)"}
+        trainer.release()  # the graph holds NCCL work: release before the group goes
         del trainer, model
         torch.cuda.synchronize()
     clk = clocks.stop()

@@ -93,7 +93,7 @@ struct GemmArgs {
   int32_t n_tiles;        // 256-token tiles
   int32_t splits;         // K ranges per tile (split-K); 1 = none
   int32_t nk;             // K stages of the whole reduction
-  float* ws_part;         // split-K: fp32 partial tiles [tiles][splits-1][128][256]
+  float* ws_part;         // split-K: fp32 partial tiles [tiles][splits][256][128]
   int32_t* ws_cnt;        // split-K: per-tile counters [2][G_SPLIT_MAX_TILES], zero between launches
 };
 
@@ -219,6 +219,17 @@ __device__ __forceinline__ WorkUnit work_unit(const GemmArgs& g, int u) {
   w.kb = int((int64_t(w.split) * g.nk) / g.splits);
   w.ke = int((int64_t(w.split + 1) * g.nk) / g.splits);
   return w;
+}
+
+// 32 lanes x 16 columns of fp32 from TMEM (thread t: row lane base + t, columns [col, col+16)).
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
 }
 
 // Named barrier 1 over the epilogue warps only.
@@ -542,9 +553,10 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       const bool row_ok = row < ld_out;  // ld_out is a multiple of 64: pairs are all in or out
       const uint32_t taddr = tmem_base + (uint32_t(32 * lq) << 16) + b * G_ACC_COLS;
       // Split-K: every K range of a tile takes a ticket; all but the last write their fp32
-      // partial to the workspace, the last adds those partials to its own accumulator and
-      // writes the output.  The last one only waits for ranges that already hold tickets,
-      // i.e. are past their main loops, so the wait cannot depend on unscheduled work.
+      // partial to the workspace slot of their range, the last sums the ranges in range
+      // order (its own from TMEM) and writes the output, so the result does not depend on
+      // which range finishes last.  The last one only waits for ranges that already hold
+      // tickets, i.e. are past their main loops, so the wait cannot depend on unscheduled work.
       int ticket = nparts;
       if (split) {
         if (leader) s_ticket[lt & 1] = atomicAdd(g.ws_cnt + wu.tile, 1);
@@ -553,9 +565,9 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       }
       // partial tiles are column-major [256 tokens][128 rows]: for one token the 32 lanes
       // of a warp (32 consecutive rows) touch one 128-byte line
-      const float* part0 = g.ws_part + int64_t(wu.tile) * nparts * (G_M * G_ACC_COLS) + prow;
+      const float* part0 = g.ws_part + int64_t(wu.tile) * (nparts + 1) * (G_M * G_ACC_COLS) + prow;
       if (ticket < nparts) {
-        float* dst = const_cast<float*>(part0) + int64_t(ticket) * (G_M * G_ACC_COLS);
+        float* dst = const_cast<float*>(part0) + int64_t(wu.split) * (G_M * G_ACC_COLS);
         for (int c0 = 32 * grp; c0 < tc.tn; c0 += 64) {
           uint32_t acc[32];
           tmem_ld_32x32b_x32(taddr + uint32_t(c0), acc);
@@ -582,13 +594,31 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         uint32_t* outp = reinterpret_cast<uint32_t*>(g.out + tc.t0 * ld_out + (row & ~int64_t(1)));
         for (int c0 = 32 * grp; c0 < tc.tn; c0 += 64) {
           uint32_t acc[32];
-          tmem_ld_32x32b_x32(taddr + uint32_t(c0), acc);
-          tmem_ld_wait();
-          for (int p = 0; p < nparts; ++p) {
-            const float* src = part0 + int64_t(p) * (G_M * G_ACC_COLS) + c0 * G_M;
+          if (!SPLIT) {
+            tmem_ld_32x32b_x32(taddr + uint32_t(c0), acc);
+            tmem_ld_wait();
+          } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              acc[j] = __float_as_uint(__uint_as_float(acc[j]) + __ldcg(src + j * G_M));
+            for (int hf = 0; hf < 2; ++hf) {  // 16 columns at a time: own values + running sum
+              uint32_t own[16];
+              tmem_ld_32x32b_x16(taddr + uint32_t(c0 + 16 * hf), own);
+              tmem_ld_wait();
+              float t[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) t[j] = 0.f;
+              for (int sp = 0; sp <= nparts; ++sp) {
+                if (sp == wu.split) {
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) t[j] += __uint_as_float(own[j]);
+                } else {
+                  const float* src = part0 + int64_t(sp) * (G_M * G_ACC_COLS) + (c0 + 16 * hf) * G_M;
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) t[j] += __ldcg(src + j * G_M);
+                }
+              }
+#pragma unroll
+              for (int j = 0; j < 16; ++j) acc[16 * hf + j] = __float_as_uint(t[j]);
+            }
           }
 #pragma unroll
           for (int jj = 0; jj < 32; jj += 2) {
@@ -724,9 +754,11 @@ static GemmPlan plan_gemm(int64_t n, int64_t m_rows, int64_t kdim, int64_t sms) 
   return p;
 }
 
+// Workspace of a split launch: the counter region, then one fp32 partial tile per K range
+// [tiles][splits][256][128] (the last range of a tile to finish leaves its slot unused).
 static int64_t plan_work_bytes(const GemmPlan& p) {
   if (p.splits <= 1) return 0;
-  return G_SPLIT_CNT_BYTES + p.tiles * (p.splits - 1) * int64_t(G_M) * G_ACC_COLS * int64_t(sizeof(float));
+  return G_SPLIT_CNT_BYTES + p.tiles * p.splits * int64_t(G_M) * G_ACC_COLS * int64_t(sizeof(float));
 }
 
 // One persistent CTA per SM (at most one per work unit).

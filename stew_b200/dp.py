@@ -60,5 +60,18 @@ def allreduce_lora_grads(params, local_labels: float, group=None) -> float:
     return total
 
 
+def allreduce_lora_grads_device(params, local_labels: torch.Tensor, group=None) -> torch.Tensor:
+    """allreduce_lora_grads with the count as a device tensor and no host synchronisation,
+    so the exchange can be captured in a CUDA graph.  Returns the global count (device)."""
+    params = list(params)
+    parts = [(p.grad if p.grad is not None else torch.zeros_like(p)).reshape(-1).float() for p in params]
+    flat = torch.cat(parts + [local_labels.reshape(1).float()])
+    if _world(group) > 1:
+        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+    total = flat[-1:].clamp_min(1.0)
+    unflatten_into_grads(params, flat[:-1] / total)
+    return total
+
+
 def lora_grad_bytes(params) -> int:
     return 4 * (sum(p.numel() for p in params) + 1)

@@ -92,6 +92,23 @@ class Layer(torch.nn.Module):
         return p["down"](swiglu(p["gate"](h), p["up"](h)))
 
 
+@dataclass
+class PackedBatch:
+    ids: torch.Tensor        # [N] token ids of the real tokens, row after row
+    positions: torch.Tensor  # [N] position inside the row
+    cu: torch.Tensor         # [B+1] int32 row starts (cumulative lengths)
+    longest: int             # longest row
+    lab_idx: torch.Tensor    # [M] packed index of every token that has a next-token label
+    labels: torch.Tensor     # [M] the label (the next token of the same row)
+
+    @property
+    def n_labels(self) -> int:
+        return int(self.lab_idx.numel())
+
+    def shape_key(self):
+        return (int(self.ids.numel()), int(self.cu.numel()), self.longest, self.n_labels)
+
+
 class QwenQLoRA(torch.nn.Module):
     def __init__(self, cfg: QwenConfig = QwenConfig(), device="cuda", seed: int = 0, weights=None):
         super().__init__()
@@ -109,21 +126,39 @@ class QwenQLoRA(torch.nn.Module):
     def lora_parameters(self):
         return [p for p in self.parameters() if p.requires_grad]
 
-    def forward(self, tokens: torch.Tensor, lengths: torch.Tensor):
-        """tokens [B, T] right-padded, lengths [B].  Returns (sum of next-token CE over the
-        labelled tokens, number of labelled tokens)."""
+    @staticmethod
+    def pack(tokens: torch.Tensor, lengths: torch.Tensor) -> "PackedBatch":
+        """Right-padded rows -> the packed real tokens and their metadata (one host read of
+        the row lengths, as the reference's unpad path does)."""
         B, T = tokens.shape
         dev = tokens.device
-        lens = lengths.tolist()
+        lens = [int(v) for v in lengths.tolist()]
         keep = torch.arange(T, device=dev)[None, :] < lengths[:, None]
         ids = tokens[keep]                                    # packed real tokens [N]
         positions = torch.cat([torch.arange(L, device=dev) for L in lens])
-        seg = torch.cat([torch.full((L,), i, device=dev) for i, L in enumerate(lens)])
         cu = torch.zeros(B + 1, dtype=torch.int32, device=dev)
         cu[1:] = torch.cumsum(lengths.to(torch.int32), 0)
-        rows = (cu, max(lens))
-        cos, sin = rope_tables(positions, self.cfg.head_dim, self.cfg.rope_theta)
-        x = self.embed[ids]
+        # next-token labels inside each row; a row's last token has none
+        starts = [0]
+        for L in lens:
+            starts.append(starts[-1] + L)
+        lab_idx = torch.cat([torch.arange(a, b - 1, device=dev) for a, b in zip(starts[:-1], starts[1:])
+                             if b - a > 1] or [torch.zeros(0, dtype=torch.long, device=dev)])
+        labels = ids[lab_idx + 1]
+        return PackedBatch(ids, positions, cu, max(lens) if lens else 0, lab_idx, labels)
+
+    def forward(self, tokens: torch.Tensor, lengths: torch.Tensor):
+        """tokens [B, T] right-padded, lengths [B].  Returns (sum of next-token CE over the
+        labelled tokens, number of labelled tokens)."""
+        pb = self.pack(tokens, lengths)
+        return self.forward_packed(pb), pb.n_labels
+
+    def forward_packed(self, pb: "PackedBatch") -> torch.Tensor:
+        """Sum of next-token CE over the labelled tokens of a packed batch.  Fixed shapes and
+        no host synchronisation, so a step can be captured in a CUDA graph."""
+        rows = (pb.cu, pb.longest)
+        cos, sin = rope_tables(pb.positions, self.cfg.head_dim, self.cfg.rope_theta)
+        x = self.embed.index_select(0, pb.ids)
         eps = self.cfg.rms_eps
         h = rms_norm(x, self.layers[0].ln1, eps)
         for i, layer in enumerate(self.layers):
@@ -131,13 +166,8 @@ class QwenQLoRA(torch.nn.Module):
             x, h = add_rms_norm(x, layer.attention(h, cos, sin, rows), layer.ln2, eps)
             nxt = self.layers[i + 1].ln1 if i + 1 < len(self.layers) else self.ln_f
             x, h = add_rms_norm(x, layer.mlp(h), nxt, eps)
-        # next-token labels inside each row; a row's last token has none
-        nxt = torch.roll(ids, -1)
-        has = torch.roll(seg, -1) == seg
-        has[-1] = False
-        logits = h[has] @ self.embed.t()
-        loss_sum = F.cross_entropy(logits.float(), nxt[has], reduction="sum")
-        return loss_sum, int(has.sum().item())
+        logits = h.index_select(0, pb.lab_idx) @ self.embed.t()
+        return F.cross_entropy(logits.float(), pb.labels, reduction="sum")
 
 
 def synthetic_batch(batch: int = 4, seq: int = 512, vocab: int = 151936, mean_frac: float = 0.57,
@@ -153,21 +183,96 @@ def synthetic_batch(batch: int = 4, seq: int = 512, vocab: int = 151936, mean_fr
 
 
 class QLoRATrainer:
-    """One QLoRA step per call: forward, backward, LoRA-grad all-reduce, AdamW."""
+    """One QLoRA step per call: forward, backward, LoRA-grad all-reduce, AdamW.
 
-    def __init__(self, model: QwenQLoRA, lr: float = 2e-4, group=None):
+    cuda_graph=True captures the whole step (forward, backward, the all-reduce and AdamW) in
+    one CUDA graph per packed-batch shape and replays it: the step's ~3,000 kernel launches
+    cost one graph launch on the host.  The packed batch is copied into the graph's static
+    input buffers each step; a new shape (token count, rows, longest row, labels) re-captures.
+    The capture's warm-up steps are undone (adapters and optimizer state restored), so every
+    call is exactly one optimizer step."""
+
+    def __init__(self, model: QwenQLoRA, lr: float = 2e-4, group=None, cuda_graph: bool = False):
         self.model = model
         self.params = model.lora_parameters()
-        self.opt = torch.optim.AdamW(self.params, lr=lr, weight_decay=0.0)
+        self.cuda_graph = cuda_graph
+        self.opt = torch.optim.AdamW(self.params, lr=lr, weight_decay=0.0, capturable=cuda_graph)
         self.group = group
+        self._graph = None
+        self._key = None
 
-    def step(self, tokens, lengths):
-        loss_sum, n_lab = self.model(tokens, lengths)
+    def _eager(self, pb):
+        loss_sum = self.model.forward_packed(pb)
         loss_sum.backward()
-        total = dp.allreduce_lora_grads(self.params, n_lab, self.group)
+        total = dp.allreduce_lora_grads(self.params, pb.n_labels, self.group)
         self.opt.step()
         self.opt.zero_grad(set_to_none=True)
-        return float(loss_sum.detach()) / max(n_lab, 1), n_lab, total
+        return loss_sum.detach(), total
+
+    def _graph_body(self):
+        loss = self.model.forward_packed(self._pb)
+        loss.backward()
+        # keep no reference to this autograd graph: a later capture must not reuse its nodes
+        self._loss = loss.detach()
+        self._total = dp.allreduce_lora_grads_device(self.params, self._n_lab, self.group)
+        self.opt.step()
+
+    def _capture(self, pb):
+        dev = pb.ids.device
+        self._graph = None
+        self._pb = PackedBatch(pb.ids.clone(), pb.positions.clone(), pb.cu.clone(), pb.longest,
+                               pb.lab_idx.clone(), pb.labels.clone())
+        self._n_lab = torch.full((1,), float(pb.n_labels), device=dev)
+        saved_p = [p.detach().clone() for p in self.params]
+        saved_s = {p: {k: v.clone() for k, v in st.items() if torch.is_tensor(v)}
+                   for p, st in self.opt.state.items()}
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):  # lazy state (optimizer moments, library handles) before capture
+                self.opt.zero_grad(set_to_none=True)
+                self._graph_body()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        # undo the warm-up steps: adapters and optimizer state as before them (state that the
+        # warm-up created starts from zero, as a fresh optimizer's would)
+        with torch.no_grad():
+            for p, sp in zip(self.params, saved_p):
+                p.copy_(sp)
+            for p, st in self.opt.state.items():
+                old = saved_s.get(p, {})
+                for k, v in st.items():
+                    if torch.is_tensor(v):
+                        if k in old:
+                            v.copy_(old[k])
+                        else:
+                            v.zero_()
+        self.opt.zero_grad(set_to_none=True)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._graph_body()
+        self._graph = g
+        self._key = pb.shape_key()
+
+    def step(self, tokens, lengths):
+        """Returns (mean loss of this rank's labelled tokens as a 0-d device tensor,
+        labelled tokens of this rank, labelled tokens over all ranks)."""
+        pb = self.model.pack(tokens, lengths)
+        n_lab = pb.n_labels
+        if not self.cuda_graph:
+            loss_sum, total = self._eager(pb)
+            return loss_sum / max(n_lab, 1), n_lab, total
+        if self._graph is None or self._key != pb.shape_key():
+            self._capture(pb)
+        for dst, src in ((self._pb.ids, pb.ids), (self._pb.positions, pb.positions), (self._pb.cu, pb.cu),
+                         (self._pb.lab_idx, pb.lab_idx), (self._pb.labels, pb.labels)):
+            dst.copy_(src)
+        self._graph.replay()
+        return self._loss.detach() / max(n_lab, 1), n_lab, self._total
+
+    def release(self):
+        """Drop the captured graph (it holds NCCL work: release before destroying the group)."""
+        self._graph = None
+        self._pb = None
 
     def lora_grad_bytes(self) -> int:
         return dp.lora_grad_bytes(self.params)

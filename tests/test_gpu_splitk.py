@@ -217,3 +217,25 @@ def test_one_workspace_across_shapes(cuda_lib):
             assert max_rel_err(y, x.double() @ W.T) <= GEMM_MAX_REL_ERR, (o, i, n)
             assert int(_counters(ws).count_nonzero()) == 0
     _flag_clear()
+
+
+def test_split_result_is_deterministic(cuda_lib):
+    """The last K range of a tile sums all ranges in range order, whichever finishes last:
+    repeated split launches are bit-identical."""
+    from stew_b200 import _lib
+    from stew_b200.nf4 import _qstate
+    L = _lib.lib()
+    out_f, in_f, n = 1536, 8960, 1170  # down projection: 60 tiles x 2 ranges
+    q, st = _weight((out_f, in_f), 77)
+    qs = _qstate(st, q.device)
+    ws = _ws(int(L.nf4b_linear_work_bytes(n, in_f, out_f, 0)))
+    x = _rand(n, in_f, 78)
+    ys = []
+    for _ in range(5):
+        y = torch.empty(n, out_f, dtype=torch.float16, device="cuda")
+        _fwd(L, x, q, qs, None, None, y, n, in_f, out_f, ws)
+        ys.append(y)
+    torch.cuda.synchronize()
+    assert all(torch.equal(ys[0], y) for y in ys[1:])
+    _flag_clear()
+
