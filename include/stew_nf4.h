@@ -147,7 +147,8 @@ int nf4b_linear_bwd_dx_ws(const void* dy, const uint8_t* packed, const nf4b_qsta
 /* LoRA weight gradients (fp32 out, overwritten):
  *   dA[rank, in]  = scale * (dY B)^T X
  *   dB[out, rank] = scale * dY^T (X A^T)
- * x fp16 [n, in], dy fp16 [n, out], xa fp16 [n, rank], dyb fp16 [n, rank].
+ * x fp16 [n, in], dy fp16 [n, out], xa fp16 [n, rank], dyb fp16 [n, rank], all 16-byte
+ * aligned; in and out multiples of 8.
  * `work` is caller-provided fp32 scratch of nf4b_lora_grads_work_bytes() bytes.  */
 int64_t nf4b_lora_grads_work_bytes(int64_t n, int64_t in_features, int64_t out_features, int32_t rank);
 int nf4b_lora_grads(const void* x, const void* dy, const void* xa, const void* dyb, float scale,

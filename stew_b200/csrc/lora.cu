@@ -30,15 +30,25 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// W(r, k) and W(r, k+1) as one half2 (k in the low half); k is even.
-__device__ __forceinline__ uint32_t ld_w_pair(const __half* w, int64_t sr, int64_t sk, int r,
-                                              int64_t k) {
-  if (sk == 1) return __ldg(reinterpret_cast<const unsigned int*>(w + r * sr + k));
-  const uint32_t lo = __ldg(reinterpret_cast<const unsigned short*>(w + r * sr + k * sk));
-  const uint32_t hi = __ldg(reinterpret_cast<const unsigned short*>(w + r * sr + (k + 1) * sk));
-  return lo | (hi << 16);
+// W(r, k .. k+7) as 8 halves (k a multiple of 8): one 16-byte load when W is K-contiguous
+// (forward: lora A [16, in]), else eight strided loads (backward: lora B [out, 16], which is
+// small and stays in L1/L2).
+template <bool WK>
+__device__ __forceinline__ uint4 ld_w8(const __half* w, int64_t sr, int64_t sk, int r, int64_t k) {
+  if (WK) return __ldg(reinterpret_cast<const uint4*>(w + r * sr + k));
+  uint32_t h[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) h[i] = __ldg(reinterpret_cast<const unsigned short*>(w + r * sr + (k + i) * sk));
+  return make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
 }
 
+// Thread (g, c) of a warp reads, per 32-wide K chunk j, the 8 consecutive values
+// [32 j + 8 c, +8) of token rows g and g+8 (two 16-byte loads) and feeds them to two k16 MMA
+// steps: fragment position 2c(+1) takes values 0-1 (step 0) / 4-5 (step 1), position
+// 2c+8(+9) values 2-3 / 6-7.  The adapter weight is read with the same assignment, so both
+// operands see one permutation of K and the dot products are those of the natural order.
+// WK: the weight is K-contiguous (sk == 1).
+template <bool WK>
 __global__ void __launch_bounds__(LP_THREADS)
     lora_project16_kernel(const __half* __restrict__ act, const __half* __restrict__ w, int64_t sr,
                           int64_t sk, __half* __restrict__ out, int64_t n, int64_t kdim) {
@@ -46,24 +56,27 @@ __global__ void __launch_bounds__(LP_THREADS)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;  // mma fragment coordinates
   const int64_t t0 = int64_t(blockIdx.x) * LP_TOK;
-  const int64_t ksteps = kdim / 16;
-  const int64_t per = (ksteps + LP_WARPS - 1) / LP_WARPS;
-  const int64_t kb = warp * per;
-  const int64_t ke = min64(ksteps, kb + per);
+  const int64_t chunks = kdim / 32;
+  const int64_t per = (chunks + LP_WARPS - 1) / LP_WARPS;
+  const int64_t jb = warp * per;
+  const int64_t je = min64(chunks, jb + per);
   const bool v0 = t0 + g < n, v1 = t0 + g + 8 < n;
-  const unsigned int* x0 = reinterpret_cast<const unsigned int*>(act + (t0 + g) * kdim);
-  const unsigned int* x1 = reinterpret_cast<const unsigned int*>(act + (t0 + g + 8) * kdim);
+  const uint4* x0 = reinterpret_cast<const uint4*>(act + (t0 + g) * kdim);
+  const uint4* x1 = reinterpret_cast<const uint4*>(act + (t0 + g + 8) * kdim);
   float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-  for (int64_t ks = kb; ks < ke; ++ks) {
-    const int64_t k = ks * 16 + 2 * c;
-    uint32_t a[4];
-    a[0] = v0 ? __ldg(x0 + (k >> 1)) : 0u;      // rows g / g+8, k..k+1
-    a[1] = v1 ? __ldg(x1 + (k >> 1)) : 0u;
-    a[2] = v0 ? __ldg(x0 + (k >> 1) + 4) : 0u;  // k+8..k+9
-    a[3] = v1 ? __ldg(x1 + (k >> 1) + 4) : 0u;
-    mma16816(d0, a, ld_w_pair(w, sr, sk, g, k), ld_w_pair(w, sr, sk, g, k + 8));
-    mma16816(d1, a, ld_w_pair(w, sr, sk, 8 + g, k), ld_w_pair(w, sr, sk, 8 + g, k + 8));
+#pragma unroll 2
+  for (int64_t j = jb; j < je; ++j) {
+    const int64_t k = 32 * j + 8 * c;
+    const uint4 xa = v0 ? __ldg(x0 + (k >> 3)) : make_uint4(0, 0, 0, 0);
+    const uint4 xb = v1 ? __ldg(x1 + (k >> 3)) : make_uint4(0, 0, 0, 0);
+    const uint4 w0 = ld_w8<WK>(w, sr, sk, g, k);      // adapter rows 0-7  (output columns of d0)
+    const uint4 w1 = ld_w8<WK>(w, sr, sk, 8 + g, k);  // adapter rows 8-15 (d1)
+    const uint32_t s0[4] = {xa.x, xb.x, xa.y, xb.y};
+    const uint32_t s1[4] = {xa.z, xb.z, xa.w, xb.w};
+    mma16816(d0, s0, w0.x, w0.y);
+    mma16816(d1, s0, w1.x, w1.y);
+    mma16816(d0, s1, w0.z, w0.w);
+    mma16816(d1, s1, w1.z, w1.w);
   }
   red[warp][g][2 * c] = d0[0];
   red[warp][g][2 * c + 1] = d0[1];
@@ -83,98 +96,168 @@ __global__ void __launch_bounds__(LP_THREADS)
 
 int lora_project16(const void* act, const void* w, int64_t w_stride_r, int64_t w_stride_k,
                    void* out, int64_t n, int64_t kdim, cudaStream_t s) {
-  NF4B_RETURN_IF(kdim % 16 != 0, NF4B_ERR_UNSUPPORTED);
-  NF4B_RETURN_IF(!aligned(act, 16) || !aligned(w, 4), NF4B_ERR_ALIGNMENT);
+  NF4B_RETURN_IF(kdim % 32 != 0, NF4B_ERR_UNSUPPORTED);
+  NF4B_RETURN_IF(!aligned(act, 16) || !aligned(w, w_stride_k == 1 ? 16 : 2), NF4B_ERR_ALIGNMENT);
   if (n == 0) return NF4B_OK;
   const int64_t ctas = (n + LP_TOK - 1) / LP_TOK;
   NF4B_RETURN_IF(ctas > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
-  lora_project16_kernel<<<unsigned(ctas), LP_THREADS, 0, s>>>(
-      static_cast<const __half*>(act), static_cast<const __half*>(w), w_stride_r, w_stride_k,
-      static_cast<__half*>(out), n, kdim);
+  if (w_stride_k == 1)
+    lora_project16_kernel<true><<<unsigned(ctas), LP_THREADS, 0, s>>>(
+        static_cast<const __half*>(act), static_cast<const __half*>(w), w_stride_r, w_stride_k,
+        static_cast<__half*>(out), n, kdim);
+  else
+    lora_project16_kernel<false><<<unsigned(ctas), LP_THREADS, 0, s>>>(
+        static_cast<const __half*>(act), static_cast<const __half*>(w), w_stride_r, w_stride_k,
+        static_cast<__half*>(out), n, kdim);
   return launch_status("lora_project16_kernel launch");
 }
 
 // ---------------------------------------------------------------- weight grads
+// G[r, c] = sum_t P[t, r] * Q[t, c] on the tensor cores: M = the 16 adapter rows, N = columns
+// of Q, K = tokens.  Both operands are contiguous along M/N, not K, so each 32-token chunk of
+// P and Q is staged in shared memory (cp.async, double-buffered) and the fragments are read
+// with ldmatrix .trans.  A CTA of 4 warps owns 256 columns (64 per warp) of one token range;
+// the ranges' partial sums go to caller-provided scratch and lora_reduce adds them up.
 constexpr int LO_THREADS = 128;
-constexpr int LO_COLS = 2 * LO_THREADS;  // 256 columns per CTA
-constexpr int LO_TSTAGE = 64;            // token rows of P staged per pass
-constexpr int LO_TARGET_CTAS = 2 * 148;  // two waves' worth of CTAs on a 148-SM B200
+constexpr int LO_COLS = 256;                   // columns per CTA
+constexpr int LO_TOK = 32;                     // tokens per staged chunk (two k16 steps)
+constexpr int LO_QROW = LO_COLS * 2 + 16;      // staged Q row, bytes (+16: conflict-free ldmatrix)
+constexpr int LO_PROW = 48;                    // staged P row, bytes (32 of data + pad)
+constexpr int LO_QBUF = LO_TOK * LO_QROW;
+constexpr int LO_PBUF = LO_TOK * LO_PROW;
+constexpr int LO_TARGET_CTAS = 2 * 148;        // two waves' worth of CTAs on a 148-SM B200
 
 static int64_t outer_splits(int64_t n, int64_t cols) {
   const int64_t col_ctas = (cols + LO_COLS - 1) / LO_COLS;
   int64_t s = (LO_TARGET_CTAS + col_ctas - 1) / col_ctas;
-  const int64_t max_s = (n + LO_TSTAGE - 1) / LO_TSTAGE;
+  const int64_t max_s = (n + LO_TOK - 1) / LO_TOK;
   if (s > max_s) s = max_s;
   return s < 1 ? 1 : s;
 }
 
-// partial[split][r][c] = sum over this split's tokens of P[t, r] * Q[t, c]
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
 __global__ void __launch_bounds__(LO_THREADS)
     lora_outer16_kernel(const __half* __restrict__ P, const __half* __restrict__ Q, int64_t n,
                         int64_t cols, int64_t tok_per_split, float* __restrict__ partial) {
-  __shared__ __align__(16) float ps[LO_TSTAGE * 16];
-  const int64_t c = int64_t(blockIdx.x) * LO_COLS + 2 * threadIdx.x;
+  __shared__ __align__(128) uint8_t qbuf[2][LO_QBUF];
+  __shared__ __align__(128) uint8_t pbuf[2][LO_PBUF];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t c0 = int64_t(blockIdx.x) * LO_COLS;
   const int64_t tb = int64_t(blockIdx.y) * tok_per_split;
   const int64_t te = min64(n, tb + tok_per_split);
-  float acc[16][2];
+
+  // stage tokens [ts, ts + 32) of P (32 B per token) and of Q's 256 columns; rows past te or
+  // columns past `cols` are zero-filled
+  auto stage = [&](int buf, int64_t ts) {
+    const uint32_t qb = smem_u32(qbuf[buf]), pb = smem_u32(pbuf[buf]);
 #pragma unroll
-  for (int r = 0; r < 16; ++r) acc[r][0] = acc[r][1] = 0.f;
-  const bool cok = c < cols;  // cols is even
-  for (int64_t ts = tb; ts < te; ts += LO_TSTAGE) {
-    const int tl = int(min64(LO_TSTAGE, te - ts));
+    for (int i = 0; i < (LO_TOK * LO_COLS / 8) / LO_THREADS; ++i) {
+      const int e = threadIdx.x + i * LO_THREADS;  // 16-byte piece: row e / 32, piece e % 32
+      const int row = e >> 5, pc = e & 31;
+      const int64_t t = ts + row, c = c0 + 8 * pc;
+      const bool ok = t < te && c < cols;
+      cp_async16(qb + row * LO_QROW + pc * 16, ok ? Q + t * cols + c : Q, ok);
+    }
+    if (threadIdx.x < LO_TOK * 2) {
+      const int row = threadIdx.x >> 1, h = threadIdx.x & 1;
+      const int64_t t = ts + row;
+      cp_async16(pb + row * LO_PROW + h * 16, t < te ? P + t * 16 + 8 * h : P, t < te);
+    }
+    cp_async_commit();
+  };
+
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  const int64_t nchunks = (te - tb + LO_TOK - 1) / LO_TOK;
+  if (nchunks > 0) stage(0, tb);
+  for (int64_t ch = 0; ch < nchunks; ++ch) {
+    const int buf = int(ch & 1);
+    if (ch + 1 < nchunks) {
+      stage(buf ^ 1, tb + (ch + 1) * LO_TOK);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
     __syncthreads();
-    for (int e = threadIdx.x; e < tl * 16; e += LO_THREADS) ps[e] = __half2float(P[ts * 16 + e]);
-    __syncthreads();
-    if (cok) {
-      // eight tokens' loads in flight before their multiply-adds
-      constexpr int U = 8;
-      int t = 0;
-      for (; t < tl; t += U) {
-        float2 q[U];
+    const uint32_t qb = smem_u32(qbuf[buf]), pb = smem_u32(pbuf[buf]);
 #pragma unroll
-        for (int u = 0; u < U; ++u)
-          q[u] = (t + u < tl) ? __half22float2(*reinterpret_cast<const __half2*>(Q + (ts + t + u) * cols + c))
-                              : make_float2(0.f, 0.f);
+    for (int ks = 0; ks < 2; ++ks) {
+      // A[r][t] = P[t][r], stored [t][r]: matrices (r 0-7 | 8-15) x (t 0-7 | 8-15)
+      uint32_t a[4];
+      {
+        const int j = lane >> 3, row = lane & 7;
+        const int t = ks * 16 + (j >> 1) * 8 + row, r = (j & 1) * 8;
+        ldsm_x4_t(pb + t * LO_PROW + r * 2, a);
+      }
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          if (t + u >= tl) break;  // rows past the staged ones hold stale values
-          const float4* pr = reinterpret_cast<const float4*>(ps + (t + u) * 16);
-#pragma unroll
-          for (int v4 = 0; v4 < 4; ++v4) {
-            const float4 p = pr[v4];
-            acc[4 * v4 + 0][0] = fmaf(p.x, q[u].x, acc[4 * v4 + 0][0]);
-            acc[4 * v4 + 0][1] = fmaf(p.x, q[u].y, acc[4 * v4 + 0][1]);
-            acc[4 * v4 + 1][0] = fmaf(p.y, q[u].x, acc[4 * v4 + 1][0]);
-            acc[4 * v4 + 1][1] = fmaf(p.y, q[u].y, acc[4 * v4 + 1][1]);
-            acc[4 * v4 + 2][0] = fmaf(p.z, q[u].x, acc[4 * v4 + 2][0]);
-            acc[4 * v4 + 2][1] = fmaf(p.z, q[u].y, acc[4 * v4 + 2][1]);
-            acc[4 * v4 + 3][0] = fmaf(p.w, q[u].x, acc[4 * v4 + 3][0]);
-            acc[4 * v4 + 3][1] = fmaf(p.w, q[u].y, acc[4 * v4 + 3][1]);
-          }
-        }
+      for (int nt = 0; nt < 8; nt += 2) {
+        // B[t][c] = Q[t][c], stored [t][c]: (t 0-7, t 8-15) for column tiles nt and nt+1
+        uint32_t b[4];
+        const int j = lane >> 3, row = lane & 7;
+        const int t = ks * 16 + (j & 1) * 8 + row;
+        const int col = 64 * warp + 8 * (nt + (j >> 1));
+        ldsm_x4_t(qb + t * LO_QROW + col * 2, b);
+        mma16816(acc[nt], a, b[0], b[1]);
+        mma16816(acc[nt + 1], a, b[2], b[3]);
       }
     }
+    __syncthreads();
   }
-  if (cok) {
-    float* dst = partial + int64_t(blockIdx.y) * 16 * cols + c;
+  // D fragment: d[0..1] = G[g][2c..2c+1], d[2..3] = G[g+8][2c..2c+1] of each 16 x 8 tile
+  const int g = lane >> 2, cq = lane & 3;
+  float* dst = partial + int64_t(blockIdx.y) * 16 * cols;
 #pragma unroll
-    for (int r = 0; r < 16; ++r)
-      *reinterpret_cast<float2*>(dst + int64_t(r) * cols) = make_float2(acc[r][0], acc[r][1]);
+  for (int nt = 0; nt < 8; ++nt) {
+    const int64_t c = c0 + 64 * warp + 8 * nt + 2 * cq;
+    if (c < cols) {
+      *reinterpret_cast<float2*>(dst + int64_t(g) * cols + c) = make_float2(acc[nt][0], acc[nt][1]);
+      *reinterpret_cast<float2*>(dst + int64_t(g + 8) * cols + c) = make_float2(acc[nt][2], acc[nt][3]);
+    }
   }
 }
 
 // out = scale * sum_s partial[s]; transpose_out: out[c][r] (dB [out, 16]) else out[r][c] (dA).
-__global__ void lora_reduce_kernel(const float* __restrict__ partial, int64_t splits, int64_t cols,
-                                   float scale, int transpose_out, float* __restrict__ out) {
-  const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;  // index into [16][cols]
-  if (e >= 16 * cols) return;
+// A CTA of 8 warps owns 32 consecutive outputs; warp w sums the splits s = w, w+8, ... and
+// the 8 warp sums are added in warp order (a fixed order: the result is deterministic).
+constexpr int LR_THREADS = 256;
+__global__ void __launch_bounds__(LR_THREADS)
+    lora_reduce_kernel(const float* __restrict__ partial, int64_t splits, int64_t cols,
+                       float scale, int transpose_out, float* __restrict__ out) {
+  __shared__ float ws[LR_THREADS / 32][33];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t e = int64_t(blockIdx.x) * 32 + lane;  // index into [16][cols]
+  const bool ok = e < 16 * cols;
   float sum = 0.f;
-  for (int64_t s = 0; s < splits; ++s) sum += partial[s * 16 * cols + e];
-  const int64_t r = e / cols, c = e - r * cols;
-  if (transpose_out)
-    out[c * 16 + r] = sum * scale;
-  else
-    out[e] = sum * scale;
+  if (ok)
+    for (int64_t sp = warp; sp < splits; sp += LR_THREADS / 32) sum += partial[sp * 16 * cols + e];
+  ws[warp][lane] = sum;
+  __syncthreads();
+  if (warp == 0 && ok) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < LR_THREADS / 32; ++w) t += ws[w][lane];
+    const int64_t r = e / cols, c = e - r * cols;
+    if (transpose_out)
+      out[c * 16 + r] = t * scale;
+    else
+      out[e] = t * scale;
+  }
 }
 
 static int outer_and_reduce(const __half* P, const __half* Q, int64_t n, int64_t cols, float scale,
@@ -186,8 +269,8 @@ static int outer_and_reduce(const __half* P, const __half* Q, int64_t n, int64_t
   int st = launch_status();
   if (st != NF4B_OK) return st;
   const int64_t total = 16 * cols;
-  lora_reduce_kernel<<<unsigned((total + 255) / 256), 256, 0, s>>>(work, splits, cols, scale,
-                                                                  transpose_out, out);
+  lora_reduce_kernel<<<unsigned((total + 31) / 32), LR_THREADS, 0, s>>>(work, splits, cols, scale,
+                                                                       transpose_out, out);
   return launch_status();
 }
 
@@ -210,8 +293,8 @@ extern "C" int nf4b_lora_grads(const void* x, const void* dy, const void* xa, co
   NF4B_RETURN_IF(!x || !dy || !xa || !dyb || !da || !db || !work, NF4B_ERR_INVALID_ARG);
   NF4B_RETURN_IF(n < 0 || in_features <= 0 || out_features <= 0, NF4B_ERR_INVALID_ARG);
   NF4B_RETURN_IF(rank != 16, NF4B_ERR_UNSUPPORTED);
-  NF4B_RETURN_IF(in_features % 2 != 0 || out_features % 2 != 0, NF4B_ERR_UNSUPPORTED);
-  NF4B_RETURN_IF(!aligned(x, 4) || !aligned(dy, 4) || !aligned(xa, 16) || !aligned(dyb, 16) ||
+  NF4B_RETURN_IF(in_features % 8 != 0 || out_features % 8 != 0, NF4B_ERR_UNSUPPORTED);
+  NF4B_RETURN_IF(!aligned(x, 16) || !aligned(dy, 16) || !aligned(xa, 16) || !aligned(dyb, 16) ||
                      !aligned(work, 8),
                  NF4B_ERR_ALIGNMENT);
   int st = check_device();
@@ -274,8 +357,8 @@ extern "C" int nf4b_lora_grads_noalloc(const void* x, const void* dy, const void
   NF4B_RETURN_IF(!x || !dy || !xa || !dyb || !da || !db, NF4B_ERR_INVALID_ARG);
   NF4B_RETURN_IF(n < 0 || in_features <= 0 || out_features <= 0, NF4B_ERR_INVALID_ARG);
   NF4B_RETURN_IF(rank != 16, NF4B_ERR_UNSUPPORTED);
-  NF4B_RETURN_IF(in_features % 2 != 0 || out_features % 2 != 0, NF4B_ERR_UNSUPPORTED);
-  NF4B_RETURN_IF(!aligned(x, 4) || !aligned(dy, 4) || !aligned(xa, 16) || !aligned(dyb, 16),
+  NF4B_RETURN_IF(in_features % 8 != 0 || out_features % 8 != 0, NF4B_ERR_UNSUPPORTED);
+  NF4B_RETURN_IF(!aligned(x, 16) || !aligned(dy, 16) || !aligned(xa, 16) || !aligned(dyb, 16),
                  NF4B_ERR_ALIGNMENT);
   const int64_t need = nf4b_lora_grads_work_bytes(n, in_features, out_features, rank);
   if (need > int64_t(NF4B_NOALLOC_SCRATCH_BYTES)) {
