@@ -144,6 +144,27 @@ int nf4b_linear_bwd_dx_ws(const void* dy, const uint8_t* packed, const nf4b_qsta
                           int64_t n, int64_t in_features, int64_t out_features,
                           void* work, int64_t work_bytes, void* stream);
 
+/* Grouped forward: up to 3 NF4 weights that read the same activation X (q/k/v, gate/up) in
+ * ONE launch; the tiles of all weights share the persistent grid, so small weights (k, v)
+ * fill SMs the large one leaves idle and X streams through one pipeline.  Each item is one
+ * nf4b_linear_fwd (its own output, bias, LoRA adapter and quant state); the split-K
+ * workspace follows nf4b_linear_fwd_ws, sized by nf4b_linear_group_work_bytes over the
+ * items' out_features.  No reference counterpart (the reference makes one F.linear call per
+ * projection).  */
+typedef struct nf4b_linear_item {
+  const uint8_t* packed;     /* packed NF4 weight [out, in]                     */
+  const nf4b_qstate* qs;
+  const void* bias;          /* fp16 [out] or NULL                              */
+  const nf4b_lora* lora;     /* or NULL                                         */
+  void* y;                   /* fp16 [n, out]                                   */
+  int64_t out_features;
+} nf4b_linear_item;
+int64_t nf4b_linear_group_work_bytes(int64_t n, int64_t in_features, const int64_t* out_features,
+                                     int32_t n_items);
+int nf4b_linear_fwd_group(const void* x, int64_t n, int64_t in_features,
+                          const nf4b_linear_item* items, int32_t n_items, void* work,
+                          int64_t work_bytes, void* stream);
+
 /* LoRA weight gradients (fp32 out, overwritten):
  *   dA[rank, in]  = scale * (dY B)^T X
  *   dB[out, rank] = scale * dY^T (X A^T)

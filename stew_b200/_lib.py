@@ -47,6 +47,12 @@ class LoraC(ctypes.Structure):
                 ("xa", c_void_p)]
 
 
+class LinearItemC(ctypes.Structure):
+    """nf4b_linear_item."""
+    _fields_ = [("packed", c_void_p), ("qs", ctypes.POINTER(QStateC)), ("bias", c_void_p),
+                ("lora", ctypes.POINTER(LoraC)), ("y", c_void_p), ("out_features", c_int64)]
+
+
 # name -> (restype, argtypes); every symbol include/*.h declares
 SIGNATURES = {
     "nf4b_dequant": (c_int32, [c_void_p, ctypes.POINTER(QStateC), c_void_p, c_int32, c_int64, c_void_p]),
@@ -66,6 +72,9 @@ SIGNATURES = {
     "nf4b_linear_bwd_dx_ws": (c_int32, [c_void_p, c_void_p, ctypes.POINTER(QStateC),
                                         ctypes.POINTER(LoraC), c_void_p, c_void_p, c_int64, c_int64,
                                         c_int64, c_void_p, c_int64, c_void_p]),
+    "nf4b_linear_group_work_bytes": (c_int64, [c_int64, c_int64, ctypes.POINTER(c_int64), c_int32]),
+    "nf4b_linear_fwd_group": (c_int32, [c_void_p, c_int64, c_int64, ctypes.POINTER(LinearItemC), c_int32,
+                                        c_void_p, c_int64, c_void_p]),
     "nf4b_lora_grads_work_bytes": (c_int64, [c_int64, c_int64, c_int64, c_int32]),
     # layer kernels of the QLoRA step (include/stew_step.h)
     "nf4b_rmsnorm_fwd": (c_int32, [c_void_p, c_void_p, c_void_p, ctypes.c_float, c_void_p, c_void_p,

@@ -54,9 +54,10 @@ constexpr int SM_A = SM_X + G_STAGES * SM_X_BYTES;
 constexpr int SM_P = SM_A + G_STAGES * SM_A_BYTES;
 constexpr int SM_LA = SM_P + G_STAGES * SM_P_BYTES;
 constexpr int SM_LB = SM_LA + SM_LA_BYTES;
-constexpr int SM_CODE = SM_LB + SM_LB_BYTES;   // 16 fp32 NF4 code
-constexpr int SM_CODE2 = SM_CODE + 64;         // 256 fp32 second-level code
-constexpr int SM_BAR = SM_CODE2 + 1024;
+constexpr int G_MAX_W = 3;                     // NF4 weights of one grouped forward launch
+constexpr int SM_CODE = SM_LB + SM_LB_BYTES;   // per weight: 16 fp32 NF4 code
+constexpr int SM_CODE2 = SM_CODE + 64 * G_MAX_W;  // per weight: 256 fp32 second-level code
+constexpr int SM_BAR = SM_CODE2 + 1024 * G_MAX_W;
 // full[S], afull[S], empty[S], acc_full[2], acc_empty[2], lora_full, lora_empty, mma_done
 constexpr int G_NUM_BARS = 3 * G_STAGES + 7;
 constexpr int SM_MISC = SM_BAR + G_NUM_BARS * 8;
@@ -71,7 +72,9 @@ static_assert(SM_ALLOC <= 232448, "shared memory budget");
 constexpr int G_SPLIT_MAX_TILES = 512;
 constexpr int64_t G_SPLIT_CNT_BYTES = 2 * G_SPLIT_MAX_TILES * 4;
 
-struct GemmArgs {
+// One NF4 weight of a launch.  A forward launch may carry up to G_MAX_W weights that share
+// the activation X (q/k/v, gate/up): their 128-row tiles are numbered one after the other.
+struct GemmW {
   const uint8_t* absmax8;
   const float* absmax32;
   const float* code2;
@@ -81,15 +84,21 @@ struct GemmArgs {
   const __half* bias;     // forward only, [out] or null
   const __half* lora_w;   // forward: lora B [out, 16]; backward: lora A [16, in]
   const __half* lora_t;   // forward: X A^T [n, 16];   backward: dY B [n, 16]
+  __half* out;            // forward: Y [n, out]; backward: dX [n, in]
+  int64_t out_f;          // out features of this weight
   float lora_scale;
   int32_t has_lora;
-  __half* out;            // forward: Y [n, out]; backward: dX [n, in]
-  int64_t n;
-  int64_t in_f;
-  int64_t out_f;
   int32_t log2_bs;
   int32_t nested;
-  int32_t m_tiles;        // 128-row weight tiles
+};
+
+struct GemmArgs {
+  GemmW w[G_MAX_W];
+  int32_t nw;             // weights in use
+  int32_t m_end[G_MAX_W]; // weight i owns global 128-row tiles [m_end[i-1], m_end[i])
+  int64_t n;
+  int64_t in_f;
+  int32_t m_tiles;        // 128-row weight tiles, all weights
   int32_t n_tiles;        // 256-token tiles
   int32_t splits;         // K ranges per tile (split-K); 1 = none
   int32_t nk;             // K stages of the whole reduction
@@ -172,20 +181,21 @@ struct ScaleSrc {
   float a;      // nested: second-level absmax; plain: absmax
 };
 
-__device__ __forceinline__ ScaleSrc load_scale_src(const GemmArgs& g, int64_t blk, bool valid) {
+__device__ __forceinline__ ScaleSrc load_scale_src(const GemmW& W, int64_t blk, bool valid) {
   ScaleSrc s{0u, 0.f};
   if (!valid) return s;
-  if (g.nested) {
-    s.q = __ldg(g.absmax8 + blk);
-    s.a = __ldg(g.absmax2 + (blk >> 8));
+  if (W.nested) {
+    s.q = __ldg(W.absmax8 + blk);
+    s.a = __ldg(W.absmax2 + (blk >> 8));
   } else {
-    s.a = __ldg(g.absmax32 + blk);
+    s.a = __ldg(W.absmax32 + blk);
   }
   return s;
 }
 
 struct TileCoord {
-  int64_t m0;   // first weight row (forward: out feature; backward: in feature)
+  int seg;      // weight of the tile (index into GemmArgs::w)
+  int64_t m0;   // first row of that weight (forward: out feature; backward: in feature)
   int64_t t0;   // first token
   int tn_real;  // tokens in this tile
   int tn;       // MMA N (tn_real rounded up to 16)
@@ -195,7 +205,8 @@ __device__ __forceinline__ TileCoord tile_coord(const GemmArgs& g, int tile) {
   TileCoord c;
   const int mt = tile / g.n_tiles;
   const int nt = tile - mt * g.n_tiles;
-  c.m0 = int64_t(mt) * G_M;
+  c.seg = (mt >= g.m_end[0]) + (mt >= g.m_end[1]);
+  c.m0 = int64_t(mt - (c.seg ? g.m_end[c.seg - 1] : 0)) * G_M;
   c.t0 = int64_t(nt) * G_NMAX;
   c.tn_real = int(min64(G_NMAX, g.n - c.t0));
   c.tn = (c.tn_real + 15) & ~15;
@@ -268,8 +279,9 @@ __device__ __forceinline__ bool wait_count(const int32_t* p, int want) {
 // SPLIT: compiled with the split-K epilogue (launches with g.splits > 1).
 template <bool BWD, bool SPLIT>
 __global__ void __launch_bounds__(G_THREADS, 1)
-    nf4_gemm_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_w,
-                    const GemmArgs g) {
+    nf4_gemm_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_w0,
+                    const __grid_constant__ CUtensorMap tm_w1, const __grid_constant__ CUtensorMap tm_w2,
+                    const __grid_constant__ GemmArgs g) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -308,10 +320,14 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tma_desc(&tm_act);
-    prefetch_tma_desc(&tm_w);
+    prefetch_tma_desc(&tm_w0);
+    if (g.nw > 1) prefetch_tma_desc(&tm_w1);
+    if (g.nw > 2) prefetch_tma_desc(&tm_w2);
   }
-  if (threadIdx.x < 16) s_code[threadIdx.x] = __ldg(g.code + threadIdx.x);
-  if (g.nested && threadIdx.x < 256) s_code2[threadIdx.x] = __ldg(g.code2 + threadIdx.x);
+  for (int i = 0; i < g.nw; ++i) {
+    if (threadIdx.x < 16) s_code[16 * i + threadIdx.x] = __ldg(g.w[i].code + threadIdx.x);
+    if (g.w[i].nested && threadIdx.x < 256) s_code2[256 * i + threadIdx.x] = __ldg(g.w[i].code2 + threadIdx.x);
+  }
   if (warp == 1) {
     tmem_alloc(tmem_slot, G_TMEM_COLS);
     tmem_relinquish();
@@ -338,10 +354,11 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           }
           mbar_arrive_expect_tx(&full[s], SM_X_BYTES + SM_P_BYTES);
           tma_load_2d(smem + SM_X + s * SM_X_BYTES, &tm_act, &full[s], k * G_K, int(tc.t0));
+          const CUtensorMap* tm_w = tc.seg == 0 ? &tm_w0 : (tc.seg == 1 ? &tm_w1 : &tm_w2);
           if (!BWD)
-            tma_load_2d(smem + SM_P + s * SM_P_BYTES, &tm_w, &full[s], k * (G_K / 2), int(tc.m0));
+            tma_load_2d(smem + SM_P + s * SM_P_BYTES, tm_w, &full[s], k * (G_K / 2), int(tc.m0));
           else
-            tma_load_2d(smem + SM_P + s * SM_P_BYTES, &tm_w, &full[s], int(tc.m0 / 2), k * G_K);
+            tma_load_2d(smem + SM_P + s * SM_P_BYTES, tm_w, &full[s], int(tc.m0 / 2), k * G_K);
         }
       }
       // no bulk copy may still be landing in this CTA's shared memory at exit
@@ -363,7 +380,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         if (!pipe_wait(&acc_empty[b], (use & 1) ^ 1, abort_flag)) break;
         tc_fence_after();
         bool acc = false;
-        if (g.has_lora && wu.split == 0) {  // the LoRA term belongs to the first K range
+        if (g.w[tc.seg].has_lora && wu.split == 0) {  // the LoRA term belongs to the first K range
           if (!pipe_wait(lora_full, lc & 1, abort_flag)) break;
           ++lc;
           tc_fence_after();
@@ -402,10 +419,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   } else if (warp < G_EPI_WARP0) {
     // ------------------------------------------------------------ decode warps
     const int d = threadIdx.x - 32 * G_DQ_WARP0;  // 0..255
-    float code[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) code[i] = s_code[i];
-    const float off = g.nested ? __ldg(g.offset) : 0.f;
+    float code[16];  // NF4 code of the current tile's weight (reloaded when the weight changes)
+    int code_seg = -1;
 
     // Per-thread geometry of the decoded tile: 256 threads, 4 packed words (32 values,
     // always inside one quantization block, so one scale) per thread and stage.
@@ -429,7 +444,15 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     for (int u = blockIdx.x; ok && u < nunits; u += gridDim.x) {
       const WorkUnit wu = work_unit(g, u);
       const TileCoord& tc = wu.tc;
-      if (g.has_lora && wu.split == 0) {
+      const GemmW& W = g.w[tc.seg];
+      if (tc.seg != code_seg) {
+        code_seg = tc.seg;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) code[i] = s_code[16 * tc.seg + i];
+      }
+      const float off = W.nested ? __ldg(W.offset) : 0.f;
+      const float* code2 = s_code2 + 256 * tc.seg;
+      if (W.has_lora && wu.split == 0) {
         if (!pipe_wait(lora_empty, (lc & 1) ^ 1, abort_flag)) break;
         ++lc;
         const uint32_t la = sbase + SM_LA;
@@ -438,10 +461,10 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           if (!BWD) {
             const int64_t o = tc.m0 + d;  // s * B[o, 0:16]
             uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0;
-            if (o < g.out_f) {
-              const uint4* src = reinterpret_cast<const uint4*>(g.lora_w + o * 16);
-              v0 = scale_pack8(__ldg(src), g.lora_scale);
-              v1 = scale_pack8(__ldg(src + 1), g.lora_scale);
+            if (o < W.out_f) {
+              const uint4* src = reinterpret_cast<const uint4*>(W.lora_w + o * 16);
+              v0 = scale_pack8(__ldg(src), W.lora_scale);
+              v1 = scale_pack8(__ldg(src + 1), W.lora_scale);
             }
             st_shared_v4(la + slab_off(d, 0), v0);
             st_shared_v4(la + slab_off(d, 1), v1);
@@ -450,7 +473,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             float v[16];
 #pragma unroll
             for (int rr = 0; rr < 16; ++rr)
-              v[rr] = (i < g.in_f) ? __half2float(g.lora_w[int64_t(rr) * g.in_f + i]) * g.lora_scale
+              v[rr] = (i < g.in_f) ? __half2float(W.lora_w[int64_t(rr) * g.in_f + i]) * W.lora_scale
                                    : 0.f;
             st_shared_v4(la + slab_off(d, 0),
                          make_uint4(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]),
@@ -467,7 +490,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           const int t = c >> 1, kc = c & 1;
           uint4 v = make_uint4(0, 0, 0, 0);
           if (t < tc.tn_real)
-            v = __ldg(reinterpret_cast<const uint4*>(g.lora_t + (tc.t0 + t) * 16 + kc * 8));
+            v = __ldg(reinterpret_cast<const uint4*>(W.lora_t + (tc.t0 + t) * 16 + kc * 8));
           st_shared_v4(lb + slab_off(t, kc), v);
         }
         fence_proxy_async_smem();
@@ -476,7 +499,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       }
 
       const int64_t col = BWD ? (tc.m0 + 64 * j + 32 * hh) : 0;
-      const bool lane_valid = BWD ? (col < g.in_f) : (tc.m0 + r < g.out_f);
+      const bool lane_valid = BWD ? (col < g.in_f) : (tc.m0 + r < W.out_f);
       // Element offset (row * in + column) of this thread's first value at stage k, and
       // its quantization block; stages step by 64 columns forward, 64 rows backward.
       const int nk = wu.ke - wu.kb;
@@ -485,20 +508,20 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       e_pos += int64_t(wu.kb) * e_step;
       auto scale_of = [&](const ScaleSrc& s) -> float {
         if (!lane_valid) return 0.f;
-        return g.nested ? __fadd_rn(__fmul_rn(s_code2[s.q], s.a), off) : s.a;
+        return W.nested ? __fadd_rn(__fmul_rn(code2[s.q], s.a), off) : s.a;
       };
       // Scale pipeline: the stage's scale is ready before its data arrives, the next
       // stage's is computed while this one decodes, and the raw absmax of the stage
       // after that is in flight.
-      float sc = scale_of(load_scale_src(g, e_pos >> g.log2_bs, lane_valid && nk > 0));
+      float sc = scale_of(load_scale_src(W, e_pos >> W.log2_bs, lane_valid && nk > 0));
       e_pos += e_step;
-      ScaleSrc raw1 = load_scale_src(g, e_pos >> g.log2_bs, lane_valid && nk > 1);
+      ScaleSrc raw1 = load_scale_src(W, e_pos >> W.log2_bs, lane_valid && nk > 1);
       e_pos += e_step;
       for (int k = 0; k < nk; ++k, ++it) {
         const int s = it % G_STAGES;
         const uint32_t ph = (it / G_STAGES) & 1;
         const Nf4Table tab = make_table(code, sc);
-        const ScaleSrc raw2 = load_scale_src(g, e_pos >> g.log2_bs, lane_valid && k + 2 < nk);
+        const ScaleSrc raw2 = load_scale_src(W, e_pos >> W.log2_bs, lane_valid && k + 2 < nk);
         e_pos += e_step;
         const float sc1 = scale_of(raw1);
 
@@ -531,7 +554,6 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     const int lq = warp & 3;
     const int grp = (warp - G_EPI_WARP0) >> 2;
     const bool odd = (lane & 1) != 0;
-    const int64_t ld_out = BWD ? g.in_f : g.out_f;
     constexpr bool split = SPLIT;
     const int nparts = SPLIT ? g.splits - 1 : 0;
     const bool leader = threadIdx.x == 32 * G_EPI_WARP0;
@@ -540,6 +562,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++lt) {
       const WorkUnit wu = work_unit(g, u);
       const TileCoord& tc = wu.tc;
+      const GemmW& W = g.w[tc.seg];
+      const int64_t ld_out = BWD ? g.in_f : W.out_f;
       const uint32_t b = lt & 1;
       const uint32_t use = lt >> 1;
       // uniform over the warp (tcgen05.ld is warp-collective) and, for split-K, over all
@@ -588,10 +612,10 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           }
           epi_bar_sync();
         }
-        const float bias_v = (!BWD && g.bias != nullptr && row_ok) ? __half2float(g.bias[row]) : 0.f;
+        const float bias_v = (!BWD && W.bias != nullptr && row_ok) ? __half2float(W.bias[row]) : 0.f;
         // the even lane of a pair writes columns (row, row+1) of token j; the odd lane the
         // same two columns of token j+1
-        uint32_t* outp = reinterpret_cast<uint32_t*>(g.out + tc.t0 * ld_out + (row & ~int64_t(1)));
+        uint32_t* outp = reinterpret_cast<uint32_t*>(W.out + tc.t0 * ld_out + (row & ~int64_t(1)));
         for (int c0 = 32 * grp; c0 < tc.tn; c0 += 64) {
           uint32_t acc[32];
           if (!SPLIT) {
@@ -730,9 +754,9 @@ constexpr int G_MAX_SPLITS = 8;
 // of its fp32 partials through L2, measured at ~3 us to write one 128 x 256 partial and
 // ~3 us per partial for the last CTA to read back (4 + 4 per partial, in stage-times).  A
 // split must beat the unsplit launch by 5 % and leave every range at least 2 stages.
-static GemmPlan plan_gemm(int64_t n, int64_t m_rows, int64_t kdim, int64_t sms) {
+static GemmPlan plan_gemm(int64_t n, int64_t m_tiles, int64_t kdim, int64_t sms) {
   GemmPlan p;
-  p.m_tiles = (m_rows + G_M - 1) / G_M;
+  p.m_tiles = m_tiles;
   p.n_tiles = (n + G_NMAX - 1) / G_NMAX;
   p.tiles = p.m_tiles * p.n_tiles;
   p.nk = int32_t(kdim / G_K);
@@ -763,10 +787,10 @@ static int64_t plan_work_bytes(const GemmPlan& p) {
 
 // One persistent CTA per SM (at most one per work unit).
 template <bool BWD>
-static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, GemmArgs g, int64_t m_rows,
-                       void* work, int64_t work_bytes, cudaStream_t s) {
+static int launch_gemm(const CUtensorMap& ta, const CUtensorMap (&tw)[G_MAX_W], GemmArgs g,
+                       int64_t m_tiles, int64_t kdim, void* work, int64_t work_bytes, cudaStream_t s) {
   const int64_t sms = sm_count_cached();
-  GemmPlan p = plan_gemm(g.n, m_rows, BWD ? g.out_f : g.in_f, sms);
+  GemmPlan p = plan_gemm(g.n, m_tiles, kdim, sms);
   if (work == nullptr) p.splits = 1;
   NF4B_RETURN_IF(p.tiles * p.splits > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
   if (p.splits > 1) {
@@ -784,9 +808,9 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, GemmArgs g,
   int st = p.splits > 1 ? set_smem_attr<BWD, true>() : set_smem_attr<BWD, false>();
   if (st != NF4B_OK) return st;
   if (p.splits > 1)
-    nf4_gemm_kernel<BWD, true><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw, g);
+    nf4_gemm_kernel<BWD, true><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw[0], tw[1], tw[2], g);
   else
-    nf4_gemm_kernel<BWD, false><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw, g);
+    nf4_gemm_kernel<BWD, false><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw[0], tw[1], tw[2], g);
   return launch_status(BWD ? "nf4_gemm_kernel<bwd> launch" : "nf4_gemm_kernel<fwd> launch");
 }
 
@@ -813,15 +837,27 @@ static int gemm_common_checks(const void* act, const uint8_t* packed, const nf4b
   return NF4B_OK;
 }
 
-static void fill_qstate_args(GemmArgs* g, const nf4b_qstate* qs, int32_t log2_bs) {
-  g->absmax8 = qs->absmax8;
-  g->absmax32 = qs->absmax32;
-  g->code2 = qs->code2;
-  g->absmax2 = qs->absmax2;
-  g->offset = qs->offset;
-  g->code = qs->code;
-  g->log2_bs = log2_bs;
-  g->nested = qs->nested ? 1 : 0;
+static void fill_qstate_args(GemmW* w, const nf4b_qstate* qs, int32_t log2_bs) {
+  w->absmax8 = qs->absmax8;
+  w->absmax32 = qs->absmax32;
+  w->code2 = qs->code2;
+  w->absmax2 = qs->absmax2;
+  w->offset = qs->offset;
+  w->code = qs->code;
+  w->log2_bs = log2_bs;
+  w->nested = qs->nested ? 1 : 0;
+}
+
+static int64_t ceil_tiles(int64_t rows) { return (rows + G_M - 1) / G_M; }
+
+// Global tile boundaries of the weights: unused entries stay past every tile.
+static void set_m_end(GemmArgs* g, const int64_t* rows, int nw) {
+  int64_t acc = 0;
+  for (int i = 0; i < G_MAX_W; ++i) {
+    if (i < nw) acc += ceil_tiles(rows[i]);
+    g->m_end[i] = i < nw ? int32_t(acc) : 0x7FFFFFFF;
+  }
+  g->nw = nw;
 }
 
 int lora_project16(const void* act, const void* w, int64_t w_stride_r, int64_t w_stride_k,
@@ -835,52 +871,81 @@ extern "C" int64_t nf4b_linear_work_bytes(int64_t n, int64_t in_features, int64_
                                           int32_t backward) {
   if (n <= 0 || in_features <= 0 || out_features <= 0) return 0;
   if (check_device() != NF4B_OK) return -1;
-  const GemmPlan p = plan_gemm(n, backward ? in_features : out_features,
+  const GemmPlan p = plan_gemm(n, ceil_tiles(backward ? in_features : out_features),
                                backward ? out_features : in_features, sm_count_cached());
   return plan_work_bytes(p);
+}
+
+extern "C" int64_t nf4b_linear_group_work_bytes(int64_t n, int64_t in_features,
+                                                const int64_t* out_features, int32_t n_items) {
+  if (n <= 0 || in_features <= 0 || !out_features || n_items < 1 || n_items > G_MAX_W) return 0;
+  if (check_device() != NF4B_OK) return -1;
+  int64_t m_tiles = 0;
+  for (int i = 0; i < n_items; ++i) m_tiles += ceil_tiles(out_features[i]);
+  return plan_work_bytes(plan_gemm(n, m_tiles, in_features, sm_count_cached()));
+}
+
+extern "C" int nf4b_linear_fwd_group(const void* x, int64_t n, int64_t in_features,
+                                     const nf4b_linear_item* items, int32_t n_items, void* work,
+                                     int64_t work_bytes, void* stream) {
+  NF4B_RETURN_IF(!items || n_items < 1, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(n_items > G_MAX_W, NF4B_ERR_UNSUPPORTED);
+  int32_t lb[G_MAX_W];
+  for (int i = 0; i < n_items; ++i) {
+    const nf4b_linear_item& it = items[i];
+    int st = gemm_common_checks(x, it.packed, it.qs, it.y, n, in_features, it.out_features, &lb[i]);
+    if (st != NF4B_OK) return st;
+    if (it.lora) {
+      NF4B_RETURN_IF(it.lora->rank != 16, NF4B_ERR_UNSUPPORTED);
+      NF4B_RETURN_IF(!it.lora->a || !it.lora->b || !it.lora->xa, NF4B_ERR_INVALID_ARG);
+      NF4B_RETURN_IF(!aligned(it.lora->a, 16) || !aligned(it.lora->b, 16) || !aligned(it.lora->xa, 16),
+                     NF4B_ERR_ALIGNMENT);
+    }
+  }
+  if (n == 0) return NF4B_OK;
+  int st = check_device();
+  if (st != NF4B_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUtensorMap ta, tw[G_MAX_W];
+  st = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, uint64_t(in_features), uint64_t(n),
+                    uint64_t(in_features) * 2, G_K, G_NMAX, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != NF4B_OK) return st;
+  GemmArgs g{};
+  int64_t rows[G_MAX_W];
+  for (int i = 0; i < n_items; ++i) {
+    const nf4b_linear_item& it = items[i];
+    st = make_tmap_2d(&tw[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, it.packed, uint64_t(in_features / 2),
+                      uint64_t(it.out_features), uint64_t(in_features / 2), G_K / 2, G_M,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != NF4B_OK) return st;
+    GemmW& w = g.w[i];
+    fill_qstate_args(&w, it.qs, lb[i]);
+    w.bias = static_cast<const __half*>(it.bias);
+    w.out = static_cast<__half*>(it.y);
+    w.out_f = it.out_features;
+    if (it.lora) {
+      st = lora_project16(x, it.lora->a, in_features, 1, it.lora->xa, n, in_features, s);
+      if (st != NF4B_OK) return st;
+      w.has_lora = 1;
+      w.lora_w = static_cast<const __half*>(it.lora->b);
+      w.lora_t = static_cast<const __half*>(it.lora->xa);
+      w.lora_scale = it.lora->scale;
+    }
+    rows[i] = it.out_features;
+  }
+  for (int i = n_items; i < G_MAX_W; ++i) tw[i] = tw[0];  // unused kernel parameters
+  set_m_end(&g, rows, n_items);
+  g.n = n;
+  g.in_f = in_features;
+  return launch_gemm<false>(ta, tw, g, g.m_end[n_items - 1], in_features, work, work_bytes, s);
 }
 
 extern "C" int nf4b_linear_fwd_ws(const void* x, const uint8_t* packed, const nf4b_qstate* qs,
                                   const void* bias, const nf4b_lora* lora, void* y, int64_t n,
                                   int64_t in_features, int64_t out_features, void* work,
                                   int64_t work_bytes, void* stream) {
-  int32_t lb = 0;
-  int st = gemm_common_checks(x, packed, qs, y, n, in_features, out_features, &lb);
-  if (st != NF4B_OK) return st;
-  if (lora) {
-    NF4B_RETURN_IF(lora->rank != 16, NF4B_ERR_UNSUPPORTED);
-    NF4B_RETURN_IF(!lora->a || !lora->b || !lora->xa, NF4B_ERR_INVALID_ARG);
-    NF4B_RETURN_IF(!aligned(lora->a, 16) || !aligned(lora->b, 16) || !aligned(lora->xa, 16),
-                   NF4B_ERR_ALIGNMENT);
-  }
-  if (n == 0) return NF4B_OK;
-  st = check_device();
-  if (st != NF4B_OK) return st;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  CUtensorMap ta, tw;
-  st = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, uint64_t(in_features), uint64_t(n),
-                    uint64_t(in_features) * 2, G_K, G_NMAX, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (st != NF4B_OK) return st;
-  st = make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, uint64_t(in_features / 2),
-                    uint64_t(out_features), uint64_t(in_features / 2), G_K / 2, G_M,
-                    CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (st != NF4B_OK) return st;
-  GemmArgs g{};
-  fill_qstate_args(&g, qs, lb);
-  g.bias = static_cast<const __half*>(bias);
-  g.out = static_cast<__half*>(y);
-  g.n = n;
-  g.in_f = in_features;
-  g.out_f = out_features;
-  if (lora) {
-    st = lora_project16(x, lora->a, in_features, 1, lora->xa, n, in_features, s);
-    if (st != NF4B_OK) return st;
-    g.has_lora = 1;
-    g.lora_w = static_cast<const __half*>(lora->b);
-    g.lora_t = static_cast<const __half*>(lora->xa);
-    g.lora_scale = lora->scale;
-  }
-  return launch_gemm<false>(ta, tw, g, out_features, work, work_bytes, s);
+  const nf4b_linear_item it{packed, qs, bias, lora, y, out_features};
+  return nf4b_linear_fwd_group(x, n, in_features, &it, 1, work, work_bytes, stream);
 }
 
 extern "C" int nf4b_linear_fwd(const void* x, const uint8_t* packed, const nf4b_qstate* qs,
@@ -916,21 +981,25 @@ extern "C" int nf4b_linear_bwd_dx_ws(const void* dy, const uint8_t* packed, cons
                     CU_TENSOR_MAP_SWIZZLE_64B);
   if (st != NF4B_OK) return st;
   GemmArgs g{};
-  fill_qstate_args(&g, qs, lb);
-  g.out = static_cast<__half*>(dx);
+  GemmW& w = g.w[0];
+  fill_qstate_args(&w, qs, lb);
+  w.out = static_cast<__half*>(dx);
+  w.out_f = out_features;
   g.n = n;
   g.in_f = in_features;
-  g.out_f = out_features;
   if (lora) {
     // dY B: B is [out, 16] row-major -> element (r, k=o) at o*16 + r
     st = lora_project16(dy, lora->b, 1, 16, dyb, n, out_features, s);
     if (st != NF4B_OK) return st;
-    g.has_lora = 1;
-    g.lora_w = static_cast<const __half*>(lora->a);
-    g.lora_t = static_cast<const __half*>(dyb);
-    g.lora_scale = lora->scale;
+    w.has_lora = 1;
+    w.lora_w = static_cast<const __half*>(lora->a);
+    w.lora_t = static_cast<const __half*>(dyb);
+    w.lora_scale = lora->scale;
   }
-  return launch_gemm<true>(ta, tw, g, in_features, work, work_bytes, s);
+  const int64_t rows = in_features;
+  set_m_end(&g, &rows, 1);
+  const CUtensorMap tws[G_MAX_W] = {tw, tw, tw};
+  return launch_gemm<true>(ta, tws, g, g.m_end[0], out_features, work, work_bytes, s);
 }
 
 extern "C" int nf4b_linear_bwd_dx(const void* dy, const uint8_t* packed, const nf4b_qstate* qs,

@@ -17,7 +17,8 @@ import ctypes
 import torch
 
 from . import _lib
-from .nf4 import _qstate, _stream, _supported, _workspace, linear_backward_dx, linear_forward
+from .nf4 import (_qstate, _stream, _supported, _workspace, _workspace_bytes, linear_backward_dx,
+                  linear_forward)
 
 LORA_RANK = 16
 
@@ -103,6 +104,133 @@ class NF4LoraFunction(torch.autograd.Function):
         if ctx.has_bias and ctx.needs_input_grad[3]:
             dbias = dy.float().sum(0).to(ctx.param_dtypes[2])
         return dx, None, None, dbias, da, db, None
+
+
+def _bwd_dx(dy, Bv, st, lora=None, dyb=None):
+    """dX of one projection (+ the adapter's dX term when lora = (a16, b16, scaling))."""
+    out_f, in_f = int(st.shape[0]), int(st.shape[1])
+    n = dy.shape[0]
+    dev = dy.device
+    dx = torch.empty(n, in_f, dtype=torch.float16, device=dev)
+    qs = _qstate(st, dev)
+    lc = None if lora is None else _lora_c(lora[0], lora[1], lora[2])
+    work, wbytes = _workspace(dev, n, in_f, out_f, True)
+    _lib.check(_lib.lib().nf4b_linear_bwd_dx_ws(
+        dy.data_ptr(), Bv.data_ptr(), ctypes.byref(qs), None if lc is None else ctypes.byref(lc),
+        None if dyb is None else dyb.data_ptr(), dx.data_ptr(), n, in_f, out_f, work, wbytes,
+        _stream(dev)), "nf4b_linear_bwd_dx_ws")
+    return dx
+
+
+def _lora_weight_grads(x2, dy, xa, dyb, scaling, in_f, out_f):
+    dev = dy.device
+    n = dy.shape[0]
+    L = _lib.lib()
+    da32 = torch.empty(LORA_RANK, in_f, dtype=torch.float32, device=dev)
+    db32 = torch.empty(out_f, LORA_RANK, dtype=torch.float32, device=dev)
+    wb = int(L.nf4b_lora_grads_work_bytes(n, in_f, out_f, LORA_RANK))
+    work = torch.empty(max(wb, 16) // 4 + 4, dtype=torch.float32, device=dev)
+    _lib.check(L.nf4b_lora_grads(x2.data_ptr(), dy.data_ptr(), xa.data_ptr(), dyb.data_ptr(), scaling,
+                                 da32.data_ptr(), db32.data_ptr(), work.data_ptr(), n, in_f, out_f,
+                                 LORA_RANK, _stream(dev)), "nf4b_lora_grads")
+    return da32, db32
+
+
+class GroupedNF4Function(torch.autograd.Function):
+    """Several NF4 projections of one input -- q/k/v, or gate/up -- each optionally with a
+    rank-16 adapter: ONE forward launch (nf4b_linear_fwd_group; the adapters' x A^T
+    projections run just before it).  Backward: one fused dX GEMM per projection (with its
+    adapter term) summed into dX, and each adapter's weight gradients.
+    specs: one (packed, quant_state, scaling or None, bias or None) per projection;
+    params: (lora_A, lora_B) of the projections whose scaling is not None, in order."""
+
+    @staticmethod
+    def forward(ctx, x, specs, *params):
+        in_f = int(specs[0][1].shape[1])
+        x2 = x.reshape(-1, in_f).contiguous()
+        n = x2.shape[0]
+        dev = x.device
+        items = (_lib.LinearItemC * len(specs))()
+        keep, outs, saved, pi = [], [], [], 0
+        with torch.cuda.device(dev):
+            for i, (packed, st, scaling, bias) in enumerate(specs):
+                out_f = int(st.shape[0])
+                y = torch.empty(n, out_f, dtype=torch.float16, device=dev)
+                qs = _qstate(st, dev)
+                b = None if bias is None else bias.to(torch.float16).contiguous()
+                lc = None
+                if scaling is not None:
+                    a16 = params[pi].to(torch.float16).contiguous()
+                    b16 = params[pi + 1].to(torch.float16).contiguous()
+                    xa = torch.empty(n, LORA_RANK, dtype=torch.float16, device=dev)
+                    lc = _lora_c(a16, b16, scaling, xa)
+                    saved.append((a16, b16, xa))
+                    pi += 2
+                keep += [y, qs, b, lc]
+                items[i].packed = packed.data_ptr()
+                items[i].qs = ctypes.pointer(qs)
+                items[i].bias = None if b is None else b.data_ptr()
+                items[i].lora = None if lc is None else ctypes.pointer(lc)
+                items[i].y = y.data_ptr()
+                items[i].out_features = out_f
+                outs.append(y)
+            outs_c = (ctypes.c_int64 * len(specs))(*[int(st.shape[0]) for _, st, _, _ in specs])
+            need = int(_lib.lib().nf4b_linear_group_work_bytes(n, in_f, outs_c, len(specs)))
+            work, wbytes = _workspace_bytes(dev, need)
+            _lib.check(_lib.lib().nf4b_linear_fwd_group(x2.data_ptr(), n, in_f, items, len(specs), work,
+                                                        wbytes, _stream(dev)), "nf4b_linear_fwd_group")
+        tensors = [x2]
+        for a16, b16, xa in saved:
+            tensors += [a16, b16, xa]
+        ctx.save_for_backward(*tensors)
+        ctx.specs = specs
+        ctx.x_shape = x.shape
+        ctx.param_dtypes = [p.dtype for p in params]
+        return tuple(y.reshape(*x.shape[:-1], y.shape[1]) for y in outs)
+
+    @staticmethod
+    def backward(ctx, *grads):
+        x2, *rest = ctx.saved_tensors
+        n, in_f = x2.shape
+        dev = x2.device
+        dx = None
+        pgrads = []
+        li = 0
+        with torch.cuda.device(dev):
+            for (packed, st, scaling, _), gy in zip(ctx.specs, grads):
+                out_f = int(st.shape[0])
+                Bv = packed.view(-1, 1)
+                if scaling is not None:
+                    a16, b16, xa = rest[3 * li:3 * li + 3]
+                    li += 1
+                if gy is None:
+                    if scaling is not None:
+                        pgrads += [None, None]
+                    continue
+                dy = gy.reshape(n, out_f).to(torch.float16).contiguous()
+                if scaling is None:
+                    part = _bwd_dx(dy, Bv, st)
+                else:
+                    dyb = torch.empty(n, LORA_RANK, dtype=torch.float16, device=dev)
+                    part = _bwd_dx(dy, Bv, st, (a16, b16, scaling), dyb)
+                    da32, db32 = _lora_weight_grads(x2, dy, xa, dyb, scaling, in_f, out_f)
+                    pgrads += [da32, db32]
+                dx = part if dx is None else dx.add_(part)
+        pgrads = [None if gr is None else gr.to(dt) for gr, dt in zip(pgrads, ctx.param_dtypes)]
+        return (None if dx is None else dx.reshape(ctx.x_shape), None, *pgrads)
+
+
+def grouped_projection(x, modules):
+    """The outputs of several NF4Linear / NF4LoraLinear modules that read the same input x,
+    computed by one grouped forward launch (up to 3 modules)."""
+    specs, params = [], []
+    for m in modules:
+        if isinstance(m, NF4LoraLinear):
+            specs.append((m.packed, m.quant_state, m.scaling, m.bias))
+            params += [m.lora_A, m.lora_B]
+        else:
+            specs.append((m.packed, m.quant_state, None, m.bias))
+    return GroupedNF4Function.apply(x, tuple(specs), *params)
 
 
 def nf4_lora_linear(x, packed, st, lora_a, lora_b, scaling, bias=None):

@@ -125,7 +125,12 @@ def _workspace(device, n: int, in_f: int, out_f: int, backward: bool):
     of `device`, or (None, 0) when this shape runs unsplit.  One workspace per stream: its
     counter words are zero between calls (allocated zeroed, left zero by every call), and
     calls on one stream never overlap."""
-    need = int(_lib.lib().nf4b_linear_work_bytes(n, in_f, out_f, 1 if backward else 0))
+    return _workspace_bytes(device, int(_lib.lib().nf4b_linear_work_bytes(n, in_f, out_f,
+                                                                          1 if backward else 0)))
+
+
+def _workspace_bytes(device, need: int):
+    """The stream's split-K workspace grown to `need` bytes ((None, 0) when need is 0)."""
     if need <= 0:
         return None, 0
     key = (device.index, torch.cuda.current_stream(device).cuda_stream)

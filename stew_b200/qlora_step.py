@@ -24,7 +24,7 @@ import torch
 import torch.nn.functional as F
 
 from . import dp
-from .lora import LORA_RANK, NF4Linear, NF4LoraLinear
+from .lora import LORA_RANK, NF4Linear, NF4LoraLinear, grouped_projection
 from .step_ops import add_rms_norm, rms_norm, rope_qk, swiglu
 from .sweep import QWEN_PROJ, qwen_model_weights
 
@@ -67,11 +67,14 @@ class Layer(torch.nn.Module):
         self.cfg = cfg
         mods = {}
         for (name, _), (packed, st) in zip(QWEN_PROJ, weights):
+            # Qwen2 has biases on q/k/v only (frozen, fp16)
+            bias = ((torch.randn(int(st.shape[0]), device=device) * 0.02).to(torch.float16)
+                    if name in ("q", "k", "v") else None)
             if name in ("q", "v"):
-                m = NF4LoraLinear(packed, st, lora_alpha=cfg.lora_alpha, device=device)
+                m = NF4LoraLinear(packed, st, lora_alpha=cfg.lora_alpha, bias=bias, device=device)
                 torch.nn.init.normal_(m.lora_B, std=0.01)
             else:
-                m = NF4Linear(packed, st)
+                m = NF4Linear(packed, st, bias=bias)
             mods[name] = m
         self.proj = torch.nn.ModuleDict(mods)
         self.register_buffer("ln1", torch.ones(cfg.hidden, device=device))
@@ -81,15 +84,16 @@ class Layer(torch.nn.Module):
         """o(attn(rope(q(h)), rope(k(h)), v(h))) for the normed input h [N, hidden]."""
         c, p = self.cfg, self.proj
         n = h.shape[0]
-        q, k = rope_qk(p["q"](h).view(n, c.heads, c.head_dim), p["k"](h).view(n, c.kv_heads, c.head_dim),
-                       cos, sin)
-        v = p["v"](h).view(n, c.kv_heads, c.head_dim)
+        q, k, v = grouped_projection(h, [p["q"], p["k"], p["v"]])  # one launch
+        q, k = rope_qk(q.view(n, c.heads, c.head_dim), k.view(n, c.kv_heads, c.head_dim), cos, sin)
+        v = v.view(n, c.kv_heads, c.head_dim)
         a = packed_causal_attention(q, k, v, rows)
         return p["o"](a.reshape(n, c.heads * c.head_dim))
 
     def mlp(self, h):
         p = self.proj
-        return p["down"](swiglu(p["gate"](h), p["up"](h)))
+        gate, up = grouped_projection(h, [p["gate"], p["up"]])  # one launch
+        return p["down"](swiglu(gate, up))
 
 
 @dataclass

@@ -56,6 +56,8 @@ def _ref_loss(model, tokens, lengths):
         W = torch.from_numpy(O.dequant_nf4(mod.packed.cpu().numpy(),
                                            to_oracle_state(mod.quant_state, mod.packed)).astype(np.float32)).cuda()
         y = h.float() @ W.t()
+        if mod.bias is not None:
+            y = y + mod.bias.float()
         if hasattr(mod, "lora_A"):
             a = mod.lora_A.detach().clone().requires_grad_(True)
             b = mod.lora_B.detach().clone().requires_grad_(True)
