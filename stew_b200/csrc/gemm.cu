@@ -201,11 +201,14 @@ struct TileCoord {
   int tn;       // MMA N (tn_real rounded up to 16)
 };
 
+// MULTI: the launch carries more than one weight (a grouped forward).  Single-weight launches
+// compile with the weight index fixed at 0, so its fields stay direct constant-bank operands.
+template <bool MULTI>
 __device__ __forceinline__ TileCoord tile_coord(const GemmArgs& g, int tile) {
   TileCoord c;
   const int mt = tile / g.n_tiles;
   const int nt = tile - mt * g.n_tiles;
-  c.seg = (mt >= g.m_end[0]) + (mt >= g.m_end[1]);
+  c.seg = MULTI ? (mt >= g.m_end[0]) + (mt >= g.m_end[1]) : 0;
   c.m0 = int64_t(mt - (c.seg ? g.m_end[c.seg - 1] : 0)) * G_M;
   c.t0 = int64_t(nt) * G_NMAX;
   c.tn_real = int(min64(G_NMAX, g.n - c.t0));
@@ -222,11 +225,12 @@ struct WorkUnit {
   int kb, ke;   // stage range [kb, ke)
 };
 
+template <bool MULTI>
 __device__ __forceinline__ WorkUnit work_unit(const GemmArgs& g, int u) {
   WorkUnit w;
   w.tile = u / g.splits;
   w.split = u - w.tile * g.splits;
-  w.tc = tile_coord(g, w.tile);
+  w.tc = tile_coord<MULTI>(g, w.tile);
   w.kb = int((int64_t(w.split) * g.nk) / g.splits);
   w.ke = int((int64_t(w.split + 1) * g.nk) / g.splits);
   return w;
@@ -277,7 +281,7 @@ __device__ __forceinline__ bool wait_count(const int32_t* p, int want) {
 }
 
 // SPLIT: compiled with the split-K epilogue (launches with g.splits > 1).
-template <bool BWD, bool SPLIT>
+template <bool BWD, bool SPLIT, bool MULTI>
 __global__ void __launch_bounds__(G_THREADS, 1)
     nf4_gemm_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_w0,
                     const __grid_constant__ CUtensorMap tm_w1, const __grid_constant__ CUtensorMap tm_w2,
@@ -343,7 +347,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < nunits; u += gridDim.x) {
-        const WorkUnit wu = work_unit(g, u);
+        const WorkUnit wu = work_unit<MULTI>(g, u);
         const TileCoord& tc = wu.tc;
         for (int k = wu.kb; k < wu.ke; ++k, ++it) {
           const int s = it % G_STAGES;
@@ -371,7 +375,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       uint32_t it = 0, lt = 0, lc = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < nunits; u += gridDim.x, ++lt) {
-        const WorkUnit wu = work_unit(g, u);
+        const WorkUnit wu = work_unit<MULTI>(g, u);
         const TileCoord& tc = wu.tc;
         const uint32_t b = lt & 1;
         const uint32_t use = lt >> 1;
@@ -380,7 +384,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         if (!pipe_wait(&acc_empty[b], (use & 1) ^ 1, abort_flag)) break;
         tc_fence_after();
         bool acc = false;
-        if (g.w[tc.seg].has_lora && wu.split == 0) {  // the LoRA term belongs to the first K range
+        if (g.w[MULTI ? tc.seg : 0].has_lora && wu.split == 0) {  // the LoRA term belongs to the first K range
           if (!pipe_wait(lora_full, lc & 1, abort_flag)) break;
           ++lc;
           tc_fence_after();
@@ -442,9 +446,9 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     uint32_t it = 0, lc = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < nunits; u += gridDim.x) {
-      const WorkUnit wu = work_unit(g, u);
+      const WorkUnit wu = work_unit<MULTI>(g, u);
       const TileCoord& tc = wu.tc;
-      const GemmW& W = g.w[tc.seg];
+      const GemmW& W = g.w[MULTI ? tc.seg : 0];
       if (tc.seg != code_seg) {
         code_seg = tc.seg;
 #pragma unroll
@@ -560,9 +564,9 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     volatile int* s_ticket = reinterpret_cast<volatile int*>(smem + SM_MISC + 8);  // [2]
     uint32_t lt = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++lt) {
-      const WorkUnit wu = work_unit(g, u);
+      const WorkUnit wu = work_unit<MULTI>(g, u);
       const TileCoord& tc = wu.tc;
-      const GemmW& W = g.w[tc.seg];
+      const GemmW& W = g.w[MULTI ? tc.seg : 0];
       const int64_t ld_out = BWD ? g.in_f : W.out_f;
       const uint32_t b = lt & 1;
       const uint32_t use = lt >> 1;
@@ -723,7 +727,7 @@ static int sm_count_cached() {
   return cached[dev];
 }
 
-template <bool BWD, bool SPLIT>
+template <bool BWD, bool SPLIT, bool MULTI>
 static int set_smem_attr() {
   static std::mutex mu;
   static bool done[64] = {false};
@@ -732,7 +736,7 @@ static int set_smem_attr() {
   if (dev < 0 || dev >= 64) return NF4B_ERR_DEVICE;
   std::lock_guard<std::mutex> lock(mu);
   if (!done[dev]) {
-    NF4B_CUDA_TRY(cudaFuncSetAttribute(nf4_gemm_kernel<BWD, SPLIT>,
+    NF4B_CUDA_TRY(cudaFuncSetAttribute(nf4_gemm_kernel<BWD, SPLIT, MULTI>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, SM_ALLOC));
     done[dev] = true;
   }
@@ -805,12 +809,23 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap (&tw)[G_MAX_W], 
   g.nk = p.nk;
   const int64_t units = p.tiles * p.splits;
   const unsigned grid = unsigned(units < sms ? units : sms);
-  int st = p.splits > 1 ? set_smem_attr<BWD, true>() : set_smem_attr<BWD, false>();
-  if (st != NF4B_OK) return st;
-  if (p.splits > 1)
-    nf4_gemm_kernel<BWD, true><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw[0], tw[1], tw[2], g);
-  else
-    nf4_gemm_kernel<BWD, false><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw[0], tw[1], tw[2], g);
+  const bool split = p.splits > 1;
+  int st;
+  if (!BWD && g.nw > 1) {
+    st = split ? set_smem_attr<BWD, true, !BWD>() : set_smem_attr<BWD, false, !BWD>();
+    if (st != NF4B_OK) return st;
+    if (split)
+      nf4_gemm_kernel<BWD, true, !BWD><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw[0], tw[1], tw[2], g);
+    else
+      nf4_gemm_kernel<BWD, false, !BWD><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw[0], tw[1], tw[2], g);
+  } else {
+    st = split ? set_smem_attr<BWD, true, false>() : set_smem_attr<BWD, false, false>();
+    if (st != NF4B_OK) return st;
+    if (split)
+      nf4_gemm_kernel<BWD, true, false><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw[0], tw[1], tw[2], g);
+    else
+      nf4_gemm_kernel<BWD, false, false><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw[0], tw[1], tw[2], g);
+  }
   return launch_status(BWD ? "nf4_gemm_kernel<bwd> launch" : "nf4_gemm_kernel<fwd> launch");
 }
 
