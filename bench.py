@@ -419,6 +419,24 @@ def profile_case():
     print("profile case done")
 
 
+def profile_step():
+    import torch
+    from stew_b200.qlora_step import QLoRATrainer, QwenConfig, QwenQLoRA, synthetic_batch
+    torch.cuda.set_device(0)
+    model = QwenQLoRA(QwenConfig(layers=4, vocab=32768), device="cuda", seed=0)
+    trainer = QLoRATrainer(model)
+    tokens, lengths = synthetic_batch(vocab=32768, seed=1000)
+    for _ in range(2):
+        trainer.step(tokens, lengths)
+    torch.cuda.synchronize()
+    # the profiled region (ncu --profile-from-start off): exactly one step
+    torch.cuda.profiler.start()
+    trainer.step(tokens, lengths)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    print("profile step ok", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -437,12 +455,18 @@ def main():
     ap.add_argument("--profile-case", action="store_true",
                     help="small single-GPU case for ncu captures: one 2-layer unpack sweep, then one "
                          "fused forward and one fused backward GEMM of the gate projection at N=2048")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="small single-GPU case for an ncu launch list of the QLoRA step: a 4-layer "
+                         "model (small vocabulary), two eager warm-up steps, then one step inside "
+                         "cudaProfilerStart/Stop (use ncu --profile-from-start off)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
     if args.profile_case:
         return profile_case()
+    if args.profile_step:
+        return profile_step()
 
     import torch
     world, rank, local = _dist()

@@ -200,7 +200,9 @@ class QLoRATrainer:
         self.model = model
         self.params = model.lora_parameters()
         self.cuda_graph = cuda_graph
-        self.opt = torch.optim.AdamW(self.params, lr=lr, weight_decay=0.0, capturable=cuda_graph)
+        # fused: one kernel for all adapters (the multi-tensor form was ~0.9 ms per step)
+        self.opt = torch.optim.AdamW(self.params, lr=lr, weight_decay=0.0, capturable=cuda_graph,
+                                     fused=True)
         self.group = group
         self._graph = None
         self._key = None

@@ -70,8 +70,11 @@ def test_host_validation_rejects_before_launch():
     qs.nested = 0
     assert L.nf4b_linear_fwd(ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.byref(qs), None, None,
                              ctypes.c_void_p(16), 4, 96, 64, None) == _lib.NF4B_ERR_UNSUPPORTED
+    # plain (not nested) state without its fp32 absmax
+    qs.absmax32 = None
     assert L.nf4b_linear_fwd(ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.byref(qs), None, None,
-                             ctypes.c_void_p(16), 4, 64, 64, None) != _lib.NF4B_OK or True
+                             ctypes.c_void_p(16), 4, 64, 64, None) == _lib.NF4B_ERR_INVALID_ARG
+    qs.absmax32 = 16
     lc = _lib.LoraC()
     lc.rank = 8
     lc.a = lc.b = lc.xa = 16
@@ -80,6 +83,17 @@ def test_host_validation_rejects_before_launch():
     assert L.nf4b_lora_grads_work_bytes(100, 1536, 256, 16) > 0
     assert L.nf4b_lora_grads_work_bytes(100, 1536, 256, 8) == -1
     assert L.nf4b_dequant_plan_bytes(0) == 0 and L.nf4b_dequant_plan_bytes(3) > 0
+    # grouped forward: at most 3 weights, at least 1
+    items = (_lib.LinearItemC * 4)()
+    assert L.nf4b_linear_fwd_group(16, 8, 64, items, 4, None, 0, None) == _lib.NF4B_ERR_UNSUPPORTED
+    assert L.nf4b_linear_fwd_group(16, 8, 64, items, 0, None, 0, None) == _lib.NF4B_ERR_INVALID_ARG
+    # layer kernels of the step: hidden not a multiple of 256, odd element counts, head_dim
+    assert L.nf4b_rmsnorm_fwd(16, None, 16, 1e-6, None, 16, 16, 4, 1000, None) == _lib.NF4B_ERR_UNSUPPORTED
+    assert L.nf4b_rmsnorm_bwd(16, 16, 16, 16, None, 16, 4, 8192, None) == _lib.NF4B_ERR_UNSUPPORTED
+    assert L.nf4b_swiglu_fwd(16, 16, 16, 12, None) == _lib.NF4B_ERR_UNSUPPORTED
+    assert L.nf4b_swiglu_bwd(16, 16, 16, 16, 16, 12, None) == _lib.NF4B_ERR_UNSUPPORTED
+    assert L.nf4b_rope_qk(16, 16, 16, 16, 16, 16, 1, 1, 1, 100, 0, None) == _lib.NF4B_ERR_UNSUPPORTED
+    assert L.nf4b_rmsnorm_fwd(None, None, 16, 1e-6, None, 16, 16, 4, 256, None) == _lib.NF4B_ERR_INVALID_ARG
 
 
 def test_supported_envelope_mirrors_reference_guard():
