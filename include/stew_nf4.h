@@ -165,6 +165,27 @@ int nf4b_linear_fwd_group(const void* x, int64_t n, int64_t in_features,
                           const nf4b_linear_item* items, int32_t n_items, void* work,
                           int64_t work_bytes, void* stream);
 
+/* Grouped backward: dX = sum_i dY_i . W_i (+ each item's LoRA dX term) for up to 3 NF4
+ * weights that read the same input in the forward (q/k/v, gate/up) -- ONE GEMM whose K
+ * dimension concatenates the items' out features, so the per-projection dX and their sum
+ * never exist.  dx fp16 [n, in] is written (not accumulated).  Each item's dyb receives
+ * dY_i . B_i when it has an adapter (for nf4b_lora_grads).  The split-K workspace follows
+ * nf4b_linear_bwd_dx_ws, sized by nf4b_linear_bwd_group_work_bytes.  No reference
+ * counterpart (autograd adds one dX per projection there).  */
+typedef struct nf4b_linear_bwd_item {
+  const void* dy;            /* fp16 [n, out] gradient of this projection's output */
+  const uint8_t* packed;     /* packed NF4 weight [out, in]                     */
+  const nf4b_qstate* qs;
+  const nf4b_lora* lora;     /* or NULL                                         */
+  void* dyb;                 /* fp16 [n, rank] when lora is given               */
+  int64_t out_features;
+} nf4b_linear_bwd_item;
+int64_t nf4b_linear_bwd_group_work_bytes(int64_t n, int64_t in_features,
+                                         const int64_t* out_features, int32_t n_items);
+int nf4b_linear_bwd_dx_group(const nf4b_linear_bwd_item* items, int32_t n_items, void* dx,
+                             int64_t n, int64_t in_features, void* work, int64_t work_bytes,
+                             void* stream);
+
 /* LoRA weight gradients (fp32 out, overwritten):
  *   dA[rank, in]  = scale * (dY B)^T X
  *   dB[out, rank] = scale * dY^T (X A^T)

@@ -47,6 +47,12 @@ class LoraC(ctypes.Structure):
                 ("xa", c_void_p)]
 
 
+class LinearBwdItemC(ctypes.Structure):
+    """nf4b_linear_bwd_item."""
+    _fields_ = [("dy", c_void_p), ("packed", c_void_p), ("qs", ctypes.POINTER(QStateC)),
+                ("lora", ctypes.POINTER(LoraC)), ("dyb", c_void_p), ("out_features", c_int64)]
+
+
 class LinearItemC(ctypes.Structure):
     """nf4b_linear_item."""
     _fields_ = [("packed", c_void_p), ("qs", ctypes.POINTER(QStateC)), ("bias", c_void_p),
@@ -75,6 +81,9 @@ SIGNATURES = {
     "nf4b_linear_group_work_bytes": (c_int64, [c_int64, c_int64, ctypes.POINTER(c_int64), c_int32]),
     "nf4b_linear_fwd_group": (c_int32, [c_void_p, c_int64, c_int64, ctypes.POINTER(LinearItemC), c_int32,
                                         c_void_p, c_int64, c_void_p]),
+    "nf4b_linear_bwd_group_work_bytes": (c_int64, [c_int64, c_int64, ctypes.POINTER(c_int64), c_int32]),
+    "nf4b_linear_bwd_dx_group": (c_int32, [ctypes.POINTER(LinearBwdItemC), c_int32, c_void_p, c_int64,
+                                           c_int64, c_void_p, c_int64, c_void_p]),
     "nf4b_lora_grads_work_bytes": (c_int64, [c_int64, c_int64, c_int64, c_int32]),
     # layer kernels of the QLoRA step (include/stew_step.h)
     "nf4b_rmsnorm_fwd": (c_int32, [c_void_p, c_void_p, c_void_p, ctypes.c_float, c_void_p, c_void_p,

@@ -95,7 +95,8 @@ struct GemmW {
 struct GemmArgs {
   GemmW w[G_MAX_W];
   int32_t nw;             // weights in use
-  int32_t m_end[G_MAX_W]; // weight i owns global 128-row tiles [m_end[i-1], m_end[i])
+  int32_t m_end[G_MAX_W]; // forward: weight i owns global 128-row tiles [m_end[i-1], m_end[i])
+  int32_t k_end[G_MAX_W]; // backward: weight i owns K stages [k_end[i-1], k_end[i]) (its out features)
   int64_t n;
   int64_t in_f;
   int32_t m_tiles;        // 128-row weight tiles, all weights
@@ -247,6 +248,13 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
       : "r"(taddr));
 }
 
+// A backward launch over several weights concatenates their K (each weight's out features):
+// stage k belongs to weight kseg(k), whose local stage is k - kbeg(kseg(k)).
+__device__ __forceinline__ int kseg(const GemmArgs& g, int k) {
+  return (k >= g.k_end[0]) + (k >= g.k_end[1]);
+}
+__device__ __forceinline__ int kbeg(const GemmArgs& g, int s) { return s ? g.k_end[s - 1] : 0; }
+
 // Named barrier 1 over the epilogue warps only.
 __device__ __forceinline__ void epi_bar_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(G_EPI_WARPS * 32) : "memory");
@@ -283,9 +291,13 @@ __device__ __forceinline__ bool wait_count(const int32_t* p, int want) {
 // SPLIT: compiled with the split-K epilogue (launches with g.splits > 1).
 template <bool BWD, bool SPLIT, bool MULTI>
 __global__ void __launch_bounds__(G_THREADS, 1)
-    nf4_gemm_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_w0,
+    nf4_gemm_kernel(const __grid_constant__ CUtensorMap tm_act0, const __grid_constant__ CUtensorMap tm_act1,
+                    const __grid_constant__ CUtensorMap tm_act2, const __grid_constant__ CUtensorMap tm_w0,
                     const __grid_constant__ CUtensorMap tm_w1, const __grid_constant__ CUtensorMap tm_w2,
                     const __grid_constant__ GemmArgs g) {
+  // BWD && MULTI: several weights along K (dX = sum_i dY_i W_i); !BWD && MULTI: several
+  // weights along M (Y_i = X W_i^T).
+  constexpr bool KCAT = BWD && MULTI;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -323,10 +335,12 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
-    prefetch_tma_desc(&tm_act);
+    prefetch_tma_desc(&tm_act0);
     prefetch_tma_desc(&tm_w0);
     if (g.nw > 1) prefetch_tma_desc(&tm_w1);
     if (g.nw > 2) prefetch_tma_desc(&tm_w2);
+    if (KCAT && g.nw > 1) prefetch_tma_desc(&tm_act1);
+    if (KCAT && g.nw > 2) prefetch_tma_desc(&tm_act2);
   }
   for (int i = 0; i < g.nw; ++i) {
     if (threadIdx.x < 16) s_code[16 * i + threadIdx.x] = __ldg(g.w[i].code + threadIdx.x);
@@ -357,12 +371,16 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[s], SM_X_BYTES + SM_P_BYTES);
-          tma_load_2d(smem + SM_X + s * SM_X_BYTES, &tm_act, &full[s], k * G_K, int(tc.t0));
-          const CUtensorMap* tm_w = tc.seg == 0 ? &tm_w0 : (tc.seg == 1 ? &tm_w1 : &tm_w2);
+          const int ws = KCAT ? kseg(g, k) : tc.seg;   // weight of this stage
+          const int kl = KCAT ? k - kbeg(g, ws) : k;  // its local K stage
+          const CUtensorMap* tm_a = ws == 0 ? &tm_act0 : (ws == 1 ? &tm_act1 : &tm_act2);
+          const CUtensorMap* tm_w = ws == 0 ? &tm_w0 : (ws == 1 ? &tm_w1 : &tm_w2);
+          tma_load_2d(smem + SM_X + s * SM_X_BYTES, KCAT ? tm_a : &tm_act0, &full[s], kl * G_K,
+                      int(tc.t0));
           if (!BWD)
-            tma_load_2d(smem + SM_P + s * SM_P_BYTES, tm_w, &full[s], k * (G_K / 2), int(tc.m0));
+            tma_load_2d(smem + SM_P + s * SM_P_BYTES, tm_w, &full[s], kl * (G_K / 2), int(tc.m0));
           else
-            tma_load_2d(smem + SM_P + s * SM_P_BYTES, tm_w, &full[s], int(tc.m0 / 2), k * G_K);
+            tma_load_2d(smem + SM_P + s * SM_P_BYTES, tm_w, &full[s], int(tc.m0 / 2), kl * G_K);
         }
       }
       // no bulk copy may still be landing in this CTA's shared memory at exit
@@ -384,15 +402,23 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         if (!pipe_wait(&acc_empty[b], (use & 1) ^ 1, abort_flag)) break;
         tc_fence_after();
         bool acc = false;
-        if (g.w[MULTI ? tc.seg : 0].has_lora && wu.split == 0) {  // the LoRA term belongs to the first K range
-          if (!pipe_wait(lora_full, lc & 1, abort_flag)) break;
+        // LoRA terms belong to the first K range; a K-concatenated backward has one slab per
+        // adapter, filled and consumed one after the other
+        for (int i = 0; wu.split == 0 && i < (KCAT ? g.nw : 1); ++i) {
+          if (!g.w[KCAT ? i : (MULTI ? tc.seg : 0)].has_lora) continue;
+          if (!pipe_wait(lora_full, lc & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
           ++lc;
           tc_fence_after();
           umma_f16(d_tmem, smem_desc_nosw(sbase + SM_LA, 128, 256),
-                   smem_desc_nosw(sbase + SM_LB, 128, 256), idesc_f16(G_M, tc.tn, false, false), 0u);
+                   smem_desc_nosw(sbase + SM_LB, 128, 256), idesc_f16(G_M, tc.tn, false, false),
+                   acc ? 1u : 0u);
           umma_commit(lora_empty);
           acc = true;
         }
+        if (!ok) break;
         for (int k = wu.kb; k < wu.ke; ++k, ++it) {
           const int s = it % G_STAGES;
           const uint32_t ph = (it / G_STAGES) & 1;
@@ -456,8 +482,15 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       }
       const float off = W.nested ? __ldg(W.offset) : 0.f;
       const float* code2 = s_code2 + 256 * tc.seg;
-      if (W.has_lora && wu.split == 0) {
-        if (!pipe_wait(lora_empty, (lc & 1) ^ 1, abort_flag)) break;
+      // one slab per adapter (a K-concatenated backward may carry several), in the order the
+      // MMA issuer consumes them
+      for (int li = 0; wu.split == 0 && li < (KCAT ? g.nw : 1); ++li) {
+        const GemmW& WL = KCAT ? g.w[li] : W;
+        if (!WL.has_lora) continue;
+        if (!pipe_wait(lora_empty, (lc & 1) ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
         ++lc;
         const uint32_t la = sbase + SM_LA;
         const uint32_t lb = sbase + SM_LB;
@@ -465,10 +498,10 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           if (!BWD) {
             const int64_t o = tc.m0 + d;  // s * B[o, 0:16]
             uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0;
-            if (o < W.out_f) {
-              const uint4* src = reinterpret_cast<const uint4*>(W.lora_w + o * 16);
-              v0 = scale_pack8(__ldg(src), W.lora_scale);
-              v1 = scale_pack8(__ldg(src + 1), W.lora_scale);
+            if (o < WL.out_f) {
+              const uint4* src = reinterpret_cast<const uint4*>(WL.lora_w + o * 16);
+              v0 = scale_pack8(__ldg(src), WL.lora_scale);
+              v1 = scale_pack8(__ldg(src + 1), WL.lora_scale);
             }
             st_shared_v4(la + slab_off(d, 0), v0);
             st_shared_v4(la + slab_off(d, 1), v1);
@@ -477,7 +510,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             float v[16];
 #pragma unroll
             for (int rr = 0; rr < 16; ++rr)
-              v[rr] = (i < g.in_f) ? __half2float(W.lora_w[int64_t(rr) * g.in_f + i]) * W.lora_scale
+              v[rr] = (i < g.in_f) ? __half2float(WL.lora_w[int64_t(rr) * g.in_f + i]) * WL.lora_scale
                                    : 0.f;
             st_shared_v4(la + slab_off(d, 0),
                          make_uint4(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]),
@@ -494,16 +527,72 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           const int t = c >> 1, kc = c & 1;
           uint4 v = make_uint4(0, 0, 0, 0);
           if (t < tc.tn_real)
-            v = __ldg(reinterpret_cast<const uint4*>(W.lora_t + (tc.t0 + t) * 16 + kc * 8));
+            v = __ldg(reinterpret_cast<const uint4*>(WL.lora_t + (tc.t0 + t) * 16 + kc * 8));
           st_shared_v4(lb + slab_off(t, kc), v);
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(lora_full);
       }
+      if (!ok) break;
 
       const int64_t col = BWD ? (tc.m0 + 64 * j + 32 * hh) : 0;
       const bool lane_valid = BWD ? (col < g.in_f) : (tc.m0 + r < W.out_f);
+      if constexpr (KCAT) {
+        // per stage: its weight, that weight's local K row and quantization block
+        struct Src {
+          ScaleSrc v;
+          int ws;
+        };
+        auto src = [&](int k) -> Src {
+          Src x{ScaleSrc{0u, 0.f}, 0};
+          if (k >= wu.ke) return x;
+          x.ws = kseg(g, k);
+          const GemmW& Wk = g.w[x.ws];
+          const int64_t e = int64_t((k - kbeg(g, x.ws)) * G_K + r) * g.in_f + col;
+          x.v = load_scale_src(Wk, e >> Wk.log2_bs, lane_valid);
+          return x;
+        };
+        auto scale_k = [&](const Src& x) -> float {
+          if (!lane_valid) return 0.f;
+          const GemmW& Wk = g.w[x.ws];
+          return Wk.nested ? __fadd_rn(__fmul_rn(s_code2[256 * x.ws + x.v.q], x.v.a), __ldg(Wk.offset))
+                           : x.v.a;
+        };
+        float sc = scale_k(src(wu.kb));
+        Src raw1 = src(wu.kb + 1);
+        for (int k = wu.kb; k < wu.ke; ++k, ++it) {
+          const int ws = kseg(g, k);
+          if (ws != code_seg) {
+            code_seg = ws;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) code[i] = s_code[16 * ws + i];
+          }
+          const int s = it % G_STAGES;
+          const uint32_t ph = (it / G_STAGES) & 1;
+          const Nf4Table tab = make_table(code, sc);
+          const Src raw2 = src(k + 2);
+          const float sc1 = scale_k(raw1);
+          if (!pipe_wait(&full[s], ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint4 wv = ld_shared_v4(sbase + SM_P + s * SM_P_BYTES + p_off);
+          const uint32_t abase = sbase + SM_A + s * SM_A_BYTES + a_off;
+          const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint4 v = decode_word_f16(tab, w[c]);
+            st_shared_v4(abase + ((uint32_t(4 * hh + c) ^ key) << 4), v);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&afull[s]);
+          sc = sc1;
+          raw1 = raw2;
+        }
+        continue;
+      }
       // Element offset (row * in + column) of this thread's first value at stage k, and
       // its quantization block; stages step by 64 columns forward, 64 rows backward.
       const int nk = wu.ke - wu.kb;
@@ -791,7 +880,7 @@ static int64_t plan_work_bytes(const GemmPlan& p) {
 
 // One persistent CTA per SM (at most one per work unit).
 template <bool BWD>
-static int launch_gemm(const CUtensorMap& ta, const CUtensorMap (&tw)[G_MAX_W], GemmArgs g,
+static int launch_gemm(const CUtensorMap (&ta)[G_MAX_W], const CUtensorMap (&tw)[G_MAX_W], GemmArgs g,
                        int64_t m_tiles, int64_t kdim, void* work, int64_t work_bytes, cudaStream_t s) {
   const int64_t sms = sm_count_cached();
   GemmPlan p = plan_gemm(g.n, m_tiles, kdim, sms);
@@ -811,21 +900,25 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap (&tw)[G_MAX_W], 
   const unsigned grid = unsigned(units < sms ? units : sms);
   const bool split = p.splits > 1;
   int st;
-  if (!BWD && g.nw > 1) {
-    st = split ? set_smem_attr<BWD, true, !BWD>() : set_smem_attr<BWD, false, !BWD>();
-    if (st != NF4B_OK) return st;
+#define NF4B_LAUNCH(SPLIT_, MULTI_)                                                             \
+  do {                                                                                         \
+    st = set_smem_attr<BWD, SPLIT_, MULTI_>();                                                 \
+    if (st != NF4B_OK) return st;                                                              \
+    nf4_gemm_kernel<BWD, SPLIT_, MULTI_><<<grid, G_THREADS, SM_ALLOC, s>>>(                    \
+        ta[0], ta[1], ta[2], tw[0], tw[1], tw[2], g);                                          \
+  } while (0)
+  if (g.nw > 1) {
     if (split)
-      nf4_gemm_kernel<BWD, true, !BWD><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw[0], tw[1], tw[2], g);
+      NF4B_LAUNCH(true, true);
     else
-      nf4_gemm_kernel<BWD, false, !BWD><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw[0], tw[1], tw[2], g);
+      NF4B_LAUNCH(false, true);
   } else {
-    st = split ? set_smem_attr<BWD, true, false>() : set_smem_attr<BWD, false, false>();
-    if (st != NF4B_OK) return st;
     if (split)
-      nf4_gemm_kernel<BWD, true, false><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw[0], tw[1], tw[2], g);
+      NF4B_LAUNCH(true, false);
     else
-      nf4_gemm_kernel<BWD, false, false><<<grid, G_THREADS, SM_ALLOC, s>>>(ta, tw[0], tw[1], tw[2], g);
+      NF4B_LAUNCH(false, false);
   }
+#undef NF4B_LAUNCH
   return launch_status(BWD ? "nf4_gemm_kernel<bwd> launch" : "nf4_gemm_kernel<fwd> launch");
 }
 
@@ -921,10 +1014,11 @@ extern "C" int nf4b_linear_fwd_group(const void* x, int64_t n, int64_t in_featur
   int st = check_device();
   if (st != NF4B_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  CUtensorMap ta, tw[G_MAX_W];
-  st = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, uint64_t(in_features), uint64_t(n),
+  CUtensorMap ta[G_MAX_W], tw[G_MAX_W];
+  st = make_tmap_2d(&ta[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, uint64_t(in_features), uint64_t(n),
                     uint64_t(in_features) * 2, G_K, G_NMAX, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != NF4B_OK) return st;
+  ta[1] = ta[2] = ta[0];
   GemmArgs g{};
   int64_t rows[G_MAX_W];
   for (int i = 0; i < n_items; ++i) {
@@ -950,6 +1044,7 @@ extern "C" int nf4b_linear_fwd_group(const void* x, int64_t n, int64_t in_featur
   }
   for (int i = n_items; i < G_MAX_W; ++i) tw[i] = tw[0];  // unused kernel parameters
   set_m_end(&g, rows, n_items);
+  for (int i = 0; i < G_MAX_W; ++i) g.k_end[i] = 0x7FFFFFFF;
   g.n = n;
   g.in_f = in_features;
   return launch_gemm<false>(ta, tw, g, g.m_end[n_items - 1], in_features, work, work_bytes, s);
@@ -970,51 +1065,86 @@ extern "C" int nf4b_linear_fwd(const void* x, const uint8_t* packed, const nf4b_
                             stream);
 }
 
+extern "C" int64_t nf4b_linear_bwd_group_work_bytes(int64_t n, int64_t in_features,
+                                                    const int64_t* out_features, int32_t n_items) {
+  if (n <= 0 || in_features <= 0 || !out_features || n_items < 1 || n_items > G_MAX_W) return 0;
+  if (check_device() != NF4B_OK) return -1;
+  int64_t kdim = 0;
+  for (int i = 0; i < n_items; ++i) kdim += out_features[i];
+  return plan_work_bytes(plan_gemm(n, ceil_tiles(in_features), kdim, sm_count_cached()));
+}
+
+extern "C" int nf4b_linear_bwd_dx_group(const nf4b_linear_bwd_item* items, int32_t n_items, void* dx,
+                                        int64_t n, int64_t in_features, void* work,
+                                        int64_t work_bytes, void* stream) {
+  NF4B_RETURN_IF(!items || n_items < 1, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(n_items > G_MAX_W, NF4B_ERR_UNSUPPORTED);
+  int32_t lb[G_MAX_W];
+  int64_t kdim = 0;
+  for (int i = 0; i < n_items; ++i) {
+    const nf4b_linear_bwd_item& it = items[i];
+    int st = gemm_common_checks(it.dy, it.packed, it.qs, dx, n, in_features, it.out_features, &lb[i]);
+    if (st != NF4B_OK) return st;
+    if (it.lora) {
+      NF4B_RETURN_IF(it.lora->rank != 16, NF4B_ERR_UNSUPPORTED);
+      NF4B_RETURN_IF(!it.lora->a || !it.lora->b || !it.dyb, NF4B_ERR_INVALID_ARG);
+      NF4B_RETURN_IF(!aligned(it.lora->a, 16) || !aligned(it.lora->b, 16) || !aligned(it.dyb, 16),
+                     NF4B_ERR_ALIGNMENT);
+    }
+    kdim += it.out_features;
+  }
+  NF4B_RETURN_IF(kdim / G_K > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
+  if (n == 0) return NF4B_OK;
+  int st = check_device();
+  if (st != NF4B_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUtensorMap ta[G_MAX_W], tw[G_MAX_W];
+  GemmArgs g{};
+  int64_t kacc = 0;
+  for (int i = 0; i < n_items; ++i) {
+    const nf4b_linear_bwd_item& it = items[i];
+    st = make_tmap_2d(&ta[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, it.dy, uint64_t(it.out_features),
+                      uint64_t(n), uint64_t(it.out_features) * 2, G_K, G_NMAX, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != NF4B_OK) return st;
+    st = make_tmap_2d(&tw[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, it.packed, uint64_t(in_features / 2),
+                      uint64_t(it.out_features), uint64_t(in_features / 2), G_M / 2, G_K,
+                      CU_TENSOR_MAP_SWIZZLE_64B);
+    if (st != NF4B_OK) return st;
+    GemmW& w = g.w[i];
+    fill_qstate_args(&w, it.qs, lb[i]);
+    w.out = static_cast<__half*>(dx);
+    w.out_f = it.out_features;
+    if (it.lora) {
+      // dY B: B is [out, 16] row-major -> element (r, k=o) at o*16 + r
+      st = lora_project16(it.dy, it.lora->b, 1, 16, it.dyb, n, it.out_features, s);
+      if (st != NF4B_OK) return st;
+      w.has_lora = 1;
+      w.lora_w = static_cast<const __half*>(it.lora->a);
+      w.lora_t = static_cast<const __half*>(it.dyb);
+      w.lora_scale = it.lora->scale;
+    }
+    kacc += it.out_features / G_K;
+    g.k_end[i] = int32_t(kacc);
+  }
+  for (int i = n_items; i < G_MAX_W; ++i) {
+    ta[i] = ta[0];  // unused kernel parameters
+    tw[i] = tw[0];
+    g.k_end[i] = 0x7FFFFFFF;
+  }
+  const int64_t rows = in_features;
+  set_m_end(&g, &rows, 1);  // all weights share the M side (the in features)
+  g.nw = n_items;
+  g.n = n;
+  g.in_f = in_features;
+  return launch_gemm<true>(ta, tw, g, g.m_end[0], kdim, work, work_bytes, s);
+}
+
 extern "C" int nf4b_linear_bwd_dx_ws(const void* dy, const uint8_t* packed, const nf4b_qstate* qs,
                                      const nf4b_lora* lora, void* dyb, void* dx, int64_t n,
                                      int64_t in_features, int64_t out_features, void* work,
                                      int64_t work_bytes, void* stream) {
-  int32_t lb = 0;
-  int st = gemm_common_checks(dy, packed, qs, dx, n, in_features, out_features, &lb);
-  if (st != NF4B_OK) return st;
-  if (lora) {
-    NF4B_RETURN_IF(lora->rank != 16, NF4B_ERR_UNSUPPORTED);
-    NF4B_RETURN_IF(!lora->a || !lora->b || !dyb, NF4B_ERR_INVALID_ARG);
-    NF4B_RETURN_IF(!aligned(lora->a, 16) || !aligned(lora->b, 16) || !aligned(dyb, 16),
-                   NF4B_ERR_ALIGNMENT);
-  }
-  if (n == 0) return NF4B_OK;
-  st = check_device();
-  if (st != NF4B_OK) return st;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  CUtensorMap ta, tw;
-  st = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, dy, uint64_t(out_features), uint64_t(n),
-                    uint64_t(out_features) * 2, G_K, G_NMAX, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (st != NF4B_OK) return st;
-  st = make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, uint64_t(in_features / 2),
-                    uint64_t(out_features), uint64_t(in_features / 2), G_M / 2, G_K,
-                    CU_TENSOR_MAP_SWIZZLE_64B);
-  if (st != NF4B_OK) return st;
-  GemmArgs g{};
-  GemmW& w = g.w[0];
-  fill_qstate_args(&w, qs, lb);
-  w.out = static_cast<__half*>(dx);
-  w.out_f = out_features;
-  g.n = n;
-  g.in_f = in_features;
-  if (lora) {
-    // dY B: B is [out, 16] row-major -> element (r, k=o) at o*16 + r
-    st = lora_project16(dy, lora->b, 1, 16, dyb, n, out_features, s);
-    if (st != NF4B_OK) return st;
-    w.has_lora = 1;
-    w.lora_w = static_cast<const __half*>(lora->a);
-    w.lora_t = static_cast<const __half*>(dyb);
-    w.lora_scale = lora->scale;
-  }
-  const int64_t rows = in_features;
-  set_m_end(&g, &rows, 1);
-  const CUtensorMap tws[G_MAX_W] = {tw, tw, tw};
-  return launch_gemm<true>(ta, tws, g, g.m_end[0], out_features, work, work_bytes, s);
+  const nf4b_linear_bwd_item it{dy, packed, qs, lora, dyb, out_features};
+  return nf4b_linear_bwd_dx_group(&it, 1, dx, n, in_features, work, work_bytes, stream);
 }
 
 extern "C" int nf4b_linear_bwd_dx(const void* dy, const uint8_t* packed, const nf4b_qstate* qs,

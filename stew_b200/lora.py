@@ -139,8 +139,9 @@ def _lora_weight_grads(x2, dy, xa, dyb, scaling, in_f, out_f):
 class GroupedNF4Function(torch.autograd.Function):
     """Several NF4 projections of one input -- q/k/v, or gate/up -- each optionally with a
     rank-16 adapter: ONE forward launch (nf4b_linear_fwd_group; the adapters' x A^T
-    projections run just before it).  Backward: one fused dX GEMM per projection (with its
-    adapter term) summed into dX, and each adapter's weight gradients.
+    projections run just before it).  Backward: ONE dX GEMM over the concatenated out features
+    (nf4b_linear_bwd_dx_group, with the adapters' dX terms), and each adapter's weight
+    gradients.
     specs: one (packed, quant_state, scaling or None, bias or None) per projection;
     params: (lora_A, lora_B) of the projections whose scaling is not None, in order."""
 
@@ -193,29 +194,55 @@ class GroupedNF4Function(torch.autograd.Function):
         x2, *rest = ctx.saved_tensors
         n, in_f = x2.shape
         dev = x2.device
+        L = _lib.lib()
+        sel, pgrads, li = [], [], 0
+        for (packed, st, scaling, _), gy in zip(ctx.specs, grads):
+            lora = None
+            if scaling is not None:
+                lora = tuple(rest[3 * li:3 * li + 3]) + (scaling,)  # a16, b16, xa, scaling
+                li += 1
+            sel.append((packed, st, lora, gy))
+        live = [x for x in sel if x[3] is not None]
         dx = None
-        pgrads = []
-        li = 0
         with torch.cuda.device(dev):
-            for (packed, st, scaling, _), gy in zip(ctx.specs, grads):
-                out_f = int(st.shape[0])
-                Bv = packed.view(-1, 1)
-                if scaling is not None:
-                    a16, b16, xa = rest[3 * li:3 * li + 3]
-                    li += 1
-                if gy is None:
-                    if scaling is not None:
-                        pgrads += [None, None]
+            if live:
+                # one GEMM over the concatenated out features: dX = sum_i dY_i W_i (+ adapters)
+                items = (_lib.LinearBwdItemC * len(live))()
+                keep = []
+                for j, (packed, st, lora, gy) in enumerate(live):
+                    out_f = int(st.shape[0])
+                    dy = gy.reshape(n, out_f).to(torch.float16).contiguous()
+                    qs = _qstate(st, dev)
+                    lc = dyb = None
+                    if lora is not None:
+                        dyb = torch.empty(n, LORA_RANK, dtype=torch.float16, device=dev)
+                        lc = _lora_c(lora[0], lora[1], lora[3])
+                    keep.append((dy, qs, lc, dyb))
+                    items[j].dy = dy.data_ptr()
+                    items[j].packed = packed.data_ptr()
+                    items[j].qs = ctypes.pointer(qs)
+                    items[j].lora = None if lc is None else ctypes.pointer(lc)
+                    items[j].dyb = None if dyb is None else dyb.data_ptr()
+                    items[j].out_features = out_f
+                dx = torch.empty(n, in_f, dtype=torch.float16, device=dev)
+                outs = (ctypes.c_int64 * len(live))(*[int(st.shape[0]) for _, st, _, _ in live])
+                need = int(L.nf4b_linear_bwd_group_work_bytes(n, in_f, outs, len(live)))
+                work, wbytes = _workspace_bytes(dev, need)
+                _lib.check(L.nf4b_linear_bwd_dx_group(items, len(live), dx.data_ptr(), n, in_f, work,
+                                                      wbytes, _stream(dev)), "nf4b_linear_bwd_dx_group")
+                kj = 0
+            for packed, st, lora, gy in sel:
+                if lora is None:
+                    if gy is not None:
+                        kj += 1
                     continue
-                dy = gy.reshape(n, out_f).to(torch.float16).contiguous()
-                if scaling is None:
-                    part = _bwd_dx(dy, Bv, st)
-                else:
-                    dyb = torch.empty(n, LORA_RANK, dtype=torch.float16, device=dev)
-                    part = _bwd_dx(dy, Bv, st, (a16, b16, scaling), dyb)
-                    da32, db32 = _lora_weight_grads(x2, dy, xa, dyb, scaling, in_f, out_f)
-                    pgrads += [da32, db32]
-                dx = part if dx is None else dx.add_(part)
+                if gy is None:
+                    pgrads += [None, None]
+                    continue
+                dy, _, _, dyb = keep[kj]
+                kj += 1
+                da32, db32 = _lora_weight_grads(x2, dy, lora[2], dyb, lora[3], in_f, int(st.shape[0]))
+                pgrads += [da32, db32]
         pgrads = [None if gr is None else gr.to(dt) for gr, dt in zip(pgrads, ctx.param_dtypes)]
         return (None if dx is None else dx.reshape(ctx.x_shape), None, *pgrads)
 

@@ -128,3 +128,69 @@ def test_grouped_projection_autograd_matches_separate(cuda_lib):
     for a, b in zip(g_grads, s_grads):
         assert max_rel_err(a, b.double()) <= 2e-3
     _check_flag()
+
+
+BWD_QKV = [(1536, 1536, 41, True), (256, 1536, 42, False), (256, 1536, 43, True)]
+BWD_GATE_UP = [(8960, 1536, 51, False), (8960, 1536, 52, False)]
+
+
+@pytest.mark.parametrize("specs", [BWD_QKV, BWD_GATE_UP, BWD_QKV[:1]], ids=["qkv", "gate_up", "q"])
+@pytest.mark.parametrize("n", [77, 1170, 2048])
+def test_grouped_backward_matches_reference_and_sum_of_singles(cuda_lib, specs, n):
+    """dX = sum_i dY_i W_i (+ 2 (dY_i B_i) A_i for adapters) in one K-concatenated GEMM."""
+    from stew_b200 import _lib
+    from stew_b200.nf4 import _qstate, _stream
+    L = _lib.lib()
+    in_f = 1536
+    items = (_lib.LinearBwdItemC * len(specs))()
+    keep = []
+    ref = torch.zeros(n, in_f, dtype=torch.float64, device="cuda")
+    for i, (out_f, _, seed, lora) in enumerate(specs):
+        q, st = _weight((out_f, in_f), seed)
+        qs = _qstate(st, q.device)
+        dy = _x(n, out_f, seed + 5, std=0.01)
+        ref += dy.double() @ _ref_weight(q, st)
+        lc = a = b = dyb = None
+        if lora:
+            g = torch.Generator(device="cuda").manual_seed(seed + 7)
+            a = ((torch.rand(16, in_f, generator=g, device="cuda") * 2 - 1) / in_f ** 0.5).half()
+            b = (torch.randn(out_f, 16, generator=g, device="cuda") * 0.05).half()
+            dyb = torch.empty(n, 16, dtype=torch.float16, device="cuda")
+            lc = _lib.LoraC()
+            lc.a, lc.b, lc.scale, lc.rank, lc.xa = a.data_ptr(), b.data_ptr(), 2.0, 16, None
+            ref += 2.0 * (dy.double() @ b.double()) @ a.double()
+        items[i].dy = dy.data_ptr()
+        items[i].packed = q.data_ptr()
+        items[i].qs = ctypes.pointer(qs)
+        items[i].lora = None if lc is None else ctypes.pointer(lc)
+        items[i].dyb = None if dyb is None else dyb.data_ptr()
+        items[i].out_features = out_f
+        # keep every buffer the C structs point to alive until the last launch
+        keep.append(dict(q=q, st=st, qs=qs, dy=dy, lc=lc, dyb=dyb, a=a, b=b, out_f=out_f))
+    outs = (ctypes.c_int64 * len(specs))(*[s[0] for s in specs])
+    need = int(L.nf4b_linear_bwd_group_work_bytes(n, in_f, outs, len(specs)))
+    ws = torch.zeros(max(need, 256), dtype=torch.uint8, device="cuda")
+    dx = torch.full((n, in_f), float("nan"), dtype=torch.float16, device="cuda")
+    _lib.check(L.nf4b_linear_bwd_dx_group(items, len(specs), dx.data_ptr(), n, in_f, ws.data_ptr(),
+                                          ws.numel(), _stream(dx.device)), "bwd group")
+    torch.cuda.synchronize()
+    assert not torch.isnan(dx).any()
+    assert max_rel_err(dx, ref) <= GEMM_MAX_REL_ERR
+    # the adapters' dY B went to dyb
+    for k in keep:
+        if k["lc"] is not None:
+            assert max_rel_err(k["dyb"], k["dy"].double() @ k["b"].double()) <= GEMM_MAX_REL_ERR
+    # same as the per-projection launches summed
+    total = torch.zeros(n, in_f, dtype=torch.float64, device="cuda")
+    for k in keep:
+        one = torch.empty(n, in_f, dtype=torch.float16, device="cuda")
+        dyb1 = torch.empty(n, 16, dtype=torch.float16, device="cuda") if k["lc"] is not None else None
+        _lib.check(L.nf4b_linear_bwd_dx(k["dy"].data_ptr(), k["q"].data_ptr(), ctypes.byref(k["qs"]),
+                                        None if k["lc"] is None else ctypes.byref(k["lc"]),
+                                        None if dyb1 is None else dyb1.data_ptr(), one.data_ptr(), n, in_f,
+                                        k["out_f"], _stream(dx.device)), "single bwd")
+        total += one.double()
+    torch.cuda.synchronize()
+    assert max_rel_err(dx, total) <= 2e-3
+    assert int(ws[:4096].count_nonzero()) == 0
+    _check_flag()
