@@ -233,8 +233,17 @@ class GemmPass:
                     arr[j].y = self.yname[name].data_ptr()
                     arr[j].out_features = out_f
                 outs = (ctypes.c_int64 * len(sel))(*[it[2] for it in sel])
-                grp_bytes = max(grp_bytes, int(self.L.nf4b_linear_group_work_bytes(n, sel[0][3], outs, len(sel))))
-                self.groups.append((sel[0][3], arr, len(sel)))
+                grp_bytes = max(grp_bytes, int(self.L.nf4b_linear_group_work_bytes(n, sel[0][3], outs, len(sel))),
+                                int(self.L.nf4b_linear_bwd_group_work_bytes(n, sel[0][3], outs, len(sel))))
+                barr = (_lib.LinearBwdItemC * len(sel))()
+                for j, (_, name, out_f, in_f, q, qs, _) in enumerate(sel):
+                    barr[j].dy = self.dy[out_f].data_ptr()
+                    barr[j].packed = q.data_ptr()
+                    barr[j].qs = ctypes.pointer(qs)
+                    barr[j].lora = None
+                    barr[j].dyb = None
+                    barr[j].out_features = out_f
+                self.groups.append((sel[0][3], arr, len(sel), barr))
         # split-K workspace (zeroed once; every call leaves its counters zero)
         self.ws_bytes = max([int(self.L.nf4b_linear_work_bytes(n, in_f, out_f, bwd))
                              for _, out_f, in_f in QWEN_PROJ for bwd in (0, 1)] + [grp_bytes])
@@ -285,9 +294,19 @@ class GemmPass:
         """The forward pass with q/k/v and gate/up each in one grouped launch (no LoRA)."""
         import torch
         stream = self.ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-        for in_f, arr, cnt in self.groups:
+        for in_f, arr, cnt, _ in self.groups:
             st = self.L.nf4b_linear_fwd_group(self.x[in_f].data_ptr(), self.n, in_f, arr, cnt,
                                               self.ws.data_ptr(), self.ws.numel(), stream)
+            assert st == 0, st
+        return len(self.groups)
+
+    def run_grouped_bwd(self):
+        """The backward dX pass with q/k/v and gate/up each as one K-concatenated GEMM."""
+        import torch
+        stream = self.ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        for in_f, _, cnt, barr in self.groups:
+            st = self.L.nf4b_linear_bwd_dx_group(barr, cnt, self.dx[in_f].data_ptr(), self.n, in_f,
+                                                 self.ws.data_ptr(), self.ws.numel(), stream)
             assert st == 0, st
         return len(self.groups)
 
@@ -511,6 +530,13 @@ def main():
             tf = gp.flops(fwd=True, bwd=False, lora=False) / (t * 1e-3) / 1e12
             res["fwd_grouped"] = {"ms_per_pass": round(t, 3), "tflops": round(tf, 1),
                                   "frac_of_peak": round(tf / tc_peak, 3),
+                                  "frac_of_sustained_peak": round(tf / tc_sustained, 3),
+                                  "launches_per_pass": 4 * args.layers}
+            t = _timed(world, gp.run_grouped_bwd, args.gemm_steps, 2) / args.gemm_steps
+            tf = gp.flops(fwd=False, bwd=True, lora=False) / (t * 1e-3) / 1e12
+            res["bwd_grouped"] = {"ms_per_pass": round(t, 3), "tflops": round(tf, 1),
+                                  "frac_of_peak": round(tf / tc_peak, 3),
+                                  "frac_of_sustained_peak": round(tf / tc_sustained, 3),
                                   "launches_per_pass": 4 * args.layers}
             res["launches_per_pass"] = gp.run(fwd=True, bwd=True, lora=True)
             res["per_shape"] = gp.per_shape()

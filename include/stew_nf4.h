@@ -213,6 +213,24 @@ int nf4b_lora_grads_noalloc(const void* x, const void* dy, const void* xa, const
                             float scale, float* da, float* db, int64_t n, int64_t in_features,
                             int64_t out_features, int32_t rank, void* stream);
 
+/* Blockwise NF4 quantizer (the weight-loading side: what bitsandbytes.functional
+ * .quantize_4bit produces, whose output nf4b_dequant unpacks).  w: fp16 or fp32 [numel]
+ * (in_dtype NF4B_F16 / NF4B_F32), numel a multiple of blocksize (32 .. 4096, power of two).
+ * Per block: absmax32[b] = max |x|; code = the number of NF4 midpoints <= x / absmax (nearest
+ * code, a value on a midpoint takes the upper one); packed[numel/2], high nibble first.
+ * nf4_mids: 15 fp32 midpoints of the 16-entry NF4 code, each the smallest fp32 >= the fp64
+ * midpoint of its neighbours (so fp32 comparisons decide as fp64 ones).
+ * Double quantization (absmax8 != NULL): offset[0] = fp32(mean of absmax32, summed in fp64
+ * in a fixed order); per block of 256: absmax2 = max |absmax32 - offset|, absmax8 = the
+ * number of code2_mids (255 midpoints of the 256-entry signed dynamic map) <= (absmax32 -
+ * offset) / absmax2.  work: device scratch of nf4b_quantize_work_bytes() bytes.
+ * All outputs are device buffers owned by the caller.  No reference counterpart in the
+ * reference's own code (it calls bitsandbytes at model load).  */
+int64_t nf4b_quantize_work_bytes(int64_t numel, int32_t blocksize);
+int nf4b_quantize(const void* w, int32_t in_dtype, int64_t numel, int32_t blocksize,
+                  const float* nf4_mids, const float* code2_mids, uint8_t* packed, float* absmax32,
+                  uint8_t* absmax8, float* absmax2, float* offset, void* work, void* stream);
+
 /* Reads (and with reset != 0 clears) the device-side flag the fused GEMMs set
  * when a pipeline wait ran out of time (the kernel then ends early instead of
  * hanging).  0 = no timeout since the last reset.  Synchronous.  */

@@ -98,6 +98,9 @@ SIGNATURES = {
                                   c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int32, c_void_p]),
     "nf4b_lora_grads_noalloc": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p,
                                           c_void_p, c_int64, c_int64, c_int64, c_int32, c_void_p]),
+    "nf4b_quantize_work_bytes": (c_int64, [c_int64, c_int32]),
+    "nf4b_quantize": (c_int32, [c_void_p, c_int32, c_int64, c_int32, c_void_p, c_void_p, c_void_p,
+                                c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "nf4b_gemm_error_flag": (c_int32, [ctypes.POINTER(c_int32), c_int32]),
     "nf4b_status_string": (ctypes.c_char_p, [c_int32]),
     "nf4b_last_error": (ctypes.c_char_p, []),
