@@ -323,7 +323,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < G_STAGES; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&afull[i], G_DQ_WARPS);
+      mbar_init(&afull[i], G_DQ_WARPS / 2);
       mbar_init(&empty[i], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -448,24 +448,25 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     }
   } else if (warp < G_EPI_WARP0) {
     // ------------------------------------------------------------ decode warps
-    const int d = threadIdx.x - 32 * G_DQ_WARP0;  // 0..255
-    float code[16];  // NF4 code of the current tile's weight (reloaded when the weight changes)
+    // Two groups of four warps; group g decodes the stages whose global index has parity g
+    // (so every ring slot has one owner), each thread one whole 64-value block row per stage:
+    // one scale and one 16-entry table per 64 values.
+    //  forward : row d of the K-major tile = weight row m0 + d, K columns 64 kl .. +63 of the
+    //            stage; packed row d of the stage is 32 B (two 16-byte chunks, unswizzled).
+    //  backward: K row r = d & 63 of the MN-major tile = weight row 64 kl + r, tile columns
+    //            64 j .. +63 with j = d >> 6 (one 128-byte row of M chunk j); packed row r has
+    //            64 B in the 64B swizzle (16-byte chunk c at c ^ ((r >> 1) & 3)), the thread's
+    //            two chunks are 2j and 2j + 1.
+    const int dq = threadIdx.x - 32 * G_DQ_WARP0;  // 0..255
+    const int grp = dq >> 7;
+    const int d = dq & 127;
+    float code[16];  // NF4 code of the current weight (reloaded when the weight changes)
     int code_seg = -1;
-
-    // Per-thread geometry of the decoded tile: 256 threads, 4 packed words (32 values,
-    // always inside one quantization block, so one scale) per thread and stage.
-    //  forward : row d >> 1 of the K-major tile (weight row m0 + (d >> 1)), K half d & 1.
-    //  backward: weight row k*64 + (d & 63) = K row of the MN-major tile; tile columns
-    //            64*(q >> 1) + 32*(q & 1) .. +32 with q = d >> 6 (64-wide M chunk q >> 1).
-    const int r = BWD ? (d & 63) : (d >> 1);
-    const int q = BWD ? (d >> 6) : (d & 1);
-    const int j = BWD ? (q >> 1) : 0;  // 64-wide M chunk (backward)
-    const int hh = BWD ? (q & 1) : q;  // which 4 of the 8 16-byte slots of the row
-    // Packed tile: forward rows of 32 B (unswizzled, already conflict-free); backward rows
-    // of 64 B loaded with the 64B swizzle (16-byte chunk c of row r at c ^ ((r >> 1) & 3)),
-    // so a warp's 8-row phase reads 8 different bank groups.
-    const uint32_t p_off = BWD ? uint32_t(r * 64 + ((q ^ ((r >> 1) & 3)) * 16))
-                               : uint32_t(r * 32 + q * 16);
+    const int r = BWD ? (d & 63) : d;
+    const int j = BWD ? (d >> 6) : 0;
+    const int sw = (r >> 1) & 3;
+    const uint32_t p_off0 = BWD ? uint32_t(r * 64 + (((2 * j) ^ sw) << 4)) : uint32_t(r * 32);
+    const uint32_t p_off1 = BWD ? uint32_t(r * 64 + (((2 * j + 1) ^ sw) << 4)) : uint32_t(r * 32 + 16);
     const uint32_t a_off = uint32_t(j * 8192 + (r >> 3) * 1024 + (r & 7) * 128);
     const uint32_t key = uint32_t(r & 7);
 
@@ -474,14 +475,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     for (int u = blockIdx.x; ok && u < nunits; u += gridDim.x) {
       const WorkUnit wu = work_unit<MULTI>(g, u);
       const TileCoord& tc = wu.tc;
-      const GemmW& W = g.w[MULTI ? tc.seg : 0];
-      if (tc.seg != code_seg) {
-        code_seg = tc.seg;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) code[i] = s_code[16 * tc.seg + i];
-      }
-      const float off = W.nested ? __ldg(W.offset) : 0.f;
-      const float* code2 = s_code2 + 256 * tc.seg;
+      const int tws = MULTI ? tc.seg : 0;  // the tile's weight (forward); weight 0 backward
+      const GemmW& W = g.w[tws];
       // one slab per adapter (a K-concatenated backward may carry several), in the order the
       // MMA issuer consumes them
       for (int li = 0; wu.split == 0 && li < (KCAT ? g.nw : 1); ++li) {
@@ -494,28 +489,28 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         ++lc;
         const uint32_t la = sbase + SM_LA;
         const uint32_t lb = sbase + SM_LB;
-        if (d < G_M) {
+        if (dq < G_M) {
           if (!BWD) {
-            const int64_t o = tc.m0 + d;  // s * B[o, 0:16]
+            const int64_t o = tc.m0 + dq;  // s * B[o, 0:16]
             uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0;
             if (o < WL.out_f) {
               const uint4* src = reinterpret_cast<const uint4*>(WL.lora_w + o * 16);
               v0 = scale_pack8(__ldg(src), WL.lora_scale);
               v1 = scale_pack8(__ldg(src + 1), WL.lora_scale);
             }
-            st_shared_v4(la + slab_off(d, 0), v0);
-            st_shared_v4(la + slab_off(d, 1), v1);
+            st_shared_v4(la + slab_off(dq, 0), v0);
+            st_shared_v4(la + slab_off(dq, 1), v1);
           } else {
-            const int64_t i = tc.m0 + d;  // s * A[0:16, i]
+            const int64_t i = tc.m0 + dq;  // s * A[0:16, i]
             float v[16];
 #pragma unroll
             for (int rr = 0; rr < 16; ++rr)
               v[rr] = (i < g.in_f) ? __half2float(WL.lora_w[int64_t(rr) * g.in_f + i]) * WL.lora_scale
                                    : 0.f;
-            st_shared_v4(la + slab_off(d, 0),
+            st_shared_v4(la + slab_off(dq, 0),
                          make_uint4(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]),
                                     pack_half2(v[4], v[5]), pack_half2(v[6], v[7])));
-            st_shared_v4(la + slab_off(d, 1),
+            st_shared_v4(la + slab_off(dq, 1),
                          make_uint4(pack_half2(v[8], v[9]), pack_half2(v[10], v[11]),
                                     pack_half2(v[12], v[13]), pack_half2(v[14], v[15])));
           }
@@ -523,7 +518,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         // token side: 256 rows x 2 chunks of 16 B
 #pragma unroll
         for (int jj = 0; jj < 2; ++jj) {
-          const int c = d + 256 * jj;
+          const int c = dq + 256 * jj;
           const int t = c >> 1, kc = c & 1;
           uint4 v = make_uint4(0, 0, 0, 0);
           if (t < tc.tn_real)
@@ -536,99 +531,76 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       }
       if (!ok) break;
 
-      const int64_t col = BWD ? (tc.m0 + 64 * j + 32 * hh) : 0;
+      const int64_t col = BWD ? (tc.m0 + 64 * j) : 0;
       const bool lane_valid = BWD ? (col < g.in_f) : (tc.m0 + r < W.out_f);
-      if constexpr (KCAT) {
-        // per stage: its weight, that weight's local K row and quantization block
-        struct Src {
-          ScaleSrc v;
-          int ws;
-        };
-        auto src = [&](int k) -> Src {
-          Src x{ScaleSrc{0u, 0.f}, 0};
-          if (k >= wu.ke) return x;
-          x.ws = kseg(g, k);
-          const GemmW& Wk = g.w[x.ws];
-          const int64_t e = int64_t((k - kbeg(g, x.ws)) * G_K + r) * g.in_f + col;
-          x.v = load_scale_src(Wk, e >> Wk.log2_bs, lane_valid);
-          return x;
-        };
-        auto scale_k = [&](const Src& x) -> float {
-          if (!lane_valid) return 0.f;
-          const GemmW& Wk = g.w[x.ws];
-          return Wk.nested ? __fadd_rn(__fmul_rn(s_code2[256 * x.ws + x.v.q], x.v.a), __ldg(Wk.offset))
-                           : x.v.a;
-        };
-        float sc = scale_k(src(wu.kb));
-        Src raw1 = src(wu.kb + 1);
-        for (int k = wu.kb; k < wu.ke; ++k, ++it) {
-          const int ws = kseg(g, k);
-          if (ws != code_seg) {
-            code_seg = ws;
-#pragma unroll
-            for (int i = 0; i < 16; ++i) code[i] = s_code[16 * ws + i];
-          }
-          const int s = it % G_STAGES;
-          const uint32_t ph = (it / G_STAGES) & 1;
-          const Nf4Table tab = make_table(code, sc);
-          const Src raw2 = src(k + 2);
-          const float sc1 = scale_k(raw1);
-          if (!pipe_wait(&full[s], ph, abort_flag)) {
-            ok = false;
-            break;
-          }
-          const uint4 wv = ld_shared_v4(sbase + SM_P + s * SM_P_BYTES + p_off);
-          const uint32_t abase = sbase + SM_A + s * SM_A_BYTES + a_off;
-          const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint4 v = decode_word_f16(tab, w[c]);
-            st_shared_v4(abase + ((uint32_t(4 * hh + c) ^ key) << 4), v);
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&afull[s]);
-          sc = sc1;
-          raw1 = raw2;
-        }
-        continue;
-      }
-      // Element offset (row * in + column) of this thread's first value at stage k, and
-      // its quantization block; stages step by 64 columns forward, 64 rows backward.
-      const int nk = wu.ke - wu.kb;
-      const int64_t e_step = BWD ? int64_t(G_K) * g.in_f : int64_t(G_K);
-      int64_t e_pos = BWD ? int64_t(r) * g.in_f + col : (tc.m0 + r) * g.in_f + 32 * hh;
-      e_pos += int64_t(wu.kb) * e_step;
-      auto scale_of = [&](const ScaleSrc& s) -> float {
-        if (!lane_valid) return 0.f;
-        return W.nested ? __fadd_rn(__fmul_rn(code2[s.q], s.a), off) : s.a;
+      // weight of stage k, and the element offset of the thread's first value in it
+      struct Src {
+        ScaleSrc v;
+        int ws;
       };
-      // Scale pipeline: the stage's scale is ready before its data arrives, the next
-      // stage's is computed while this one decodes, and the raw absmax of the stage
-      // after that is in flight.
-      float sc = scale_of(load_scale_src(W, e_pos >> W.log2_bs, lane_valid && nk > 0));
-      e_pos += e_step;
-      ScaleSrc raw1 = load_scale_src(W, e_pos >> W.log2_bs, lane_valid && nk > 1);
-      e_pos += e_step;
-      for (int k = 0; k < nk; ++k, ++it) {
-        const int s = it % G_STAGES;
-        const uint32_t ph = (it / G_STAGES) & 1;
+      auto src = [&](int k) -> Src {
+        Src x{ScaleSrc{0u, 0.f}, KCAT ? 0 : tws};
+        if (k >= wu.ke) return x;
+        if (KCAT) x.ws = kseg(g, k);
+        const GemmW& Wk = g.w[KCAT ? x.ws : tws];
+        const int kl = KCAT ? k - kbeg(g, x.ws) : k;
+        const int64_t e = BWD ? int64_t(kl * G_K + r) * g.in_f + col : (tc.m0 + r) * g.in_f + int64_t(kl) * G_K;
+        x.v = load_scale_src(Wk, e >> Wk.log2_bs, lane_valid);
+        return x;
+      };
+      auto scale_of = [&](const Src& x) -> float {
+        if (!lane_valid) return 0.f;
+        const GemmW& Wk = g.w[KCAT ? x.ws : tws];
+        const int sg = KCAT ? x.ws : tws;
+        return Wk.nested ? __fadd_rn(__fmul_rn(s_code2[256 * sg + x.v.q], x.v.a), __ldg(Wk.offset)) : x.v.a;
+      };
+      // blocksize 32: the second 32 values of a row are their own block
+      auto second_half_scale = [&](int k) -> float {
+        Src x{ScaleSrc{0u, 0.f}, KCAT ? kseg(g, k) : tws};
+        const GemmW& Wk = g.w[x.ws];
+        const int kl = KCAT ? k - kbeg(g, x.ws) : k;
+        const int64_t e = BWD ? int64_t(kl * G_K + r) * g.in_f + col + 32
+                              : (tc.m0 + r) * g.in_f + int64_t(kl) * G_K + 32;
+        x.v = load_scale_src(Wk, e >> Wk.log2_bs, lane_valid);
+        return scale_of(x);
+      };
+      // this group's stages of the unit: k0, k0 + 2, ...; scales of the next two in flight
+      const int k0 = wu.kb + ((int(it & 1u) == grp) ? 0 : 1);
+      float sc = scale_of(src(k0));
+      Src raw1 = src(k0 + 2);
+      for (int k = k0; k < wu.ke; k += 2) {
+        const int ws = KCAT ? kseg(g, k) : tws;
+        if (ws != code_seg) {
+          code_seg = ws;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) code[i] = s_code[16 * ws + i];
+        }
+        const uint32_t its = it + uint32_t(k - wu.kb);
+        const int s = its % G_STAGES;
+        const uint32_t ph = (its / G_STAGES) & 1;
         const Nf4Table tab = make_table(code, sc);
-        const ScaleSrc raw2 = load_scale_src(W, e_pos >> W.log2_bs, lane_valid && k + 2 < nk);
-        e_pos += e_step;
+        const Src raw2 = src(k + 4);
         const float sc1 = scale_of(raw1);
-
         if (!pipe_wait(&full[s], ph, abort_flag)) {
           ok = false;
           break;
         }
-        const uint4 wv = ld_shared_v4(sbase + SM_P + s * SM_P_BYTES + p_off);
+        const uint4 w0 = ld_shared_v4(sbase + SM_P + s * SM_P_BYTES + p_off0);
+        const uint4 w1 = ld_shared_v4(sbase + SM_P + s * SM_P_BYTES + p_off1);
         const uint32_t abase = sbase + SM_A + s * SM_A_BYTES + a_off;
-        const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
+        const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w};
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint4 v = decode_word_f16(tab, w[c]);
-          st_shared_v4(abase + ((uint32_t(4 * hh + c) ^ key) << 4), v);
+        for (int c = 0; c < 4; ++c) st_shared_v4(abase + ((uint32_t(c) ^ key) << 4), decode_word_f16(tab, wa[c]));
+        const uint32_t wb[4] = {w1.x, w1.y, w1.z, w1.w};
+        if (g.w[ws].log2_bs == 5) {
+          const Nf4Table tab2 = make_table(code, second_half_scale(k));
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            st_shared_v4(abase + ((uint32_t(4 + c) ^ key) << 4), decode_word_f16(tab2, wb[c]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            st_shared_v4(abase + ((uint32_t(4 + c) ^ key) << 4), decode_word_f16(tab, wb[c]));
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -636,6 +608,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         sc = sc1;
         raw1 = raw2;
       }
+      it += uint32_t(wu.ke - wu.kb);
     }
   } else {
     // --------------------------------------------------------------- epilogue
