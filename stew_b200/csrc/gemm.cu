@@ -452,7 +452,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     // (so every ring slot has one owner), each thread one whole 64-value block row per stage:
     // one scale and one 16-entry table per 64 values.
     //  forward : row d of the K-major tile = weight row m0 + d, K columns 64 kl .. +63 of the
-    //            stage; packed row d of the stage is 32 B (two 16-byte chunks, unswizzled).
+    //            stage; packed row d of the stage is 32 B in the 32B swizzle (16-byte chunk c
+    //            at c ^ ((d >> 2) & 1)), so a warp's 16-byte loads hit all 32 banks.
     //  backward: K row r = d & 63 of the MN-major tile = weight row 64 kl + r, tile columns
     //            64 j .. +63 with j = d >> 6 (one 128-byte row of M chunk j); packed row r has
     //            64 B in the 64B swizzle (16-byte chunk c at c ^ ((r >> 1) & 3)), the thread's
@@ -465,8 +466,10 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     const int r = BWD ? (d & 63) : d;
     const int j = BWD ? (d >> 6) : 0;
     const int sw = (r >> 1) & 3;
-    const uint32_t p_off0 = BWD ? uint32_t(r * 64 + (((2 * j) ^ sw) << 4)) : uint32_t(r * 32);
-    const uint32_t p_off1 = BWD ? uint32_t(r * 64 + (((2 * j + 1) ^ sw) << 4)) : uint32_t(r * 32 + 16);
+    const uint32_t sw32 = uint32_t((r >> 2) & 1);
+    const uint32_t p_off0 = BWD ? uint32_t(r * 64 + (((2 * j) ^ sw) << 4)) : uint32_t(r * 32) + (sw32 << 4);
+    const uint32_t p_off1 = BWD ? uint32_t(r * 64 + (((2 * j + 1) ^ sw) << 4))
+                                : uint32_t(r * 32) + ((1u ^ sw32) << 4);
     const uint32_t a_off = uint32_t(j * 8192 + (r >> 3) * 1024 + (r & 7) * 128);
     const uint32_t key = uint32_t(r & 7);
 
@@ -548,11 +551,13 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         x.v = load_scale_src(Wk, e >> Wk.log2_bs, lane_valid);
         return x;
       };
+      const float off_t = W.nested ? __ldg(W.offset) : 0.f;  // the tile's weight
       auto scale_of = [&](const Src& x) -> float {
         if (!lane_valid) return 0.f;
         const GemmW& Wk = g.w[KCAT ? x.ws : tws];
         const int sg = KCAT ? x.ws : tws;
-        return Wk.nested ? __fadd_rn(__fmul_rn(s_code2[256 * sg + x.v.q], x.v.a), __ldg(Wk.offset)) : x.v.a;
+        const float off = KCAT ? (Wk.nested ? __ldg(Wk.offset) : 0.f) : off_t;
+        return Wk.nested ? __fadd_rn(__fmul_rn(s_code2[256 * sg + x.v.q], x.v.a), off) : x.v.a;
       };
       // blocksize 32: the second 32 values of a row are their own block
       auto second_half_scale = [&](int k) -> float {
@@ -998,7 +1003,7 @@ extern "C" int nf4b_linear_fwd_group(const void* x, int64_t n, int64_t in_featur
     const nf4b_linear_item& it = items[i];
     st = make_tmap_2d(&tw[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, it.packed, uint64_t(in_features / 2),
                       uint64_t(it.out_features), uint64_t(in_features / 2), G_K / 2, G_M,
-                      CU_TENSOR_MAP_SWIZZLE_NONE);
+                      CU_TENSOR_MAP_SWIZZLE_32B);
     if (st != NF4B_OK) return st;
     GemmW& w = g.w[i];
     fill_qstate_args(&w, it.qs, lb[i]);
