@@ -236,6 +236,13 @@ int nf4b_quantize(const void* w, int32_t in_dtype, int64_t numel, int32_t blocks
  * hanging).  0 = no timeout since the last reset.  Synchronous.  */
 int nf4b_gemm_error_flag(int* value, int reset);
 
+/* Launch geometry of the fused GEMMs on the current device: *sms = SMs (one persistent CTA
+ * each), *pair_slots = 2-CTA clusters that can be resident at once (0 when the device runs
+ * none; pairs of CTAs then never run).  The environment variable STEW_NF4_PAIR chooses
+ * between the two tilings: "0" single CTAs only, "1" pairs whenever pair_slots > 0, unset
+ * or empty the built-in choice.  */
+int nf4b_gemm_geometry(int* sms, int* pair_slots);
+
 /* The CUDA error behind the last NF4B_ERR_CUDA returned on the calling host
  * thread ("<call>: <cudaErrorName> (<description>)"), or "" if none.  */
 const char* nf4b_last_error(void);

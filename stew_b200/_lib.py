@@ -102,6 +102,7 @@ SIGNATURES = {
     "nf4b_quantize": (c_int32, [c_void_p, c_int32, c_int64, c_int32, c_void_p, c_void_p, c_void_p,
                                 c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "nf4b_gemm_error_flag": (c_int32, [ctypes.POINTER(c_int32), c_int32]),
+    "nf4b_gemm_geometry": (c_int32, [ctypes.POINTER(c_int32), ctypes.POINTER(c_int32)]),
     "nf4b_status_string": (ctypes.c_char_p, [c_int32]),
     "nf4b_last_error": (ctypes.c_char_p, []),
     "nf4b_version": (ctypes.c_char_p, []),
@@ -163,3 +164,10 @@ def gemm_error_flag(reset: bool = True) -> int:
     v = c_int32(0)
     check(lib().nf4b_gemm_error_flag(ctypes.byref(v), 1 if reset else 0), "nf4b_gemm_error_flag")
     return int(v.value)
+
+
+def gemm_geometry() -> tuple:
+    """(SMs, resident 2-CTA clusters) the fused GEMMs plan with on the current device."""
+    a, b = c_int32(0), c_int32(0)
+    check(lib().nf4b_gemm_geometry(ctypes.byref(a), ctypes.byref(b)), "nf4b_gemm_geometry")
+    return a.value, b.value

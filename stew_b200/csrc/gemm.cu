@@ -25,7 +25,9 @@
 //
 // Every pipeline wait is bounded (~2 s); on expiry the CTA raises an abort flag,
 // records the failure in g_gemm_error, and winds down without hanging the GPU.
+#include <cstdlib>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "nf4_decode.cuh"
@@ -35,7 +37,6 @@ namespace nf4b {
 constexpr int G_M = 128;       // MMA M: weight rows per tile
 constexpr int G_NMAX = 256;    // MMA N: tokens per tile
 constexpr int G_K = 64;        // K per pipeline stage (one 128-byte swizzle row of fp16)
-constexpr int G_STAGES = 4;
 constexpr int G_DQ_WARPS = 8;
 constexpr int G_EPI_WARPS = 8;
 constexpr int G_DQ_WARP0 = 2;
@@ -44,26 +45,35 @@ constexpr int G_THREADS = 32 * (G_EPI_WARP0 + G_EPI_WARPS);
 constexpr int G_ACC_COLS = 256;                        // one accumulator
 constexpr int G_TMEM_COLS = 2 * G_ACC_COLS;            // double-buffered
 
-constexpr int SM_X_BYTES = G_NMAX * 128;   // activation stage
-constexpr int SM_A_BYTES = G_M * 128;      // decoded weight stage
-constexpr int SM_P_BYTES = 4096;           // packed weight stage (128 x 32 B or 64 x 64 B)
-constexpr int SM_LA_BYTES = G_M * 32;      // LoRA slab, weight side [128][16] fp16
-constexpr int SM_LB_BYTES = G_NMAX * 32;   // LoRA slab, token side [256][16] fp16
-constexpr int SM_X = 0;
-constexpr int SM_A = SM_X + G_STAGES * SM_X_BYTES;
-constexpr int SM_P = SM_A + G_STAGES * SM_A_BYTES;
-constexpr int SM_LA = SM_P + G_STAGES * SM_P_BYTES;
-constexpr int SM_LB = SM_LA + SM_LA_BYTES;
-constexpr int G_MAX_W = 3;                     // NF4 weights of one grouped forward launch
-constexpr int SM_CODE = SM_LB + SM_LB_BYTES;   // per weight: 16 fp32 NF4 code
-constexpr int SM_CODE2 = SM_CODE + 64 * G_MAX_W;  // per weight: 256 fp32 second-level code
-constexpr int SM_BAR = SM_CODE2 + 1024 * G_MAX_W;
-// full[S], afull[S], empty[S], acc_full[2], acc_empty[2], lora_full, lora_empty, mma_done
-constexpr int G_NUM_BARS = 3 * G_STAGES + 7;
-constexpr int SM_MISC = SM_BAR + G_NUM_BARS * 8;
-constexpr int SM_TOTAL = SM_MISC + 16;
-constexpr int SM_ALLOC = SM_TOTAL + 1024;  // slack to align the base to 1024 B
-static_assert(SM_ALLOC <= 232448, "shared memory budget");
+constexpr int G_MAX_W = 3;  // NF4 weights of one grouped forward launch
+
+// Shared-memory layout of one CTA.  PAIR: the CTA is half of a 2-CTA cluster whose MMA
+// (cta_group::2) covers 256 weight rows x up to 256 tokens; each CTA holds its own 128
+// decoded weight rows and half of the token tile, which frees room for a fifth stage.
+template <bool PAIR>
+struct Smem {
+  static constexpr int STAGES = PAIR ? 5 : 4;
+  static constexpr int X_ROWS = PAIR ? G_NMAX / 2 : G_NMAX;  // token rows per CTA and stage
+  static constexpr int X_BYTES = X_ROWS * 128;               // activation stage
+  static constexpr int A_BYTES = G_M * 128;                  // decoded weight stage
+  static constexpr int P_BYTES = 4096;                       // packed stage (128 x 32 B or 64 x 64 B)
+  static constexpr int LA_BYTES = G_M * 32;                  // LoRA slab, weight side [128][16] fp16
+  static constexpr int LB_BYTES = X_ROWS * 32;               // LoRA slab, token side [rows][16] fp16
+  static constexpr int X = 0;
+  static constexpr int A = X + STAGES * X_BYTES;
+  static constexpr int P = A + STAGES * A_BYTES;
+  static constexpr int LA = P + STAGES * P_BYTES;
+  static constexpr int LB = LA + LA_BYTES;
+  static constexpr int CODE = LB + LB_BYTES;         // per weight: 16 fp32 NF4 code
+  static constexpr int CODE2 = CODE + 64 * G_MAX_W;  // per weight: 256 fp32 second-level code
+  static constexpr int BAR = CODE2 + 1024 * G_MAX_W;
+  // full[S], afull[S], empty[S], acc_full[2], acc_empty[2], lora_full, lora_empty, mma_done
+  static constexpr int NUM_BARS = 3 * STAGES + 7;
+  static constexpr int MISC = BAR + NUM_BARS * 8;
+  static constexpr int TOTAL = MISC + 16;
+  static constexpr int ALLOC = TOTAL + 1024;  // slack to align the base to 1024 B
+};
+static_assert(Smem<false>::ALLOC <= 232448 && Smem<true>::ALLOC <= 232448, "shared memory budget");
 
 // Split-K workspace: a fixed counter region (arrivals at [0, G_SPLIT_MAX_TILES), finished
 // partials at [G_SPLIT_MAX_TILES, 2 * G_SPLIT_MAX_TILES)), then the fp32 partial tiles.  The
@@ -103,6 +113,7 @@ struct GemmArgs {
   int32_t n_tiles;        // 256-token tiles
   int32_t splits;         // K ranges per tile (split-K); 1 = none
   int32_t nk;             // K stages of the whole reduction
+  uint32_t k16;           // 1 << 16 (a run-time multiplier for the decode's shifts)
   float* ws_part;         // split-K: fp32 partial tiles [tiles][splits][256][128]
   int32_t* ws_cnt;        // split-K: per-tile counters [2][G_SPLIT_MAX_TILES], zero between launches
 };
@@ -111,24 +122,36 @@ __device__ int g_gemm_error;
 
 constexpr long long kWaitLimitCycles = 4000000000ll;  // ~2 s at 1.9 GHz
 
-__device__ __forceinline__ bool pipe_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
+// Longest time a waiting thread stays suspended in one try_wait: waiting warps sleep in
+// hardware until the phase completes instead of spinning on issue slots that the decode
+// warps need, and still look at the abort flag and the clock about once a millisecond.
+constexpr uint32_t kSuspendHintNs = 1000000u;
+
+// Bounded pipeline wait.  On expiry the abort flag of this CTA and, through `peer_abort` (a
+// shared::cluster address, 0 for none), that of the other CTA of a pair are raised.
+__device__ __forceinline__ bool pipe_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          uint32_t peer_abort) {
+  // a phase that has already completed (the MMA issuer's usual case) is seen without the
+  // suspend/resume cost of try_wait
+  if (mbar_test_wait(bar, parity)) return true;
+  if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
+  for (;;) {
     if (*abort_flag) return false;
     if (clock64() - t0 > kWaitLimitCycles) {
       *abort_flag = 1;
+      if (peer_abort) st_cluster_u32(peer_abort, 1u);
       atomicExch(&g_gemm_error, 1);
       return false;
     }
+    if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
   }
-  return true;
 }
 
 // Time-bounded wait that ignores the abort flag (used to drain in-flight work).
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   const long long t0 = clock64();
-  while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
+  while (!mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) {
     if (clock64() - t0 > kWaitLimitCycles) {
       atomicExch(&g_gemm_error, 2);
       return;
@@ -204,13 +227,14 @@ struct TileCoord {
 
 // MULTI: the launch carries more than one weight (a grouped forward).  Single-weight launches
 // compile with the weight index fixed at 0, so its fields stay direct constant-bank operands.
-template <bool MULTI>
-__device__ __forceinline__ TileCoord tile_coord(const GemmArgs& g, int tile) {
+// PAIR: tiles are 256 weight rows, of which CTA `rank` of the pair owns rows 128 rank ..
+template <bool MULTI, bool PAIR>
+__device__ __forceinline__ TileCoord tile_coord(const GemmArgs& g, int tile, uint32_t rank) {
   TileCoord c;
   const int mt = tile / g.n_tiles;
   const int nt = tile - mt * g.n_tiles;
   c.seg = MULTI ? (mt >= g.m_end[0]) + (mt >= g.m_end[1]) : 0;
-  c.m0 = int64_t(mt - (c.seg ? g.m_end[c.seg - 1] : 0)) * G_M;
+  c.m0 = int64_t(mt - (c.seg ? g.m_end[c.seg - 1] : 0)) * (PAIR ? 2 * G_M : G_M) + int64_t(rank) * G_M;
   c.t0 = int64_t(nt) * G_NMAX;
   c.tn_real = int(min64(G_NMAX, g.n - c.t0));
   c.tn = (c.tn_real + 15) & ~15;
@@ -226,12 +250,12 @@ struct WorkUnit {
   int kb, ke;   // stage range [kb, ke)
 };
 
-template <bool MULTI>
-__device__ __forceinline__ WorkUnit work_unit(const GemmArgs& g, int u) {
+template <bool MULTI, bool PAIR>
+__device__ __forceinline__ WorkUnit work_unit(const GemmArgs& g, int u, uint32_t rank) {
   WorkUnit w;
   w.tile = u / g.splits;
   w.split = u - w.tile * g.splits;
-  w.tc = tile_coord<MULTI>(g, w.tile);
+  w.tc = tile_coord<MULTI, PAIR>(g, w.tile, rank);
   w.kb = int((int64_t(w.split) * g.nk) / g.splits);
   w.ke = int((int64_t(w.split + 1) * g.nk) / g.splits);
   return w;
@@ -289,7 +313,8 @@ __device__ __forceinline__ bool wait_count(const int32_t* p, int want) {
 }
 
 // SPLIT: compiled with the split-K epilogue (launches with g.splits > 1).
-template <bool BWD, bool SPLIT, bool MULTI>
+// PAIR: launched as 2-CTA clusters; CTA rank 0 issues cta_group::2 MMAs over both CTAs' tiles.
+template <bool BWD, bool SPLIT, bool MULTI, bool PAIR>
 __global__ void __launch_bounds__(G_THREADS, 1)
     nf4_gemm_kernel(const __grid_constant__ CUtensorMap tm_act0, const __grid_constant__ CUtensorMap tm_act1,
                     const __grid_constant__ CUtensorMap tm_act2, const __grid_constant__ CUtensorMap tm_w0,
@@ -298,6 +323,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   // BWD && MULTI: several weights along K (dX = sum_i dY_i W_i); !BWD && MULTI: several
   // weights along M (Y_i = X W_i^T).
   constexpr bool KCAT = BWD && MULTI;
+  using L = Smem<PAIR>;
+  constexpr int NS = L::STAGES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -305,32 +332,60 @@ __global__ void __launch_bounds__(G_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SM_BAR);
-  uint64_t* afull = full + G_STAGES;
-  uint64_t* empty = afull + G_STAGES;
-  uint64_t* acc_full = empty + G_STAGES;  // [2]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR);
+  uint64_t* afull = full + NS;
+  uint64_t* empty = afull + NS;
+  uint64_t* acc_full = empty + NS;        // [2]
   uint64_t* acc_empty = acc_full + 2;     // [2]
   uint64_t* lora_full = acc_empty + 2;
   uint64_t* lora_empty = lora_full + 1;
   uint64_t* mma_done = lora_empty + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM_MISC);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SM_MISC + 4);
-  float* s_code = reinterpret_cast<float*>(smem + SM_CODE);
-  float* s_code2 = reinterpret_cast<float*>(smem + SM_CODE2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC + 4);
+  float* s_code = reinterpret_cast<float*>(smem + L::CODE);
+  float* s_code2 = reinterpret_cast<float*>(smem + L::CODE2);
 
   const int nunits = g.m_tiles * g.n_tiles * g.splits;
+  // PAIR: this CTA's rank in its cluster, the cluster's index, and the barriers of rank 0
+  // (the MMA issuer) that both CTAs arrive on, as shared::cluster addresses.
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int unit0 = PAIR ? int(cluster_id_x()) : int(blockIdx.x);
+  const int ustride = PAIR ? int(cluster_count_x()) : int(gridDim.x);
+  const uint32_t peer_abort = PAIR ? mapa_shared(smem_u32((const void*)abort_flag), rank ^ 1u) : 0u;
+  const uint32_t afull_l = PAIR ? mapa_shared(smem_u32(afull), 0u) : smem_u32(afull);
+  const uint32_t acc_empty_l = PAIR ? mapa_shared(smem_u32(acc_empty), 0u) : smem_u32(acc_empty);
+  const uint32_t lora_full_l = PAIR ? mapa_shared(smem_u32(lora_full), 0u) : smem_u32(lora_full);
+  auto pwait = [&](uint64_t* bar, uint32_t ph) { return pipe_wait(bar, ph, abort_flag, peer_abort); };
+  // arrival (one per warp) on a barrier that the MMA issuer waits on: `bar` is this CTA's
+  // copy, `bar_l` the issuer's copy as a shared::cluster address
+  auto arrive_issuer = [&](uint64_t* bar, uint32_t bar_l) {
+    if (PAIR)
+      mbar_arrive_cl(bar_l);
+    else
+      mbar_arrive(bar);
+  };
+  // MMA completion -> barrier `bar` of this CTA and, for a pair, the same barrier of rank 1
+  auto commit_both = [&](uint64_t* bar) {
+    if (PAIR) {
+      umma_commit_pair(smem_u32(bar));
+      umma_commit_pair(mapa_shared(smem_u32(bar), 1u));
+    } else {
+      umma_commit(bar);
+    }
+  };
+  constexpr uint32_t kPeers = PAIR ? 2u : 1u;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < G_STAGES; ++i) {
+    for (int i = 0; i < NS; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&afull[i], G_DQ_WARPS / 2);
+      mbar_init(&afull[i], kPeers * (G_DQ_WARPS / 2));
       mbar_init(&empty[i], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], G_EPI_WARPS);
+      mbar_init(&acc_empty[b], kPeers * G_EPI_WARPS);
     }
-    mbar_init(lora_full, G_DQ_WARPS);
+    mbar_init(lora_full, kPeers * G_DQ_WARPS);
     mbar_init(lora_empty, 1);
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -347,11 +402,18 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     if (g.w[i].nested && threadIdx.x < 256) s_code2[256 * i + threadIdx.x] = __ldg(g.w[i].code2 + threadIdx.x);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, G_TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tmem_slot, G_TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, G_TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // a pair: both CTAs' barriers initialised and TMEM allocated before any remote arrival/MMA
+  if (PAIR) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -360,90 +422,119 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < nunits; u += gridDim.x) {
-        const WorkUnit wu = work_unit<MULTI>(g, u);
+      for (int u = unit0; ok && u < nunits; u += ustride) {
+        const WorkUnit wu = work_unit<MULTI, PAIR>(g, u, rank);
         const TileCoord& tc = wu.tc;
+        // a pair's MMA reads tokens [0, tn/2) of the tile from rank 0 and [tn/2, tn) from rank 1
+        const int trow = int(tc.t0) + (PAIR ? int(rank) * (tc.tn >> 1) : 0);
         for (int k = wu.kb; k < wu.ke; ++k, ++it) {
-          const int s = it % G_STAGES;
-          const uint32_t ph = (it / G_STAGES) & 1;
-          if (!pipe_wait(&empty[s], ph ^ 1, abort_flag)) {
+          const int s = it % NS;
+          const uint32_t ph = (it / NS) & 1;
+          if (!pwait(&empty[s], ph ^ 1)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], SM_X_BYTES + SM_P_BYTES);
+          mbar_arrive_expect_tx(&full[s], L::X_BYTES + L::P_BYTES);
           const int ws = KCAT ? kseg(g, k) : tc.seg;   // weight of this stage
           const int kl = KCAT ? k - kbeg(g, ws) : k;  // its local K stage
           const CUtensorMap* tm_a = ws == 0 ? &tm_act0 : (ws == 1 ? &tm_act1 : &tm_act2);
           const CUtensorMap* tm_w = ws == 0 ? &tm_w0 : (ws == 1 ? &tm_w1 : &tm_w2);
-          tma_load_2d(smem + SM_X + s * SM_X_BYTES, KCAT ? tm_a : &tm_act0, &full[s], kl * G_K,
-                      int(tc.t0));
+          tma_load_2d(smem + L::X + s * L::X_BYTES, KCAT ? tm_a : &tm_act0, &full[s], kl * G_K, trow);
           if (!BWD)
-            tma_load_2d(smem + SM_P + s * SM_P_BYTES, tm_w, &full[s], kl * (G_K / 2), int(tc.m0));
+            tma_load_2d(smem + L::P + s * L::P_BYTES, tm_w, &full[s], kl * (G_K / 2), int(tc.m0));
           else
-            tma_load_2d(smem + SM_P + s * SM_P_BYTES, tm_w, &full[s], int(tc.m0 / 2), kl * G_K);
+            tma_load_2d(smem + L::P + s * L::P_BYTES, tm_w, &full[s], int(tc.m0 / 2), kl * G_K);
         }
       }
       // no bulk copy may still be landing in this CTA's shared memory at exit
-      for (uint32_t j = (it > G_STAGES ? it - G_STAGES : 0); j < it; ++j)
-        drain_wait(&full[j % G_STAGES], (j / G_STAGES) & 1);
+      for (uint32_t j = (it > uint32_t(NS) ? it - NS : 0); j < it; ++j)
+        drain_wait(&full[j % NS], (j / NS) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // (a pair: rank 0 issues for both CTAs; rank 1 only waits for the last MMA before its
+    // TMEM is released)
+    if (lane == 0 && rank == 0) {
       uint32_t it = 0, lt = 0, lc = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < nunits; u += gridDim.x, ++lt) {
-        const WorkUnit wu = work_unit<MULTI>(g, u);
+      const uint64_t ad0 = BWD ? smem_desc_sw128(sbase + L::A, 8192, 1024) : smem_desc_sw128(sbase + L::A, 16, 1024);
+      const uint64_t bd0 = smem_desc_sw128(sbase + L::X, 16, 1024);
+      for (int u = unit0; ok && u < nunits; u += ustride, ++lt) {
+        const WorkUnit wu = work_unit<MULTI, PAIR>(g, u, rank);
         const TileCoord& tc = wu.tc;
         const uint32_t b = lt & 1;
         const uint32_t use = lt >> 1;
         const uint32_t d_tmem = tmem_base + b * G_ACC_COLS;
-        const uint32_t idesc = idesc_f16(G_M, tc.tn, BWD, false);
-        if (!pipe_wait(&acc_empty[b], (use & 1) ^ 1, abort_flag)) break;
+        constexpr int MM = PAIR ? 2 * G_M : G_M;
+        const uint32_t idesc = idesc_f16(MM, tc.tn, BWD, false);
+        if (!pwait(&acc_empty[b], (use & 1) ^ 1)) break;
         tc_fence_after();
         bool acc = false;
         // LoRA terms belong to the first K range; a K-concatenated backward has one slab per
         // adapter, filled and consumed one after the other
         for (int i = 0; wu.split == 0 && i < (KCAT ? g.nw : 1); ++i) {
           if (!g.w[KCAT ? i : (MULTI ? tc.seg : 0)].has_lora) continue;
-          if (!pipe_wait(lora_full, lc & 1, abort_flag)) {
+          if (!pwait(lora_full, lc & 1)) {
             ok = false;
             break;
           }
           ++lc;
           tc_fence_after();
-          umma_f16(d_tmem, smem_desc_nosw(sbase + SM_LA, 128, 256),
-                   smem_desc_nosw(sbase + SM_LB, 128, 256), idesc_f16(G_M, tc.tn, false, false),
-                   acc ? 1u : 0u);
-          umma_commit(lora_empty);
+          const uint64_t ad = smem_desc_nosw(sbase + L::LA, 128, 256);
+          const uint64_t bd = smem_desc_nosw(sbase + L::LB, 128, 256);
+          const uint32_t id = idesc_f16(MM, tc.tn, false, false);
+          if (PAIR)
+            umma_f16_pair(d_tmem, ad, bd, id, acc ? 1u : 0u);
+          else
+            umma_f16(d_tmem, ad, bd, id, acc ? 1u : 0u);
+          commit_both(lora_empty);
           acc = true;
         }
         if (!ok) break;
-        for (int k = wu.kb; k < wu.ke; ++k, ++it) {
-          const int s = it % G_STAGES;
-          const uint32_t ph = (it / G_STAGES) & 1;
-          if (!pipe_wait(&full[s], ph, abort_flag) || !pipe_wait(&afull[s], ph, abort_flag)) {
-            ok = false;
-            break;
-          }
+        // The issuing thread shares its SM sub-partition with decode warps, so its loop is
+        // kept short: afull alone is awaited (every decode warp arrives only after its own
+        // full[s], so the stage's tokens have landed too -- for a pair, rank 1's half as
+        // well), and the descriptors are slot-0 descriptors plus constant offsets (the ring
+        // lies below 256 KB, so the 14-bit address field of a descriptor never carries).
+        // The next stage's barrier is tested (without blocking) between this stage's MMAs, so
+        // that test overlaps their issue and a ready stage follows without a wait.
+        uint32_t s = it % NS, ph = (it / NS) & 1;
+        bool ready = wu.kb < wu.ke && pwait(&afull[s], ph);
+        if (wu.kb < wu.ke && !ready) ok = false;
+        for (int k = wu.kb; ok && k < wu.ke; ++k, ++it) {
           tc_fence_after();
-          const uint32_t a_base = sbase + SM_A + s * SM_A_BYTES;
-          const uint32_t x_base = sbase + SM_X + s * SM_X_BYTES;
+          const uint64_t ad = ad0 + uint64_t(s * (L::A_BYTES >> 4));
+          const uint64_t bd = bd0 + uint64_t(s * (L::X_BYTES >> 4));
+          const uint32_t s1 = (s + 1 == uint32_t(NS)) ? 0u : s + 1;
+          const uint32_t ph1 = (s + 1 == uint32_t(NS)) ? (ph ^ 1u) : ph;
+          bool next_ready = false;
 #pragma unroll
           for (int kk = 0; kk < G_K / 16; ++kk) {
-            // K-major 128B swizzle: advance 32 B per 16 K; MN-major: two 8-row atoms.
-            const uint64_t ad = BWD ? smem_desc_sw128(a_base + kk * 2048, 8192, 1024)
-                                    : smem_desc_sw128(a_base + kk * 32, 16, 1024);
-            const uint64_t bd = smem_desc_sw128(x_base + kk * 32, 16, 1024);
-            umma_f16(d_tmem, ad, bd, idesc, (acc || kk > 0) ? 1u : 0u);
+            // K-major 128B swizzle: advance 32 B per 16 K; MN-major: two 8-row atoms (2 KB).
+            const uint64_t a_kk = ad + uint64_t(kk * (BWD ? 2048 / 16 : 32 / 16));
+            const uint64_t b_kk = bd + uint64_t(kk * (32 / 16));
+            if (PAIR)
+              umma_f16_pair(d_tmem, a_kk, b_kk, idesc, (acc || kk > 0) ? 1u : 0u);
+            else
+              umma_f16(d_tmem, a_kk, b_kk, idesc, (acc || kk > 0) ? 1u : 0u);
+            if (kk == 0 && k + 1 < wu.ke) next_ready = mbar_test_wait(&afull[s1], ph1);
           }
           acc = true;
-          umma_commit(&empty[s]);
+          commit_both(&empty[s]);
+          s = s1;
+          ph = ph1;
+          if (k + 1 < wu.ke && !next_ready && !pwait(&afull[s], ph)) {
+            ok = false;
+            ++it;
+            break;
+          }
         }
-        umma_commit(&acc_full[b]);
+        commit_both(&acc_full[b]);
       }
       // every MMA must be complete before TMEM is released
-      umma_commit(mma_done);
+      commit_both(mma_done);
+      drain_wait(mma_done, 0);
+    } else if (PAIR && lane == 0) {
       drain_wait(mma_done, 0);
     }
   } else if (warp < G_EPI_WARP0) {
@@ -472,11 +563,12 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                                 : uint32_t(r * 32) + ((1u ^ sw32) << 4);
     const uint32_t a_off = uint32_t(j * 8192 + (r >> 3) * 1024 + (r & 7) * 128);
     const uint32_t key = uint32_t(r & 7);
+    const uint32_t k16 = g.k16, k31 = g.k16 << 15;
 
     uint32_t it = 0, lc = 0;
     bool ok = true;
-    for (int u = blockIdx.x; ok && u < nunits; u += gridDim.x) {
-      const WorkUnit wu = work_unit<MULTI>(g, u);
+    for (int u = unit0; ok && u < nunits; u += ustride) {
+      const WorkUnit wu = work_unit<MULTI, PAIR>(g, u, rank);
       const TileCoord& tc = wu.tc;
       const int tws = MULTI ? tc.seg : 0;  // the tile's weight (forward); weight 0 backward
       const GemmW& W = g.w[tws];
@@ -485,13 +577,13 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       for (int li = 0; wu.split == 0 && li < (KCAT ? g.nw : 1); ++li) {
         const GemmW& WL = KCAT ? g.w[li] : W;
         if (!WL.has_lora) continue;
-        if (!pipe_wait(lora_empty, (lc & 1) ^ 1, abort_flag)) {
+        if (!pwait(lora_empty, (lc & 1) ^ 1)) {
           ok = false;
           break;
         }
         ++lc;
-        const uint32_t la = sbase + SM_LA;
-        const uint32_t lb = sbase + SM_LB;
+        const uint32_t la = sbase + L::LA;
+        const uint32_t lb = sbase + L::LB;
         if (dq < G_M) {
           if (!BWD) {
             const int64_t o = tc.m0 + dq;  // s * B[o, 0:16]
@@ -518,19 +610,21 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                                     pack_half2(v[12], v[13]), pack_half2(v[14], v[15])));
           }
         }
-        // token side: 256 rows x 2 chunks of 16 B
+        // token side: X_ROWS rows x 2 chunks of 16 B (a pair: this CTA's half of the tile)
+        const int thalf = PAIR ? (tc.tn >> 1) : G_NMAX;
+        const int tbase = PAIR ? int(rank) * thalf : 0;
 #pragma unroll
-        for (int jj = 0; jj < 2; ++jj) {
+        for (int jj = 0; jj < L::X_ROWS / 128; ++jj) {
           const int c = dq + 256 * jj;
           const int t = c >> 1, kc = c & 1;
           uint4 v = make_uint4(0, 0, 0, 0);
-          if (t < tc.tn_real)
-            v = __ldg(reinterpret_cast<const uint4*>(WL.lora_t + (tc.t0 + t) * 16 + kc * 8));
+          if (t < thalf && tbase + t < tc.tn_real)
+            v = __ldg(reinterpret_cast<const uint4*>(WL.lora_t + (tc.t0 + tbase + t) * 16 + kc * 8));
           st_shared_v4(lb + slab_off(t, kc), v);
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(lora_full);
+        if (lane == 0) arrive_issuer(lora_full, lora_full_l);
       }
       if (!ok) break;
 
@@ -581,35 +675,36 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           for (int i = 0; i < 16; ++i) code[i] = s_code[16 * ws + i];
         }
         const uint32_t its = it + uint32_t(k - wu.kb);
-        const int s = its % G_STAGES;
-        const uint32_t ph = (its / G_STAGES) & 1;
+        const int s = its % NS;
+        const uint32_t ph = (its / NS) & 1;
         const Nf4Table tab = make_table(code, sc);
         const Src raw2 = src(k + 4);
         const float sc1 = scale_of(raw1);
-        if (!pipe_wait(&full[s], ph, abort_flag)) {
+        if (!pwait(&full[s], ph)) {
           ok = false;
           break;
         }
-        const uint4 w0 = ld_shared_v4(sbase + SM_P + s * SM_P_BYTES + p_off0);
-        const uint4 w1 = ld_shared_v4(sbase + SM_P + s * SM_P_BYTES + p_off1);
-        const uint32_t abase = sbase + SM_A + s * SM_A_BYTES + a_off;
+        const uint4 w0 = ld_shared_v4(sbase + L::P + s * L::P_BYTES + p_off0);
+        const uint4 w1 = ld_shared_v4(sbase + L::P + s * L::P_BYTES + p_off1);
+        const uint32_t abase = sbase + L::A + s * L::A_BYTES + a_off;
         const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w};
 #pragma unroll
-        for (int c = 0; c < 4; ++c) st_shared_v4(abase + ((uint32_t(c) ^ key) << 4), decode_word_f16(tab, wa[c]));
+        for (int c = 0; c < 4; ++c)
+          st_shared_v4(abase + ((uint32_t(c) ^ key) << 4), decode_word_f16_mh(tab, wa[c], k16, k31));
         const uint32_t wb[4] = {w1.x, w1.y, w1.z, w1.w};
         if (g.w[ws].log2_bs == 5) {
           const Nf4Table tab2 = make_table(code, second_half_scale(k));
 #pragma unroll
           for (int c = 0; c < 4; ++c)
-            st_shared_v4(abase + ((uint32_t(4 + c) ^ key) << 4), decode_word_f16(tab2, wb[c]));
+            st_shared_v4(abase + ((uint32_t(4 + c) ^ key) << 4), decode_word_f16_mh(tab2, wb[c], k16, k31));
         } else {
 #pragma unroll
           for (int c = 0; c < 4; ++c)
-            st_shared_v4(abase + ((uint32_t(4 + c) ^ key) << 4), decode_word_f16(tab, wb[c]));
+            st_shared_v4(abase + ((uint32_t(4 + c) ^ key) << 4), decode_word_f16_mh(tab, wb[c], k16, k31));
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&afull[s]);
+        if (lane == 0) arrive_issuer(&afull[s], afull_l + 8u * uint32_t(s));
         sc = sc1;
         raw1 = raw2;
       }
@@ -619,19 +714,22 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     // --------------------------------------------------------------- epilogue
     // Warp w may only read TMEM lanes 32*(w%4)..+31 (the tile's weight rows); the two
     // groups of four warps take alternate 32-column chunks.  Lanes 2i and 2i+1 hold
-    // adjacent weight rows, i.e. adjacent output columns, so one shuffle per pair of
-    // tokens lets each lane store a 4-byte half2: the even lane writes token j, the odd
-    // lane token j+1.
+    // adjacent weight rows, i.e. adjacent output columns: each lane packs its two tokens
+    // j, j+1 into a half2, swaps it with its neighbour, and one byte permute gives the even
+    // lane (row, row+1) of token j and the odd lane the same two columns of token j+1.
     const int lq = warp & 3;
     const int grp = (warp - G_EPI_WARP0) >> 2;
     const bool odd = (lane & 1) != 0;
+    const uint32_t xsel = odd ? 0x3276u : 0x5410u;
     constexpr bool split = SPLIT;
     const int nparts = SPLIT ? g.splits - 1 : 0;
     const bool leader = threadIdx.x == 32 * G_EPI_WARP0;
-    volatile int* s_ticket = reinterpret_cast<volatile int*>(smem + SM_MISC + 8);  // [2]
+    volatile int* s_ticket = reinterpret_cast<volatile int*>(smem + L::MISC + 8);  // [2]
     uint32_t lt = 0;
-    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++lt) {
-      const WorkUnit wu = work_unit<MULTI>(g, u);
+    for (int u = unit0; u < nunits; u += ustride, ++lt) {
+      const WorkUnit wu = work_unit<MULTI, PAIR>(g, u, rank);
+      // split-K bookkeeping is per CTA: a pair's two 128-row halves are separate tiles there
+      const int ctile = PAIR ? 2 * wu.tile + int(rank) : wu.tile;
       const TileCoord& tc = wu.tc;
       const GemmW& W = g.w[MULTI ? tc.seg : 0];
       const int64_t ld_out = BWD ? g.in_f : W.out_f;
@@ -639,7 +737,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       const uint32_t use = lt >> 1;
       // uniform over the warp (tcgen05.ld is warp-collective) and, for split-K, over all
       // epilogue warps (they meet at named barriers below)
-      bool ok = pipe_wait(&acc_full[b], use & 1, abort_flag);
+      bool ok = pwait(&acc_full[b], use & 1);
       ok = split ? epi_bar_and(ok) : __all_sync(0xffffffffu, ok);
       tc_fence_after();
       if (!ok) break;
@@ -654,13 +752,13 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       // tickets, i.e. are past their main loops, so the wait cannot depend on unscheduled work.
       int ticket = nparts;
       if (split) {
-        if (leader) s_ticket[lt & 1] = atomicAdd(g.ws_cnt + wu.tile, 1);
+        if (leader) s_ticket[lt & 1] = atomicAdd(g.ws_cnt + ctile, 1);
         epi_bar_sync();
         ticket = s_ticket[lt & 1];
       }
       // partial tiles are column-major [256 tokens][128 rows]: for one token the 32 lanes
       // of a warp (32 consecutive rows) touch one 128-byte line
-      const float* part0 = g.ws_part + int64_t(wu.tile) * (nparts + 1) * (G_M * G_ACC_COLS) + prow;
+      const float* part0 = g.ws_part + int64_t(ctile) * (nparts + 1) * (G_M * G_ACC_COLS) + prow;
       if (ticket < nparts) {
         float* dst = const_cast<float*>(part0) + int64_t(wu.split) * (G_M * G_ACC_COLS);
         for (int c0 = 32 * grp; c0 < tc.tn; c0 += 64) {
@@ -672,21 +770,37 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         }
         __threadfence();
         epi_bar_sync();
-        if (leader) atomicAdd(g.ws_cnt + G_SPLIT_MAX_TILES + wu.tile, 1);
+        if (leader) atomicAdd(g.ws_cnt + G_SPLIT_MAX_TILES + ctile, 1);
       } else {
         if (split) {
           if (leader) {
-            if (!wait_count(g.ws_cnt + G_SPLIT_MAX_TILES + wu.tile, nparts)) *abort_flag = 1;
-            g.ws_cnt[wu.tile] = 0;  // every range of the tile has arrived: reset for reuse
-            g.ws_cnt[G_SPLIT_MAX_TILES + wu.tile] = 0;
+            if (!wait_count(g.ws_cnt + G_SPLIT_MAX_TILES + ctile, nparts)) *abort_flag = 1;
+            g.ws_cnt[ctile] = 0;  // every range of the tile has arrived: reset for reuse
+            g.ws_cnt[G_SPLIT_MAX_TILES + ctile] = 0;
             __threadfence();
           }
           epi_bar_sync();
         }
-        const float bias_v = (!BWD && W.bias != nullptr && row_ok) ? __half2float(W.bias[row]) : 0.f;
-        // the even lane of a pair writes columns (row, row+1) of token j; the odd lane the
-        // same two columns of token j+1
-        uint32_t* outp = reinterpret_cast<uint32_t*>(W.out + tc.t0 * ld_out + (row & ~int64_t(1)));
+        const bool has_bias = !BWD && W.bias != nullptr;
+        const float bias_v = (has_bias && row_ok) ? __half2float(W.bias[row]) : 0.f;
+        // this lane's first token of a chunk is c0 + odd; it stores every other token
+        uint32_t* outp = reinterpret_cast<uint32_t*>(W.out + (tc.t0 + (odd ? 1 : 0)) * ld_out +
+                                                     (row & ~int64_t(1)));
+        // 16 half2 stores of one 32-token chunk; lim: the lane's stores with jj < lim land
+        auto emit = [&](const uint32_t (&acc)[32], int c0, auto bias_c, int lim) {
+          uint32_t* p = outp + ((int64_t(c0) * ld_out) >> 1);
+#pragma unroll
+          for (int jj = 0; jj < 32; jj += 2) {
+            float v0 = __uint_as_float(acc[jj]), v1 = __uint_as_float(acc[jj + 1]);
+            if (decltype(bias_c)::value) {
+              v0 += bias_v;
+              v1 += bias_v;
+            }
+            const uint32_t own = pack_half2(v0, v1);  // tokens c0+jj, c0+jj+1 of this row
+            const uint32_t h = prmt(own, __shfl_xor_sync(0xffffffffu, own, 1), xsel);
+            if (jj < lim) p[int64_t(jj >> 1) * ld_out] = h;
+          }
+        };
         for (int c0 = 32 * grp; c0 < tc.tn; c0 += 64) {
           uint32_t acc[32];
           if (!SPLIT) {
@@ -715,29 +829,40 @@ __global__ void __launch_bounds__(G_THREADS, 1)
               for (int j = 0; j < 16; ++j) acc[16 * hf + j] = __float_as_uint(t[j]);
             }
           }
-#pragma unroll
-          for (int jj = 0; jj < 32; jj += 2) {
-            const float v0 = __uint_as_float(acc[jj]) + bias_v;      // token c0+jj
-            const float v1 = __uint_as_float(acc[jj + 1]) + bias_v;  // token c0+jj+1
-            // even lane sends its token-(j+1) value, odd lane its token-j value
-            const float other = __shfl_xor_sync(0xffffffffu, odd ? v0 : v1, 1);
-            const int tok = c0 + jj + (odd ? 1 : 0);
-            const uint32_t h = odd ? pack_half2(other, v1) : pack_half2(v0, other);
-            if (row_ok && tok < tc.tn_real) outp[(int64_t(tok) * ld_out) >> 1] = h;
+          // stores of token c0 + jj + odd land while that token is in the tile; the paths
+          // below are warp-uniform (emit shuffles across the warp)
+          const int lim = row_ok ? tc.tn_real - c0 - (odd ? 1 : 0) : 0;
+          const bool whole = __all_sync(0xffffffffu, lim >= 32);
+          if (has_bias) {
+            if (whole)
+              emit(acc, c0, std::true_type(), 32);
+            else
+              emit(acc, c0, std::true_type(), lim);
+          } else {
+            if (whole)
+              emit(acc, c0, std::false_type(), 32);
+            else
+              emit(acc, c0, std::false_type(), lim);
           }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if (lane == 0) arrive_issuer(&acc_empty[b], acc_empty_l + 8u * b);
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  // a pair: neither CTA leaves (or frees TMEM) while the other may still touch its shared
+  // memory or barriers
+  if (PAIR) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, G_TMEM_COLS);
+    if (PAIR)
+      tmem_dealloc_pair(tmem_base, G_TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, G_TMEM_COLS);
   }
 }
 
@@ -794,7 +919,7 @@ static int sm_count_cached() {
   return cached[dev];
 }
 
-template <bool BWD, bool SPLIT, bool MULTI>
+template <bool BWD, bool SPLIT, bool MULTI, bool PAIR>
 static int set_smem_attr() {
   static std::mutex mu;
   static bool done[64] = {false};
@@ -803,100 +928,193 @@ static int set_smem_attr() {
   if (dev < 0 || dev >= 64) return NF4B_ERR_DEVICE;
   std::lock_guard<std::mutex> lock(mu);
   if (!done[dev]) {
-    NF4B_CUDA_TRY(cudaFuncSetAttribute(nf4_gemm_kernel<BWD, SPLIT, MULTI>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SM_ALLOC));
+    NF4B_CUDA_TRY(cudaFuncSetAttribute(nf4_gemm_kernel<BWD, SPLIT, MULTI, PAIR>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, Smem<PAIR>::ALLOC));
     done[dev] = true;
   }
   return NF4B_OK;
 }
 
-// Tiling of one launch: 128-row weight tiles x 256-token tiles, each tile's K stages
-// split into `splits` ranges when there are fewer tiles than SMs.
+// Launch configuration of a 2-CTA cluster launch of `grid` CTAs.
+struct PairLaunch {
+  cudaLaunchConfig_t cfg;
+  cudaLaunchAttribute attr[1];
+  PairLaunch(unsigned grid, cudaStream_t s) : cfg{}, attr{} {
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(G_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = Smem<true>::ALLOC;
+    cfg.stream = s;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+};
+
+// CTA pairs (2-CTA clusters, one CTA per SM) that can be resident at once; 0 when the
+// device cannot run them.
+static int pair_slots_cached() {
+  static std::mutex mu;
+  static int cached[64] = {0};  // 0: not asked yet; -1: unavailable
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (set_smem_attr<false, false, false, true>() == NF4B_OK) {
+      PairLaunch pl(2u * unsigned(sm_count_cached()), nullptr);
+      if (cudaOccupancyMaxActiveClusters(&n, nf4_gemm_kernel<false, false, false, true>, &pl.cfg) !=
+          cudaSuccess)
+        n = 0;
+    }
+    cudaGetLastError();  // a refused query leaves no sticky error behind
+    cached[dev] = n > 0 ? n : -1;
+  }
+  return cached[dev] > 0 ? cached[dev] : 0;
+}
+
+// Tiling of one launch.  Single CTAs: 128-row weight tiles x 256-token tiles on one CTA per
+// SM.  Pairs: 256-row tiles (each weight's rows rounded up to 256) on 2-CTA clusters.  The
+// K stages of a tile may be split into `splits` ranges when there are fewer tiles than slots.
 struct GemmPlan {
   int64_t m_tiles, n_tiles, tiles;
   int32_t nk;
   int32_t splits;
+  bool pair;
+  int64_t slots;  // CTAs (single) or clusters (pair) resident at once
 };
 
 constexpr int G_MAX_SPLITS = 8;
 
-// Split-K choice from a cost model in stage-times (~0.7 us) of the busiest SM: a unit costs
+// Split-K choice from a cost model in stage-times (~0.7 us) of the busiest slot: a unit costs
 // its stages plus ~3 stages of pipeline fill and drain; a split tile adds the round trip
 // of its fp32 partials through L2, measured at ~3 us to write one 128 x 256 partial and
 // ~3 us per partial for the last CTA to read back (4 + 4 per partial, in stage-times).  A
 // split must beat the unsplit launch by 5 % and leave every range at least 2 stages.
-static GemmPlan plan_gemm(int64_t n, int64_t m_tiles, int64_t kdim, int64_t sms) {
-  GemmPlan p;
-  p.m_tiles = m_tiles;
-  p.n_tiles = (n + G_NMAX - 1) / G_NMAX;
-  p.tiles = p.m_tiles * p.n_tiles;
-  p.nk = int32_t(kdim / G_K);
-  p.splits = 1;
-  if (p.tiles <= 0 || p.tiles >= sms || p.tiles > G_SPLIT_MAX_TILES) return p;
+static void plan_splits(GemmPlan* p, int64_t max_tiles) {
+  p->splits = 1;
+  if (p->tiles <= 0 || p->tiles >= p->slots || p->tiles > max_tiles) return;
   auto cost = [&](int64_t sp) {
-    const int64_t waves = (p.tiles * sp + sms - 1) / sms;
+    const int64_t waves = (p->tiles * sp + p->slots - 1) / p->slots;
     const double reduce = sp > 1 ? 4.0 + 4.0 * double(sp - 1) : 0.0;
-    return double(waves) * double((p.nk + sp - 1) / sp + 3) + reduce;
+    return double(waves) * double((p->nk + sp - 1) / sp + 3) + reduce;
   };
   double best = cost(1);
-  for (int sp = 2; sp <= G_MAX_SPLITS && p.nk / sp >= 2; ++sp) {
+  for (int sp = 2; sp <= G_MAX_SPLITS && p->nk / sp >= 2; ++sp) {
     const double c = cost(sp);
     if (c < 0.95 * best) {
       best = c;
-      p.splits = sp;
+      p->splits = sp;
     }
   }
-  return p;
+}
+
+// Pair mode from STEW_NF4_PAIR: "0" never, "1" whenever the device runs pairs, otherwise
+// automatic.
+static int pair_mode_env() {
+  const char* v = std::getenv("STEW_NF4_PAIR");
+  if (v == nullptr || v[0] == '\0') return -1;
+  return v[0] == '0' ? 0 : 1;
+}
+
+// rows: the M-side rows of each weight of the launch (forward: out features of each grouped
+// weight; backward: the in features, once).  kdim: the reduction length.
+static GemmPlan plan_gemm(int64_t n, const int64_t* rows, int nrows, int64_t kdim) {
+  GemmPlan single{};
+  single.n_tiles = (n + G_NMAX - 1) / G_NMAX;
+  single.nk = int32_t(kdim / G_K);
+  single.pair = false;
+  single.slots = sm_count_cached();
+  single.m_tiles = 0;
+  for (int i = 0; i < nrows; ++i) single.m_tiles += (rows[i] + G_M - 1) / G_M;
+  single.tiles = single.m_tiles * single.n_tiles;
+  plan_splits(&single, G_SPLIT_MAX_TILES);
+  const int mode = pair_mode_env();
+  const int64_t pslots = mode == 0 ? 0 : pair_slots_cached();
+  if (pslots <= 0) return single;
+  GemmPlan pair = single;
+  pair.pair = true;
+  pair.slots = pslots;
+  pair.m_tiles = 0;
+  for (int i = 0; i < nrows; ++i) pair.m_tiles += (rows[i] + 2 * G_M - 1) / (2 * G_M);
+  pair.tiles = pair.m_tiles * pair.n_tiles;
+  plan_splits(&pair, G_SPLIT_MAX_TILES / 2);
+  if (mode == 1) return pair;
+  // automatic: single CTAs (pairs measured level with them on every Qwen2.5-1.5B shape; they
+  // halve the L2 -> SM token traffic but add a cross-CTA hop to every stage)
+  return single;
 }
 
 // Workspace of a split launch: the counter region, then one fp32 partial tile per K range
-// [tiles][splits][256][128] (the last range of a tile to finish leaves its slot unused).
+// and CTA tile [cta tiles][splits][256][128] (the last range of a tile to finish leaves its
+// slot unused).
 static int64_t plan_work_bytes(const GemmPlan& p) {
   if (p.splits <= 1) return 0;
-  return G_SPLIT_CNT_BYTES + p.tiles * p.splits * int64_t(G_M) * G_ACC_COLS * int64_t(sizeof(float));
+  const int64_t cta_tiles = p.pair ? 2 * p.tiles : p.tiles;
+  return G_SPLIT_CNT_BYTES + cta_tiles * p.splits * int64_t(G_M) * G_ACC_COLS * int64_t(sizeof(float));
 }
 
-// One persistent CTA per SM (at most one per work unit).
+// Token rows of the activation tile one CTA loads per stage.
+static uint32_t act_box_rows(const GemmPlan& p) { return p.pair ? G_NMAX / 2 : G_NMAX; }
+
+template <bool BWD, bool SPLIT, bool MULTI, bool PAIR>
+static int launch_variant(unsigned grid, const CUtensorMap (&ta)[G_MAX_W], const CUtensorMap (&tw)[G_MAX_W],
+                          const GemmArgs& g, cudaStream_t s) {
+  int st = set_smem_attr<BWD, SPLIT, MULTI, PAIR>();
+  if (st != NF4B_OK) return st;
+  if (!PAIR) {
+    nf4_gemm_kernel<BWD, SPLIT, MULTI, PAIR><<<grid, G_THREADS, Smem<PAIR>::ALLOC, s>>>(
+        ta[0], ta[1], ta[2], tw[0], tw[1], tw[2], g);
+  } else {
+    PairLaunch pl(grid, s);
+    NF4B_CUDA_TRY(cudaLaunchKernelEx(&pl.cfg, nf4_gemm_kernel<BWD, SPLIT, MULTI, PAIR>, ta[0], ta[1],
+                                     ta[2], tw[0], tw[1], tw[2], g));
+  }
+  return NF4B_OK;
+}
+
+// One persistent CTA per SM, or one 2-CTA cluster per pair slot (at most one per work unit).
 template <bool BWD>
-static int launch_gemm(const CUtensorMap (&ta)[G_MAX_W], const CUtensorMap (&tw)[G_MAX_W], GemmArgs g,
-                       int64_t m_tiles, int64_t kdim, void* work, int64_t work_bytes, cudaStream_t s) {
-  const int64_t sms = sm_count_cached();
-  GemmPlan p = plan_gemm(g.n, m_tiles, kdim, sms);
-  if (work == nullptr) p.splits = 1;
-  NF4B_RETURN_IF(p.tiles * p.splits > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
-  if (p.splits > 1) {
-    NF4B_RETURN_IF(work_bytes < plan_work_bytes(p), NF4B_ERR_INVALID_ARG);
+static int launch_gemm(const GemmPlan& p, const CUtensorMap (&ta)[G_MAX_W], const CUtensorMap (&tw)[G_MAX_W],
+                       GemmArgs g, void* work, int64_t work_bytes, cudaStream_t s) {
+  GemmPlan q = p;
+  if (work == nullptr) q.splits = 1;
+  NF4B_RETURN_IF(q.tiles * q.splits > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
+  if (q.splits > 1) {
+    NF4B_RETURN_IF(work_bytes < plan_work_bytes(q), NF4B_ERR_INVALID_ARG);
     NF4B_RETURN_IF(!aligned(work, 256), NF4B_ERR_ALIGNMENT);
     g.ws_cnt = static_cast<int32_t*>(work);
     g.ws_part = reinterpret_cast<float*>(static_cast<uint8_t*>(work) + G_SPLIT_CNT_BYTES);
   }
-  g.m_tiles = int32_t(p.m_tiles);
-  g.n_tiles = int32_t(p.n_tiles);
-  g.splits = p.splits;
-  g.nk = p.nk;
-  const int64_t units = p.tiles * p.splits;
-  const unsigned grid = unsigned(units < sms ? units : sms);
-  const bool split = p.splits > 1;
+  g.m_tiles = int32_t(q.m_tiles);
+  g.n_tiles = int32_t(q.n_tiles);
+  g.splits = q.splits;
+  g.nk = q.nk;
+  g.k16 = 1u << 16;
+  const int64_t units = q.tiles * q.splits;
+  const int64_t slots = units < q.slots ? units : q.slots;
+  const unsigned grid = unsigned(q.pair ? 2 * slots : slots);
+  const bool split = q.splits > 1;
+  const bool multi = g.nw > 1;
   int st;
-#define NF4B_LAUNCH(SPLIT_, MULTI_)                                                             \
-  do {                                                                                         \
-    st = set_smem_attr<BWD, SPLIT_, MULTI_>();                                                 \
-    if (st != NF4B_OK) return st;                                                              \
-    nf4_gemm_kernel<BWD, SPLIT_, MULTI_><<<grid, G_THREADS, SM_ALLOC, s>>>(                    \
-        ta[0], ta[1], ta[2], tw[0], tw[1], tw[2], g);                                          \
-  } while (0)
-  if (g.nw > 1) {
-    if (split)
-      NF4B_LAUNCH(true, true);
+  if (q.pair) {
+    if (multi)
+      st = split ? launch_variant<BWD, true, true, true>(grid, ta, tw, g, s)
+                 : launch_variant<BWD, false, true, true>(grid, ta, tw, g, s);
     else
-      NF4B_LAUNCH(false, true);
+      st = split ? launch_variant<BWD, true, false, true>(grid, ta, tw, g, s)
+                 : launch_variant<BWD, false, false, true>(grid, ta, tw, g, s);
   } else {
-    if (split)
-      NF4B_LAUNCH(true, false);
+    if (multi)
+      st = split ? launch_variant<BWD, true, true, false>(grid, ta, tw, g, s)
+                 : launch_variant<BWD, false, true, false>(grid, ta, tw, g, s);
     else
-      NF4B_LAUNCH(false, false);
+      st = split ? launch_variant<BWD, true, false, false>(grid, ta, tw, g, s)
+                 : launch_variant<BWD, false, false, false>(grid, ta, tw, g, s);
   }
-#undef NF4B_LAUNCH
+  if (st != NF4B_OK) return st;
   return launch_status(BWD ? "nf4_gemm_kernel<bwd> launch" : "nf4_gemm_kernel<fwd> launch");
 }
 
@@ -934,13 +1152,13 @@ static void fill_qstate_args(GemmW* w, const nf4b_qstate* qs, int32_t log2_bs) {
   w->nested = qs->nested ? 1 : 0;
 }
 
-static int64_t ceil_tiles(int64_t rows) { return (rows + G_M - 1) / G_M; }
-
-// Global tile boundaries of the weights: unused entries stay past every tile.
-static void set_m_end(GemmArgs* g, const int64_t* rows, int nw) {
+// Global tile boundaries of the weights (tiles of 128 rows, 256 for pairs): unused entries
+// stay past every tile.
+static void set_m_end(GemmArgs* g, const int64_t* rows, int nw, bool pair) {
+  const int64_t tr = pair ? 2 * G_M : G_M;
   int64_t acc = 0;
   for (int i = 0; i < G_MAX_W; ++i) {
-    if (i < nw) acc += ceil_tiles(rows[i]);
+    if (i < nw) acc += (rows[i] + tr - 1) / tr;
     g->m_end[i] = i < nw ? int32_t(acc) : 0x7FFFFFFF;
   }
   g->nw = nw;
@@ -957,18 +1175,15 @@ extern "C" int64_t nf4b_linear_work_bytes(int64_t n, int64_t in_features, int64_
                                           int32_t backward) {
   if (n <= 0 || in_features <= 0 || out_features <= 0) return 0;
   if (check_device() != NF4B_OK) return -1;
-  const GemmPlan p = plan_gemm(n, ceil_tiles(backward ? in_features : out_features),
-                               backward ? out_features : in_features, sm_count_cached());
-  return plan_work_bytes(p);
+  const int64_t rows = backward ? in_features : out_features;
+  return plan_work_bytes(plan_gemm(n, &rows, 1, backward ? out_features : in_features));
 }
 
 extern "C" int64_t nf4b_linear_group_work_bytes(int64_t n, int64_t in_features,
                                                 const int64_t* out_features, int32_t n_items) {
   if (n <= 0 || in_features <= 0 || !out_features || n_items < 1 || n_items > G_MAX_W) return 0;
   if (check_device() != NF4B_OK) return -1;
-  int64_t m_tiles = 0;
-  for (int i = 0; i < n_items; ++i) m_tiles += ceil_tiles(out_features[i]);
-  return plan_work_bytes(plan_gemm(n, m_tiles, in_features, sm_count_cached()));
+  return plan_work_bytes(plan_gemm(n, out_features, n_items, in_features));
 }
 
 extern "C" int nf4b_linear_fwd_group(const void* x, int64_t n, int64_t in_features,
@@ -992,13 +1207,15 @@ extern "C" int nf4b_linear_fwd_group(const void* x, int64_t n, int64_t in_featur
   int st = check_device();
   if (st != NF4B_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int64_t rows[G_MAX_W];
+  for (int i = 0; i < n_items; ++i) rows[i] = items[i].out_features;
+  const GemmPlan plan = plan_gemm(n, rows, n_items, in_features);
   CUtensorMap ta[G_MAX_W], tw[G_MAX_W];
   st = make_tmap_2d(&ta[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, uint64_t(in_features), uint64_t(n),
-                    uint64_t(in_features) * 2, G_K, G_NMAX, CU_TENSOR_MAP_SWIZZLE_128B);
+                    uint64_t(in_features) * 2, G_K, act_box_rows(plan), CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != NF4B_OK) return st;
   ta[1] = ta[2] = ta[0];
   GemmArgs g{};
-  int64_t rows[G_MAX_W];
   for (int i = 0; i < n_items; ++i) {
     const nf4b_linear_item& it = items[i];
     st = make_tmap_2d(&tw[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, it.packed, uint64_t(in_features / 2),
@@ -1018,14 +1235,13 @@ extern "C" int nf4b_linear_fwd_group(const void* x, int64_t n, int64_t in_featur
       w.lora_t = static_cast<const __half*>(it.lora->xa);
       w.lora_scale = it.lora->scale;
     }
-    rows[i] = it.out_features;
   }
   for (int i = n_items; i < G_MAX_W; ++i) tw[i] = tw[0];  // unused kernel parameters
-  set_m_end(&g, rows, n_items);
+  set_m_end(&g, rows, n_items, plan.pair);
   for (int i = 0; i < G_MAX_W; ++i) g.k_end[i] = 0x7FFFFFFF;
   g.n = n;
   g.in_f = in_features;
-  return launch_gemm<false>(ta, tw, g, g.m_end[n_items - 1], in_features, work, work_bytes, s);
+  return launch_gemm<false>(plan, ta, tw, g, work, work_bytes, s);
 }
 
 extern "C" int nf4b_linear_fwd_ws(const void* x, const uint8_t* packed, const nf4b_qstate* qs,
@@ -1049,7 +1265,7 @@ extern "C" int64_t nf4b_linear_bwd_group_work_bytes(int64_t n, int64_t in_featur
   if (check_device() != NF4B_OK) return -1;
   int64_t kdim = 0;
   for (int i = 0; i < n_items; ++i) kdim += out_features[i];
-  return plan_work_bytes(plan_gemm(n, ceil_tiles(in_features), kdim, sm_count_cached()));
+  return plan_work_bytes(plan_gemm(n, &in_features, 1, kdim));
 }
 
 extern "C" int nf4b_linear_bwd_dx_group(const nf4b_linear_bwd_item* items, int32_t n_items, void* dx,
@@ -1076,13 +1292,15 @@ extern "C" int nf4b_linear_bwd_dx_group(const nf4b_linear_bwd_item* items, int32
   int st = check_device();
   if (st != NF4B_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const GemmPlan plan = plan_gemm(n, &in_features, 1, kdim);
   CUtensorMap ta[G_MAX_W], tw[G_MAX_W];
   GemmArgs g{};
   int64_t kacc = 0;
   for (int i = 0; i < n_items; ++i) {
     const nf4b_linear_bwd_item& it = items[i];
     st = make_tmap_2d(&ta[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, it.dy, uint64_t(it.out_features),
-                      uint64_t(n), uint64_t(it.out_features) * 2, G_K, G_NMAX, CU_TENSOR_MAP_SWIZZLE_128B);
+                      uint64_t(n), uint64_t(it.out_features) * 2, G_K, act_box_rows(plan),
+                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (st != NF4B_OK) return st;
     st = make_tmap_2d(&tw[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, it.packed, uint64_t(in_features / 2),
                       uint64_t(it.out_features), uint64_t(in_features / 2), G_M / 2, G_K,
@@ -1109,12 +1327,11 @@ extern "C" int nf4b_linear_bwd_dx_group(const nf4b_linear_bwd_item* items, int32
     tw[i] = tw[0];
     g.k_end[i] = 0x7FFFFFFF;
   }
-  const int64_t rows = in_features;
-  set_m_end(&g, &rows, 1);  // all weights share the M side (the in features)
+  set_m_end(&g, &in_features, 1, plan.pair);  // all weights share the M side (the in features)
   g.nw = n_items;
   g.n = n;
   g.in_f = in_features;
-  return launch_gemm<true>(ta, tw, g, g.m_end[0], kdim, work, work_bytes, s);
+  return launch_gemm<true>(plan, ta, tw, g, work, work_bytes, s);
 }
 
 extern "C" int nf4b_linear_bwd_dx_ws(const void* dy, const uint8_t* packed, const nf4b_qstate* qs,
@@ -1139,5 +1356,14 @@ extern "C" int nf4b_gemm_error_flag(int* value, int reset) {
     const int zero = 0;
     NF4B_CUDA_TRY(cudaMemcpyToSymbol(g_gemm_error, &zero, sizeof(int)));
   }
+  return NF4B_OK;
+}
+
+extern "C" int nf4b_gemm_geometry(int* sms, int* pair_slots) {
+  NF4B_RETURN_IF(sms == nullptr || pair_slots == nullptr, NF4B_ERR_INVALID_ARG);
+  const int st = check_device();
+  if (st != NF4B_OK) return st;
+  *sms = sm_count_cached();
+  *pair_slots = pair_slots_cached();
   return NF4B_OK;
 }

@@ -8,7 +8,8 @@
 //   entries 0..7 : prmt(L0, L1, nibbles)          (valid where nibble < 8)
 //   entries 8..15: prmt(L2, L3, nibbles & 0x7777) (valid where nibble >= 8)
 //   pick per byte by nibble bit 3, then interleave low/high planes into half2.
-// Cost: 11 integer ops per 4 values + 32 ops per table (16 fmul, 8 cvt, 8 prmt).
+// Cost: 11 integer ops per 4 values + 32 ops per table (16 fmul, 8 cvt, 8 prmt); the
+// multiply-high form below moves 5 of every 23 per word to the FMA pipe.
 #pragma once
 
 #include "common.cuh"
@@ -50,6 +51,27 @@ __device__ __forceinline__ uint2 lookup4(const Nf4Table& t, uint32_t s) {
   const uint32_t lo = prmt(prmt(t.l0, t.l1, s), prmt(t.l2, t.l3, m), sel);
   const uint32_t hi = prmt(prmt(t.h0, t.h1, s), prmt(t.h2, t.h3, m), sel);
   return make_uint2(prmt(lo, hi, 0x4051u), prmt(lo, hi, 0x6273u));
+}
+
+// lookup4 with the nibble masks precomputed: m = s & 0x7777, sel = ((s >> 1) & 0x4444) | 0x3210
+// (only the low 16 bits of each operand are read).
+__device__ __forceinline__ uint2 lookup4_pre(const Nf4Table& t, uint32_t s, uint32_t m, uint32_t sel) {
+  const uint32_t lo = prmt(prmt(t.l0, t.l1, s), prmt(t.l2, t.l3, m), sel);
+  const uint32_t hi = prmt(prmt(t.h0, t.h1, s), prmt(t.h2, t.h3, m), sel);
+  return make_uint2(prmt(lo, hi, 0x4051u), prmt(lo, hi, 0x6273u));
+}
+
+// As decode_word_f16, with the masks made once per word and its right shifts done as integer
+// multiply-high, (x * 2^(32-s)) >> 32, which issue on the FMA pipe and leave the ALU pipe --
+// the one the byte permutes saturate -- 18 instead of 23 instructions per word.  k16 = 1 << 16
+// and k31 = 1 << 31 arrive as run-time values so the compiler keeps the multiplies.
+__device__ __forceinline__ uint4 decode_word_f16_mh(const Nf4Table& t, uint32_t w, uint32_t k16,
+                                                    uint32_t k31) {
+  const uint32_t m = w & 0x77777777u;
+  const uint32_t sel = (__umulhi(w, k31) & 0x44444444u) | 0x32103210u;
+  const uint2 a = lookup4_pre(t, w, m, sel);
+  const uint2 b = lookup4_pre(t, __umulhi(w, k16), __umulhi(m, k16), __umulhi(sel, k16));
+  return make_uint4(a.x, a.y, b.x, b.y);
 }
 
 // One packed 32-bit word (8 values) -> 16 bytes of fp16 in memory order.
