@@ -438,13 +438,14 @@ def profile_case():
     print("profile case done")
 
 
-def profile_step():
+def profile_step(full: bool = False):
     import torch
     from stew_b200.qlora_step import QLoRATrainer, QwenConfig, QwenQLoRA, synthetic_batch
     torch.cuda.set_device(0)
-    model = QwenQLoRA(QwenConfig(layers=4, vocab=32768), device="cuda", seed=0)
+    cfg = QwenConfig() if full else QwenConfig(layers=4, vocab=32768)
+    model = QwenQLoRA(cfg, device="cuda", seed=0)
     trainer = QLoRATrainer(model)
-    tokens, lengths = synthetic_batch(vocab=32768, seed=1000)
+    tokens, lengths = synthetic_batch(vocab=cfg.vocab, seed=1000)
     for _ in range(2):
         trainer.step(tokens, lengths)
     torch.cuda.synchronize()
@@ -478,6 +479,8 @@ def main():
                     help="small single-GPU case for an ncu launch list of the QLoRA step: a 4-layer "
                          "model (small vocabulary), two eager warm-up steps, then one step inside "
                          "cudaProfilerStart/Stop (use ncu --profile-from-start off)")
+    ap.add_argument("--profile-full", action="store_true",
+                    help="with --profile-step: the full 28-layer model and vocabulary")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -485,7 +488,7 @@ def main():
     if args.profile_case:
         return profile_case()
     if args.profile_step:
-        return profile_step()
+        return profile_step(full=args.profile_full)
 
     import torch
     world, rank, local = _dist()

@@ -10,6 +10,7 @@
  *   nf4b_rope_qk                     <- solution/rope.py:24-52 rope_kernel (forward, and INVERSE
  *                                       for the backward) applied to q and k in one launch
  *   nf4b_swiglu_fwd / _bwd           <- solution/swiglu.py:15-40
+ *   nf4b_ce_fwd / _bwd               <- solution/head_loss.py (loss, then softmax - onehot)
  * Activations are fp16, row-major.
  */
 #ifndef STEW_STEP_H
@@ -49,6 +50,18 @@ int nf4b_swiglu_fwd(const void* gate, const void* up, void* out, int64_t n, void
 /* dgate = fp16(fp16(dout*up) * silu'(gate)), dup = fp16(dout * fp16(silu(gate))).  */
 int nf4b_swiglu_bwd(const void* dout, const void* gate, const void* up, void* dgate, void* dup,
                     int64_t n, void* stream);
+
+/* Next-token cross-entropy of the LM head over fp16 logits [rows, vocab] (vocab a multiple of
+ * 8, rows 16-byte aligned) with int64 labels [rows] -- the reference's fused head loss
+ * (solution/head_loss.py: per-row loss, then the gradient softmax - onehot in place):
+ *   nf4b_ce_fwd: loss[r] = logsumexp(logits[r]) - logits[r, labels[r]] (fp32; 0 where the
+ *                label is outside [0, vocab), e.g. -100), lse[r] = logsumexp(logits[r]);
+ *   nf4b_ce_bwd: logits[r, j] <- fp16(g * (exp(logits[r, j] - lse[r]) - [j == labels[r]])) in
+ *                place, g = *gscale (device fp32), zero rows for ignored labels.  */
+int nf4b_ce_fwd(const void* logits, const int64_t* labels, float* loss, float* lse, int64_t rows,
+                int64_t vocab, void* stream);
+int nf4b_ce_bwd(void* logits, const int64_t* labels, const float* lse, const float* gscale,
+                int64_t rows, int64_t vocab, void* stream);
 
 #ifdef __cplusplus
 }

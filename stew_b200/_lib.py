@@ -94,6 +94,8 @@ SIGNATURES = {
                                c_int32, c_int32, c_int32, c_int32, c_void_p]),
     "nf4b_swiglu_fwd": (c_int32, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "nf4b_swiglu_bwd": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "nf4b_ce_fwd": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p]),
+    "nf4b_ce_bwd": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p]),
     "nf4b_lora_grads": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p,
                                   c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int32, c_void_p]),
     "nf4b_lora_grads_noalloc": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p,

@@ -18,7 +18,10 @@
 
 namespace nf4b {
 
-constexpr int NORM_WARPS = 8;         // rows per 256-thread CTA
+// Two rows (one warp each) per 64-thread CTA: a ~1,300-row batch spreads over every SM.  The
+// kernels are instantiated per row width (NC chunks of 256 features), so a row occupies only
+// the registers it needs and many warps fit on an SM.
+constexpr int NORM_WARPS = 2;
 constexpr int NORM_MAX_CHUNKS = 16;   // 16 x 256 = 4096 features per row at most
 
 __device__ __forceinline__ void h8_to_f(uint4 v, float (&f)[8]) {
@@ -49,19 +52,21 @@ __device__ __forceinline__ float round_h(float v) { return __half2float(__float2
 
 // Forward RMSNorm of one row; `delta` (nullable) is added first (fused residual add) and the
 // fp16 sum written to `sum`.
+template <int NC>
 __global__ void __launch_bounds__(32 * NORM_WARPS)
     rmsnorm_fwd_kernel(const __half* __restrict__ x, const __half* __restrict__ delta,
                        const float* __restrict__ w, float eps, __half* __restrict__ sum,
-                       __half* __restrict__ y, float* __restrict__ rstd, int64_t rows, int hidden) {
+                       __half* __restrict__ y, float* __restrict__ rstd, int64_t rows) {
+  constexpr int hidden = NC * 256;
   const int lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * NORM_WARPS + (threadIdx.x >> 5);
   if (row >= rows) return;
-  const int nc = hidden >> 8;  // 256-value chunks: lane owns values [chunk*256 + lane*8, +8)
+  constexpr int nc = NC;  // 256-value chunks: lane owns values [chunk*256 + lane*8, +8)
   const __half* xr = x + row * hidden;
-  uint4 v[NORM_MAX_CHUNKS];
+  uint4 v[NC];
   float ss = 0.f;
 #pragma unroll
-  for (int c = 0; c < NORM_MAX_CHUNKS; ++c) {
+  for (int c = 0; c < NC; ++c) {
     if (c < nc) {
       const int off = c * 256 + lane * 8;
       v[c] = *reinterpret_cast<const uint4*>(xr + off);
@@ -84,7 +89,7 @@ __global__ void __launch_bounds__(32 * NORM_WARPS)
   const float r = rsqrtf(ss / float(hidden) + eps);
   if (lane == 0) rstd[row] = r;
 #pragma unroll
-  for (int c = 0; c < NORM_MAX_CHUNKS; ++c) {
+  for (int c = 0; c < NC; ++c) {
     if (c < nc) {
       const int off = c * 256 + lane * 8;
       float f[8];
@@ -100,20 +105,21 @@ __global__ void __launch_bounds__(32 * NORM_WARPS)
 }
 
 // Backward: dx = r * (w dy - xn * mean(w dy xn)) (+ dsum), xn = x r.
+template <int NC>
 __global__ void __launch_bounds__(32 * NORM_WARPS)
     rmsnorm_bwd_kernel(const __half* __restrict__ dy, const __half* __restrict__ x,
                        const float* __restrict__ w, const float* __restrict__ rstd,
-                       const __half* __restrict__ dsum, __half* __restrict__ dx, int64_t rows,
-                       int hidden) {
+                       const __half* __restrict__ dsum, __half* __restrict__ dx, int64_t rows) {
+  constexpr int hidden = NC * 256;
   const int lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * NORM_WARPS + (threadIdx.x >> 5);
   if (row >= rows) return;
-  const int nc = hidden >> 8;
+  constexpr int nc = NC;
   const float r = rstd[row];
-  uint4 xv[NORM_MAX_CHUNKS], gv[NORM_MAX_CHUNKS];
+  uint4 xv[NC], gv[NC];
   float dot = 0.f;
 #pragma unroll
-  for (int c = 0; c < NORM_MAX_CHUNKS; ++c) {
+  for (int c = 0; c < NC; ++c) {
     if (c < nc) {
       const int off = c * 256 + lane * 8;
       xv[c] = *reinterpret_cast<const uint4*>(x + row * hidden + off);
@@ -130,7 +136,7 @@ __global__ void __launch_bounds__(32 * NORM_WARPS)
   }
   const float cmean = warp_sum(dot) / float(hidden);
 #pragma unroll
-  for (int c = 0; c < NORM_MAX_CHUNKS; ++c) {
+  for (int c = 0; c < NC; ++c) {
     if (c < nc) {
       const int off = c * 256 + lane * 8;
       float a[8], g[8], o[8];
@@ -227,6 +233,98 @@ __global__ void swiglu_bwd_kernel(const __half* __restrict__ dm, const __half* _
   reinterpret_cast<uint4*>(du)[i] = f_to_h8(ou);
 }
 
+// ---------------------------------------------------------------- LM-head cross-entropy
+// One CTA per row of fp16 logits [rows, vocab] (the counterpart of the reference's fused head
+// loss, solution/head_loss.py: loss and, in a second pass over the row, the gradient
+// softmax - onehot written in place over the logits).  Forward: each thread keeps an online
+// maximum and sum of exponentials over its 8-wide vectors (online softmax, Milakov and
+// Gimelshein 2018), the CTA merges the pairs, and loss = logsumexp - logit[label] in fp32.
+constexpr int CE_THREADS = 512;
+
+__device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
+  if (m2 == -INFINITY) return;
+  if (m == -INFINITY) {
+    m = m2;
+    s = s2;
+    return;
+  }
+  if (m2 > m) {
+    s = s * expf(m - m2) + s2;
+    m = m2;
+  } else {
+    s = s + s2 * expf(m2 - m);
+  }
+}
+
+__global__ void __launch_bounds__(CE_THREADS)
+    ce_fwd_kernel(const __half* __restrict__ logits, const int64_t* __restrict__ labels,
+                  float* __restrict__ loss, float* __restrict__ lse_out, int64_t vocab) {
+  const int64_t row = blockIdx.x;
+  const __half* x = logits + row * vocab;
+  float m = -INFINITY, s = 0.f;
+  const int64_t nv = vocab >> 3;  // 8-wide vectors (rows are 16-byte aligned: vocab % 8 == 0)
+  for (int64_t i = threadIdx.x; i < nv; i += CE_THREADS) {
+    float f[8];
+    h8_to_f(*reinterpret_cast<const uint4*>(x + 8 * i), f);
+    float vm = f[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) vm = fmaxf(vm, f[j]);
+    if (vm > m) {
+      s = (m == -INFINITY) ? 0.f : s * expf(m - vm);
+      m = vm;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += expf(f[j] - m);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    lse_merge(m, s, m2, s2);
+  }
+  __shared__ float sm[CE_THREADS / 32], ssum[CE_THREADS / 32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sm[warp] = m;
+    ssum[warp] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float mm = sm[0], st = ssum[0];
+    for (int w = 1; w < CE_THREADS / 32; ++w) lse_merge(mm, st, sm[w], ssum[w]);
+    const float lse = mm + logf(st);
+    lse_out[row] = lse;
+    const int64_t t = labels[row];
+    loss[row] = (t < 0 || t >= vocab) ? 0.f : lse - __half2float(x[t]);
+  }
+}
+
+// Backward, in place: logits[r, j] <- fp16(g * (exp(logits[r, j] - lse[r]) - [j == label[r]])),
+// g = *gscale (the incoming gradient of the summed loss times a power-of-two scale that keeps
+// the small probabilities of a 151,936-entry row out of fp16's subnormal range); rows whose
+// label is outside [0, vocab) (ignored) get zeros.
+__global__ void __launch_bounds__(CE_THREADS)
+    ce_bwd_kernel(__half* __restrict__ logits, const int64_t* __restrict__ labels,
+                  const float* __restrict__ lse_in, const float* __restrict__ gscale, int64_t vocab) {
+  const int64_t row = blockIdx.x;
+  __half* x = logits + row * vocab;
+  const int64_t t = labels[row];
+  const bool ignored = t < 0 || t >= vocab;
+  const float g = ignored ? 0.f : *gscale;
+  const float lse = lse_in[row];
+  const int64_t nv = vocab >> 3;
+  for (int64_t i = threadIdx.x; i < nv; i += CE_THREADS) {
+    float f[8];
+    h8_to_f(*reinterpret_cast<const uint4*>(x + 8 * i), f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float p = expf(f[j] - lse) - ((8 * i + j) == t ? 1.f : 0.f);
+      f[j] = g * p;
+    }
+    *reinterpret_cast<uint4*>(x + 8 * i) = f_to_h8(f);
+  }
+}
+
 static int norm_checks(int64_t rows, int64_t hidden) {
   NF4B_RETURN_IF(rows < 0 || hidden <= 0, NF4B_ERR_INVALID_ARG);
   NF4B_RETURN_IF(hidden % 256 != 0 || hidden > 256 * NORM_MAX_CHUNKS, NF4B_ERR_UNSUPPORTED);
@@ -251,9 +349,25 @@ extern "C" int nf4b_rmsnorm_fwd(const void* x, const void* delta, const float* w
   if (rows == 0) return NF4B_OK;
   st = check_device();
   if (st != NF4B_OK) return st;
-  rmsnorm_fwd_kernel<<<norm_grid(rows), 32 * NORM_WARPS, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(x), static_cast<const __half*>(delta), w, eps,
-      static_cast<__half*>(sum), static_cast<__half*>(y), rstd, rows, int(hidden));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const __half* xh = static_cast<const __half*>(x);
+  const __half* dh = static_cast<const __half*>(delta);
+  __half* sh = static_cast<__half*>(sum);
+  __half* yh = static_cast<__half*>(y);
+  switch (hidden >> 8) {
+#define NF4B_NORM_FWD(NC_)                                                                        \
+  case NC_:                                                                                       \
+    rmsnorm_fwd_kernel<NC_><<<norm_grid(rows), 32 * NORM_WARPS, 0, s>>>(xh, dh, w, eps, sh, yh, rstd, \
+                                                                       rows);                      \
+    break;
+    NF4B_NORM_FWD(1) NF4B_NORM_FWD(2) NF4B_NORM_FWD(3) NF4B_NORM_FWD(4) NF4B_NORM_FWD(5)
+    NF4B_NORM_FWD(6) NF4B_NORM_FWD(7) NF4B_NORM_FWD(8) NF4B_NORM_FWD(9) NF4B_NORM_FWD(10)
+    NF4B_NORM_FWD(11) NF4B_NORM_FWD(12) NF4B_NORM_FWD(13) NF4B_NORM_FWD(14) NF4B_NORM_FWD(15)
+    NF4B_NORM_FWD(16)
+#undef NF4B_NORM_FWD
+    default:
+      return NF4B_ERR_UNSUPPORTED;
+  }
   return launch_status("rmsnorm_fwd_kernel launch");
 }
 
@@ -269,9 +383,24 @@ extern "C" int nf4b_rmsnorm_bwd(const void* dy, const void* x, const float* w, c
   if (rows == 0) return NF4B_OK;
   st = check_device();
   if (st != NF4B_OK) return st;
-  rmsnorm_bwd_kernel<<<norm_grid(rows), 32 * NORM_WARPS, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(dy), static_cast<const __half*>(x), w, rstd,
-      static_cast<const __half*>(dsum), static_cast<__half*>(dx), rows, int(hidden));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const __half* gh = static_cast<const __half*>(dy);
+  const __half* xh = static_cast<const __half*>(x);
+  const __half* dsh = static_cast<const __half*>(dsum);
+  __half* dxh = static_cast<__half*>(dx);
+  switch (hidden >> 8) {
+#define NF4B_NORM_BWD(NC_)                                                                          \
+  case NC_:                                                                                         \
+    rmsnorm_bwd_kernel<NC_><<<norm_grid(rows), 32 * NORM_WARPS, 0, s>>>(gh, xh, w, rstd, dsh, dxh, rows); \
+    break;
+    NF4B_NORM_BWD(1) NF4B_NORM_BWD(2) NF4B_NORM_BWD(3) NF4B_NORM_BWD(4) NF4B_NORM_BWD(5)
+    NF4B_NORM_BWD(6) NF4B_NORM_BWD(7) NF4B_NORM_BWD(8) NF4B_NORM_BWD(9) NF4B_NORM_BWD(10)
+    NF4B_NORM_BWD(11) NF4B_NORM_BWD(12) NF4B_NORM_BWD(13) NF4B_NORM_BWD(14) NF4B_NORM_BWD(15)
+    NF4B_NORM_BWD(16)
+#undef NF4B_NORM_BWD
+    default:
+      return NF4B_ERR_UNSUPPORTED;
+  }
   return launch_status("rmsnorm_bwd_kernel launch");
 }
 
@@ -324,4 +453,32 @@ extern "C" int nf4b_swiglu_bwd(const void* dout, const void* gate, const void* u
       static_cast<const __half*>(dout), static_cast<const __half*>(gate), static_cast<const __half*>(up),
       static_cast<__half*>(dgate), static_cast<__half*>(dup), n8);
   return launch_status("swiglu_bwd_kernel launch");
+}
+
+extern "C" int nf4b_ce_fwd(const void* logits, const int64_t* labels, float* loss, float* lse,
+                           int64_t rows, int64_t vocab, void* stream) {
+  NF4B_RETURN_IF(rows < 0 || vocab <= 0, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(rows > 0 && (!logits || !labels || !loss || !lse), NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(vocab % 8 != 0 || rows > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
+  NF4B_RETURN_IF(!aligned(logits, 16), NF4B_ERR_ALIGNMENT);
+  if (rows == 0) return NF4B_OK;
+  int st = check_device();
+  if (st != NF4B_OK) return st;
+  ce_fwd_kernel<<<unsigned(rows), CE_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(logits), labels, loss, lse, vocab);
+  return launch_status("ce_fwd_kernel launch");
+}
+
+extern "C" int nf4b_ce_bwd(void* logits, const int64_t* labels, const float* lse, const float* gscale,
+                           int64_t rows, int64_t vocab, void* stream) {
+  NF4B_RETURN_IF(rows < 0 || vocab <= 0, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(rows > 0 && (!logits || !labels || !lse || !gscale), NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(vocab % 8 != 0 || rows > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
+  NF4B_RETURN_IF(!aligned(logits, 16), NF4B_ERR_ALIGNMENT);
+  if (rows == 0) return NF4B_OK;
+  int st = check_device();
+  if (st != NF4B_OK) return st;
+  ce_bwd_kernel<<<unsigned(rows), CE_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<__half*>(logits), labels, lse, gscale, vocab);
+  return launch_status("ce_bwd_kernel launch");
 }

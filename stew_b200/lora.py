@@ -39,14 +39,21 @@ def _fusable(x, st, lora_a, lora_b) -> bool:
             and lora_a.shape == (LORA_RANK, in_f) and lora_b.shape == (out_f, LORA_RANK))
 
 
+def _half_of(p: torch.Tensor) -> torch.Tensor:
+    """fp16 form of an adapter matrix: the model's shared fp16 shadow of its adapters (one
+    copy kernel per step refreshes all of them) when it keeps one, else a conversion."""
+    h = getattr(p, "_stew_half", None)
+    return h if h is not None else p.to(torch.float16).contiguous()
+
+
 class NF4LoraFunction(torch.autograd.Function):
     """y = x W^T (+ bias) + (x A^T) B^T * scaling, W the NF4 weight (packed, st)."""
 
     @staticmethod
     def forward(ctx, x, packed, st, bias, lora_a, lora_b, scaling):
         out_f, in_f = int(st.shape[0]), int(st.shape[1])
-        a16 = lora_a.to(torch.float16).contiguous()
-        b16 = lora_b.to(torch.float16).contiguous()
+        a16 = _half_of(lora_a)
+        b16 = _half_of(lora_b)
         x2 = x.reshape(-1, in_f).contiguous()
         n = x2.shape[0]
         Bv = packed.view(-1, 1)
@@ -161,8 +168,8 @@ class GroupedNF4Function(torch.autograd.Function):
                 b = None if bias is None else bias.to(torch.float16).contiguous()
                 lc = None
                 if scaling is not None:
-                    a16 = params[pi].to(torch.float16).contiguous()
-                    b16 = params[pi + 1].to(torch.float16).contiguous()
+                    a16 = _half_of(params[pi])
+                    b16 = _half_of(params[pi + 1])
                     xa = torch.empty(n, LORA_RANK, dtype=torch.float16, device=dev)
                     lc = _lora_c(a16, b16, scaling, xa)
                     saved.append((a16, b16, xa))

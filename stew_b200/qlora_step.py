@@ -25,7 +25,7 @@ import torch.nn.functional as F
 
 from . import dp
 from .lora import LORA_RANK, NF4Linear, NF4LoraLinear, grouped_projection
-from .step_ops import add_rms_norm, rms_norm, rope_qk, swiglu
+from .step_ops import add_rms_norm, head_cross_entropy, rms_norm, rope_qk, swiglu
 from .sweep import QWEN_PROJ, qwen_model_weights
 
 
@@ -52,13 +52,12 @@ def rope_tables(positions: torch.Tensor, head_dim: int, theta: float):
 
 def packed_causal_attention(q, k, v, rows):
     """Causal attention inside each packed row: q [N, H, D], k/v [N, KH, D] (grouped-query
-    heads), rows = (cu_seqlens int32 [B+1], longest row).  The variable-length flash kernel
-    sees only the real tokens, no [N, N] mask."""
+    heads, H a multiple of KH), rows = (cu_seqlens int32 [B+1], longest row).  The
+    variable-length flash kernel sees only the real tokens, no [N, N] mask, and reads the
+    shared k/v heads directly (no expanded copies, no head-sum in the backward)."""
     from torch.nn.attention.varlen import varlen_attn
     cu, longest = rows
-    r = q.shape[1] // k.shape[1]
-    return varlen_attn(q, k.repeat_interleave(r, 1), v.repeat_interleave(r, 1), cu, cu, longest,
-                       longest, window_size=(-1, 0))
+    return varlen_attn(q, k, v, cu, cu, longest, longest, window_size=(-1, 0))
 
 
 class Layer(torch.nn.Module):
@@ -126,9 +125,27 @@ class QwenQLoRA(torch.nn.Module):
         self.layers = torch.nn.ModuleList(
             [Layer(cfg, ws[7 * i:7 * i + 7], device) for i in range(cfg.layers)])
         self.register_buffer("ln_f", torch.ones(cfg.hidden, device=device))
+        # The adapters live in one fp32 buffer (each parameter a view of it) with an fp16
+        # shadow of the same layout: one copy kernel per step gives every projection its fp16
+        # A and B, instead of one conversion per matrix (112 launches a step).
+        params = self.lora_parameters()
+        total = sum(p.numel() for p in params)
+        self._lora_flat = torch.empty(total, dtype=torch.float32, device=device)
+        self._lora_half = torch.empty(total, dtype=torch.float16, device=device)
+        off = 0
+        for p in params:
+            n = p.numel()
+            self._lora_flat[off:off + n].copy_(p.detach().reshape(-1))
+            p.data = self._lora_flat[off:off + n].view_as(p)
+            p._stew_half = self._lora_half[off:off + n].view_as(p)
+            off += n
 
     def lora_parameters(self):
         return [p for p in self.parameters() if p.requires_grad]
+
+    def refresh_lora_half(self):
+        """The fp16 shadow of the adapters from their current fp32 values."""
+        self._lora_half.copy_(self._lora_flat)
 
     @staticmethod
     def pack(tokens: torch.Tensor, lengths: torch.Tensor) -> "PackedBatch":
@@ -161,6 +178,7 @@ class QwenQLoRA(torch.nn.Module):
         """Sum of next-token CE over the labelled tokens of a packed batch.  Fixed shapes and
         no host synchronisation, so a step can be captured in a CUDA graph."""
         rows = (pb.cu, pb.longest)
+        self.refresh_lora_half()
         cos, sin = rope_tables(pb.positions, self.cfg.head_dim, self.cfg.rope_theta)
         x = self.embed.index_select(0, pb.ids)
         eps = self.cfg.rms_eps
@@ -170,8 +188,8 @@ class QwenQLoRA(torch.nn.Module):
             x, h = add_rms_norm(x, layer.attention(h, cos, sin, rows), layer.ln2, eps)
             nxt = self.layers[i + 1].ln1 if i + 1 < len(self.layers) else self.ln_f
             x, h = add_rms_norm(x, layer.mlp(h), nxt, eps)
-        logits = h.index_select(0, pb.lab_idx) @ self.embed.t()
-        return F.cross_entropy(logits.float(), pb.labels, reduction="sum")
+        # LM head + summed next-token CE, fused (the reference's solution/head_loss.py)
+        return head_cross_entropy(h.index_select(0, pb.lab_idx), self.embed, pb.labels)
 
 
 def synthetic_batch(batch: int = 4, seq: int = 512, vocab: int = 151936, mean_frac: float = 0.57,

@@ -1,8 +1,9 @@
 """Autograd wrappers of the layer kernels of the packed-token QLoRA step (C ABI
 include/stew_step.h): RMSNorm, RMSNorm fused with the residual add, rotary embedding of q and
-k, and SwiGLU -- the counterparts of the reference's solution/rmsnorm.py (RMSNormFn :59-92,
-AddRMSNormFn :192-233), solution/rope.py (:71-92) and solution/swiglu.py (:42-66).  fp16
-activations, fp32 math; the CUDA kernels are the only implementation (no torch fallback)."""
+k, SwiGLU and the LM head's cross-entropy -- the counterparts of the reference's
+solution/rmsnorm.py (RMSNormFn :59-92, AddRMSNormFn :192-233), solution/rope.py (:71-92),
+solution/swiglu.py (:42-66) and solution/head_loss.py.  fp16 activations, fp32 math; the CUDA
+kernels are the only implementation (no torch fallback)."""
 from __future__ import annotations
 
 import torch
@@ -147,3 +148,43 @@ def rope_qk(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tens
 def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     """fp16(fp16(silu(gate)) * up)."""
     return _SwiGLU.apply(gate, up)
+
+
+# The backward's softmax - onehot is written as fp16 times this power of two (exact to divide
+# out): a 151,936-entry row's probabilities are ~1e-5 and would otherwise sit in fp16's
+# subnormal range.
+CE_GRAD_SCALE = 1024.0
+
+
+class _HeadCrossEntropy(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h, embed, labels):
+        h2 = _c(h)
+        logits = h2 @ embed.t()  # [rows, vocab] fp16 (cuBLAS)
+        rows, vocab = logits.shape
+        lab = _c(labels.to(torch.int64))
+        loss = torch.empty(rows, dtype=torch.float32, device=h.device)
+        lse = torch.empty(rows, dtype=torch.float32, device=h.device)
+        _lib.check(_lib.lib().nf4b_ce_fwd(logits.data_ptr(), lab.data_ptr(), loss.data_ptr(), lse.data_ptr(),
+                                          rows, vocab, _stream(h.device)), "nf4b_ce_fwd")
+        ctx.save_for_backward(logits, lab, lse, embed)
+        return loss.sum()
+
+    @staticmethod
+    def backward(ctx, g):
+        logits, lab, lse, embed = ctx.saved_tensors
+        rows, vocab = logits.shape
+        gs = (g.float() * CE_GRAD_SCALE).reshape(1).contiguous()
+        # softmax - onehot over the logits' own storage (they are not needed afterwards)
+        _lib.check(_lib.lib().nf4b_ce_bwd(logits.data_ptr(), lab.data_ptr(), lse.data_ptr(), gs.data_ptr(),
+                                          rows, vocab, _stream(logits.device)), "nf4b_ce_bwd")
+        dh = logits @ embed
+        dh.mul_(1.0 / CE_GRAD_SCALE)
+        return dh, None, None
+
+
+def head_cross_entropy(h: torch.Tensor, embed: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+    """Sum over rows of CE(h @ embed^T, labels): fp16 logits from one GEMM, then the fused
+    loss kernel; the gradient of h only (the embedding is frozen).  Labels outside
+    [0, vocab) are ignored."""
+    return _HeadCrossEntropy.apply(h, embed, labels)

@@ -93,6 +93,12 @@ def test_host_validation_rejects_before_launch():
     assert L.nf4b_swiglu_fwd(16, 16, 16, 12, None) == _lib.NF4B_ERR_UNSUPPORTED
     assert L.nf4b_swiglu_bwd(16, 16, 16, 16, 16, 12, None) == _lib.NF4B_ERR_UNSUPPORTED
     assert L.nf4b_rope_qk(16, 16, 16, 16, 16, 16, 1, 1, 1, 100, 0, None) == _lib.NF4B_ERR_UNSUPPORTED
+    # head cross-entropy: vocab not a multiple of 8, missing buffers, misaligned logits
+    assert L.nf4b_ce_fwd(16, 16, 16, 16, 4, 1001, None) == _lib.NF4B_ERR_UNSUPPORTED
+    assert L.nf4b_ce_bwd(16, 16, 16, 16, 4, 1001, None) == _lib.NF4B_ERR_UNSUPPORTED
+    assert L.nf4b_ce_fwd(16, None, 16, 16, 4, 1000, None) == _lib.NF4B_ERR_INVALID_ARG
+    assert L.nf4b_ce_bwd(18, 16, 16, 16, 4, 1000, None) == _lib.NF4B_ERR_ALIGNMENT
+    assert L.nf4b_ce_fwd(16, 16, 16, 16, 0, 1000, None) == _lib.NF4B_OK
     assert L.nf4b_rmsnorm_fwd(None, None, 16, 1e-6, None, 16, 16, 4, 256, None) == _lib.NF4B_ERR_INVALID_ARG
 
 

@@ -55,7 +55,13 @@ def _worker(rank, world, port, q, fail_rank):
         m = TinyLoRA()
         loss, n = m(*_rows(rank))
         loss.backward()
+        # the graph-capturable form (count as a tensor, no host sync) on a copy of the grads
+        m2 = TinyLoRA()
+        m2.a.grad, m2.b.grad = m.a.grad.clone(), m.b.grad.clone()
+        total_dev = dp.allreduce_lora_grads_device([m2.a, m2.b], torch.tensor(float(n)))
         total = dp.allreduce_lora_grads([m.a, m.b], n)
+        assert float(total_dev) == total
+        assert torch.equal(m2.a.grad, m.a.grad) and torch.equal(m2.b.grad, m.b.grad)
         q.put((rank, "ok", total, m.a.grad.clone(), m.b.grad.clone()))
     except Exception as e:  # noqa: BLE001
         q.put((rank, "error", repr(e), None, None))
@@ -103,9 +109,15 @@ def test_single_process_needs_no_group():
     loss, n = m(*_rows(3))
     loss.backward()
     ga = m.a.grad.clone()
+    gb = m.b.grad.clone()
     total = dp.allreduce_lora_grads([m.a, m.b], n)
     assert total == n
     torch.testing.assert_close(m.a.grad, ga / n)
+    # the capturable form divides in place without the flat buffer when there is no group
+    m.a.grad, m.b.grad = ga.clone(), gb.clone()
+    total_dev = dp.allreduce_lora_grads_device([m.a, m.b], torch.tensor(float(n)))
+    assert float(total_dev) == n
+    assert torch.equal(m.a.grad, ga / n) and torch.equal(m.b.grad, gb / n)
 
 
 @pytest.mark.timeout(180)

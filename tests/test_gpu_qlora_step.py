@@ -139,3 +139,19 @@ def test_training_steps_lower_the_loss(cuda_lib):
     losses = [float(trainer.step(tokens, lengths)[0]) for _ in range(4)]
     assert losses[-1] < losses[0]
     assert trainer.lora_grad_bytes() == 4 * (2 * (16 * 1536 + 1536 * 16 + 16 * 1536 + 256 * 16) + 1)
+
+
+def test_adapter_fp16_shadow_follows_the_optimizer(cuda_lib):
+    """The adapters are views of one fp32 buffer with one fp16 shadow; every forward refreshes
+    the shadow, so the projections always see the current (optimizer-updated) adapters."""
+    from stew_b200.qlora_step import QLoRATrainer, synthetic_batch
+    model = _small_model()
+    trainer = QLoRATrainer(model, lr=5e-3)
+    tokens, lengths = synthetic_batch(batch=2, seq=96, vocab=model.cfg.vocab, seed=4)
+    before = [p.detach().clone() for p in trainer.params]
+    trainer.step(tokens, lengths)
+    assert any(not torch.equal(b, p.detach()) for b, p in zip(before, trainer.params))
+    model(tokens, lengths)
+    for p in trainer.params:
+        assert p.data_ptr() >= model._lora_flat.data_ptr()
+        assert torch.equal(p._stew_half, p.detach().to(torch.float16))

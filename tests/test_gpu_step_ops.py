@@ -121,3 +121,29 @@ def test_step_ops_argument_checks(cuda_lib):
     assert L.nf4b_rmsnorm_fwd(16, None, 16, 1e-6, None, 16, 16, 4, 1000, None) == _lib.NF4B_ERR_UNSUPPORTED
     assert L.nf4b_swiglu_fwd(16, 16, 16, 12, None) == _lib.NF4B_ERR_UNSUPPORTED
     assert L.nf4b_rope_qk(16, 16, 16, 16, 16, 16, 1, 1, 1, 100, 0, None) == _lib.NF4B_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("rows,vocab,hidden", [(1, 1000, 64), (77, 4096, 256), (1307, 151936, 1536)])
+def test_head_cross_entropy_forward_backward(cuda_lib, rows, vocab, hidden):
+    """Fused LM-head loss (nf4b_ce_fwd/_bwd) against F.cross_entropy on the same fp16 logits
+    in fp32: the summed loss within 1e-5 relative (summation order), dh within 2e-3 of
+    max |ref| (fp16 gradient of the logits, scaled by 1024 on the way); ignored labels (-100)
+    add nothing."""
+    from stew_b200.step_ops import head_cross_entropy
+    g = torch.Generator(device="cuda").manual_seed(rows + vocab)
+    h = (torch.randn(rows, hidden, generator=g, device="cuda") * 2.0).half()
+    emb = (torch.randn(vocab, hidden, generator=g, device="cuda") * 0.05).half()
+    labels = torch.randint(0, vocab, (rows,), generator=g, device="cuda")
+    if rows > 2:
+        labels[::7] = -100
+    hx = h.clone().requires_grad_(True)
+    loss = head_cross_entropy(hx, emb, labels)
+    loss.backward()
+    hr = h.clone().requires_grad_(True)
+    logits = hr @ emb.t()  # the same fp16 GEMM
+    ref = F.cross_entropy(logits.float(), labels, reduction="sum", ignore_index=-100)
+    ref.backward()
+    assert abs(float(loss) - float(ref)) <= 1e-5 * abs(float(ref)) + 1e-4
+    assert _rel(hx.grad, hr.grad.float()) <= GRAD_TOL
+    if rows > 2:  # an ignored row's gradient is exactly zero
+        assert float(hx.grad[0].abs().max()) == 0.0
