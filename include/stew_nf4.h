@@ -197,6 +197,26 @@ int nf4b_lora_grads(const void* x, const void* dy, const void* xa, const void* d
                     float* da, float* db, void* work, int64_t n, int64_t in_features,
                     int64_t out_features, int32_t rank, void* stream);
 
+/* The weight gradients of several adapters (e.g. q and v of one layer, whose backward runs at
+ * the same time) in two launches in total: every adapter's dA and dB outer products in one,
+ * all their reductions in the next.  Same math as nf4b_lora_grads per item; rank 16; at most 3
+ * items.  `work`: fp32 scratch of nf4b_lora_grads_group_work_bytes(items, n_items, n) bytes
+ * (the items' partial sums side by side; -1 for invalid items).  */
+typedef struct nf4b_lora_grads_item {
+  const void* x;        /* fp16 [n, in_features], the projection's input        */
+  const void* dy;       /* fp16 [n, out_features], the gradient of its output   */
+  const void* xa;       /* fp16 [n, 16], x A^T from the forward                  */
+  const void* dyb;      /* fp16 [n, 16], dY B from the backward dX GEMM          */
+  float scale;          /* lora_alpha / r                                        */
+  float* da;            /* fp32 [16, in_features] out                            */
+  float* db;            /* fp32 [out_features, 16] out                           */
+  int64_t in_features;
+  int64_t out_features;
+} nf4b_lora_grads_item;
+int64_t nf4b_lora_grads_group_work_bytes(const nf4b_lora_grads_item* items, int32_t n_items, int64_t n);
+int nf4b_lora_grads_group(const nf4b_lora_grads_item* items, int32_t n_items, void* work,
+                          int64_t work_bytes, int64_t n, void* stream);
+
 /* nf4b_lora_grads without the `work` argument, for callers that cannot call
  * cudaMalloc on this path (inside a framework that already holds the device's memory
  * in its own pool, or in a loop where allocating is not allowed).  It allocates

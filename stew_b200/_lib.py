@@ -59,6 +59,13 @@ class LinearItemC(ctypes.Structure):
                 ("lora", ctypes.POINTER(LoraC)), ("y", c_void_p), ("out_features", c_int64)]
 
 
+class LoraGradsItemC(ctypes.Structure):
+    """nf4b_lora_grads_item."""
+    _fields_ = [("x", c_void_p), ("dy", c_void_p), ("xa", c_void_p), ("dyb", c_void_p),
+                ("scale", c_float), ("da", c_void_p), ("db", c_void_p), ("in_features", c_int64),
+                ("out_features", c_int64)]
+
+
 # name -> (restype, argtypes); every symbol include/*.h declares
 SIGNATURES = {
     "nf4b_dequant": (c_int32, [c_void_p, ctypes.POINTER(QStateC), c_void_p, c_int32, c_int64, c_void_p]),
@@ -85,6 +92,9 @@ SIGNATURES = {
     "nf4b_linear_bwd_dx_group": (c_int32, [ctypes.POINTER(LinearBwdItemC), c_int32, c_void_p, c_int64,
                                            c_int64, c_void_p, c_int64, c_void_p]),
     "nf4b_lora_grads_work_bytes": (c_int64, [c_int64, c_int64, c_int64, c_int32]),
+    "nf4b_lora_grads_group_work_bytes": (c_int64, [ctypes.POINTER(LoraGradsItemC), c_int32, c_int64]),
+    "nf4b_lora_grads_group": (c_int32, [ctypes.POINTER(LoraGradsItemC), c_int32, c_void_p, c_int64,
+                                        c_int64, c_void_p]),
     # layer kernels of the QLoRA step (include/stew_step.h)
     "nf4b_rmsnorm_fwd": (c_int32, [c_void_p, c_void_p, c_void_p, ctypes.c_float, c_void_p, c_void_p,
                                    c_void_p, c_int64, c_int64, c_void_p]),

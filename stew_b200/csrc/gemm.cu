@@ -1164,8 +1164,9 @@ static void set_m_end(GemmArgs* g, const int64_t* rows, int nw, bool pair) {
   g->nw = nw;
 }
 
-int lora_project16(const void* act, const void* w, int64_t w_stride_r, int64_t w_stride_k,
-                   void* out, int64_t n, int64_t kdim, cudaStream_t s);  // lora.cu
+int lora_project16_multi(const void* const* act, const void* const* w, int64_t w_stride_r,
+                         int64_t w_stride_k, void* const* out, const int64_t* kdim, int n_jobs,
+                         int64_t n, cudaStream_t s);  // lora.cu
 
 }  // namespace nf4b
 
@@ -1216,6 +1217,12 @@ extern "C" int nf4b_linear_fwd_group(const void* x, int64_t n, int64_t in_featur
   if (st != NF4B_OK) return st;
   ta[1] = ta[2] = ta[0];
   GemmArgs g{};
+  // the adapters' rank-16 projections, batched into one launch
+  const void* pj_act[G_MAX_W];
+  const void* pj_w[G_MAX_W];
+  void* pj_out[G_MAX_W];
+  int64_t pj_k[G_MAX_W];
+  int npj = 0;
   for (int i = 0; i < n_items; ++i) {
     const nf4b_linear_item& it = items[i];
     st = make_tmap_2d(&tw[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, it.packed, uint64_t(in_features / 2),
@@ -1228,13 +1235,21 @@ extern "C" int nf4b_linear_fwd_group(const void* x, int64_t n, int64_t in_featur
     w.out = static_cast<__half*>(it.y);
     w.out_f = it.out_features;
     if (it.lora) {
-      st = lora_project16(x, it.lora->a, in_features, 1, it.lora->xa, n, in_features, s);
-      if (st != NF4B_OK) return st;
+      // X A^T of every adapter of the group: one launch below
+      pj_act[npj] = x;
+      pj_w[npj] = it.lora->a;
+      pj_out[npj] = it.lora->xa;
+      pj_k[npj] = in_features;
+      ++npj;
       w.has_lora = 1;
       w.lora_w = static_cast<const __half*>(it.lora->b);
       w.lora_t = static_cast<const __half*>(it.lora->xa);
       w.lora_scale = it.lora->scale;
     }
+  }
+  if (npj > 0) {
+    st = lora_project16_multi(pj_act, pj_w, in_features, 1, pj_out, pj_k, npj, n, s);
+    if (st != NF4B_OK) return st;
   }
   for (int i = n_items; i < G_MAX_W; ++i) tw[i] = tw[0];  // unused kernel parameters
   set_m_end(&g, rows, n_items, plan.pair);
@@ -1295,6 +1310,12 @@ extern "C" int nf4b_linear_bwd_dx_group(const nf4b_linear_bwd_item* items, int32
   const GemmPlan plan = plan_gemm(n, &in_features, 1, kdim);
   CUtensorMap ta[G_MAX_W], tw[G_MAX_W];
   GemmArgs g{};
+  // the adapters' rank-16 projections, batched into one launch
+  const void* pj_act[G_MAX_W];
+  const void* pj_w[G_MAX_W];
+  void* pj_out[G_MAX_W];
+  int64_t pj_k[G_MAX_W];
+  int npj = 0;
   int64_t kacc = 0;
   for (int i = 0; i < n_items; ++i) {
     const nf4b_linear_bwd_item& it = items[i];
@@ -1311,9 +1332,13 @@ extern "C" int nf4b_linear_bwd_dx_group(const nf4b_linear_bwd_item* items, int32
     w.out = static_cast<__half*>(dx);
     w.out_f = it.out_features;
     if (it.lora) {
-      // dY B: B is [out, 16] row-major -> element (r, k=o) at o*16 + r
-      st = lora_project16(it.dy, it.lora->b, 1, 16, it.dyb, n, it.out_features, s);
-      if (st != NF4B_OK) return st;
+      // dY B: B is [out, 16] row-major -> element (r, k=o) at o*16 + r; every adapter of the
+      // group in one launch below
+      pj_act[npj] = it.dy;
+      pj_w[npj] = it.lora->b;
+      pj_out[npj] = it.dyb;
+      pj_k[npj] = it.out_features;
+      ++npj;
       w.has_lora = 1;
       w.lora_w = static_cast<const __half*>(it.lora->a);
       w.lora_t = static_cast<const __half*>(it.dyb);
@@ -1321,6 +1346,10 @@ extern "C" int nf4b_linear_bwd_dx_group(const nf4b_linear_bwd_item* items, int32
     }
     kacc += it.out_features / G_K;
     g.k_end[i] = int32_t(kacc);
+  }
+  if (npj > 0) {
+    st = lora_project16_multi(pj_act, pj_w, 1, 16, pj_out, pj_k, npj, n, s);
+    if (st != NF4B_OK) return st;
   }
   for (int i = n_items; i < G_MAX_W; ++i) {
     ta[i] = ta[0];  // unused kernel parameters

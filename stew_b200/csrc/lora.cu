@@ -11,6 +11,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "stew_nf4.h"
 
 namespace nf4b {
 
@@ -48,10 +49,27 @@ __device__ __forceinline__ uint4 ld_w8(const __half* w, int64_t sr, int64_t sk, 
 // 2c+8(+9) values 2-3 / 6-7.  The adapter weight is read with the same assignment, so both
 // operands see one permutation of K and the dot products are those of the natural order.
 // WK: the weight is K-contiguous (sk == 1).
+// One projection of a launch (blockIdx.y picks it; all of a launch's share n and WK).
+struct ProjJob {
+  const __half* act;
+  const __half* w;
+  int64_t sr, sk;
+  __half* out;
+  int64_t kdim;
+};
+constexpr int LP_MAX_JOBS = 3;
+struct ProjJobs {
+  ProjJob j[LP_MAX_JOBS];
+};
+
 template <bool WK>
 __global__ void __launch_bounds__(LP_THREADS)
-    lora_project16_kernel(const __half* __restrict__ act, const __half* __restrict__ w, int64_t sr,
-                          int64_t sk, __half* __restrict__ out, int64_t n, int64_t kdim) {
+    lora_project16_kernel(const __grid_constant__ ProjJobs jobs, int64_t n) {
+  const ProjJob& job = jobs.j[blockIdx.y];
+  const __half* __restrict__ act = job.act;
+  const __half* __restrict__ w = job.w;
+  const int64_t sr = job.sr, sk = job.sk, kdim = job.kdim;
+  __half* __restrict__ out = job.out;
   __shared__ float red[LP_WARPS][LP_TOK][17];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;  // mma fragment coordinates
@@ -94,22 +112,34 @@ __global__ void __launch_bounds__(LP_THREADS)
   if (t0 + t < n) out[(t0 + t) * 16 + r] = __float2half_rn(sum);
 }
 
-int lora_project16(const void* act, const void* w, int64_t w_stride_r, int64_t w_stride_k,
-                   void* out, int64_t n, int64_t kdim, cudaStream_t s) {
-  NF4B_RETURN_IF(kdim % 32 != 0, NF4B_ERR_UNSUPPORTED);
-  NF4B_RETURN_IF(!aligned(act, 16) || !aligned(w, w_stride_k == 1 ? 16 : 2), NF4B_ERR_ALIGNMENT);
+// Several rank-16 projections over the same n tokens in one launch (the adapters of a grouped
+// forward, X A_i^T, or of a grouped backward, dY_i B_i); every job's weight has the same
+// layout (K-contiguous or not).
+int lora_project16_multi(const void* const* act, const void* const* w, int64_t w_stride_r,
+                         int64_t w_stride_k, void* const* out, const int64_t* kdim, int n_jobs,
+                         int64_t n, cudaStream_t s) {
+  NF4B_RETURN_IF(n_jobs < 1 || n_jobs > LP_MAX_JOBS, NF4B_ERR_UNSUPPORTED);
+  ProjJobs js{};
+  for (int i = 0; i < n_jobs; ++i) {
+    NF4B_RETURN_IF(kdim[i] % 32 != 0, NF4B_ERR_UNSUPPORTED);
+    NF4B_RETURN_IF(!aligned(act[i], 16) || !aligned(w[i], w_stride_k == 1 ? 16 : 2), NF4B_ERR_ALIGNMENT);
+    js.j[i] = ProjJob{static_cast<const __half*>(act[i]), static_cast<const __half*>(w[i]), w_stride_r,
+                      w_stride_k, static_cast<__half*>(out[i]), kdim[i]};
+  }
   if (n == 0) return NF4B_OK;
   const int64_t ctas = (n + LP_TOK - 1) / LP_TOK;
   NF4B_RETURN_IF(ctas > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
+  const dim3 grid{unsigned(ctas), unsigned(n_jobs), 1u};
   if (w_stride_k == 1)
-    lora_project16_kernel<true><<<unsigned(ctas), LP_THREADS, 0, s>>>(
-        static_cast<const __half*>(act), static_cast<const __half*>(w), w_stride_r, w_stride_k,
-        static_cast<__half*>(out), n, kdim);
+    lora_project16_kernel<true><<<grid, LP_THREADS, 0, s>>>(js, n);
   else
-    lora_project16_kernel<false><<<unsigned(ctas), LP_THREADS, 0, s>>>(
-        static_cast<const __half*>(act), static_cast<const __half*>(w), w_stride_r, w_stride_k,
-        static_cast<__half*>(out), n, kdim);
+    lora_project16_kernel<false><<<grid, LP_THREADS, 0, s>>>(js, n);
   return launch_status("lora_project16_kernel launch");
+}
+
+int lora_project16(const void* act, const void* w, int64_t w_stride_r, int64_t w_stride_k,
+                   void* out, int64_t n, int64_t kdim, cudaStream_t s) {
+  return lora_project16_multi(&act, &w, w_stride_r, w_stride_k, &out, &kdim, 1, n, s);
 }
 
 // ---------------------------------------------------------------- weight grads
@@ -151,15 +181,50 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
                : "r"(addr));
 }
 
+// One outer product of a launch: its CTAs are [cta0, cta0 + col tiles * splits); its reduce
+// blocks (32 outputs each) are [red0, red0 + ceil(16 cols / 32)).
+struct OuterJob {
+  const __half* P;
+  const __half* Q;
+  float* partial;    // [splits][16][cols]
+  float* out;        // [16][cols], or [cols][16] when transpose
+  int64_t cols;
+  int64_t splits;
+  int64_t tps;       // tokens per split
+  float scale;
+  int32_t transpose;
+  int32_t cta0;
+  int32_t red0;
+};
+constexpr int LO_MAX_JOBS = 6;  // dA and dB of up to three adapters
+struct OuterJobs {
+  OuterJob j[LO_MAX_JOBS];
+  int32_t n;
+};
+
+__device__ __forceinline__ int find_job(const OuterJobs& js, int bid, bool reduce) {
+  int k = 0;
+  for (int i = 1; i < js.n; ++i)
+    if (bid >= (reduce ? js.j[i].red0 : js.j[i].cta0)) k = i;
+  return k;
+}
+
 __global__ void __launch_bounds__(LO_THREADS)
-    lora_outer16_kernel(const __half* __restrict__ P, const __half* __restrict__ Q, int64_t n,
-                        int64_t cols, int64_t tok_per_split, float* __restrict__ partial) {
+    lora_outer16_kernel(const __grid_constant__ OuterJobs jobs, int64_t n) {
   __shared__ __align__(128) uint8_t qbuf[2][LO_QBUF];
   __shared__ __align__(128) uint8_t pbuf[2][LO_PBUF];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t c0 = int64_t(blockIdx.x) * LO_COLS;
-  const int64_t tb = int64_t(blockIdx.y) * tok_per_split;
-  const int64_t te = min64(n, tb + tok_per_split);
+  const OuterJob& job = jobs.j[find_job(jobs, int(blockIdx.x), false)];
+  const __half* __restrict__ P = job.P;
+  const __half* __restrict__ Q = job.Q;
+  const int64_t cols = job.cols;
+  const int64_t col_tiles = (cols + LO_COLS - 1) / LO_COLS;
+  const int64_t local = int64_t(blockIdx.x) - job.cta0;
+  const int64_t split = local / col_tiles;
+  const int64_t c0 = (local - split * col_tiles) * LO_COLS;
+  const int64_t tb = split * job.tps;
+  const int64_t te = min64(n, tb + job.tps);
+  float* __restrict__ partial = job.partial;
 
   // stage tokens [ts, ts + 32) of P (32 B per token) and of Q's 256 columns; rows past te or
   // columns past `cols` are zero-filled
@@ -221,7 +286,7 @@ __global__ void __launch_bounds__(LO_THREADS)
   }
   // D fragment: d[0..1] = G[g][2c..2c+1], d[2..3] = G[g+8][2c..2c+1] of each 16 x 8 tile
   const int g = lane >> 2, cq = lane & 3;
-  float* dst = partial + int64_t(blockIdx.y) * 16 * cols;
+  float* dst = partial + split * 16 * cols;
 #pragma unroll
   for (int nt = 0; nt < 8; ++nt) {
     const int64_t c = c0 + 64 * warp + 8 * nt + 2 * cq;
@@ -237,11 +302,16 @@ __global__ void __launch_bounds__(LO_THREADS)
 // the 8 warp sums are added in warp order (a fixed order: the result is deterministic).
 constexpr int LR_THREADS = 256;
 __global__ void __launch_bounds__(LR_THREADS)
-    lora_reduce_kernel(const float* __restrict__ partial, int64_t splits, int64_t cols,
-                       float scale, int transpose_out, float* __restrict__ out) {
+    lora_reduce_kernel(const __grid_constant__ OuterJobs jobs) {
   __shared__ float ws[LR_THREADS / 32][33];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t e = int64_t(blockIdx.x) * 32 + lane;  // index into [16][cols]
+  const OuterJob& job = jobs.j[find_job(jobs, int(blockIdx.x), true)];
+  const float* __restrict__ partial = job.partial;
+  const int64_t splits = job.splits, cols = job.cols;
+  const float scale = job.scale;
+  const int transpose_out = job.transpose;
+  float* __restrict__ out = job.out;
+  const int64_t e = int64_t(blockIdx.x - job.red0) * 32 + lane;  // index into [16][cols]
   const bool ok = e < 16 * cols;
   float sum = 0.f;
   if (ok)
@@ -260,18 +330,46 @@ __global__ void __launch_bounds__(LR_THREADS)
   }
 }
 
-static int outer_and_reduce(const __half* P, const __half* Q, int64_t n, int64_t cols, float scale,
-                            int transpose_out, float* out, float* work, cudaStream_t s) {
-  const int64_t splits = outer_splits(n, cols);
-  const int64_t tps = (n + splits - 1) / splits;
-  dim3 grid(unsigned((cols + LO_COLS - 1) / LO_COLS), unsigned(splits));
-  lora_outer16_kernel<<<grid, LO_THREADS, 0, s>>>(P, Q, n, cols, tps, work);
+// Partial-sum floats of one job.
+static int64_t outer_floats(int64_t n, int64_t cols) { return outer_splits(n, cols) * 16 * cols; }
+
+// Appends one outer product (G = P^T Q over n tokens, scaled, optionally transposed) to a launch
+// table; its partial sums start at `partial`.
+static void add_job(OuterJobs* js, const __half* P, const __half* Q, int64_t n, int64_t cols,
+                    float scale, int transpose, float* out, float* partial, int64_t* ctas,
+                    int64_t* reds) {
+  OuterJob& j = js->j[js->n++];
+  j.P = P;
+  j.Q = Q;
+  j.partial = partial;
+  j.out = out;
+  j.cols = cols;
+  j.splits = outer_splits(n, cols);
+  j.tps = (n + j.splits - 1) / j.splits;
+  j.scale = scale;
+  j.transpose = transpose;
+  j.cta0 = int32_t(*ctas);
+  j.red0 = int32_t(*reds);
+  *ctas += j.splits * ((cols + LO_COLS - 1) / LO_COLS);
+  *reds += (16 * cols + 31) / 32;
+}
+
+// One launch of the outer products of a table, then one launch of their reductions.
+static int run_jobs(const OuterJobs& js, int64_t n, int64_t ctas, int64_t reds, cudaStream_t s) {
+  NF4B_RETURN_IF(ctas > 0x7FFFFFFFll || reds > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
+  lora_outer16_kernel<<<unsigned(ctas), LO_THREADS, 0, s>>>(js, n);
   int st = launch_status();
   if (st != NF4B_OK) return st;
-  const int64_t total = 16 * cols;
-  lora_reduce_kernel<<<unsigned((total + 31) / 32), LR_THREADS, 0, s>>>(work, splits, cols, scale,
-                                                                       transpose_out, out);
+  lora_reduce_kernel<<<unsigned(reds), LR_THREADS, 0, s>>>(js);
   return launch_status();
+}
+
+static int outer_and_reduce(const __half* P, const __half* Q, int64_t n, int64_t cols, float scale,
+                            int transpose_out, float* out, float* work, cudaStream_t s) {
+  OuterJobs js{};
+  int64_t ctas = 0, reds = 0;
+  add_job(&js, P, Q, n, cols, scale, transpose_out, out, work, &ctas, &reds);
+  return run_jobs(js, n, ctas, reds, s);
 }
 
 }  // namespace nf4b
@@ -312,6 +410,61 @@ extern "C" int nf4b_lora_grads(const void* x, const void* dy, const void* xa, co
   // dB[o, r] = s * sum_t dy[t, o] xa[t, r]  (computed as G[r, o], written transposed)
   return outer_and_reduce(static_cast<const __half*>(xa), static_cast<const __half*>(dy), n,
                           out_features, scale, 1, db, static_cast<float*>(work), s);
+}
+
+// ------------------------------------------------- several adapters in two launches
+extern "C" int64_t nf4b_lora_grads_group_work_bytes(const nf4b_lora_grads_item* items, int32_t n_items,
+                                                    int64_t n) {
+  if (!items || n_items < 1 || n_items > LO_MAX_JOBS / 2 || n < 0) return -1;
+  int64_t floats = 0;
+  for (int i = 0; i < n_items; ++i) {
+    if (items[i].in_features <= 0 || items[i].out_features <= 0) return -1;
+    floats += outer_floats(n, items[i].in_features) + outer_floats(n, items[i].out_features);
+  }
+  return floats * int64_t(sizeof(float));
+}
+
+extern "C" int nf4b_lora_grads_group(const nf4b_lora_grads_item* items, int32_t n_items, void* work,
+                                     int64_t work_bytes, int64_t n, void* stream) {
+  NF4B_RETURN_IF(!items || n_items < 1 || n < 0, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(n_items > LO_MAX_JOBS / 2, NF4B_ERR_UNSUPPORTED);
+  for (int i = 0; i < n_items; ++i) {
+    const nf4b_lora_grads_item& it = items[i];
+    NF4B_RETURN_IF(!it.x || !it.dy || !it.xa || !it.dyb || !it.da || !it.db, NF4B_ERR_INVALID_ARG);
+    NF4B_RETURN_IF(it.in_features <= 0 || it.out_features <= 0, NF4B_ERR_INVALID_ARG);
+    NF4B_RETURN_IF(it.in_features % 8 != 0 || it.out_features % 8 != 0, NF4B_ERR_UNSUPPORTED);
+    NF4B_RETURN_IF(!aligned(it.x, 16) || !aligned(it.dy, 16) || !aligned(it.xa, 16) || !aligned(it.dyb, 16),
+                   NF4B_ERR_ALIGNMENT);
+  }
+  const int64_t need = nf4b_lora_grads_group_work_bytes(items, n_items, n);
+  NF4B_RETURN_IF(need < 0, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(need > 0 && (!work || work_bytes < need), NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(need > 0 && !aligned(work, 8), NF4B_ERR_ALIGNMENT);
+  int st = check_device();
+  if (st != NF4B_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n == 0) {
+    for (int i = 0; i < n_items; ++i) {
+      NF4B_CUDA_TRY(cudaMemsetAsync(items[i].da, 0, size_t(16 * items[i].in_features) * sizeof(float), s));
+      NF4B_CUDA_TRY(cudaMemsetAsync(items[i].db, 0, size_t(16 * items[i].out_features) * sizeof(float), s));
+    }
+    return NF4B_OK;
+  }
+  OuterJobs js{};
+  int64_t ctas = 0, reds = 0;
+  float* part = static_cast<float*>(work);
+  for (int i = 0; i < n_items; ++i) {
+    const nf4b_lora_grads_item& it = items[i];
+    // dA[r, i] = s * sum_t dyb[t, r] x[t, i]
+    add_job(&js, static_cast<const __half*>(it.dyb), static_cast<const __half*>(it.x), n, it.in_features,
+            it.scale, 0, it.da, part, &ctas, &reds);
+    part += outer_floats(n, it.in_features);
+    // dB[o, r] = s * sum_t dy[t, o] xa[t, r]  (computed as G[r, o], written transposed)
+    add_job(&js, static_cast<const __half*>(it.xa), static_cast<const __half*>(it.dy), n, it.out_features,
+            it.scale, 1, it.db, part, &ctas, &reds);
+    part += outer_floats(n, it.out_features);
+  }
+  return run_jobs(js, n, ctas, reds, s);
 }
 
 // ------------------------------------------------- entry point without allocation

@@ -238,6 +238,8 @@ class GroupedNF4Function(torch.autograd.Function):
                 _lib.check(L.nf4b_linear_bwd_dx_group(items, len(live), dx.data_ptr(), n, in_f, work,
                                                       wbytes, _stream(dev)), "nf4b_linear_bwd_dx_group")
                 kj = 0
+            # every adapter's dA, dB in one outer-product launch and one reduction launch
+            gitems, slots = [], []
             for packed, st, lora, gy in sel:
                 if lora is None:
                     if gy is not None:
@@ -248,8 +250,21 @@ class GroupedNF4Function(torch.autograd.Function):
                     continue
                 dy, _, _, dyb = keep[kj]
                 kj += 1
-                da32, db32 = _lora_weight_grads(x2, dy, lora[2], dyb, lora[3], in_f, int(st.shape[0]))
+                out_f = int(st.shape[0])
+                da32 = torch.empty(LORA_RANK, in_f, dtype=torch.float32, device=dev)
+                db32 = torch.empty(out_f, LORA_RANK, dtype=torch.float32, device=dev)
+                it = _lib.LoraGradsItemC()
+                it.x, it.dy, it.xa, it.dyb = x2.data_ptr(), dy.data_ptr(), lora[2].data_ptr(), dyb.data_ptr()
+                it.scale, it.da, it.db = float(lora[3]), da32.data_ptr(), db32.data_ptr()
+                it.in_features, it.out_features = in_f, out_f
+                gitems.append(it)
                 pgrads += [da32, db32]
+            if gitems:
+                arr = (_lib.LoraGradsItemC * len(gitems))(*gitems)
+                wb = int(L.nf4b_lora_grads_group_work_bytes(arr, len(gitems), n))
+                work = torch.empty(max(wb, 16) // 4 + 4, dtype=torch.float32, device=dev)
+                _lib.check(L.nf4b_lora_grads_group(arr, len(gitems), work.data_ptr(), work.numel() * 4, n,
+                                                   _stream(dev)), "nf4b_lora_grads_group")
         pgrads = [None if gr is None else gr.to(dt) for gr, dt in zip(pgrads, ctx.param_dtypes)]
         return (None if dx is None else dx.reshape(ctx.x_shape), None, *pgrads)
 

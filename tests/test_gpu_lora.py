@@ -81,3 +81,46 @@ def test_lora_module_trains(cuda_lib):
         losses.append(loss.item())
     assert losses[-1] < losses[0]
     assert [p.shape for p in m.parameters()] == [torch.Size([16, 512]), torch.Size([256, 16])]
+
+
+@pytest.mark.parametrize("n", [1, 77, 1311])
+def test_grouped_lora_grads_match_per_adapter_calls(cuda_lib, n):
+    """nf4b_lora_grads_group (q and v adapters of one layer: dA, dB of both in one outer-product
+    launch and one reduction launch) gives the same dA / dB, bit for bit, as one
+    nf4b_lora_grads call per adapter (same token splits, same reduction order), and matches
+    the fp64 products."""
+    import ctypes
+    from stew_b200 import _lib
+    L = _lib.lib()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    g = torch.Generator(device="cuda").manual_seed(n)
+    x = torch.randn(n, 1536, generator=g, device="cuda").half()
+    shapes = [(1536, 2.0), (256, 2.0)]
+    items, refs, keep = [], [], []
+    for out_f, s in shapes:
+        dy = (torch.randn(n, out_f, generator=g, device="cuda") * 0.01).half()
+        xa = torch.randn(n, 16, generator=g, device="cuda").half()
+        dyb = (torch.randn(n, 16, generator=g, device="cuda") * 0.1).half()
+        da = torch.full((16, 1536), float("nan"), device="cuda")
+        db = torch.full((out_f, 16), float("nan"), device="cuda")
+        it = _lib.LoraGradsItemC()
+        it.x, it.dy, it.xa, it.dyb = x.data_ptr(), dy.data_ptr(), xa.data_ptr(), dyb.data_ptr()
+        it.scale, it.da, it.db, it.in_features, it.out_features = s, da.data_ptr(), db.data_ptr(), 1536, out_f
+        items.append(it)
+        keep.append((dy, xa, dyb, da, db, out_f, s))
+    arr = (_lib.LoraGradsItemC * 2)(*items)
+    wb = int(L.nf4b_lora_grads_group_work_bytes(arr, 2, n))
+    assert wb > 0
+    work = torch.empty(wb // 4 + 4, device="cuda")
+    assert L.nf4b_lora_grads_group(arr, 2, work.data_ptr(), wb, n, stream) == 0, L.nf4b_last_error()
+    assert L.nf4b_lora_grads_group(arr, 2, work.data_ptr(), wb - 4, n, stream) == _lib.NF4B_ERR_INVALID_ARG
+    for dy, xa, dyb, da, db, out_f, s in keep:
+        da1 = torch.empty(16, 1536, device="cuda")
+        db1 = torch.empty(out_f, 16, device="cuda")
+        w1 = torch.empty(int(L.nf4b_lora_grads_work_bytes(n, 1536, out_f, 16)) // 4 + 4, device="cuda")
+        assert L.nf4b_lora_grads(x.data_ptr(), dy.data_ptr(), xa.data_ptr(), dyb.data_ptr(), s, da1.data_ptr(),
+                                 db1.data_ptr(), w1.data_ptr(), n, 1536, out_f, 16, stream) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(da, da1) and torch.equal(db, db1)
+        assert max_rel_err(da, s * dyb.double().T @ x.double()) <= 1e-3
+        assert max_rel_err(db, s * dy.double().T @ xa.double()) <= 1e-3
