@@ -114,6 +114,7 @@ struct GemmArgs {
   int32_t splits;         // K ranges per tile (split-K); 1 = none
   int32_t nk;             // K stages of the whole reduction
   uint32_t k16;           // 1 << 16 (a run-time multiplier for the decode's shifts)
+  int32_t tile_n;         // tokens per tile: 256, or 128 for launches with few tiles
   float* ws_part;         // split-K: fp32 partial tiles [tiles][splits][256][128]
   int32_t* ws_cnt;        // split-K: per-tile counters [2][G_SPLIT_MAX_TILES], zero between launches
 };
@@ -235,8 +236,8 @@ __device__ __forceinline__ TileCoord tile_coord(const GemmArgs& g, int tile, uin
   const int nt = tile - mt * g.n_tiles;
   c.seg = MULTI ? (mt >= g.m_end[0]) + (mt >= g.m_end[1]) : 0;
   c.m0 = int64_t(mt - (c.seg ? g.m_end[c.seg - 1] : 0)) * (PAIR ? 2 * G_M : G_M) + int64_t(rank) * G_M;
-  c.t0 = int64_t(nt) * G_NMAX;
-  c.tn_real = int(min64(G_NMAX, g.n - c.t0));
+  c.t0 = int64_t(nt) * g.tile_n;
+  c.tn_real = int(min64(g.tile_n, g.n - c.t0));
   c.tn = (c.tn_real + 15) & ~15;
   return c;
 }
@@ -434,7 +435,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], L::X_BYTES + L::P_BYTES);
+          // the token box is the tile width (a pair: half of 256)
+          mbar_arrive_expect_tx(&full[s], (PAIR ? L::X_BYTES : g.tile_n * 128) + L::P_BYTES);
           const int ws = KCAT ? kseg(g, k) : tc.seg;   // weight of this stage
           const int kl = KCAT ? k - kbeg(g, ws) : k;  // its local K stage
           const CUtensorMap* tm_a = ws == 0 ? &tm_act0 : (ws == 1 ? &tm_act1 : &tm_act2);
@@ -982,33 +984,49 @@ struct GemmPlan {
   int64_t m_tiles, n_tiles, tiles;
   int32_t nk;
   int32_t splits;
+  int32_t tile_n;  // tokens per tile
   bool pair;
   int64_t slots;  // CTAs (single) or clusters (pair) resident at once
 };
 
 constexpr int G_MAX_SPLITS = 8;
 
-// Split-K choice from a cost model in stage-times (~0.7 us) of the busiest slot: a unit costs
-// its stages plus ~3 stages of pipeline fill and drain; a split tile adds the round trip
-// of its fp32 partials through L2, measured at ~3 us to write one 128 x 256 partial and
-// ~3 us per partial for the last CTA to read back (4 + 4 per partial, in stage-times).  A
-// split must beat the unsplit launch by 5 % and leave every range at least 2 stages.
-static void plan_splits(GemmPlan* p, int64_t max_tiles) {
+// Cost model in stage-times of a 256-token tile (~0.7 us) of the busiest slot: a unit costs its
+// stages plus ~3 of pipeline fill and drain; a split tile adds the round trip of its fp32
+// partials through L2, measured at ~3 us to write one 128 x 256 partial and ~3 us per partial
+// for the last CTA to read back (4 + 4 per partial).  A 128-token tile's stage costs ~0.55 of
+// a 256-token one (the decode of the weight stage is the same, the MMA half) and its partials
+// half as much.
+static double plan_cost(int64_t tiles, int64_t slots, int32_t nk, int64_t sp, int32_t tile_n) {
+  const double stage = tile_n == 256 ? 1.0 : 0.55;
+  const double red = tile_n == 256 ? 4.0 : 2.0;
+  const int64_t waves = (tiles * sp + slots - 1) / slots;
+  const double reduce = sp > 1 ? red * double(sp) : 0.0;
+  return double(waves) * (stage * double((nk + sp - 1) / sp) + 3.0) + reduce;
+}
+
+// Split-K choice: a split must beat the unsplit launch by 5 % and leave every range at least 2
+// stages.  Returns the plan's cost.
+static double plan_splits(GemmPlan* p, int64_t max_tiles) {
   p->splits = 1;
-  if (p->tiles <= 0 || p->tiles >= p->slots || p->tiles > max_tiles) return;
-  auto cost = [&](int64_t sp) {
-    const int64_t waves = (p->tiles * sp + p->slots - 1) / p->slots;
-    const double reduce = sp > 1 ? 4.0 + 4.0 * double(sp - 1) : 0.0;
-    return double(waves) * double((p->nk + sp - 1) / sp + 3) + reduce;
-  };
-  double best = cost(1);
+  double best = plan_cost(p->tiles, p->slots, p->nk, 1, p->tile_n);
+  if (p->tiles <= 0 || p->tiles >= p->slots || p->tiles > max_tiles) return best;
   for (int sp = 2; sp <= G_MAX_SPLITS && p->nk / sp >= 2; ++sp) {
-    const double c = cost(sp);
+    const double c = plan_cost(p->tiles, p->slots, p->nk, sp, p->tile_n);
     if (c < 0.95 * best) {
       best = c;
       p->splits = sp;
     }
   }
+  return best;
+}
+
+// Token tile width from STEW_NF4_TILE_N: "128" or "256" forces it (single CTAs), otherwise the
+// cost model chooses.
+static int tile_n_env() {
+  const char* v = std::getenv("STEW_NF4_TILE_N");
+  if (v == nullptr || v[0] == '\0') return 0;
+  return std::atoi(v) == 128 ? 128 : 256;
 }
 
 // Pair mode from STEW_NF4_PAIR: "0" never, "1" whenever the device runs pairs, otherwise
@@ -1023,6 +1041,7 @@ static int pair_mode_env() {
 // weight; backward: the in features, once).  kdim: the reduction length.
 static GemmPlan plan_gemm(int64_t n, const int64_t* rows, int nrows, int64_t kdim) {
   GemmPlan single{};
+  single.tile_n = G_NMAX;
   single.n_tiles = (n + G_NMAX - 1) / G_NMAX;
   single.nk = int32_t(kdim / G_K);
   single.pair = false;
@@ -1030,11 +1049,22 @@ static GemmPlan plan_gemm(int64_t n, const int64_t* rows, int nrows, int64_t kdi
   single.m_tiles = 0;
   for (int i = 0; i < nrows; ++i) single.m_tiles += (rows[i] + G_M - 1) / G_M;
   single.tiles = single.m_tiles * single.n_tiles;
-  plan_splits(&single, G_SPLIT_MAX_TILES);
+  const double c256 = plan_splits(&single, G_SPLIT_MAX_TILES);
+  // 128-token tiles: twice the tiles (the weight decoded twice as often per token), for
+  // launches that would otherwise leave SMs idle or split K
+  GemmPlan narrow = single;
+  narrow.tile_n = G_NMAX / 2;
+  narrow.n_tiles = (n + narrow.tile_n - 1) / narrow.tile_n;
+  narrow.tiles = narrow.m_tiles * narrow.n_tiles;
+  const double c128 = plan_splits(&narrow, G_SPLIT_MAX_TILES);
+  const int tn_env = tile_n_env();
+  if (tn_env == 128 || (tn_env == 0 && c128 < 0.95 * c256)) single = narrow;
   const int mode = pair_mode_env();
   const int64_t pslots = mode == 0 ? 0 : pair_slots_cached();
   if (pslots <= 0) return single;
   GemmPlan pair = single;
+  pair.tile_n = G_NMAX;
+  pair.n_tiles = (n + G_NMAX - 1) / G_NMAX;
   pair.pair = true;
   pair.slots = pslots;
   pair.m_tiles = 0;
@@ -1057,7 +1087,7 @@ static int64_t plan_work_bytes(const GemmPlan& p) {
 }
 
 // Token rows of the activation tile one CTA loads per stage.
-static uint32_t act_box_rows(const GemmPlan& p) { return p.pair ? G_NMAX / 2 : G_NMAX; }
+static uint32_t act_box_rows(const GemmPlan& p) { return p.pair ? G_NMAX / 2 : uint32_t(p.tile_n); }
 
 template <bool BWD, bool SPLIT, bool MULTI, bool PAIR>
 static int launch_variant(unsigned grid, const CUtensorMap (&ta)[G_MAX_W], const CUtensorMap (&tw)[G_MAX_W],
@@ -1093,6 +1123,7 @@ static int launch_gemm(const GemmPlan& p, const CUtensorMap (&ta)[G_MAX_W], cons
   g.splits = q.splits;
   g.nk = q.nk;
   g.k16 = 1u << 16;
+  g.tile_n = q.tile_n;
   const int64_t units = q.tiles * q.splits;
   const int64_t slots = units < q.slots ? units : q.slots;
   const unsigned grid = unsigned(q.pair ? 2 * slots : slots);

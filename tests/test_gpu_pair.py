@@ -188,3 +188,29 @@ def test_pair_grouped_forward_and_backward(pair_available, monkeypatch):
         _same(a, b, split)
     _same(res["1dx"], res["0dx"], res["1split"] or res["0split"])
     _check_flag()
+
+
+@pytest.mark.parametrize("shape", [(1536, 1536), (256, 1536), (8960, 1536), (1536, 8960), (384, 512)],
+                         ids=lambda s: f"{s[0]}x{s[1]}")
+@pytest.mark.parametrize("n", [1, 77, 300, 1311])
+def test_narrow_token_tiles_match_wide(cuda_lib, monkeypatch, shape, n):
+    """128-token tiles (STEW_NF4_TILE_N=128, what the planner picks for launches with few
+    tiles) against 256-token tiles: the same K order per output, so bit-equal unless either
+    plan splits K; both within the GEMM tolerance of the reference."""
+    out_f, in_f = shape
+    q, st = _weight(shape, 700 + out_f % 89 + n)
+    w = _ref_weight(q, st)
+    x = _x(n, in_f, 15 + n)
+    dy = _x(n, out_f, 19 + n, std=0.01)
+    monkeypatch.setenv("STEW_NF4_TILE_N", "128")
+    y1, s1 = _run_fwd(monkeypatch, "0", x, q, st, out_f)
+    d1, t1 = _run_bwd(monkeypatch, "0", dy, q, st, in_f)
+    monkeypatch.setenv("STEW_NF4_TILE_N", "256")
+    y0, s0 = _run_fwd(monkeypatch, "0", x, q, st, out_f)
+    d0, t0 = _run_bwd(monkeypatch, "0", dy, q, st, in_f)
+    assert not torch.isnan(y1).any() and not torch.isnan(d1).any()
+    _same(y1, y0, s1 or s0)
+    _same(d1, d0, t1 or t0)
+    assert max_rel_err(y1, x.double() @ w.T) <= GEMM_MAX_REL_ERR
+    assert max_rel_err(d1, dy.double() @ w) <= GEMM_MAX_REL_ERR
+    _check_flag()

@@ -18,6 +18,13 @@ from tests.helpers import GEMM_MAX_REL_ERR, max_rel_err, to_oracle_state
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(autouse=True)
+def _wide_tiles(monkeypatch):
+    """The split-K plans under test are those of 256-token tiles (the planner would give these
+    shapes 128-token tiles without a split; that tiling is covered in test_gpu_pair.py)."""
+    monkeypatch.setenv("STEW_NF4_TILE_N", "256")
+
 SPLIT_VS_UNSPLIT = 1e-3
 
 
