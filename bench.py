@@ -556,7 +556,14 @@ def main():
         from stew_b200.qlora_step import QLoRATrainer, QwenConfig, QwenQLoRA, step_flops, synthetic_batch
         model = QwenQLoRA(QwenConfig(), device="cuda", seed=0, weights=weights)
         trainer = QLoRATrainer(model, cuda_graph=True)
-        tokens, lengths = synthetic_batch(seed=1000 + rank)
+        # the global batch: 4 rows per rank (seeds 1000 + r), dealt to the ranks by length so
+        # the step, which ends with the slowest rank, is not set by one long shard
+        from stew_b200.dp import balanced_shards
+        rows = [synthetic_batch(seed=1000 + r) for r in range(world)]
+        all_tok = torch.cat([t for t, _ in rows])
+        all_len = torch.cat([l for _, l in rows])
+        mine = balanced_shards(all_len.tolist(), world, 4)[rank]
+        tokens, lengths = all_tok[mine].contiguous(), all_len[mine].contiguous()
         real = torch.tensor([float(lengths.sum())], device="cuda")
         if world > 1:
             import torch.distributed as dist
@@ -564,7 +571,8 @@ def main():
         t = _timed(world, lambda: trainer.step(tokens, lengths), args.step_steps, 2) / args.step_steps
         fl = step_flops(model.cfg, int(lengths.sum()))
         step = {"workload": "Qwen2.5-1.5B QLoRA step: 28 layers, NF4 projections, LoRA r=16 on q/v, "
-                            "4 right-padded rows x 512 per rank (~57% real tokens, packed), fwd+bwd, "
+                            "4 right-padded rows x 512 per rank (~57% real tokens, packed; the "
+                            "global batch's rows dealt to the ranks by length), fwd+bwd, "
                             "LoRA-grad all-reduce, AdamW; the step replayed from one CUDA graph",
                 "ms_per_step": round(t, 3), "tokens_per_s": round(real.item() / (t * 1e-3), 1),
                 "real_tokens_per_step_all_ranks": int(real.item()),

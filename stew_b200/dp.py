@@ -88,5 +88,25 @@ def allreduce_lora_grads_device(params, local_labels: torch.Tensor, group=None) 
     return total
 
 
+def balanced_shards(lengths, world: int, rows_per_rank: int):
+    """Length-balanced assignment of a global batch of `world * rows_per_rank` rows to the
+    ranks, `rows_per_rank` rows each: rows are dealt longest first to the rank with the fewest
+    tokens that still has room (greedy longest-processing-time).  A data-parallel step ends
+    with the slowest rank, so dealing rows by length instead of in order keeps the ranks'
+    token counts close (the per-rank spread is at most one row's length).  The gradients do
+    not depend on the assignment: they are summed over all rows and divided by the global
+    labelled-token count.  Returns the row indices of each rank, in ascending order."""
+    lengths = [int(v) for v in lengths]
+    assert len(lengths) == world * rows_per_rank, "global batch must have world * rows_per_rank rows"
+    order = sorted(range(len(lengths)), key=lambda i: (-lengths[i], i))
+    load = [0] * world
+    shards = [[] for _ in range(world)]
+    for i in order:
+        r = min((k for k in range(world) if len(shards[k]) < rows_per_rank), key=lambda k: (load[k], k))
+        shards[r].append(i)
+        load[r] += lengths[i]
+    return [sorted(s) for s in shards]
+
+
 def lora_grad_bytes(params) -> int:
     return 4 * (sum(p.numel() for p in params) + 1)

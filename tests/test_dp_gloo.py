@@ -125,3 +125,21 @@ def test_failed_rank_ends_peer_collective_with_error():
     out = _run(2, fail_rank=1)
     assert out[1][0] == "error" and "injected failure" in out[1][1]
     assert out[0][0] == "error", "the surviving rank must not hang or succeed"
+
+
+def test_balanced_shards_partition_and_spread():
+    """Every row goes to exactly one rank, each rank gets its rows_per_rank rows, and the
+    ranks' token counts differ by at most the longest row (greedy longest-first bound)."""
+    import random
+    rng = random.Random(0)
+    for world in (1, 2, 4, 8):
+        lengths = [rng.randint(58, 512) for _ in range(4 * world)]
+        shards = dp.balanced_shards(lengths, world, 4)
+        assert sorted(i for s in shards for i in s) == list(range(4 * world))
+        assert all(len(s) == 4 for s in shards)
+        loads = [sum(lengths[i] for i in s) for s in shards]
+        assert max(loads) - min(loads) <= max(lengths)
+    # the bench's 4-rank global batch: in-order shards spread 787..1585 tokens
+    lengths = [442, 232, 206, 431, 78, 276, 360, 425, 410, 508, 198, 469, 110, 400, 138, 139]
+    loads = [sum(lengths[i] for i in s) for s in dp.balanced_shards(lengths, 4, 4)]
+    assert max(loads) - min(loads) <= 60
