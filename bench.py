@@ -563,7 +563,8 @@ def main():
         all_tok = torch.cat([t for t, _ in rows])
         all_len = torch.cat([l for _, l in rows])
         mine = balanced_shards(all_len.tolist(), world, 4)[rank]
-        tokens, lengths = all_tok[mine].contiguous(), all_len[mine].contiguous()
+        # the row lengths travel with the batch on the host, as a data loader has them
+        tokens, lengths = all_tok[mine].contiguous(), all_len[mine].cpu()
         real = torch.tensor([float(lengths.sum())], device="cuda")
         if world > 1:
             import torch.distributed as dist

@@ -149,24 +149,34 @@ class QwenQLoRA(torch.nn.Module):
 
     @staticmethod
     def pack(tokens: torch.Tensor, lengths: torch.Tensor) -> "PackedBatch":
-        """Right-padded rows -> the packed real tokens and their metadata (one host read of
-        the row lengths, as the reference's unpad path does)."""
+        """Right-padded rows -> the packed real tokens and their metadata.  The row lengths are
+        read on the host (a host tensor is used as is; a device one costs one read, as the
+        reference's unpad path does), the index arrays are built there and sent in one copy,
+        and the tokens are gathered with one index_select: no data-dependent device
+        synchronisation, so the host can queue the next step while the GPU runs this one."""
         B, T = tokens.shape
         dev = tokens.device
-        lens = [int(v) for v in lengths.tolist()]
-        keep = torch.arange(T, device=dev)[None, :] < lengths[:, None]
-        ids = tokens[keep]                                    # packed real tokens [N]
-        positions = torch.cat([torch.arange(L, device=dev) for L in lens])
-        cu = torch.zeros(B + 1, dtype=torch.int32, device=dev)
-        cu[1:] = torch.cumsum(lengths.to(torch.int32), 0)
-        # next-token labels inside each row; a row's last token has none
+        lens_t = lengths.detach().to("cpu", torch.int64) if lengths.is_cuda else lengths.to(torch.int64)
+        lens = [int(v) for v in lens_t.tolist()]
         starts = [0]
         for L in lens:
             starts.append(starts[-1] + L)
-        lab_idx = torch.cat([torch.arange(a, b - 1, device=dev) for a, b in zip(starts[:-1], starts[1:])
-                             if b - a > 1] or [torch.zeros(0, dtype=torch.long, device=dev)])
-        labels = ids[lab_idx + 1]
-        return PackedBatch(ids, positions, cu, max(lens) if lens else 0, lab_idx, labels)
+        n = starts[-1]
+        gather = torch.cat([torch.arange(L, dtype=torch.int64) + b * T for b, L in enumerate(lens)]
+                           or [torch.zeros(0, dtype=torch.int64)])
+        positions = torch.cat([torch.arange(L, dtype=torch.int64) for L in lens]
+                              or [torch.zeros(0, dtype=torch.int64)])
+        # next-token labels inside each row; a row's last token has none
+        lab_idx = torch.cat([torch.arange(a, b - 1, dtype=torch.int64) for a, b in zip(starts[:-1], starts[1:])
+                             if b - a > 1] or [torch.zeros(0, dtype=torch.int64)])
+        m = int(lab_idx.numel())
+        host = torch.cat([gather, positions, lab_idx, torch.tensor(starts, dtype=torch.int64)])
+        dv = host.to(dev, non_blocking=True)
+        gather_d, positions_d, lab_d = dv[:n], dv[n:2 * n], dv[2 * n:2 * n + m]
+        cu = dv[2 * n + m:].to(torch.int32)
+        ids = tokens.reshape(-1).index_select(0, gather_d)
+        labels = ids.index_select(0, lab_d + 1)
+        return PackedBatch(ids, positions_d, cu, max(lens) if lens else 0, lab_d, labels)
 
     def forward(self, tokens: torch.Tensor, lengths: torch.Tensor):
         """tokens [B, T] right-padded, lengths [B].  Returns (sum of next-token CE over the
