@@ -41,6 +41,22 @@ class QwenConfig:
     rope_theta: float = 1e6
     rms_eps: float = 1e-6
     lora_alpha: float = 32.0
+    # MLP memory cap (the reference's unpad path, solution/unpad.py:48-57): with more than this
+    # many real tokens, the first layers recompute gate/up + SwiGLU in the backward instead of
+    # keeping them.  None: never (a B200's 180 GB holds every layer's activations).
+    mlp_token_budget: int | None = None
+
+
+MLP_SAVED_SHARE = 0.63  # share of a layer's saved activations that recomputing gate/up removes
+
+
+def mlp_recompute_layers(n_tokens: int, layers: int, budget: int | None) -> int:
+    """How many of `layers` layers recompute their MLP's gate/up for a batch of n real tokens
+    so the activations kept stay within `budget` tokens' worth per layer at the peak (the
+    reference's rule, solution/unpad.py:52-57)."""
+    if budget is None or n_tokens <= budget:
+        return 0
+    return min(layers, math.ceil(layers * (n_tokens - budget) / (n_tokens * MLP_SAVED_SHARE)))
 
 
 def rope_tables(positions: torch.Tensor, head_dim: int, theta: float):
@@ -89,10 +105,22 @@ class Layer(torch.nn.Module):
         a = packed_causal_attention(q, k, v, rows)
         return p["o"](a.reshape(n, c.heads * c.head_dim))
 
-    def mlp(self, h):
+    def _gate_up(self, h):
         p = self.proj
         gate, up = grouped_projection(h, [p["gate"], p["up"]])  # one launch
-        return p["down"](swiglu(gate, up))
+        return swiglu(gate, up)
+
+    def mlp(self, h, recompute: bool = False):
+        """down(SwiGLU(gate(h), up(h))); recompute: keep only h and recompute gate/up and the
+        SwiGLU in the backward (activation checkpointing of the block)."""
+        if recompute and torch.is_grad_enabled():
+            from torch.utils.checkpoint import checkpoint
+            # no RNG in the block (dropout 0): skipping the RNG-state save/restore keeps the
+            # recompute capturable in the step's CUDA graph
+            m = checkpoint(self._gate_up, h, use_reentrant=False, preserve_rng_state=False)
+        else:
+            m = self._gate_up(h)
+        return self.proj["down"](m)
 
 
 @dataclass
@@ -193,11 +221,12 @@ class QwenQLoRA(torch.nn.Module):
         x = self.embed.index_select(0, pb.ids)
         eps = self.cfg.rms_eps
         h = rms_norm(x, self.layers[0].ln1, eps)
+        n_rec = mlp_recompute_layers(int(pb.ids.numel()), len(self.layers), self.cfg.mlp_token_budget)
         for i, layer in enumerate(self.layers):
             # residual adds fused into the following norm: x += attn; h = norm(x); x += mlp; h = ...
             x, h = add_rms_norm(x, layer.attention(h, cos, sin, rows), layer.ln2, eps)
             nxt = self.layers[i + 1].ln1 if i + 1 < len(self.layers) else self.ln_f
-            x, h = add_rms_norm(x, layer.mlp(h), nxt, eps)
+            x, h = add_rms_norm(x, layer.mlp(h, recompute=i < n_rec), nxt, eps)
         # LM head + summed next-token CE, fused (the reference's solution/head_loss.py)
         return head_cross_entropy(h.index_select(0, pb.lab_idx), self.embed, pb.labels)
 
@@ -289,10 +318,15 @@ class QLoRATrainer:
 
     def step(self, tokens, lengths):
         """Returns (mean loss of this rank's labelled tokens as a 0-d device tensor,
-        labelled tokens of this rank, labelled tokens over all ranks)."""
+        labelled tokens of this rank, labelled tokens over all ranks).  With cuda_graph=True,
+        a batch large enough for the MLP memory cap to recompute activations runs eagerly."""
         pb = self.model.pack(tokens, lengths)
         n_lab = pb.n_labels
-        if not self.cuda_graph:
+        # steps that recompute MLP activations (the memory cap) run eagerly: torch's checkpoint
+        # recomputation does not capture into a CUDA graph
+        recompute = mlp_recompute_layers(int(pb.ids.numel()), len(self.model.layers),
+                                         self.model.cfg.mlp_token_budget) > 0
+        if not self.cuda_graph or recompute:
             loss_sum, total = self._eager(pb)
             return loss_sum / max(n_lab, 1), n_lab, total
         if self._graph is None or self._key != pb.shape_key():

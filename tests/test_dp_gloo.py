@@ -143,3 +143,14 @@ def test_balanced_shards_partition_and_spread():
     lengths = [442, 232, 206, 431, 78, 276, 360, 425, 410, 508, 198, 469, 110, 400, 138, 139]
     loads = [sum(lengths[i] for i in s) for s in dp.balanced_shards(lengths, 4, 4)]
     assert max(loads) - min(loads) <= 60
+
+
+def test_mlp_recompute_layer_count_follows_the_reference_rule():
+    """min(layers, ceil(layers * (n - budget) / (n * 0.63))) above the budget, 0 at or below it
+    (solution/unpad.py:52-57); no budget never recomputes."""
+    from stew_b200.qlora_step import mlp_recompute_layers
+    assert mlp_recompute_layers(1000, 28, 1000) == 0
+    assert mlp_recompute_layers(1170, 28, 1000) == 7      # ceil(28 * 170 / 737.1) = ceil(6.46)
+    assert mlp_recompute_layers(2048, 28, 1000) == 23     # ceil(28 * 1048 / 1290.24) = ceil(22.7)
+    assert mlp_recompute_layers(100000, 28, 1000) == 28
+    assert mlp_recompute_layers(5000, 28, None) == 0
