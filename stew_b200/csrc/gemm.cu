@@ -47,13 +47,17 @@ constexpr int G_TMEM_COLS = 2 * G_ACC_COLS;            // double-buffered
 
 constexpr int G_MAX_W = 3;  // NF4 weights of one grouped forward launch
 
-// Shared-memory layout of one CTA.  PAIR: the CTA is half of a 2-CTA cluster whose MMA
-// (cta_group::2) covers 256 weight rows x up to 256 tokens; each CTA holds its own 128
-// decoded weight rows and half of the token tile, which frees room for a fifth stage.
+// Tokens of a pair tile: two cta_group::2 MMAs of up to 256 tokens each share one decoded
+// weight stage, so a pair decodes each weight stage once per 512 tokens.
+constexpr int G_PAIR_TILE_N = 2 * G_NMAX;
+
+// Shared-memory layout of one CTA.  PAIR: the CTA is half of a 2-CTA cluster whose two MMAs
+// (cta_group::2) cover 256 weight rows x up to 2 x 256 tokens; each CTA holds its own 128
+// decoded weight rows and, per MMA, half of its tokens (two 128-row halves per stage).
 template <bool PAIR>
 struct Smem {
-  static constexpr int STAGES = PAIR ? 5 : 4;
-  static constexpr int X_ROWS = PAIR ? G_NMAX / 2 : G_NMAX;  // token rows per CTA and stage
+  static constexpr int STAGES = 4;
+  static constexpr int X_ROWS = G_NMAX;                      // token rows per CTA and stage
   static constexpr int X_BYTES = X_ROWS * 128;               // activation stage
   static constexpr int A_BYTES = G_M * 128;                  // decoded weight stage
   static constexpr int P_BYTES = 4096;                       // packed stage (128 x 32 B or 64 x 64 B)
@@ -80,6 +84,9 @@ static_assert(Smem<false>::ALLOC <= 232448 && Smem<true>::ALLOC <= 232448, "shar
 // region does not depend on the launch's shape, so one zeroed workspace serves any sequence
 // of calls on a stream.
 constexpr int G_SPLIT_MAX_TILES = 512;
+// Tokens of one CTA's fp32 partial tile: the accumulator columns of a tile.
+template <bool PAIR>
+constexpr int acc_tokens() { return PAIR ? G_PAIR_TILE_N : G_ACC_COLS; }
 constexpr int64_t G_SPLIT_CNT_BYTES = 2 * G_SPLIT_MAX_TILES * 4;
 
 // One NF4 weight of a launch.  A forward launch may carry up to G_MAX_W weights that share
@@ -114,7 +121,7 @@ struct GemmArgs {
   int32_t splits;         // K ranges per tile (split-K); 1 = none
   int32_t nk;             // K stages of the whole reduction
   uint32_t k16;           // 1 << 16 (a run-time multiplier for the decode's shifts)
-  int32_t tile_n;         // tokens per tile: 256, or 128 for launches with few tiles
+  int32_t tile_n;         // tokens per tile: 256 or 128 (single CTAs), 512 (pairs)
   float* ws_part;         // split-K: fp32 partial tiles [tiles][splits][256][128]
   int32_t* ws_cnt;        // split-K: per-tile counters [2][G_SPLIT_MAX_TILES], zero between launches
 };
@@ -426,8 +433,13 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       for (int u = unit0; ok && u < nunits; u += ustride) {
         const WorkUnit wu = work_unit<MULTI, PAIR>(g, u, rank);
         const TileCoord& tc = wu.tc;
-        // a pair's MMA reads tokens [0, tn/2) of the tile from rank 0 and [tn/2, tn) from rank 1
-        const int trow = int(tc.t0) + (PAIR ? int(rank) * (tc.tn >> 1) : 0);
+        // A pair tile's MMA h (h = 0, 1) covers tokens [256 h, 256 h + n_h) of the tile, n_h =
+        // min(tn - 256 h, 256); it reads the first n_h / 2 of them from rank 0 and the rest
+        // from rank 1, as one 128-row box per half and CTA.
+        const int nh = (PAIR && tc.tn > G_NMAX) ? 2 : 1;
+        int trow[2];
+        for (int h = 0; h < 2; ++h)
+          trow[h] = int(tc.t0) + (PAIR ? h * G_NMAX + int(rank) * (min(tc.tn - h * G_NMAX, G_NMAX) >> 1) : 0);
         for (int k = wu.kb; k < wu.ke; ++k, ++it) {
           const int s = it % NS;
           const uint32_t ph = (it / NS) & 1;
@@ -435,13 +447,15 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             ok = false;
             break;
           }
-          // the token box is the tile width (a pair: half of 256)
-          mbar_arrive_expect_tx(&full[s], (PAIR ? L::X_BYTES : g.tile_n * 128) + L::P_BYTES);
+          // the token box is the tile width (a pair: one 128-row box per MMA)
+          mbar_arrive_expect_tx(&full[s], (PAIR ? nh * (G_NMAX / 2) * 128 : g.tile_n * 128) + L::P_BYTES);
           const int ws = KCAT ? kseg(g, k) : tc.seg;   // weight of this stage
           const int kl = KCAT ? k - kbeg(g, ws) : k;  // its local K stage
           const CUtensorMap* tm_a = ws == 0 ? &tm_act0 : (ws == 1 ? &tm_act1 : &tm_act2);
           const CUtensorMap* tm_w = ws == 0 ? &tm_w0 : (ws == 1 ? &tm_w1 : &tm_w2);
-          tma_load_2d(smem + L::X + s * L::X_BYTES, KCAT ? tm_a : &tm_act0, &full[s], kl * G_K, trow);
+          for (int h = 0; h < nh; ++h)
+            tma_load_2d(smem + L::X + s * L::X_BYTES + h * (G_NMAX / 2) * 128, KCAT ? tm_a : &tm_act0,
+                        &full[s], kl * G_K, trow[h]);
           if (!BWD)
             tma_load_2d(smem + L::P + s * L::P_BYTES, tm_w, &full[s], kl * (G_K / 2), int(tc.m0));
           else
@@ -464,14 +478,37 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       for (int u = unit0; ok && u < nunits; u += ustride, ++lt) {
         const WorkUnit wu = work_unit<MULTI, PAIR>(g, u, rank);
         const TileCoord& tc = wu.tc;
-        const uint32_t b = lt & 1;
-        const uint32_t use = lt >> 1;
-        const uint32_t d_tmem = tmem_base + b * G_ACC_COLS;
+        // Single CTAs: one 256-column accumulator per tile, two alternating between tiles
+        // (acc_full / acc_empty[b]).  Pairs: one 512-column accumulator per tile, MMA h writing
+        // columns [256 h, 256 h + n_h) (token 256 h + c of the tile); acc_full / acc_empty[h]
+        // hand half h to the epilogue and back, so the drain of half 0 overlaps the tile's last
+        // half-1 MMAs and the next tile's half-0 MMAs overlap the drain of half 1.
+        const uint32_t b = PAIR ? 0u : (lt & 1);
+        const uint32_t epar = PAIR ? ((lt & 1) ^ 1) : (((lt >> 1) & 1) ^ 1);
+        const int n0 = PAIR ? min(tc.tn, G_NMAX) : tc.tn;
+        const int n1 = PAIR ? tc.tn - n0 : 0;
         constexpr int MM = PAIR ? 2 * G_M : G_M;
-        const uint32_t idesc = idesc_f16(MM, tc.tn, BWD, false);
-        if (!pwait(&acc_empty[b], (use & 1) ^ 1)) break;
+        const uint32_t d0 = tmem_base + b * G_ACC_COLS;
+        const uint32_t d1 = tmem_base + G_NMAX;
+        const uint32_t id0 = idesc_f16(MM, n0, BWD, false);
+        const uint32_t id1 = idesc_f16(MM, n1 > 0 ? n1 : 16, BWD, false);
+        if (!pwait(&acc_empty[b], epar)) break;
+        // a pair's half 1 is awaited before its first MMA (or, when the tile has no half-1
+        // tokens, before acc_full[1] is committed, so that barrier never runs two phases ahead
+        // of the epilogue)
+        bool free1 = !PAIR;
+        auto take1 = [&]() -> bool {
+          if (!free1) free1 = pwait(&acc_empty[1], epar);
+          return free1;
+        };
+        auto mma = [&](uint32_t d, uint64_t a, uint64_t bd, uint32_t id, bool accum) {
+          if (PAIR)
+            umma_f16_pair(d, a, bd, id, accum ? 1u : 0u);
+          else
+            umma_f16(d, a, bd, id, accum ? 1u : 0u);
+        };
         tc_fence_after();
-        bool acc = false;
+        bool acc0 = false, acc1 = false;
         // LoRA terms belong to the first K range; a K-concatenated backward has one slab per
         // adapter, filled and consumed one after the other
         for (int i = 0; wu.split == 0 && i < (KCAT ? g.nw : 1); ++i) {
@@ -484,13 +521,19 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           tc_fence_after();
           const uint64_t ad = smem_desc_nosw(sbase + L::LA, 128, 256);
           const uint64_t bd = smem_desc_nosw(sbase + L::LB, 128, 256);
-          const uint32_t id = idesc_f16(MM, tc.tn, false, false);
-          if (PAIR)
-            umma_f16_pair(d_tmem, ad, bd, id, acc ? 1u : 0u);
-          else
-            umma_f16(d_tmem, ad, bd, id, acc ? 1u : 0u);
+          mma(d0, ad, bd, idesc_f16(MM, n0, false, false), acc0);
+          acc0 = true;
+          if (PAIR && n1 > 0) {
+            if (!take1()) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            // the slab's token rows of half 1 start at row 128 (4 KB)
+            mma(d1, ad, bd + uint64_t(4096 >> 4), idesc_f16(MM, n1, false, false), acc1);
+            acc1 = true;
+          }
           commit_both(lora_empty);
-          acc = true;
         }
         if (!ok) break;
         // The issuing thread shares its SM sub-partition with decode warps, so its loop is
@@ -503,6 +546,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         uint32_t s = it % NS, ph = (it / NS) & 1;
         bool ready = wu.kb < wu.ke && pwait(&afull[s], ph);
         if (wu.kb < wu.ke && !ready) ok = false;
+        bool done0 = false;
         for (int k = wu.kb; ok && k < wu.ke; ++k, ++it) {
           tc_fence_after();
           const uint64_t ad = ad0 + uint64_t(s * (L::A_BYTES >> 4));
@@ -515,13 +559,30 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             // K-major 128B swizzle: advance 32 B per 16 K; MN-major: two 8-row atoms (2 KB).
             const uint64_t a_kk = ad + uint64_t(kk * (BWD ? 2048 / 16 : 32 / 16));
             const uint64_t b_kk = bd + uint64_t(kk * (32 / 16));
-            if (PAIR)
-              umma_f16_pair(d_tmem, a_kk, b_kk, idesc, (acc || kk > 0) ? 1u : 0u);
-            else
-              umma_f16(d_tmem, a_kk, b_kk, idesc, (acc || kk > 0) ? 1u : 0u);
+            mma(d0, a_kk, b_kk, id0, acc0 || kk > 0);
             if (kk == 0 && k + 1 < wu.ke) next_ready = mbar_test_wait(&afull[s1], ph1);
           }
-          acc = true;
+          acc0 = true;
+          if (PAIR && k + 1 == wu.ke) {
+            commit_both(&acc_full[0]);
+            done0 = true;
+          }
+          if (PAIR && n1 > 0) {
+            if (!take1()) {
+              ok = false;
+              ++it;
+              break;
+            }
+            tc_fence_after();
+            // the same decoded weight stage against the stage's second token half (16 KB on)
+#pragma unroll
+            for (int kk = 0; kk < G_K / 16; ++kk) {
+              const uint64_t a_kk = ad + uint64_t(kk * (BWD ? 2048 / 16 : 32 / 16));
+              const uint64_t b_kk = bd + uint64_t((L::X_BYTES / 2) >> 4) + uint64_t(kk * (32 / 16));
+              mma(d1, a_kk, b_kk, id1, acc1 || kk > 0);
+            }
+            acc1 = true;
+          }
           commit_both(&empty[s]);
           s = s1;
           ph = ph1;
@@ -531,7 +592,11 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             break;
           }
         }
-        commit_both(&acc_full[b]);
+        if (!done0) commit_both(&acc_full[b]);
+        if (PAIR) {
+          if (!take1()) ok = false;
+          commit_both(&acc_full[1]);
+        }
       }
       // every MMA must be complete before TMEM is released
       commit_both(mma_done);
@@ -612,16 +677,24 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                                     pack_half2(v[12], v[13]), pack_half2(v[14], v[15])));
           }
         }
-        // token side: X_ROWS rows x 2 chunks of 16 B (a pair: this CTA's half of the tile)
-        const int thalf = PAIR ? (tc.tn >> 1) : G_NMAX;
-        const int tbase = PAIR ? int(rank) * thalf : 0;
+        // token side: X_ROWS rows x 2 chunks of 16 B.  A pair: slab row t is row t & 127 of
+        // MMA half h = t >> 7 in this CTA, i.e. token 256 h + rank n_h / 2 + (t & 127) of the
+        // tile, present when t & 127 < n_h / 2.
 #pragma unroll
         for (int jj = 0; jj < L::X_ROWS / 128; ++jj) {
           const int c = dq + 256 * jj;
           const int t = c >> 1, kc = c & 1;
+          int tok = t;
+          bool in = true;
+          if (PAIR) {
+            const int h = t >> 7, tl = t & 127;
+            const int nhalf = min(tc.tn - h * G_NMAX, G_NMAX) / 2;
+            tok = h * G_NMAX + int(rank) * nhalf + tl;
+            in = tl < nhalf;
+          }
           uint4 v = make_uint4(0, 0, 0, 0);
-          if (t < thalf && tbase + t < tc.tn_real)
-            v = __ldg(reinterpret_cast<const uint4*>(WL.lora_t + (tc.t0 + tbase + t) * 16 + kc * 8));
+          if (in && tok < tc.tn_real)
+            v = __ldg(reinterpret_cast<const uint4*>(WL.lora_t + (tc.t0 + tok) * 16 + kc * 8));
           st_shared_v4(lb + slab_off(t, kc), v);
         }
         fence_proxy_async_smem();
@@ -735,11 +808,15 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       const TileCoord& tc = wu.tc;
       const GemmW& W = g.w[MULTI ? tc.seg : 0];
       const int64_t ld_out = BWD ? g.in_f : W.out_f;
-      const uint32_t b = lt & 1;
-      const uint32_t use = lt >> 1;
+      // single CTAs: accumulator b of two; a pair: the tile's 512 columns, handed over in two
+      // halves (acc_full[0] / [1]); split-K takes both halves at once
+      const uint32_t b = PAIR ? 0u : (lt & 1);
+      const uint32_t fpar = PAIR ? (lt & 1) : ((lt >> 1) & 1);
+      constexpr bool by_half = PAIR && !SPLIT;
       // uniform over the warp (tcgen05.ld is warp-collective) and, for split-K, over all
       // epilogue warps (they meet at named barriers below)
-      bool ok = pwait(&acc_full[b], use & 1);
+      bool ok = pwait(&acc_full[b], fpar);
+      if (PAIR && SPLIT) ok = ok && pwait(&acc_full[1], fpar);
       ok = split ? epi_bar_and(ok) : __all_sync(0xffffffffu, ok);
       tc_fence_after();
       if (!ok) break;
@@ -747,6 +824,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       const int64_t row = tc.m0 + prow;
       const bool row_ok = row < ld_out;  // ld_out is a multiple of 64: pairs are all in or out
       const uint32_t taddr = tmem_base + (uint32_t(32 * lq) << 16) + b * G_ACC_COLS;
+      constexpr int ACC_T = acc_tokens<PAIR>();
+      bool fail = false;
       // Split-K: every K range of a tile takes a ticket; all but the last write their fp32
       // partial to the workspace slot of their range, the last sums the ranges in range
       // order (its own from TMEM) and writes the output, so the result does not depend on
@@ -758,11 +837,11 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         epi_bar_sync();
         ticket = s_ticket[lt & 1];
       }
-      // partial tiles are column-major [256 tokens][128 rows]: for one token the 32 lanes
-      // of a warp (32 consecutive rows) touch one 128-byte line
-      const float* part0 = g.ws_part + int64_t(ctile) * (nparts + 1) * (G_M * G_ACC_COLS) + prow;
+      // partial tiles are column-major [tokens][128 rows]: for one token the 32 lanes of a
+      // warp (32 consecutive rows) touch one 128-byte line
+      const float* part0 = g.ws_part + int64_t(ctile) * (nparts + 1) * (G_M * ACC_T) + prow;
       if (ticket < nparts) {
-        float* dst = const_cast<float*>(part0) + int64_t(wu.split) * (G_M * G_ACC_COLS);
+        float* dst = const_cast<float*>(part0) + int64_t(wu.split) * (G_M * ACC_T);
         for (int c0 = 32 * grp; c0 < tc.tn; c0 += 64) {
           uint32_t acc[32];
           tmem_ld_32x32b_x32(taddr + uint32_t(c0), acc);
@@ -803,54 +882,78 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             if (jj < lim) p[int64_t(jj >> 1) * ld_out] = h;
           }
         };
-        for (int c0 = 32 * grp; c0 < tc.tn; c0 += 64) {
-          uint32_t acc[32];
-          if (!SPLIT) {
-            tmem_ld_32x32b_x32(taddr + uint32_t(c0), acc);
-            tmem_ld_wait();
-          } else {
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {  // 16 columns at a time: own values + running sum
-              uint32_t own[16];
-              tmem_ld_32x32b_x16(taddr + uint32_t(c0 + 16 * hf), own);
-              tmem_ld_wait();
-              float t[16];
-#pragma unroll
-              for (int j = 0; j < 16; ++j) t[j] = 0.f;
-              for (int sp = 0; sp <= nparts; ++sp) {
-                if (sp == wu.split) {
-#pragma unroll
-                  for (int j = 0; j < 16; ++j) t[j] += __uint_as_float(own[j]);
-                } else {
-                  const float* src = part0 + int64_t(sp) * (G_M * G_ACC_COLS) + (c0 + 16 * hf) * G_M;
-#pragma unroll
-                  for (int j = 0; j < 16; ++j) t[j] += __ldcg(src + j * G_M);
-                }
-              }
-#pragma unroll
-              for (int j = 0; j < 16; ++j) acc[16 * hf + j] = __float_as_uint(t[j]);
+        for (int h = 0; h < (by_half ? 2 : 1); ++h) {
+          const int cb = by_half ? h * G_NMAX : 0;
+          const int ce = (by_half && h == 0) ? min(tc.tn, G_NMAX) : tc.tn;
+          if (by_half && h == 1) {
+            // half 0 drained: hand it back to the MMA issuer, then take half 1
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) arrive_issuer(&acc_empty[0], acc_empty_l);
+            const bool ok1 = __all_sync(0xffffffffu, pwait(&acc_full[1], fpar));
+            tc_fence_after();
+            if (!ok1) {
+              fail = true;
+              break;
             }
           }
-          // stores of token c0 + jj + odd land while that token is in the tile; the paths
-          // below are warp-uniform (emit shuffles across the warp)
-          const int lim = row_ok ? tc.tn_real - c0 - (odd ? 1 : 0) : 0;
-          const bool whole = __all_sync(0xffffffffu, lim >= 32);
-          if (has_bias) {
-            if (whole)
-              emit(acc, c0, std::true_type(), 32);
-            else
-              emit(acc, c0, std::true_type(), lim);
-          } else {
-            if (whole)
-              emit(acc, c0, std::false_type(), 32);
-            else
-              emit(acc, c0, std::false_type(), lim);
+          for (int c0 = cb + 32 * grp; c0 < ce; c0 += 64) {
+            uint32_t acc[32];
+            if (!SPLIT) {
+              tmem_ld_32x32b_x32(taddr + uint32_t(c0), acc);
+              tmem_ld_wait();
+            } else {
+#pragma unroll
+              for (int hf = 0; hf < 2; ++hf) {  // 16 columns at a time: own values + running sum
+                uint32_t own[16];
+                tmem_ld_32x32b_x16(taddr + uint32_t(c0 + 16 * hf), own);
+                tmem_ld_wait();
+                float t[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) t[j] = 0.f;
+                for (int sp = 0; sp <= nparts; ++sp) {
+                  if (sp == wu.split) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) t[j] += __uint_as_float(own[j]);
+                  } else {
+                    const float* src = part0 + int64_t(sp) * (G_M * ACC_T) + (c0 + 16 * hf) * G_M;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) t[j] += __ldcg(src + j * G_M);
+                  }
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) acc[16 * hf + j] = __float_as_uint(t[j]);
+              }
+            }
+            // stores of token c0 + jj + odd land while that token is in the tile; the paths
+            // below are warp-uniform (emit shuffles across the warp)
+            const int lim = row_ok ? tc.tn_real - c0 - (odd ? 1 : 0) : 0;
+            const bool whole = __all_sync(0xffffffffu, lim >= 32);
+            if (has_bias) {
+              if (whole)
+                emit(acc, c0, std::true_type(), 32);
+              else
+                emit(acc, c0, std::true_type(), lim);
+            } else {
+              if (whole)
+                emit(acc, c0, std::false_type(), 32);
+              else
+                emit(acc, c0, std::false_type(), lim);
+            }
           }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) arrive_issuer(&acc_empty[b], acc_empty_l + 8u * b);
+      if (lane == 0) {
+        if (!PAIR) {
+          arrive_issuer(&acc_empty[b], acc_empty_l + 8u * b);
+        } else {
+          if (SPLIT) arrive_issuer(&acc_empty[0], acc_empty_l);
+          if (!fail) arrive_issuer(&acc_empty[1], acc_empty_l + 8u);
+        }
+      }
+      if (fail) break;
     }
   }
 
@@ -977,8 +1080,9 @@ static int pair_slots_cached() {
   return cached[dev] > 0 ? cached[dev] : 0;
 }
 
-// Tiling of one launch.  Single CTAs: 128-row weight tiles x 256-token tiles on one CTA per
-// SM.  Pairs: 256-row tiles (each weight's rows rounded up to 256) on 2-CTA clusters.  The
+// Tiling of one launch.  Single CTAs: 128-row weight tiles x 256-token (or 128-token) tiles
+// on one CTA per SM.  Pairs: 256-row x 512-token tiles (each weight's rows rounded up to 256)
+// on 2-CTA clusters.  The
 // K stages of a tile may be split into `splits` ranges when there are fewer tiles than slots.
 struct GemmPlan {
   int64_t m_tiles, n_tiles, tiles;
@@ -996,13 +1100,17 @@ constexpr int G_MAX_SPLITS = 8;
 // partials through L2, measured at ~3 us to write one 128 x 256 partial and ~3 us per partial
 // for the last CTA to read back (4 + 4 per partial).  A 128-token tile's stage costs ~0.55 of
 // a 256-token one (the decode of the weight stage is the same, the MMA half) and its partials
-// half as much.
+// half as much.  A pair's 512-token tile (two MMAs per decoded stage, on two SMs) runs a stage
+// in ~1.35 and adds ~8 per tile (its single accumulator leaves the 512-column drain exposed);
+// its CTAs' partials are twice as large.  (Fitted to CUDA-event times of the seven
+// Qwen2.5-1.5B projection shapes, forward and backward, at 1170, 2048 and 8192 tokens.)
 static double plan_cost(int64_t tiles, int64_t slots, int32_t nk, int64_t sp, int32_t tile_n) {
-  const double stage = tile_n == 256 ? 1.0 : 0.55;
-  const double red = tile_n == 256 ? 4.0 : 2.0;
+  const double stage = tile_n == 128 ? 0.55 : (tile_n == 256 ? 1.0 : 1.35);
+  const double fill = tile_n == G_PAIR_TILE_N ? 8.0 : 3.0;
+  const double red = double(tile_n) / 64.0;
   const int64_t waves = (tiles * sp + slots - 1) / slots;
   const double reduce = sp > 1 ? red * double(sp) : 0.0;
-  return double(waves) * (stage * double((nk + sp - 1) / sp) + 3.0) + reduce;
+  return double(waves) * (stage * double((nk + sp - 1) / sp) + fill) + reduce;
 }
 
 // Split-K choice: a split must beat the unsplit launch by 5 % and leave every range at least 2
@@ -1058,32 +1166,36 @@ static GemmPlan plan_gemm(int64_t n, const int64_t* rows, int nrows, int64_t kdi
   narrow.tiles = narrow.m_tiles * narrow.n_tiles;
   const double c128 = plan_splits(&narrow, G_SPLIT_MAX_TILES);
   const int tn_env = tile_n_env();
-  if (tn_env == 128 || (tn_env == 0 && c128 < 0.95 * c256)) single = narrow;
-  const int mode = pair_mode_env();
+  const bool use128 = tn_env == 128 || (tn_env == 0 && c128 < 0.95 * c256);
+  if (use128) single = narrow;
+  const double c_single = use128 ? c128 : c256;
+  // a forced token tile width (STEW_NF4_TILE_N) also keeps automatic plans on single CTAs
+  const int mode = tn_env != 0 && pair_mode_env() != 1 ? 0 : pair_mode_env();
   const int64_t pslots = mode == 0 ? 0 : pair_slots_cached();
   if (pslots <= 0) return single;
   GemmPlan pair = single;
-  pair.tile_n = G_NMAX;
-  pair.n_tiles = (n + G_NMAX - 1) / G_NMAX;
+  pair.tile_n = G_PAIR_TILE_N;
+  pair.n_tiles = (n + G_PAIR_TILE_N - 1) / G_PAIR_TILE_N;
   pair.pair = true;
   pair.slots = pslots;
   pair.m_tiles = 0;
   for (int i = 0; i < nrows; ++i) pair.m_tiles += (rows[i] + 2 * G_M - 1) / (2 * G_M);
   pair.tiles = pair.m_tiles * pair.n_tiles;
-  plan_splits(&pair, G_SPLIT_MAX_TILES / 2);
+  const double c_pair = plan_splits(&pair, G_SPLIT_MAX_TILES / 2);
   if (mode == 1) return pair;
-  // automatic: single CTAs (pairs measured level with them on every Qwen2.5-1.5B shape; they
-  // halve the L2 -> SM token traffic but add a cross-CTA hop to every stage)
-  return single;
+  // automatic: pairs when their tiles need no split-K (a pair's 512-token partials made
+  // split plans slower than modelled) and the model puts them 5 % ahead of single CTAs
+  return (pair.splits == 1 && c_pair < 0.95 * c_single) ? pair : single;
 }
 
 // Workspace of a split launch: the counter region, then one fp32 partial tile per K range
-// and CTA tile [cta tiles][splits][256][128] (the last range of a tile to finish leaves its
-// slot unused).
+// and CTA tile [cta tiles][splits][256 tokens (a pair: 512)][128] (the last range of a tile
+// to finish leaves its slot unused).
 static int64_t plan_work_bytes(const GemmPlan& p) {
   if (p.splits <= 1) return 0;
   const int64_t cta_tiles = p.pair ? 2 * p.tiles : p.tiles;
-  return G_SPLIT_CNT_BYTES + cta_tiles * p.splits * int64_t(G_M) * G_ACC_COLS * int64_t(sizeof(float));
+  const int64_t acc_t = p.pair ? acc_tokens<true>() : acc_tokens<false>();
+  return G_SPLIT_CNT_BYTES + cta_tiles * p.splits * int64_t(G_M) * acc_t * int64_t(sizeof(float));
 }
 
 // Token rows of the activation tile one CTA loads per stage.
