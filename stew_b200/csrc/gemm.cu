@@ -903,26 +903,23 @@ __global__ void __launch_bounds__(G_THREADS, 1)
               tmem_ld_32x32b_x32(taddr + uint32_t(c0), acc);
               tmem_ld_wait();
             } else {
+              // the 32 columns summed in range order, one range per round (this CTA's own
+              // range from TMEM): the reduction is bound by L2 round trips, so each round has
+              // all 32 loads of a thread in flight
 #pragma unroll
-              for (int hf = 0; hf < 2; ++hf) {  // 16 columns at a time: own values + running sum
-                uint32_t own[16];
-                tmem_ld_32x32b_x16(taddr + uint32_t(c0 + 16 * hf), own);
-                tmem_ld_wait();
-                float t[16];
+              for (int j = 0; j < 32; ++j) acc[j] = __float_as_uint(0.f);
+              for (int sp = 0; sp <= nparts; ++sp) {
+                uint32_t v[32];
+                if (sp == wu.split) {
+                  tmem_ld_32x32b_x32(taddr + uint32_t(c0), v);
+                  tmem_ld_wait();
+                } else {
+                  const float* src = part0 + int64_t(sp) * (G_M * ACC_T) + c0 * G_M;
 #pragma unroll
-                for (int j = 0; j < 16; ++j) t[j] = 0.f;
-                for (int sp = 0; sp <= nparts; ++sp) {
-                  if (sp == wu.split) {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) t[j] += __uint_as_float(own[j]);
-                  } else {
-                    const float* src = part0 + int64_t(sp) * (G_M * ACC_T) + (c0 + 16 * hf) * G_M;
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) t[j] += __ldcg(src + j * G_M);
-                  }
+                  for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__ldcg(src + j * G_M));
                 }
 #pragma unroll
-                for (int j = 0; j < 16; ++j) acc[16 * hf + j] = __float_as_uint(t[j]);
+                for (int j = 0; j < 32; ++j) acc[j] = __float_as_uint(__uint_as_float(acc[j]) + __uint_as_float(v[j]));
               }
             }
             // stores of token c0 + jj + odd land while that token is in the tile; the paths
@@ -1183,9 +1180,8 @@ static GemmPlan plan_gemm(int64_t n, const int64_t* rows, int nrows, int64_t kdi
   pair.tiles = pair.m_tiles * pair.n_tiles;
   const double c_pair = plan_splits(&pair, G_SPLIT_MAX_TILES / 2);
   if (mode == 1) return pair;
-  // automatic: pairs when their tiles need no split-K (a pair's 512-token partials made
-  // split plans slower than modelled) and the model puts them 5 % ahead of single CTAs
-  return (pair.splits == 1 && c_pair < 0.95 * c_single) ? pair : single;
+  // automatic: pairs when the model puts them 5 % ahead of single CTAs
+  return c_pair < 0.95 * c_single ? pair : single;
 }
 
 // Workspace of a split launch: the counter region, then one fp32 partial tile per K range
