@@ -258,9 +258,10 @@ int nf4b_gemm_error_flag(int* value, int reset);
 
 /* Launch geometry of the fused GEMMs on the current device: *sms = SMs (one persistent CTA
  * each), *pair_slots = 2-CTA clusters that can be resident at once (0 when the device runs
- * none; pairs of CTAs then never run).  The environment variable STEW_NF4_PAIR chooses
- * between the two tilings: "0" single CTAs only, "1" pairs whenever pair_slots > 0, unset
- * or empty the built-in choice.  */
+ * none; pairs of CTAs then never run).  Pairs tile 256 weight rows x 512 tokens, single CTAs
+ * 128 rows x 256 (or 128) tokens; a cost model picks per launch.  The environment variable
+ * STEW_NF4_PAIR overrides it: "0" single CTAs only, "1" pairs whenever pair_slots > 0, unset
+ * or empty the cost model.  */
 int nf4b_gemm_geometry(int* sms, int* pair_slots);
 
 /* The CUDA error behind the last NF4B_ERR_CUDA returned on the calling host

@@ -14,6 +14,9 @@
 // 256 tokens) with stride gridDim.x; the 4-stage shared-memory ring and the stage
 // counters run on across tiles, and the two 256-column accumulators in TMEM alternate
 // between tiles, so a tile's epilogue overlaps the next tile's main loop.
+// Pairs (PAIR): 2-CTA clusters walk 256-row x 512-token tiles; each decoded weight stage
+// feeds two cta_group::2 MMAs (tokens [0, 256) and [256, 512) of the tile), halving the
+// decode per FLOP, into one 512-column accumulator that the epilogue drains in halves.
 //   warp 0      TMA producer: activation tile [256 tok x 64] fp16 (128B swizzle) and
 //               the packed weight tile (4 KB) per stage.
 //   warp 1      TMEM allocation (512 columns) + single-thread tcgen05.mma issuer.
@@ -1170,15 +1173,22 @@ static GemmPlan plan_gemm(int64_t n, const int64_t* rows, int nrows, int64_t kdi
   const int mode = tn_env != 0 && pair_mode_env() != 1 ? 0 : pair_mode_env();
   const int64_t pslots = mode == 0 ? 0 : pair_slots_cached();
   if (pslots <= 0) return single;
+  // Pair tiles are near MMA-bound, so the tokens are dealt evenly over the fewest 512-token
+  // tiles (a multiple of 32 each; e.g. 1311 tokens: 448 + 448 + 415, not 512 + 512 + 287):
+  // the longest unit of a wave is what the launch waits for.
   GemmPlan pair = single;
-  pair.tile_n = G_PAIR_TILE_N;
   pair.n_tiles = (n + G_PAIR_TILE_N - 1) / G_PAIR_TILE_N;
+  pair.tile_n = G_PAIR_TILE_N;
   pair.pair = true;
   pair.slots = pslots;
   pair.m_tiles = 0;
   for (int i = 0; i < nrows; ++i) pair.m_tiles += (rows[i] + 2 * G_M - 1) / (2 * G_M);
   pair.tiles = pair.m_tiles * pair.n_tiles;
   const double c_pair = plan_splits(&pair, G_SPLIT_MAX_TILES / 2);
+  if (pair.n_tiles > 0) {
+    const int64_t even = ((n + pair.n_tiles - 1) / pair.n_tiles + 31) / 32 * 32;
+    pair.tile_n = int32_t(even < G_PAIR_TILE_N ? even : G_PAIR_TILE_N);
+  }
   if (mode == 1) return pair;
   // automatic: pairs when the model puts them 5 % ahead of single CTAs
   return c_pair < 0.95 * c_single ? pair : single;

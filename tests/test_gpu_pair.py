@@ -1,13 +1,15 @@
-"""GPU: the 2-CTA cluster tiling of the fused NF4 GEMMs (STEW_NF4_PAIR=1: 256-row tiles, one
-cta_group::2 MMA over both CTAs of a pair) against the single-CTA tiling (STEW_NF4_PAIR=0) and
-against the fp64 product of the oracle-dequantised weights.
+"""GPU: the 2-CTA cluster tiling of the fused NF4 GEMMs (STEW_NF4_PAIR=1: 256-row x 512-token
+tiles, two cta_group::2 MMAs over both CTAs of a pair per decoded weight stage) against the
+single-CTA tiling (STEW_NF4_PAIR=0) and against the fp64 product of the oracle-dequantised
+weights.
 
 Unsplit, both tilings run the same K order per output, so their outputs must agree bit for
 bit; when either plan splits K (few tiles) the fp32 partial sums are added in another order and
 the two agree within 1e-3 of max |y|.  Both must be within the GEMM tolerance of the
 reference (max |y - ref| / max |ref| <= 2e-3).  Covered: the Qwen2.5-1.5B shapes, weights
 whose row count leaves the second CTA of the last pair partly or wholly outside the weight
-(192, 384 rows), ragged token counts (the two CTAs split a partial token tile at N/2), bias,
+(192, 384 rows), ragged token counts (a partial tile with or without tokens in its second
+MMA, each MMA's tokens split between the two CTAs at n_h/2), bias,
 LoRA, split-K plans (few tiles), grouped forward (q/k/v) and the K-concatenated grouped
 backward."""
 import ctypes
