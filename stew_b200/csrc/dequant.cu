@@ -22,6 +22,8 @@
 #include <mutex>
 #include <vector>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "nf4_decode.cuh"
 
@@ -330,6 +332,17 @@ int check_device() {
     cached_ok = (major == 10);
   }
   return cached_ok ? NF4B_OK : NF4B_ERR_DEVICE;
+}
+
+bool pdl_enabled(cudaStream_t s) {
+  const char* v = std::getenv("STEW_PDL");
+  if (v != nullptr && v[0] == '0') return false;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cs) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return cs == cudaStreamCaptureStatusNone;
 }
 
 }  // namespace nf4b

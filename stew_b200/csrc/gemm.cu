@@ -408,10 +408,6 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     if (KCAT && g.nw > 1) prefetch_tma_desc(&tm_act1);
     if (KCAT && g.nw > 2) prefetch_tma_desc(&tm_act2);
   }
-  for (int i = 0; i < g.nw; ++i) {
-    if (threadIdx.x < 16) s_code[16 * i + threadIdx.x] = __ldg(g.w[i].code + threadIdx.x);
-    if (g.w[i].nested && threadIdx.x < 256) s_code2[256 * i + threadIdx.x] = __ldg(g.w[i].code2 + threadIdx.x);
-  }
   if (warp == 1) {
     if (PAIR) {
       tmem_alloc_pair(tmem_slot, G_TMEM_COLS);
@@ -420,6 +416,13 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       tmem_alloc(tmem_slot, G_TMEM_COLS);
       tmem_relinquish();
     }
+  }
+  // everything above overlaps the previous kernel of the stream (programmatic launch); global
+  // memory is touched only after it has completed
+  grid_dep_wait();
+  for (int i = 0; i < g.nw; ++i) {
+    if (threadIdx.x < 16) s_code[16 * i + threadIdx.x] = __ldg(g.w[i].code + threadIdx.x);
+    if (g.w[i].nested && threadIdx.x < 256) s_code2[256 * i + threadIdx.x] = __ldg(g.w[i].code2 + threadIdx.x);
   }
   tc_fence_before();
   __syncthreads();
@@ -1040,11 +1043,12 @@ static int set_smem_attr() {
   return NF4B_OK;
 }
 
-// Launch configuration of a 2-CTA cluster launch of `grid` CTAs.
+// Launch configuration of a 2-CTA cluster launch of `grid` CTAs (programmatic launch as for
+// single CTAs, unless `pdl` is false).
 struct PairLaunch {
   cudaLaunchConfig_t cfg;
-  cudaLaunchAttribute attr[1];
-  PairLaunch(unsigned grid, cudaStream_t s) : cfg{}, attr{} {
+  cudaLaunchAttribute attr[2];
+  PairLaunch(unsigned grid, cudaStream_t s, bool pdl) : cfg{}, attr{} {
     cfg.gridDim = dim3(grid, 1, 1);
     cfg.blockDim = dim3(G_THREADS, 1, 1);
     cfg.dynamicSmemBytes = Smem<true>::ALLOC;
@@ -1053,8 +1057,10 @@ struct PairLaunch {
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl ? 2 : 1;
   }
 };
 
@@ -1069,7 +1075,7 @@ static int pair_slots_cached() {
   if (cached[dev] == 0) {
     int n = 0;
     if (set_smem_attr<false, false, false, true>() == NF4B_OK) {
-      PairLaunch pl(2u * unsigned(sm_count_cached()), nullptr);
+      PairLaunch pl(2u * unsigned(sm_count_cached()), nullptr, false);
       if (cudaOccupancyMaxActiveClusters(&n, nf4_gemm_kernel<false, false, false, true>, &pl.cfg) !=
           cudaSuccess)
         n = 0;
@@ -1213,10 +1219,10 @@ static int launch_variant(unsigned grid, const CUtensorMap (&ta)[G_MAX_W], const
   int st = set_smem_attr<BWD, SPLIT, MULTI, PAIR>();
   if (st != NF4B_OK) return st;
   if (!PAIR) {
-    nf4_gemm_kernel<BWD, SPLIT, MULTI, PAIR><<<grid, G_THREADS, Smem<PAIR>::ALLOC, s>>>(
-        ta[0], ta[1], ta[2], tw[0], tw[1], tw[2], g);
+    NF4B_CUDA_TRY(launch_pdl(nf4_gemm_kernel<BWD, SPLIT, MULTI, PAIR>, dim3(grid), dim3(G_THREADS),
+                             size_t(Smem<PAIR>::ALLOC), s, ta[0], ta[1], ta[2], tw[0], tw[1], tw[2], g));
   } else {
-    PairLaunch pl(grid, s);
+    PairLaunch pl(grid, s, pdl_enabled(s));
     NF4B_CUDA_TRY(cudaLaunchKernelEx(&pl.cfg, nf4_gemm_kernel<BWD, SPLIT, MULTI, PAIR>, ta[0], ta[1],
                                      ta[2], tw[0], tw[1], tw[2], g));
   }

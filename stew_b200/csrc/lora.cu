@@ -65,6 +65,7 @@ struct ProjJobs {
 template <bool WK>
 __global__ void __launch_bounds__(LP_THREADS)
     lora_project16_kernel(const __grid_constant__ ProjJobs jobs, int64_t n) {
+  grid_dep_wait();  // programmatic launch: no global access before the wait
   const ProjJob& job = jobs.j[blockIdx.y];
   const __half* __restrict__ act = job.act;
   const __half* __restrict__ w = job.w;
@@ -131,9 +132,11 @@ int lora_project16_multi(const void* const* act, const void* const* w, int64_t w
   NF4B_RETURN_IF(ctas > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
   const dim3 grid{unsigned(ctas), unsigned(n_jobs), 1u};
   if (w_stride_k == 1)
-    lora_project16_kernel<true><<<grid, LP_THREADS, 0, s>>>(js, n);
+    NF4B_CUDA_TRY(launch_pdl(lora_project16_kernel<true>, dim3(grid), dim3(LP_THREADS), size_t(0),
+                             s, js, n));
   else
-    lora_project16_kernel<false><<<grid, LP_THREADS, 0, s>>>(js, n);
+    NF4B_CUDA_TRY(launch_pdl(lora_project16_kernel<false>, dim3(grid), dim3(LP_THREADS), size_t(0),
+                             s, js, n));
   return launch_status("lora_project16_kernel launch");
 }
 
@@ -211,6 +214,7 @@ __device__ __forceinline__ int find_job(const OuterJobs& js, int bid, bool reduc
 
 __global__ void __launch_bounds__(LO_THREADS)
     lora_outer16_kernel(const __grid_constant__ OuterJobs jobs, int64_t n) {
+  grid_dep_wait();  // programmatic launch: no global access before the wait
   __shared__ __align__(128) uint8_t qbuf[2][LO_QBUF];
   __shared__ __align__(128) uint8_t pbuf[2][LO_PBUF];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -303,6 +307,7 @@ __global__ void __launch_bounds__(LO_THREADS)
 constexpr int LR_THREADS = 256;
 __global__ void __launch_bounds__(LR_THREADS)
     lora_reduce_kernel(const __grid_constant__ OuterJobs jobs) {
+  grid_dep_wait();  // programmatic launch: no global access before the wait
   __shared__ float ws[LR_THREADS / 32][33];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const OuterJob& job = jobs.j[find_job(jobs, int(blockIdx.x), true)];
@@ -357,10 +362,12 @@ static void add_job(OuterJobs* js, const __half* P, const __half* Q, int64_t n, 
 // One launch of the outer products of a table, then one launch of their reductions.
 static int run_jobs(const OuterJobs& js, int64_t n, int64_t ctas, int64_t reds, cudaStream_t s) {
   NF4B_RETURN_IF(ctas > 0x7FFFFFFFll || reds > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
-  lora_outer16_kernel<<<unsigned(ctas), LO_THREADS, 0, s>>>(js, n);
+  NF4B_CUDA_TRY(launch_pdl(lora_outer16_kernel, dim3(unsigned(ctas)), dim3(LO_THREADS), size_t(0),
+                           s, js, n));
   int st = launch_status();
   if (st != NF4B_OK) return st;
-  lora_reduce_kernel<<<unsigned(reds), LR_THREADS, 0, s>>>(js);
+  NF4B_CUDA_TRY(launch_pdl(lora_reduce_kernel, dim3(unsigned(reds)), dim3(LR_THREADS), size_t(0), s,
+                           js));
   return launch_status();
 }
 

@@ -57,6 +57,7 @@ __global__ void __launch_bounds__(32 * NORM_WARPS)
     rmsnorm_fwd_kernel(const __half* __restrict__ x, const __half* __restrict__ delta,
                        const float* __restrict__ w, float eps, __half* __restrict__ sum,
                        __half* __restrict__ y, float* __restrict__ rstd, int64_t rows) {
+  grid_dep_wait();  // programmatic launch: no global access before the wait
   constexpr int hidden = NC * 256;
   const int lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * NORM_WARPS + (threadIdx.x >> 5);
@@ -110,6 +111,7 @@ __global__ void __launch_bounds__(32 * NORM_WARPS)
     rmsnorm_bwd_kernel(const __half* __restrict__ dy, const __half* __restrict__ x,
                        const float* __restrict__ w, const float* __restrict__ rstd,
                        const __half* __restrict__ dsum, __half* __restrict__ dx, int64_t rows) {
+  grid_dep_wait();  // programmatic launch: no global access before the wait
   constexpr int hidden = NC * 256;
   const int lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * NORM_WARPS + (threadIdx.x >> 5);
@@ -160,6 +162,7 @@ __global__ void rope_qk_kernel(const __half* __restrict__ q, const __half* __res
                                const float* __restrict__ cosv, const float* __restrict__ sinv,
                                __half* __restrict__ qo, __half* __restrict__ ko, int64_t tokens,
                                int hq, int hk, int head_dim, int inverse) {
+  grid_dep_wait();  // programmatic launch: no global access before the wait
   const int d = head_dim >> 1;
   const int per_head = d >> 3;  // threads per (token, head)
   const int64_t per_tok = int64_t(hq + hk) * per_head;
@@ -201,6 +204,7 @@ __device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, __fadd_rn
 // SwiGLU: 8 values per thread.
 __global__ void swiglu_fwd_kernel(const __half* __restrict__ g, const __half* __restrict__ u,
                                   __half* __restrict__ m, int64_t n8) {
+  grid_dep_wait();  // programmatic launch: no global access before the wait
   const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n8) return;
   float gf[8], uf[8], o[8];
@@ -215,6 +219,7 @@ __global__ void swiglu_fwd_kernel(const __half* __restrict__ g, const __half* __
 __global__ void swiglu_bwd_kernel(const __half* __restrict__ dm, const __half* __restrict__ g,
                                   const __half* __restrict__ u, __half* __restrict__ dg,
                                   __half* __restrict__ du, int64_t n8) {
+  grid_dep_wait();  // programmatic launch: no global access before the wait
   const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n8) return;
   float df[8], gf[8], uf[8], og[8], ou[8];
@@ -259,6 +264,7 @@ __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2
 __global__ void __launch_bounds__(CE_THREADS)
     ce_fwd_kernel(const __half* __restrict__ logits, const int64_t* __restrict__ labels,
                   float* __restrict__ loss, float* __restrict__ lse_out, int64_t vocab) {
+  grid_dep_wait();  // programmatic launch: no global access before the wait
   const int64_t row = blockIdx.x;
   const __half* x = logits + row * vocab;
   float m = -INFINITY, s = 0.f;
@@ -306,6 +312,7 @@ __global__ void __launch_bounds__(CE_THREADS)
 __global__ void __launch_bounds__(CE_THREADS)
     ce_bwd_kernel(__half* __restrict__ logits, const int64_t* __restrict__ labels,
                   const float* __restrict__ lse_in, const float* __restrict__ gscale, int64_t vocab) {
+  grid_dep_wait();  // programmatic launch: no global access before the wait
   const int64_t row = blockIdx.x;
   __half* x = logits + row * vocab;
   const int64_t t = labels[row];
@@ -355,10 +362,10 @@ extern "C" int nf4b_rmsnorm_fwd(const void* x, const void* delta, const float* w
   __half* sh = static_cast<__half*>(sum);
   __half* yh = static_cast<__half*>(y);
   switch (hidden >> 8) {
-#define NF4B_NORM_FWD(NC_)                                                                        \
-  case NC_:                                                                                       \
-    rmsnorm_fwd_kernel<NC_><<<norm_grid(rows), 32 * NORM_WARPS, 0, s>>>(xh, dh, w, eps, sh, yh, rstd, \
-                                                                       rows);                      \
+#define NF4B_NORM_FWD(NC_)                                                                     \
+  case NC_:                                                                                    \
+    NF4B_CUDA_TRY(launch_pdl(rmsnorm_fwd_kernel<NC_>, dim3(norm_grid(rows)), dim3(32 * NORM_WARPS), \
+                             size_t(0), s, xh, dh, w, eps, sh, yh, rstd, rows));              \
     break;
     NF4B_NORM_FWD(1) NF4B_NORM_FWD(2) NF4B_NORM_FWD(3) NF4B_NORM_FWD(4) NF4B_NORM_FWD(5)
     NF4B_NORM_FWD(6) NF4B_NORM_FWD(7) NF4B_NORM_FWD(8) NF4B_NORM_FWD(9) NF4B_NORM_FWD(10)
@@ -389,9 +396,10 @@ extern "C" int nf4b_rmsnorm_bwd(const void* dy, const void* x, const float* w, c
   const __half* dsh = static_cast<const __half*>(dsum);
   __half* dxh = static_cast<__half*>(dx);
   switch (hidden >> 8) {
-#define NF4B_NORM_BWD(NC_)                                                                          \
-  case NC_:                                                                                         \
-    rmsnorm_bwd_kernel<NC_><<<norm_grid(rows), 32 * NORM_WARPS, 0, s>>>(gh, xh, w, rstd, dsh, dxh, rows); \
+#define NF4B_NORM_BWD(NC_)                                                                     \
+  case NC_:                                                                                    \
+    NF4B_CUDA_TRY(launch_pdl(rmsnorm_bwd_kernel<NC_>, dim3(norm_grid(rows)), dim3(32 * NORM_WARPS), \
+                             size_t(0), s, gh, xh, w, rstd, dsh, dxh, rows));                 \
     break;
     NF4B_NORM_BWD(1) NF4B_NORM_BWD(2) NF4B_NORM_BWD(3) NF4B_NORM_BWD(4) NF4B_NORM_BWD(5)
     NF4B_NORM_BWD(6) NF4B_NORM_BWD(7) NF4B_NORM_BWD(8) NF4B_NORM_BWD(9) NF4B_NORM_BWD(10)
@@ -418,10 +426,11 @@ extern "C" int nf4b_rope_qk(const void* q, const void* k, const float* cos_t, co
   if (threads == 0) return NF4B_OK;
   int st = check_device();
   if (st != NF4B_OK) return st;
-  rope_qk_kernel<<<unsigned((threads + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(q), static_cast<const __half*>(k), cos_t, sin_t,
-      static_cast<__half*>(q_out), static_cast<__half*>(k_out), tokens, q_heads, k_heads, head_dim,
-      inverse);
+  NF4B_CUDA_TRY(launch_pdl(rope_qk_kernel, dim3(unsigned((threads + 255) / 256)), dim3(256),
+                           size_t(0), static_cast<cudaStream_t>(stream),
+                           static_cast<const __half*>(q), static_cast<const __half*>(k), cos_t,
+                           sin_t, static_cast<__half*>(q_out), static_cast<__half*>(k_out), tokens,
+                           q_heads, k_heads, head_dim, inverse));
   return launch_status("rope_qk_kernel launch");
 }
 
@@ -433,8 +442,10 @@ extern "C" int nf4b_swiglu_fwd(const void* gate, const void* up, void* out, int6
   int st = check_device();
   if (st != NF4B_OK) return st;
   const int64_t n8 = n / 8;
-  swiglu_fwd_kernel<<<unsigned((n8 + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(gate), static_cast<const __half*>(up), static_cast<__half*>(out), n8);
+  NF4B_CUDA_TRY(launch_pdl(swiglu_fwd_kernel, dim3(unsigned((n8 + 255) / 256)), dim3(256),
+                           size_t(0), static_cast<cudaStream_t>(stream),
+                           static_cast<const __half*>(gate), static_cast<const __half*>(up),
+                           static_cast<__half*>(out), n8));
   return launch_status("swiglu_fwd_kernel launch");
 }
 
@@ -449,9 +460,11 @@ extern "C" int nf4b_swiglu_bwd(const void* dout, const void* gate, const void* u
   int st = check_device();
   if (st != NF4B_OK) return st;
   const int64_t n8 = n / 8;
-  swiglu_bwd_kernel<<<unsigned((n8 + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(dout), static_cast<const __half*>(gate), static_cast<const __half*>(up),
-      static_cast<__half*>(dgate), static_cast<__half*>(dup), n8);
+  NF4B_CUDA_TRY(launch_pdl(swiglu_bwd_kernel, dim3(unsigned((n8 + 255) / 256)), dim3(256),
+                           size_t(0), static_cast<cudaStream_t>(stream),
+                           static_cast<const __half*>(dout), static_cast<const __half*>(gate),
+                           static_cast<const __half*>(up), static_cast<__half*>(dgate),
+                           static_cast<__half*>(dup), n8));
   return launch_status("swiglu_bwd_kernel launch");
 }
 
@@ -464,8 +477,9 @@ extern "C" int nf4b_ce_fwd(const void* logits, const int64_t* labels, float* los
   if (rows == 0) return NF4B_OK;
   int st = check_device();
   if (st != NF4B_OK) return st;
-  ce_fwd_kernel<<<unsigned(rows), CE_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(logits), labels, loss, lse, vocab);
+  NF4B_CUDA_TRY(launch_pdl(ce_fwd_kernel, dim3(unsigned(rows)), dim3(CE_THREADS), size_t(0),
+                           static_cast<cudaStream_t>(stream), static_cast<const __half*>(logits),
+                           labels, loss, lse, vocab));
   return launch_status("ce_fwd_kernel launch");
 }
 
@@ -478,7 +492,8 @@ extern "C" int nf4b_ce_bwd(void* logits, const int64_t* labels, const float* lse
   if (rows == 0) return NF4B_OK;
   int st = check_device();
   if (st != NF4B_OK) return st;
-  ce_bwd_kernel<<<unsigned(rows), CE_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<__half*>(logits), labels, lse, gscale, vocab);
+  NF4B_CUDA_TRY(launch_pdl(ce_bwd_kernel, dim3(unsigned(rows)), dim3(CE_THREADS), size_t(0),
+                           static_cast<cudaStream_t>(stream), static_cast<__half*>(logits), labels,
+                           lse, gscale, vocab));
   return launch_status("ce_bwd_kernel launch");
 }
