@@ -22,9 +22,10 @@
 //   warp 1      TMEM allocation (512 columns) + single-thread tcgen05.mma issuer.
 //   warps 2-9   decode the packed tile in registers (nf4_decode.cuh) straight into the
 //               128B-swizzled fp16 operand layout (K-major forward, MN-major backward).
-//   warps 10-13 epilogue: tcgen05.ld of the finished accumulator -> fp16 -> global.
-// LoRA is one extra K=16 MMA ("slab") into the tile's accumulator: the rank-16 token
-// activations (X A^T or dY B, from lora.cu) against the scaled adapter weight.
+//   warps 10-17 epilogue: tcgen05.ld of the finished accumulator -> fp16 -> global.
+// LoRA is one extra K=16 MMA ("slab") into the tile's accumulator (a pair tile: one per
+// token half): the rank-16 token activations (X A^T or dY B, from lora.cu) against the scaled
+// adapter weight.
 //
 // Every pipeline wait is bounded (~2 s); on expiry the CTA raises an abort flag,
 // records the failure in g_gemm_error, and winds down without hanging the GPU.
