@@ -47,6 +47,10 @@ WORKLOAD = ("Qwen2.5-1.5B whole-model NF4 unpack sweep: 28 layers x {q 1536x1536
             "fp16 out")
 
 
+# Real tokens in each rank's batch of the QLoRA step: 4 rows x 512 at ~57 % real tokens.
+STEP_TOKENS_PER_RANK = 1170
+
+
 def _peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -195,12 +199,15 @@ class GemmPass:
         self.y = {o: torch.empty(n, o, device=dev, dtype=torch.float16) for o in (256, 1536, 8960)}
         self.dx = {k: torch.empty(n, k, device=dev, dtype=torch.float16) for k in (1536, 8960)}
         self.items = []
+        self.states = {}
         self.lora = {}
         bound = 1.0 / 1536 ** 0.5
         for li in range(layers):
             for pi, (name, out_f, in_f) in enumerate(QWEN_PROJ):
                 q, st = weights[li * len(QWEN_PROJ) + pi]
                 qs = _qstate(st, dev)
+                if li == 0:
+                    self.states[name] = st
                 lc = None
                 if name in LORA_ON:
                     a = ((torch.rand(16, in_f, generator=g, device=dev) * 2 - 1) * bound).half()
@@ -315,6 +322,69 @@ class GemmPass:
         stream = self.ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
         return sum(self._launch(it, fwd, bwd, lora, stream) for it in self.items)
 
+    def vs_cublas(self, reps=20):
+        """Each projection shape of layer 0 without the adapter, three ways, each `reps`
+        launches replayed from a CUDA graph: the fused kernel; the reference's composition on
+        the GPU -- this library's unpack kernel, then torch's fp16 F.linear (cuBLAS) for the
+        forward and matmul(dY, W) for the backward (solution/nf4.py:148-152; bitsandbytes
+        MatMul4Bit.backward); and a dense fp16 cuBLAS GEMM on the already-unpacked weight (what
+        an unquantised layer costs).  Speed-ups are times ratios (> 1: the fused kernel is
+        faster)."""
+        import torch
+        import torch.nn.functional as F
+        from stew_b200.nf4 import dequantize_nf4
+        out = {}
+
+        def graph_us(fn):
+            for _ in range(2):
+                fn()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(reps):
+                    fn()
+            graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            del graph
+            return e0.elapsed_time(e1) * 1e3 / reps
+
+        for item in self.items[:7]:
+            _, name, out_f, in_f, q, qs, _ = item
+            st = self.states[name]
+            W = dequantize_nf4(q, st)
+            x, dy = self.x[in_f], self.dy[out_f]
+            res = {}
+            for tag, fwd in (("fwd", True), ("bwd", False)):
+                def fused():
+                    s0 = self.ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+                    self._launch(item, fwd, not fwd, False, s0)
+                if fwd:
+                    def unfused():
+                        F.linear(x, dequantize_nf4(q, st))
+
+                    def dense():
+                        F.linear(x, W)
+                else:
+                    def unfused():
+                        torch.matmul(dy, dequantize_nf4(q, st))
+
+                    def dense():
+                        torch.matmul(dy, W)
+                t_f, t_u, t_d = graph_us(fused), graph_us(unfused), graph_us(dense)
+                fl = 2 * self.n * in_f * out_f
+                res[tag] = {"fused_us": round(t_f, 1), "unfused_us": round(t_u, 1), "dense_us": round(t_d, 1),
+                            "fused_tflops": round(fl / (t_f * 1e-6) / 1e12, 1),
+                            "dense_tflops": round(fl / (t_d * 1e-6) / 1e12, 1),
+                            "fused_vs_unfused": round(t_u / t_f, 3), "fused_vs_dense": round(t_d / t_f, 3)}
+            del W
+            out[f"{name} {out_f}x{in_f}"] = res
+        return out
+
     def per_shape(self, reps=20):
         """Each of the 7 projection shapes of layer 0 alone: forward (+ LoRA on q/v) and
         backward dX (+ the LoRA dX term and dA/dB on q/v), `reps` launches replayed from a
@@ -404,14 +474,16 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    steps = max(1, min(args.steps, 20))
-    warmup = max(1, min(args.warmup, 3))
+    # the caller's step counts as they are: a step is a 1-layer sample (~75 ms on 16 cores),
+    # so the default 50 + 5 steps take a few seconds
+    steps, warmup = args.steps, args.warmup
     cb = cpu_baseline(steps, warmup)
     line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "GB/s",
             "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": cb["ms_per_step"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "nf4 (u8) -> fp16, fp32 math", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "sample": cb["sample"]},
+            "config": {"workload": WORKLOAD, "sample": cb["sample"], "cpu_cores": cb["cores"],
+                       "l2": "host path: no GPU cache involved"},
             "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -445,7 +517,7 @@ def profile_step(full: bool = False):
     cfg = QwenConfig() if full else QwenConfig(layers=4, vocab=32768)
     model = QwenQLoRA(cfg, device="cuda", seed=0)
     trainer = QLoRATrainer(model)
-    tokens, lengths = synthetic_batch(vocab=cfg.vocab, seed=1000)
+    tokens, lengths = synthetic_batch(vocab=cfg.vocab, seed=1000, total=STEP_TOKENS_PER_RANK)
     for _ in range(2):
         trainer.step(tokens, lengths)
     torch.cuda.synchronize()
@@ -467,6 +539,8 @@ def main():
     ap.add_argument("--gemm-n", type=str, default="1170,2048,8192")
     ap.add_argument("--gemm-steps", type=int, default=5)
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-chunks", type=int, default=14,
+                    help="groups of matrices the end-to-end sweep pipelines over (copies overlap)")
     ap.add_argument("--step-steps", type=int, default=5)
     ap.add_argument("--no-step", action="store_true")
     ap.add_argument("--no-gemm", action="store_true")
@@ -524,18 +598,18 @@ def main():
             for tag, kw in (("fwd", dict(fwd=True, bwd=False, lora=False)),
                             ("bwd", dict(fwd=False, bwd=True, lora=False)),
                             ("fwd_bwd_lora", dict(fwd=True, bwd=True, lora=True))):
-                t = _timed(world, lambda: gp.run(**kw), args.gemm_steps, 2) / args.gemm_steps
+                t = _timed(world, lambda: gp.run(**kw), args.gemm_steps, 3) / args.gemm_steps
                 tf = gp.flops(**kw) / (t * 1e-3) / 1e12
                 res[tag] = {"ms_per_pass": round(t, 3), "tflops": round(tf, 1),
                             "frac_of_peak": round(tf / tc_peak, 3),
                             "frac_of_sustained_peak": round(tf / tc_sustained, 3)}
-            t = _timed(world, gp.run_grouped, args.gemm_steps, 2) / args.gemm_steps
+            t = _timed(world, gp.run_grouped, args.gemm_steps, 3) / args.gemm_steps
             tf = gp.flops(fwd=True, bwd=False, lora=False) / (t * 1e-3) / 1e12
             res["fwd_grouped"] = {"ms_per_pass": round(t, 3), "tflops": round(tf, 1),
                                   "frac_of_peak": round(tf / tc_peak, 3),
                                   "frac_of_sustained_peak": round(tf / tc_sustained, 3),
                                   "launches_per_pass": 4 * args.layers}
-            t = _timed(world, gp.run_grouped_bwd, args.gemm_steps, 2) / args.gemm_steps
+            t = _timed(world, gp.run_grouped_bwd, args.gemm_steps, 3) / args.gemm_steps
             tf = gp.flops(fwd=False, bwd=True, lora=False) / (t * 1e-3) / 1e12
             res["bwd_grouped"] = {"ms_per_pass": round(t, 3), "tflops": round(tf, 1),
                                   "frac_of_peak": round(tf / tc_peak, 3),
@@ -543,6 +617,7 @@ def main():
                                   "launches_per_pass": 4 * args.layers}
             res["launches_per_pass"] = gp.run(fwd=True, bwd=True, lora=True)
             res["per_shape"] = gp.per_shape()
+            res["vs_cublas"] = gp.vs_cublas()
             for shape in res["per_shape"].values():
                 for t in shape.values():
                     t["frac_of_peak"] = round(t["tflops"] / tc_peak, 3)
@@ -556,27 +631,30 @@ def main():
         from stew_b200.qlora_step import QLoRATrainer, QwenConfig, QwenQLoRA, step_flops, synthetic_batch
         model = QwenQLoRA(QwenConfig(), device="cuda", seed=0, weights=weights)
         trainer = QLoRATrainer(model, cuda_graph=True)
-        # the global batch: 4 rows per rank (seeds 1000 + r), dealt to the ranks by length so
-        # the step, which ends with the slowest rank, is not set by one long shard
-        from stew_b200.dp import balanced_shards
-        rows = [synthetic_batch(seed=1000 + r) for r in range(world)]
-        all_tok = torch.cat([t for t, _ in rows])
-        all_len = torch.cat([l for _, l in rows])
-        mine = balanced_shards(all_len.tolist(), world, 4)[rank]
+        # every rank its own batch of 4 right-padded rows x 512 (seed 1000 + rank) holding
+        # exactly 1,170 real tokens (57 % of the rows, the workload's figure), so each rank does
+        # the same work and the step time, which the slowest rank sets, measures scaling alone;
         # the row lengths travel with the batch on the host, as a data loader has them
-        tokens, lengths = all_tok[mine].contiguous(), all_len[mine].cpu()
-        real = torch.tensor([float(lengths.sum())], device="cuda")
+        tokens, lengths = synthetic_batch(seed=1000 + rank, total=STEP_TOKENS_PER_RANK)
+        lengths = lengths.cpu()
+        per_rank = torch.tensor([float(lengths.sum())], device="cuda")
         if world > 1:
             import torch.distributed as dist
-            dist.all_reduce(real)
-        t = _timed(world, lambda: trainer.step(tokens, lengths), args.step_steps, 2) / args.step_steps
+            gathered = [torch.zeros_like(per_rank) for _ in range(world)]
+            dist.all_gather(gathered, per_rank)
+            per_rank = torch.cat(gathered)
+        per_rank = [int(v) for v in per_rank.tolist()]
+        t = _timed(world, lambda: trainer.step(tokens, lengths), args.step_steps, 3) / args.step_steps
         fl = step_flops(model.cfg, int(lengths.sum()))
         step = {"workload": "Qwen2.5-1.5B QLoRA step: 28 layers, NF4 projections, LoRA r=16 on q/v, "
-                            "4 right-padded rows x 512 per rank (~57% real tokens, packed; the "
-                            "global batch's rows dealt to the ranks by length), fwd+bwd, "
-                            "LoRA-grad all-reduce, AdamW; the step replayed from one CUDA graph",
-                "ms_per_step": round(t, 3), "tokens_per_s": round(real.item() / (t * 1e-3), 1),
-                "real_tokens_per_step_all_ranks": int(real.item()),
+                            "4 right-padded rows x 512 per rank with 1,170 real tokens (57 %, "
+                            "uniform-random row lengths; packed), fwd+bwd, "
+                            + (f"LoRA-grad all-reduce in {trainer.buckets} layer buckets overlapping "
+                               "the backward, " if world > 1 else "")
+                            + "AdamW; the step replayed from one CUDA graph",
+                "ms_per_step": round(t, 3), "tokens_per_s": round(sum(per_rank) / (t * 1e-3), 1),
+                "real_tokens_per_step_all_ranks": sum(per_rank),
+                "real_tokens_per_rank": per_rank,
                 "allreduce_bytes": trainer.lora_grad_bytes(),
                 "nf4_gemm_tflops_in_step_rank0": round(fl["nf4_gemm"] / (t * 1e-3) / 1e12, 1),
                 "scaling": "weak (each rank its own 4 rows)"}
@@ -593,23 +671,17 @@ def main():
             parts = [q, st.absmax] + ([st.state2.absmax] if st.nested else [])
             host_in.append([(p, torch.empty(p.shape, dtype=p.dtype, pin_memory=True).copy_(p)) for p in parts])
         host_out = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in sweep.outputs]
-        h2d = sum(h.numel() * h.element_size() for parts in host_in for _, h in parts)
-        d2h = sum(h.numel() * h.element_size() for h in host_out)
-
-        def e2e_step():
-            for parts in host_in:
-                for dev_t, host_t in parts:
-                    dev_t.copy_(host_t, non_blocking=True)
-            sweep.run()
-            for dev_t, host_t in zip(sweep.outputs, host_out):
-                host_t.copy_(dev_t, non_blocking=True)
-
-        t = _timed(world, e2e_step, args.e2e_steps, 1) / args.e2e_steps
+        from stew_b200.sweep import PipelinedSweep
+        pipe = PipelinedSweep(weights, host_in, host_out, chunks=args.e2e_chunks)
+        assert pipe.algorithmic_bytes() == algo
+        t = _timed(world, pipe.run, args.e2e_steps, 3) / args.e2e_steps
         e2e = {"value": round(world * algo / (t * 1e-3) / 1e9, 2), "unit": "GB/s",
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(t, 2),
-               "path": "pinned host -> device copies, DequantSweep.run (nf4b_dequant_batched), "
-                       "device -> pinned host copies"}
-        del host_in, host_out
+               "h2d_bytes_per_step": pipe.h2d_bytes, "d2h_bytes_per_step": pipe.d2h_bytes,
+               "ms_per_step": round(t, 2), "chunks": len(pipe.groups),
+               "path": "pinned host -> device copies (one stream), PipelinedSweep: one "
+                       "nf4b_dequant_batched launch per group of matrices (a second stream), "
+                       "device -> pinned host copies (a third stream); groups overlap"}
+        del host_in, host_out, pipe
 
     if _lib.gemm_error_flag(reset=True) != 0:
         raise RuntimeError("a GEMM pipeline wait timed out during the bench")

@@ -127,7 +127,8 @@ int nf4b_linear_bwd_dx(const void* dy, const uint8_t* packed, const nf4b_qstate*
  *               nf4b_linear_work_bytes(n, in, out, backward) bytes (0 = no split for
  *               this shape on the current device: any pointer, or NULL, will do);
  *               its leading counter words must be zero before the first call and every
- *               successful call leaves them zero, so allocate it zeroed once and reuse it.
+ *               call leaves them zero -- also one whose pipeline wait ran out (the last
+ *               CTA to leave a launch clears them) -- so allocate it zeroed once and reuse it.
  *               Calls that may run concurrently (different streams) need distinct
  *               workspaces.  work == NULL runs unsplit.
  *   work_bytes  size of `work`; smaller than required -> NF4B_ERR_INVALID_ARG.
@@ -227,7 +228,10 @@ int nf4b_lora_grads_group(const nf4b_lora_grads_item* items, int32_t n_items, vo
  * NF4B_ERR_UNSUPPORTED with a message in nf4b_last_error().  All calls share the
  * array, so calls that overlap on the GPU race; each call writes all it reads.  The
  * first call on a device looks up the array's device address; make that first call
- * before any stream capture.  No counterpart in the reference.  */
+ * before any stream capture.  The address is cached for the life of the process: after a
+ * cudaDeviceReset (or a reset of the primary context) the library's module is loaded
+ * again and this entry point must not be used on that device any more.  No counterpart in
+ * the reference.  */
 #define NF4B_NOALLOC_SCRATCH_BYTES (8 << 20)
 int nf4b_lora_grads_noalloc(const void* x, const void* dy, const void* xa, const void* dyb,
                             float scale, float* da, float* db, int64_t n, int64_t in_features,
@@ -255,6 +259,13 @@ int nf4b_quantize(const void* w, int32_t in_dtype, int64_t numel, int32_t blocks
  * when a pipeline wait ran out of time (the kernel then ends early instead of
  * hanging).  0 = no timeout since the last reset.  Synchronous.  */
 int nf4b_gemm_error_flag(int* value, int reset);
+
+/* Test hook for the split-K bookkeeping.  Arms a one-shot fault: the next fused-GEMM launch
+ * of this process that splits K has work unit `unit` skip its ticket, as a K range that gave
+ * up in its main loop would (that tile's output is then not written and the error flag reads
+ * 4).  The launch still leaves the workspace's counters zero, so the call after it is correct.
+ * No GPU fault is involved.  No counterpart in the reference.  */
+int nf4b_test_drop_split_ticket(int32_t unit);
 
 /* Launch geometry of the fused GEMMs on the current device: *sms = SMs (one persistent CTA
  * each), *pair_slots = 2-CTA clusters that can be resident at once (0 when the device runs

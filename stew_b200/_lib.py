@@ -114,6 +114,7 @@ SIGNATURES = {
     "nf4b_quantize": (c_int32, [c_void_p, c_int32, c_int64, c_int32, c_void_p, c_void_p, c_void_p,
                                 c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "nf4b_gemm_error_flag": (c_int32, [ctypes.POINTER(c_int32), c_int32]),
+    "nf4b_test_drop_split_ticket": (c_int32, [c_int32]),
     "nf4b_gemm_geometry": (c_int32, [ctypes.POINTER(c_int32), ctypes.POINTER(c_int32)]),
     "nf4b_status_string": (ctypes.c_char_p, [c_int32]),
     "nf4b_last_error": (ctypes.c_char_p, []),

@@ -29,6 +29,7 @@
 //
 // Every pipeline wait is bounded (~2 s); on expiry the CTA raises an abort flag,
 // records the failure in g_gemm_error, and winds down without hanging the GPU.
+#include <atomic>
 #include <cstdlib>
 #include <mutex>
 #include <type_traits>
@@ -84,14 +85,17 @@ struct Smem {
 static_assert(Smem<false>::ALLOC <= 232448 && Smem<true>::ALLOC <= 232448, "shared memory budget");
 
 // Split-K workspace: a fixed counter region (arrivals at [0, G_SPLIT_MAX_TILES), finished
-// partials at [G_SPLIT_MAX_TILES, 2 * G_SPLIT_MAX_TILES)), then the fp32 partial tiles.  The
-// region does not depend on the launch's shape, so one zeroed workspace serves any sequence
-// of calls on a stream.
+// partials at [G_SPLIT_MAX_TILES, 2 * G_SPLIT_MAX_TILES), the launch's exit count at
+// G_SPLIT_EXIT, padded to 256 B so the partial tiles keep whole 128-byte lines), then the
+// fp32 partial tiles.  The region does not depend on the launch's shape, so one zeroed
+// workspace serves any sequence of calls on a stream: the last CTA to leave a launch clears
+// every counter the launch used, also when a range gave up before taking its ticket.
 constexpr int G_SPLIT_MAX_TILES = 512;
+constexpr int G_SPLIT_EXIT = 2 * G_SPLIT_MAX_TILES;
 // Tokens of one CTA's fp32 partial tile: the accumulator columns of a tile.
 template <bool PAIR>
 constexpr int acc_tokens() { return PAIR ? G_PAIR_TILE_N : G_ACC_COLS; }
-constexpr int64_t G_SPLIT_CNT_BYTES = 2 * G_SPLIT_MAX_TILES * 4;
+constexpr int64_t G_SPLIT_CNT_BYTES = 2 * G_SPLIT_MAX_TILES * 4 + 256;
 
 // One NF4 weight of a launch.  A forward launch may carry up to G_MAX_W weights that share
 // the activation X (q/k/v, gate/up): their 128-row tiles are numbered one after the other.
@@ -127,7 +131,9 @@ struct GemmArgs {
   uint32_t k16;           // 1 << 16 (a run-time multiplier for the decode's shifts)
   int32_t tile_n;         // tokens per tile: 256 or 128 (single CTAs), 512 (pairs)
   float* ws_part;         // split-K: fp32 partial tiles [tiles][splits][256][128]
-  int32_t* ws_cnt;        // split-K: per-tile counters [2][G_SPLIT_MAX_TILES], zero between launches
+  int32_t* ws_cnt;        // split-K: per-tile counters [2][G_SPLIT_MAX_TILES] + exit count, zero
+                          // between launches
+  int32_t drop_ticket_unit;  // test hook: this work unit skips its ticket (-1: none)
 };
 
 __device__ int g_gemm_error;
@@ -840,14 +846,18 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       // tickets, i.e. are past their main loops, so the wait cannot depend on unscheduled work.
       int ticket = nparts;
       if (split) {
-        if (leader) s_ticket[lt & 1] = atomicAdd(g.ws_cnt + ctile, 1);
+        // the test hook's unit behaves as a range that gave up before its ticket: it takes
+        // none and writes nothing, so no range of its tile sums the partials
+        if (leader) s_ticket[lt & 1] = u == g.drop_ticket_unit ? -1 : atomicAdd(g.ws_cnt + ctile, 1);
         epi_bar_sync();
         ticket = s_ticket[lt & 1];
       }
       // partial tiles are column-major [tokens][128 rows]: for one token the 32 lanes of a
       // warp (32 consecutive rows) touch one 128-byte line
       const float* part0 = g.ws_part + int64_t(ctile) * (nparts + 1) * (G_M * ACC_T) + prow;
-      if (ticket < nparts) {
+      if (ticket < 0) {
+        if (leader) atomicExch(&g_gemm_error, 4);
+      } else if (ticket < nparts) {
         float* dst = const_cast<float*>(part0) + int64_t(wu.split) * (G_M * ACC_T);
         for (int c0 = 32 * grp; c0 < tc.tn; c0 += 64) {
           uint32_t acc[32];
@@ -963,6 +973,21 @@ __global__ void __launch_bounds__(G_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (SPLIT && threadIdx.x == 0) {
+    // the last CTA to get here clears the counters of every tile of the launch (the last
+    // range of a tile has normally done so already; a range that gave up may have left its
+    // tile's counts behind) and the exit count itself
+    __threadfence();
+    if (atomicAdd(g.ws_cnt + G_SPLIT_EXIT, 1) == int(gridDim.x) - 1) {
+      const int ctiles = g.m_tiles * g.n_tiles * (PAIR ? 2 : 1);
+      for (int i = 0; i < ctiles; ++i) {
+        g.ws_cnt[i] = 0;
+        g.ws_cnt[G_SPLIT_MAX_TILES + i] = 0;
+      }
+      g.ws_cnt[G_SPLIT_EXIT] = 0;
+      __threadfence();
+    }
+  }
   // a pair: neither CTA leaves (or frees TMEM) while the other may still touch its shared
   // memory or barriers
   if (PAIR) cluster_sync_all();
@@ -1230,6 +1255,10 @@ static int launch_variant(unsigned grid, const CUtensorMap (&ta)[G_MAX_W], const
   return NF4B_OK;
 }
 
+// Test hook (nf4b_test_drop_split_ticket): the work unit that the next split-K launch of this
+// process skips the ticket of; -1 when unarmed.
+static std::atomic<int> g_drop_ticket_unit{-1};
+
 // One persistent CTA per SM, or one 2-CTA cluster per pair slot (at most one per work unit).
 template <bool BWD>
 static int launch_gemm(const GemmPlan& p, const CUtensorMap (&ta)[G_MAX_W], const CUtensorMap (&tw)[G_MAX_W],
@@ -1249,6 +1278,7 @@ static int launch_gemm(const GemmPlan& p, const CUtensorMap (&ta)[G_MAX_W], cons
   g.nk = q.nk;
   g.k16 = 1u << 16;
   g.tile_n = q.tile_n;
+  g.drop_ticket_unit = q.splits > 1 ? g_drop_ticket_unit.exchange(-1) : -1;
   const int64_t units = q.tiles * q.splits;
   const int64_t slots = units < q.slots ? units : q.slots;
   const unsigned grid = unsigned(q.pair ? 2 * slots : slots);
@@ -1541,6 +1571,12 @@ extern "C" int nf4b_gemm_error_flag(int* value, int reset) {
     const int zero = 0;
     NF4B_CUDA_TRY(cudaMemcpyToSymbol(g_gemm_error, &zero, sizeof(int)));
   }
+  return NF4B_OK;
+}
+
+extern "C" int nf4b_test_drop_split_ticket(int32_t unit) {
+  NF4B_RETURN_IF(unit < 0, NF4B_ERR_INVALID_ARG);
+  g_drop_ticket_unit.store(unit);
   return NF4B_OK;
 }
 

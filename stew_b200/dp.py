@@ -11,6 +11,8 @@ G-rank step equals a 1-rank step over the concatenated batches.
 """
 from __future__ import annotations
 
+import math
+
 import torch
 import torch.distributed as dist
 
@@ -86,6 +88,107 @@ def allreduce_lora_grads_device(params, local_labels: torch.Tensor, group=None) 
     total = count.clamp_min(1.0)
     torch._foreach_div_(grads, total.reshape(()))
     return total
+
+
+class BucketedGradAllReduce:
+    """The LoRA-gradient all-reduce in buckets of consecutive layers, each launched from the
+    backward as soon as its gradients are complete -- layers finish in reverse order (27 ... 0),
+    so the exchange of the later layers' bucket overlaps the backward of the earlier layers.
+
+    Each bucket is one flat fp32 buffer (allocated once, so a CUDA graph replays the same
+    memory); a post-accumulate-grad hook on every adapter parameter counts the bucket's
+    gradients and, with the last one, copies them into the buffer and all-reduces it on a
+    side stream (which waits for the backward's stream up to that point).  The bucket that
+    completes last (the one holding layer 0) also carries this rank's labelled-token count.
+    `finish()` joins the side stream, divides every gradient by the global count (the loss
+    normalisation of solution/head_loss.py:164-169, taken over all ranks) and writes the
+    results back into .grad -- the same values as allreduce_lora_grads_device.
+
+    param_groups: the adapter parameters layer by layer (layer 0 first)."""
+
+    def __init__(self, param_groups, group=None, n_buckets: int = 4):
+        self.group = group
+        groups = [list(g) for g in param_groups if len(g)]
+        per = max(1, math.ceil(len(groups) / max(1, n_buckets)))
+        self.buckets = [[p for g in groups[i:i + per] for p in g] for i in range(0, len(groups), per)]
+        dev = self.buckets[0][0].device
+        # layer 0's bucket is the last to complete: it carries the count
+        self.flat = [torch.zeros(sum(p.numel() for p in b) + (1 if i == 0 else 0), dtype=torch.float32,
+                                 device=dev) for i, b in enumerate(self.buckets)]
+        self._where = {}
+        for i, b in enumerate(self.buckets):
+            for p in b:
+                self._where[p] = i
+        self._ready = [0] * len(self.buckets)
+        self._launched = [False] * len(self.buckets)
+        self.count = None
+        self.stream = torch.cuda.Stream(dev) if dev.type == "cuda" else None
+        self._handles = [p.register_post_accumulate_grad_hook(self._hook) for b in self.buckets for p in b]
+
+    def __len__(self):
+        return len(self.buckets)
+
+    def _hook(self, p):
+        i = self._where[p]
+        self._ready[i] += 1
+        if self._ready[i] == len(self.buckets[i]):
+            self._launch(i)
+
+    def _launch(self, i):
+        b, flat = self.buckets[i], self.flat[i]
+        n = flat.numel() - (1 if i == 0 else 0)
+        if self.stream is not None:
+            self.stream.wait_stream(torch.cuda.current_stream(flat.device))
+            ctx = torch.cuda.stream(self.stream)
+        else:
+            ctx = _NullCtx()
+        with ctx:
+            torch.cat([p.grad.reshape(-1).float() for p in b], out=flat[:n])
+            if i == 0:
+                if self.count is None:
+                    raise RuntimeError("BucketedGradAllReduce: set .count before the backward")
+                flat[n:].copy_(self.count.reshape(1))
+            if _world(self.group) > 1:
+                dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group)
+        self._launched[i] = True
+
+    def finish(self) -> torch.Tensor:
+        """Join the exchange, normalise by the global labelled-token count, write the grads.
+        Returns the global count (device tensor)."""
+        for i, b in enumerate(self.buckets):  # a bucket whose grads never came: zeros
+            if not self._launched[i]:
+                for p in b:
+                    if p.grad is None:
+                        p.grad = torch.zeros_like(p)
+                self._launch(i)
+        if self.stream is not None:
+            torch.cuda.current_stream(self.flat[0].device).wait_stream(self.stream)
+        total = self.flat[0][-1:].clamp_min(1.0)
+        grads, views = [], []
+        for i, b in enumerate(self.buckets):
+            n = self.flat[i].numel() - (1 if i == 0 else 0)
+            body = self.flat[i][:n]
+            body.div_(total)
+            for p, v in zip(b, body.split([p.numel() for p in b])):
+                grads.append(p.grad)
+                views.append(v.view_as(p))
+        torch._foreach_copy_(grads, views)
+        self._ready = [0] * len(self.buckets)
+        self._launched = [False] * len(self.buckets)
+        return total
+
+    def remove(self):
+        for h in self._handles:
+            h.remove()
+        self._handles = []
+
+
+class _NullCtx:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
 
 
 def balanced_shards(lengths, world: int, rows_per_rank: int):

@@ -17,8 +17,7 @@ import ctypes
 import torch
 
 from . import _lib
-from .nf4 import (_qstate, _stream, _supported, _workspace, _workspace_bytes, linear_backward_dx,
-                  linear_forward)
+from .nf4 import _qstate, _stream, _supported, _workspace, _workspace_bytes
 
 LORA_RANK = 16
 
@@ -111,36 +110,6 @@ class NF4LoraFunction(torch.autograd.Function):
         if ctx.has_bias and ctx.needs_input_grad[3]:
             dbias = dy.float().sum(0).to(ctx.param_dtypes[2])
         return dx, None, None, dbias, da, db, None
-
-
-def _bwd_dx(dy, Bv, st, lora=None, dyb=None):
-    """dX of one projection (+ the adapter's dX term when lora = (a16, b16, scaling))."""
-    out_f, in_f = int(st.shape[0]), int(st.shape[1])
-    n = dy.shape[0]
-    dev = dy.device
-    dx = torch.empty(n, in_f, dtype=torch.float16, device=dev)
-    qs = _qstate(st, dev)
-    lc = None if lora is None else _lora_c(lora[0], lora[1], lora[2])
-    work, wbytes = _workspace(dev, n, in_f, out_f, True)
-    _lib.check(_lib.lib().nf4b_linear_bwd_dx_ws(
-        dy.data_ptr(), Bv.data_ptr(), ctypes.byref(qs), None if lc is None else ctypes.byref(lc),
-        None if dyb is None else dyb.data_ptr(), dx.data_ptr(), n, in_f, out_f, work, wbytes,
-        _stream(dev)), "nf4b_linear_bwd_dx_ws")
-    return dx
-
-
-def _lora_weight_grads(x2, dy, xa, dyb, scaling, in_f, out_f):
-    dev = dy.device
-    n = dy.shape[0]
-    L = _lib.lib()
-    da32 = torch.empty(LORA_RANK, in_f, dtype=torch.float32, device=dev)
-    db32 = torch.empty(out_f, LORA_RANK, dtype=torch.float32, device=dev)
-    wb = int(L.nf4b_lora_grads_work_bytes(n, in_f, out_f, LORA_RANK))
-    work = torch.empty(max(wb, 16) // 4 + 4, dtype=torch.float32, device=dev)
-    _lib.check(L.nf4b_lora_grads(x2.data_ptr(), dy.data_ptr(), xa.data_ptr(), dyb.data_ptr(), scaling,
-                                 da32.data_ptr(), db32.data_ptr(), work.data_ptr(), n, in_f, out_f,
-                                 LORA_RANK, _stream(dev)), "nf4b_lora_grads")
-    return da32, db32
 
 
 class GroupedNF4Function(torch.autograd.Function):
@@ -283,11 +252,16 @@ def grouped_projection(x, modules):
 
 
 def nf4_lora_linear(x, packed, st, lora_a, lora_b, scaling, bias=None):
-    """Functional entry: fused when the envelope allows, else base + adapter composed
-    from the fused base GEMM and plain torch for the adapter."""
+    """Functional entry: the fused op inside its envelope (fp16 x, feature counts that are
+    multiples of 64, a rank-16 adapter); outside it the base projection (MatMul4Bit, which
+    warns when it is not fused either) plus the adapter in torch, as peft composes it, with a
+    one-time warning."""
     if _supported(packed, st) and _fusable(x, st, lora_a, lora_b):
         return NF4LoraFunction.apply(x, packed, st, bias, lora_a, lora_b, scaling)
-    from .nf4 import matmul_4bit
+    from .nf4 import _warn_once, matmul_4bit
+    _warn_once(f"lora:{x.dtype}:{tuple(lora_a.shape)}",
+               f"adapter {tuple(lora_a.shape)} on {x.dtype} input is outside the fused envelope: "
+               "base projection + torch adapter")
     y = matmul_4bit(x, packed.t(), st, bias=bias)
     return y + (x @ lora_a.to(x.dtype).t()) @ lora_b.to(x.dtype).t() * scaling
 
@@ -366,11 +340,3 @@ def patch_peft_lora():
     forward._stew_b200 = True
     cls.forward = forward
 
-
-def linear_forward_unfused(x, packed, st, bias=None):
-    """The base layer alone (fused unpack + GEMM)."""
-    return linear_forward(x, packed.view(-1, 1), st, bias)
-
-
-def linear_backward_unfused(dy, packed, st):
-    return linear_backward_dx(dy, packed.view(-1, 1), st)

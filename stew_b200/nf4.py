@@ -10,16 +10,25 @@ Mirrors evilandangry/stew solution/nf4.py name for name:
                                                and backward (fused nf4b_linear_bwd_dx)
 
 plus `MatMul4Bit` / `matmul_4bit`, the same autograd contract for callers that do not
-have bitsandbytes.  Differences from the reference, by design:
+have bitsandbytes.  Behaviour:
   * the forward and the input-gradient backward never write the fp16 weight to HBM:
-    the unpack runs inside the tensor-core GEMM;
-  * a kernel error raises (no silent `_BROKEN` latch, no CPU fallback); inputs outside
-    the envelope are still handed to the original bitsandbytes function, as nf4.py:112.
+    the unpack runs inside the tensor-core GEMM (fp16 activations, feature counts that
+    are multiples of 64, 16-byte aligned rows -- the fused envelope, `_fused_ok`);
+  * activations outside the fused envelope (bf16/fp32 under another autocast, odd
+    feature counts) take the reference's own composition, the unpack kernel followed by
+    F.linear / matmul (nf4.py:148-152), with a one-time warning naming the cause;
+  * the patched bitsandbytes entry points keep the reference's latch (nf4.py:104-112):
+    an error inside the fast path sets `_BROKEN`, warns once, and that call and every
+    later one go to bitsandbytes' original function ("never break training because of
+    the speed-up");
+  * the library itself must be present: `apply()` loads it first and raises when it is
+    missing, and `MatMul4Bit` / `dequantize_nf4` raise; there is no CPU fallback.
 """
 from __future__ import annotations
 
 import ctypes
 import sys
+import warnings
 
 import torch
 
@@ -27,6 +36,14 @@ from . import _lib, codebooks
 from ._lib import NF4Unsupported, QStateC
 
 _CODE: dict = {}
+_BROKEN = False     # the patched bitsandbytes functions fell back for good (nf4.py:25-26)
+_WARNED: set = set()
+
+
+def _warn_once(key: str, msg: str) -> None:
+    if key not in _WARNED:
+        _WARNED.add(key)
+        warnings.warn(f"stew_b200: {msg}", RuntimeWarning, stacklevel=3)
 
 
 def _code(device) -> torch.Tensor:
@@ -142,13 +159,24 @@ def _workspace_bytes(device, need: int):
 
 
 def _fused_ok(A: torch.Tensor, out_f: int, in_f: int) -> bool:
+    """The fused kernels' envelope: fp16 activations, feature counts that are multiples
+    of 64 (one K stage), 16-byte aligned rows."""
     return (A.dtype == torch.float16 and in_f % 64 == 0 and out_f % 64 == 0
             and A.data_ptr() % 16 == 0)
 
 
+def _unfused_reason(A: torch.Tensor, out_f: int, in_f: int) -> str:
+    if A.dtype != torch.float16:
+        return f"{A.dtype} activations"
+    if in_f % 64 or out_f % 64:
+        return f"feature counts {out_f}x{in_f} not multiples of 64"
+    return "activations not 16-byte aligned"
+
+
 def linear_forward(A: torch.Tensor, Bv: torch.Tensor, st, bias=None) -> torch.Tensor:
-    """Y = A W^T (+ bias) for the NF4 weight (Bv, st): the fused tensor-core kernel for
-    fp16 inputs, else the reference's composition (unpack, then F.linear), nf4.py:148-152."""
+    """Y = A W^T (+ bias) for the NF4 weight (Bv, st): the fused tensor-core kernel inside
+    its envelope (`_fused_ok`); outside it, the reference's composition (the unpack kernel,
+    then F.linear, nf4.py:148-152) with a one-time warning."""
     out_f, in_f = int(st.shape[0]), int(st.shape[1])
     if _fused_ok(A, out_f, in_f) and (bias is None or bias.dtype == torch.float16):
         x = A.reshape(-1, in_f).contiguous()
@@ -162,6 +190,8 @@ def linear_forward(A: torch.Tensor, Bv: torch.Tensor, st, bias=None) -> torch.Te
                 None, y.data_ptr(), x.shape[0], in_f, out_f, work, wbytes, _stream(A.device)),
                 "nf4b_linear_fwd_ws")
         return y.reshape(*A.shape[:-1], out_f)
+    why = _unfused_reason(A, out_f, in_f) if not _fused_ok(A, out_f, in_f) else "a non-fp16 bias"
+    _warn_once("fwd:" + why, f"{why}: the forward runs the unpack kernel + F.linear (not fused)")
     weight = dequantize_nf4(Bv, st).to(A.dtype)
     return torch.nn.functional.linear(A, weight, bias)
 
@@ -179,6 +209,8 @@ def linear_backward_dx(grad_output: torch.Tensor, Bv: torch.Tensor, st) -> torch
                 dy.data_ptr(), Bv.data_ptr(), ctypes.byref(qs), None, None, dx.data_ptr(),
                 dy.shape[0], in_f, out_f, work, wbytes, _stream(dy.device)), "nf4b_linear_bwd_dx_ws")
         return dx.reshape(*grad_output.shape[:-1], in_f)
+    why = _unfused_reason(grad_output, out_f, in_f)
+    _warn_once("bwd:" + why, f"{why}: the backward runs the unpack kernel + matmul (not fused)")
     weight = dequantize_nf4(Bv, st).to(grad_output.dtype)
     return torch.matmul(grad_output, weight)
 
@@ -233,6 +265,15 @@ def matmul_4bit(A, B, quant_state, out=None, bias=None):
 
 
 # ------------------------------------------------------------------ bitsandbytes patches
+def _latch(err: Exception) -> None:
+    """The reference's `_BROKEN` latch (nf4.py:104-112, :147-150): after the first error in
+    a patched fast path, this process uses bitsandbytes' original functions."""
+    global _BROKEN
+    _BROKEN = True
+    _warn_once("broken", f"fast path failed ({err!r}); bitsandbytes' original functions are "
+                         "used from now on")
+
+
 def patch_bnb_dequant():
     """Rebind bitsandbytes.functional.dequantize_4bit (and every bitsandbytes module
     attribute aliasing it, nf4.py:116-119) to the sm_100a unpack; then patch MatMul4Bit."""
@@ -244,10 +285,13 @@ def patch_bnb_dequant():
 
     def dequantize_4bit(A, quant_state=None, absmax=None, out=None, blocksize=64,
                         quant_type="fp4"):
-        if absmax is None and out is None and _supported(A, quant_state):
-            out_ = dequantize_nf4(A, quant_state)
-            # bitsandbytes' rule: a (1, n) packed view gets the result transposed back
-            return out_.t() if A.shape[0] == 1 else out_
+        if not _BROKEN and absmax is None and out is None and _supported(A, quant_state):
+            try:
+                out_ = dequantize_nf4(A, quant_state)
+                # bitsandbytes' rule: a (1, n) packed view gets the result transposed back
+                return out_.t() if A.shape[0] == 1 else out_
+            except Exception as e:  # noqa: BLE001  (nf4.py:110-111)
+                _latch(e)
         return orig(A, quant_state, absmax, out, blocksize, quant_type)
 
     dequantize_4bit._stew_b200 = True
@@ -273,13 +317,20 @@ def _patch_matmul4bit_forward():
     orig_b = cls.backward
 
     def forward(ctx, A, B, out=None, bias=None, quant_state=None):
-        if _forward_guard(A, B, out, quant_state):
-            return _forward_impl(ctx, A, B, bias, quant_state)
+        if not _BROKEN and _forward_guard(A, B, out, quant_state):
+            try:
+                return _forward_impl(ctx, A, B, bias, quant_state)
+            except Exception as e:  # noqa: BLE001  (nf4.py:150-151)
+                _latch(e)
+                ctx._stew_b200 = False
         return orig_f(ctx, A, B, out, bias, quant_state)
 
     def backward(ctx, grad_output):
-        if getattr(ctx, "_stew_b200", False):
-            return _backward_impl(ctx, grad_output)
+        if not _BROKEN and getattr(ctx, "_stew_b200", False):
+            try:
+                return _backward_impl(ctx, grad_output)
+            except Exception as e:  # noqa: BLE001  (same latch; ctx holds bitsandbytes' fields)
+                _latch(e)
         return orig_b(ctx, grad_output)
 
     forward._stew_b200 = True

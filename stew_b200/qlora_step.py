@@ -47,7 +47,9 @@ class QwenConfig:
     mlp_token_budget: int | None = None
 
 
-MLP_SAVED_SHARE = 0.63  # share of a layer's saved activations that recomputing gate/up removes
+# Fraction of one layer's kept activations that belong to the MLP's gate/up/SwiGLU block,
+# i.e. what a layer that recomputes that block in its backward stops keeping.
+MLP_SAVED_SHARE = 0.63
 
 
 def mlp_recompute_layers(n_tokens: int, layers: int, budget: int | None) -> int:
@@ -232,12 +234,27 @@ class QwenQLoRA(torch.nn.Module):
 
 
 def synthetic_batch(batch: int = 4, seq: int = 512, vocab: int = 151936, mean_frac: float = 0.57,
-                    seed: int = 0, device="cuda"):
+                    seed: int = 0, device="cuda", total: int | None = None):
     """4 right-padded rows of 512 with uniform-random real lengths averaging 57% of the row
-    (about 1170 real tokens), token ids uniform over the vocabulary."""
+    (about 1170 real tokens), token ids uniform over the vocabulary.  `total`: the drawn
+    lengths are then shifted, row by row and within [lo, seq], until they sum to exactly
+    `total` real tokens (so every data-parallel rank can get the same amount of work)."""
     g = torch.Generator().manual_seed(seed)
     lo, hi = int(seq * (2 * mean_frac - 1.0)), seq
     lengths = torch.randint(lo, hi + 1, (batch,), generator=g)
+    if total is not None:
+        if not batch * lo <= total <= batch * hi:
+            raise ValueError(f"total {total} outside [{batch * lo}, {batch * hi}]")
+        lens = [int(v) for v in lengths]
+        while sum(lens) != total:
+            diff = total - sum(lens)
+            step = 1 if diff > 0 else -1
+            share = max(1, abs(diff) // batch)
+            for i in range(batch):
+                room = (hi - lens[i]) if step > 0 else (lens[i] - lo)
+                d = min(share, room, abs(total - sum(lens)))
+                lens[i] += step * d
+        lengths = torch.tensor(lens, dtype=lengths.dtype)
     tokens = torch.randint(0, vocab, (batch, seq), generator=g)
     tokens[torch.arange(seq)[None, :] >= lengths[:, None]] = 0
     return tokens.to(device), lengths.to(device)
@@ -253,31 +270,52 @@ class QLoRATrainer:
     The capture's warm-up steps are undone (adapters and optimizer state restored), so every
     call is exactly one optimizer step."""
 
-    def __init__(self, model: QwenQLoRA, lr: float = 2e-4, group=None, cuda_graph: bool = False):
+    def __init__(self, model: QwenQLoRA, lr: float = 2e-4, group=None, cuda_graph: bool = False,
+                 buckets: int = 4):
         self.model = model
         self.params = model.lora_parameters()
         self.cuda_graph = cuda_graph
+        # data parallel: the LoRA-grad all-reduce in `buckets` groups of layers, each launched
+        # from the backward as soon as its layers' gradients are complete (dp.BucketedGradAllReduce)
+        self._reducer = None
+        if dp._world(group) > 1 and buckets > 0:
+            layer_params = [[p for p in layer.parameters() if p.requires_grad] for layer in model.layers]
+            self._reducer = dp.BucketedGradAllReduce(layer_params, group, n_buckets=buckets)
+        self.buckets = len(self._reducer) if self._reducer is not None else 0
         # fused: one kernel for all adapters (the multi-tensor form was ~0.9 ms per step)
         self.opt = torch.optim.AdamW(self.params, lr=lr, weight_decay=0.0, capturable=cuda_graph,
                                      fused=True)
         self.group = group
         self._graph = None
         self._key = None
+        # one side stream for every capture's warm-up: per-stream state keyed by the stream
+        # (the GEMMs' split-K workspace) is then created once, not once per re-capture
+        self._side = None
 
     def _eager(self, pb):
         loss_sum = self.model.forward_packed(pb)
-        loss_sum.backward()
-        total = dp.allreduce_lora_grads(self.params, pb.n_labels, self.group)
+        if self._reducer is not None:
+            self._reducer.count = torch.full((1,), float(pb.n_labels), device=pb.ids.device)
+            loss_sum.backward()
+            total = float(self._reducer.finish())
+        else:
+            loss_sum.backward()
+            total = dp.allreduce_lora_grads(self.params, pb.n_labels, self.group)
         self.opt.step()
         self.opt.zero_grad(set_to_none=True)
         return loss_sum.detach(), total
 
     def _graph_body(self):
         loss = self.model.forward_packed(self._pb)
+        if self._reducer is not None:
+            self._reducer.count = self._n_lab
         loss.backward()
         # keep no reference to this autograd graph: a later capture must not reuse its nodes
         self._loss = loss.detach()
-        self._total = dp.allreduce_lora_grads_device(self.params, self._n_lab, self.group)
+        if self._reducer is not None:
+            self._total = self._reducer.finish()
+        else:
+            self._total = dp.allreduce_lora_grads_device(self.params, self._n_lab, self.group)
         self.opt.step()
 
     def _capture(self, pb):
@@ -289,7 +327,9 @@ class QLoRATrainer:
         saved_p = [p.detach().clone() for p in self.params]
         saved_s = {p: {k: v.clone() for k, v in st.items() if torch.is_tensor(v)}
                    for p, st in self.opt.state.items()}
-        side = torch.cuda.Stream(dev)
+        if self._side is None:
+            self._side = torch.cuda.Stream(dev)
+        side = self._side
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
             for _ in range(2):  # lazy state (optimizer moments, library handles) before capture

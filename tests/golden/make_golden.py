@@ -32,7 +32,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 from oracle import nf4_oracle as O  # noqa: E402
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("STEW_REFERENCE")
+if not REF:
+    sys.exit("usage: make_golden.py <path to the reference checkout> (or set STEW_REFERENCE)")
 
 # (name, shape, blocksize, nested, out dtype, store full arrays?, input kind)
 CASES = [

@@ -16,6 +16,12 @@ GOLDEN_DIR = os.path.join(HERE, "golden")
 # GEMM tolerance: max |y - ref| / max |ref| over the output, ref = fp64 product of the
 # reference-dequantised weights (fp32-accumulated fp16 GEMM + one fp16 output rounding).
 GEMM_MAX_REL_ERR = 2e-3
+# Elementwise form of the same bound: max |y - ref| / |ref| over every entry whose |ref| is
+# at least ELEM_FLOOR of max |ref| (below it, fp32 accumulation error of a near-cancelling
+# sum dominates the entry's own size), so one bad tile of small values cannot hide behind
+# the output's largest entry.
+ELEM_REL_ERR = 2e-3
+ELEM_FLOOR = 0.05
 
 
 def golden():
@@ -84,3 +90,20 @@ def seeded_weight(shape, seed, device="cpu"):
 def max_rel_err(y: torch.Tensor, ref: torch.Tensor) -> float:
     ref = ref.double()
     return float((y.double() - ref).abs().max() / ref.abs().max().clamp_min(1e-30))
+
+
+def elem_rel_err(y: torch.Tensor, ref: torch.Tensor, floor: float = ELEM_FLOOR) -> float:
+    """max |y - ref| / |ref| over the entries with |ref| >= floor * max |ref|."""
+    ref = ref.double()
+    a = ref.abs()
+    keep = a >= floor * a.max()
+    if not bool(keep.any()):
+        return 0.0
+    return float(((y.double() - ref).abs()[keep] / a[keep]).max())
+
+
+def assert_gemm_close(y: torch.Tensor, ref: torch.Tensor, what: str = "") -> None:
+    """Both GEMM bounds: max-normalised and elementwise above the floor."""
+    m, e = max_rel_err(y, ref), elem_rel_err(y, ref)
+    assert m <= GEMM_MAX_REL_ERR, f"{what} max-normalised error {m:.3e}"
+    assert e <= ELEM_REL_ERR, f"{what} elementwise error {e:.3e} (|ref| >= {ELEM_FLOOR} max)"

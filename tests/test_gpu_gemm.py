@@ -3,14 +3,15 @@
 Reference: the fp64 product of the oracle-dequantised weight (bit-identical to the
 reference unpack) -- i.e. what nf4.py:148-152 (unpack, then F.linear) and bitsandbytes'
 MatMul4Bit.backward compute, before their fp16 output rounding.
-Tolerance (written here, used everywhere below): max |y - ref| / max |ref| <= 2e-3.
+Tolerances (tests/helpers.py, used everywhere below): max |y - ref| / max |ref| <= 2e-3, and
+elementwise |y - ref| / |ref| <= 2e-3 over the entries with |ref| >= 0.05 max |ref|.
 """
 import numpy as np
 import pytest
 import torch
 
 from oracle import nf4_oracle as O
-from tests.helpers import GEMM_MAX_REL_ERR, max_rel_err, to_oracle_state
+from tests.helpers import GEMM_MAX_REL_ERR, assert_gemm_close, max_rel_err, to_oracle_state
 
 pytestmark = pytest.mark.gpu
 
@@ -59,10 +60,10 @@ def test_matmul4bit_forward_backward_contract(cuda_lib, nested, with_bias):
     ref = x.detach().double() @ W.T + (0 if bias is None else bias.double())
     ref_dx = g.double() @ W
     assert y.shape == ref.shape and y.dtype == torch.float16
-    assert max_rel_err(y, ref) <= GEMM_MAX_REL_ERR
+    assert_gemm_close(y, ref, "MatMul4Bit fwd")
     torch.testing.assert_close(y.double(), ref, rtol=2e-3, atol=2e-3)
     assert x.grad.dtype == torch.float16
-    assert max_rel_err(x.grad, ref_dx) <= GEMM_MAX_REL_ERR
+    assert_gemm_close(x.grad, ref_dx, "MatMul4Bit dX")
     torch.testing.assert_close(x.grad.double(), ref_dx, rtol=2e-3, atol=2e-3)
     _check_flag()
 
@@ -70,15 +71,15 @@ def test_matmul4bit_forward_backward_contract(cuda_lib, nested, with_bias):
 @pytest.mark.parametrize("n", [1170, 2048, 8192])
 @pytest.mark.parametrize("proj", list(QWEN))
 def test_fused_forward_qwen_shapes(cuda_lib, proj, n):
+    """Every projection shape at every token count: the planner picks the tiling (single,
+    128-token, pair, split-K) per shape and N, so each case can take a different path."""
     from stew_b200.nf4 import linear_forward
-    if n == 8192 and proj in ("k", "v", "o"):
-        pytest.skip("same kernel paths as q at this N")
     out_f, in_f = QWEN[proj]
     q, st = _weight((out_f, in_f), 100 + list(QWEN).index(proj))
     x = _x(n, in_f, 7)
     y = linear_forward(x, q.view(-1, 1), st)
     ref = x.double() @ _ref_weight(q, st).T
-    assert max_rel_err(y, ref) <= GEMM_MAX_REL_ERR
+    assert_gemm_close(y, ref, f"{proj} fwd N={n}")
     _check_flag()
 
 
@@ -87,15 +88,13 @@ def test_fused_forward_qwen_shapes(cuda_lib, proj, n):
 def test_fused_backward_qwen_shapes(cuda_lib, proj, n):
     """dX = dY W with dY ~ N(0, 1e-2) (std 0.01)."""
     from stew_b200.nf4 import linear_backward_dx
-    if n == 8192 and proj in ("k", "v", "o"):
-        pytest.skip("same kernel paths as q at this N")
     out_f, in_f = QWEN[proj]
     q, st = _weight((out_f, in_f), 200 + list(QWEN).index(proj))
     dy = _x(n, out_f, 9, std=0.01)
     dx = linear_backward_dx(dy, q.view(-1, 1), st)
     ref = dy.double() @ _ref_weight(q, st)
     assert dx.shape == (n, in_f)
-    assert max_rel_err(dx, ref) <= GEMM_MAX_REL_ERR
+    assert_gemm_close(dx, ref, f"{proj} bwd N={n}")
     _check_flag()
 
 
@@ -106,9 +105,9 @@ def test_ragged_token_counts(cuda_lib, n):
     q, st = _weight((384, 320), 5)
     W = _ref_weight(q, st)
     x = _x(n, 320, n)
-    assert max_rel_err(linear_forward(x, q.view(-1, 1), st), x.double() @ W.T) <= GEMM_MAX_REL_ERR
+    assert_gemm_close(linear_forward(x, q.view(-1, 1), st), x.double() @ W.T, f"fwd N={n}")
     dy = _x(n, 384, n + 1)
-    assert max_rel_err(linear_backward_dx(dy, q.view(-1, 1), st), dy.double() @ W) <= GEMM_MAX_REL_ERR
+    assert_gemm_close(linear_backward_dx(dy, q.view(-1, 1), st), dy.double() @ W, f"bwd N={n}")
     _check_flag()
 
 
@@ -119,9 +118,9 @@ def test_blocksizes_and_plain_absmax(cuda_lib, blocksize, nested):
     q, st = _weight((256, 512), blocksize + int(nested), blocksize=blocksize, nested=nested)
     W = _ref_weight(q, st)
     x = _x(300, 512, 3)
-    assert max_rel_err(linear_forward(x, q.view(-1, 1), st), x.double() @ W.T) <= GEMM_MAX_REL_ERR
+    assert_gemm_close(linear_forward(x, q.view(-1, 1), st), x.double() @ W.T, "fwd")
     dy = _x(300, 256, 4)
-    assert max_rel_err(linear_backward_dx(dy, q.view(-1, 1), st), dy.double() @ W) <= GEMM_MAX_REL_ERR
+    assert_gemm_close(linear_backward_dx(dy, q.view(-1, 1), st), dy.double() @ W, "bwd")
     _check_flag()
 
 
@@ -139,4 +138,4 @@ def test_forward_bias_and_outputs_exact_layout(cuda_lib):
                                           None, y.data_ptr(), 77, 256, 192, _stream(x.device)), "fwd")
     ref = x.double() @ _ref_weight(q, st).T + bias.double()
     assert not torch.isnan(y).any()
-    assert max_rel_err(y, ref) <= GEMM_MAX_REL_ERR
+    assert_gemm_close(y, ref, "fwd + bias")

@@ -55,8 +55,9 @@ def _ws(nbytes):
 
 
 def _counters(ws, m_rows=None, n=None):
-    """The workspace's leading counter region (4 KB, the same for every shape)."""
-    return ws[:4096]
+    """The workspace's leading counter region (per-tile arrivals and finished partials, 4 KB,
+    then the launch's exit count; the same for every shape)."""
+    return ws[:4096 + 4]
 
 
 def _fwd(L, x, q, qs, bias, lc, y, n, in_f, out_f, ws):
@@ -246,3 +247,42 @@ def test_split_result_is_deterministic(cuda_lib):
     assert all(torch.equal(ys[0], y) for y in ys[1:])
     _flag_clear()
 
+
+
+@pytest.mark.parametrize("pair", ["0", "1"])
+def test_counters_recover_after_a_range_gives_up(cuda_lib, monkeypatch, pair):
+    """A K range that gives up before taking its ticket (a pipeline wait that ran out) leaves
+    its tile's counts behind; the last CTA to leave the launch clears them, so the next call on
+    the same workspace is correct.  The give-up is injected on the host (a one-shot hook makes
+    work unit 0 skip its ticket): no wait actually runs out and nothing faults."""
+    from stew_b200 import _lib
+    from stew_b200.nf4 import _qstate
+    monkeypatch.setenv("STEW_NF4_PAIR", pair)
+    L = _lib.lib()
+    out_f, in_f, n = 1536, 8960, 1170  # down projection: split on single CTAs and on pairs
+    need = int(L.nf4b_linear_work_bytes(n, in_f, out_f, 0))
+    assert need > 0
+    q, st = _weight((out_f, in_f), 91)
+    qs = _qstate(st, q.device)
+    ws = _ws(need)
+    x = _rand(n, in_f, 92)
+    _flag_clear()
+    assert L.nf4b_test_drop_split_ticket(-1) == _lib.NF4B_ERR_INVALID_ARG
+    assert L.nf4b_test_drop_split_ticket(0) == _lib.NF4B_OK
+    y_bad = torch.zeros(n, out_f, dtype=torch.float16, device="cuda")
+    _fwd(L, x, q, qs, None, None, y_bad, n, in_f, out_f, ws)
+    torch.cuda.synchronize()
+    assert _lib.gemm_error_flag(reset=True) == 4, "the dropped ticket is recorded"
+    assert int(_counters(ws).count_nonzero()) == 0, "counters left behind by the dropped range"
+    ref = x.double() @ _ref_weight(q, st).T
+    ys = []
+    for _ in range(2):  # the hook was one-shot: both calls are whole and identical
+        y = torch.full((n, out_f), float("nan"), dtype=torch.float16, device="cuda")
+        _fwd(L, x, q, qs, None, None, y, n, in_f, out_f, ws)
+        ys.append(y)
+    torch.cuda.synchronize()
+    assert not torch.isnan(ys[0]).any()
+    assert max_rel_err(ys[0], ref) <= GEMM_MAX_REL_ERR
+    assert torch.equal(ys[0], ys[1])
+    assert int(_counters(ws).count_nonzero()) == 0
+    _flag_clear()
