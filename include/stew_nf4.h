@@ -81,17 +81,25 @@ typedef struct nf4b_dequant_job {
 /* Size in bytes of the device-side plan nf4b_dequant_batched needs for n_jobs jobs.  */
 int64_t nf4b_dequant_plan_bytes(int32_t n_jobs);
 
-/* Build the device-side plan of a batched sweep: validates `jobs` (host array),
- * copies them and a CTA->job table into `plan_dev` (nf4b_dequant_plan_bytes(n_jobs)
- * bytes of 16-byte aligned device memory owned by the caller) with one
- * cudaMemcpyAsync on `stream`, and returns the launch size in *n_ctas.
- * The plan stays valid while the buffers it names do.  */
+/* Build the device-side plan of a batched sweep: validates `jobs` (host array; a job of
+ * numel 0 may have NULL pointers), copies them and the prefix sums of their work into
+ * `plan_dev` (nf4b_dequant_plan_bytes(n_jobs) bytes of 16-byte aligned device memory owned
+ * by the caller) with one cudaMemcpyAsync on `stream`, and returns the launch descriptor in
+ * *launch (the CTA count in the low 32 bits, the kernel variant above them): pass it to
+ * nf4b_dequant_batched unchanged.  The plan stays valid while the buffers it names do.  */
 int nf4b_dequant_plan(const nf4b_dequant_job* jobs, int32_t n_jobs, void* plan_dev,
-                      int64_t* n_ctas, void* stream);
+                      int64_t* launch, void* stream);
 
 /* Unpack every job of a plan in ONE launch (replaces a loop of dequantize_nf4
- * calls, e.g. the 196 per-step unpacks of tools/bench_nf4.py:47).  */
-int nf4b_dequant_batched(const void* plan_dev, int32_t n_jobs, int64_t n_ctas, void* stream);
+ * calls, e.g. the 196 per-step unpacks of tools/bench_nf4.py:47).  `launch`: as returned by
+ * nf4b_dequant_plan.  */
+int nf4b_dequant_batched(const void* plan_dev, int32_t n_jobs, int64_t launch, void* stream);
+
+/* Reads (and with reset != 0 clears) the device-side flag the unpack kernel sets when a
+ * wait for one of its bulk copies ran out of time (the kernel then ends early instead of
+ * hanging).  0 = no timeout since the last reset.  Synchronous.  No counterpart in the
+ * reference.  */
+int nf4b_dequant_error_flag(int* value, int reset);
 
 /* LoRA adapter operands of a fused linear (peft lora.Linear, r = rank).
  * A is [rank, in] fp16 (lora_A.weight), B is [out, rank] fp16 (lora_B.weight),

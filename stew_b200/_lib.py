@@ -114,6 +114,7 @@ SIGNATURES = {
     "nf4b_quantize": (c_int32, [c_void_p, c_int32, c_int64, c_int32, c_void_p, c_void_p, c_void_p,
                                 c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "nf4b_gemm_error_flag": (c_int32, [ctypes.POINTER(c_int32), c_int32]),
+    "nf4b_dequant_error_flag": (c_int32, [ctypes.POINTER(c_int32), c_int32]),
     "nf4b_test_drop_split_ticket": (c_int32, [c_int32]),
     "nf4b_gemm_geometry": (c_int32, [ctypes.POINTER(c_int32), ctypes.POINTER(c_int32)]),
     "nf4b_status_string": (ctypes.c_char_p, [c_int32]),
@@ -176,6 +177,12 @@ def check(status: int, what: str) -> None:
 def gemm_error_flag(reset: bool = True) -> int:
     v = c_int32(0)
     check(lib().nf4b_gemm_error_flag(ctypes.byref(v), 1 if reset else 0), "nf4b_gemm_error_flag")
+    return int(v.value)
+
+
+def dequant_error_flag(reset: bool = True) -> int:
+    v = c_int32(0)
+    check(lib().nf4b_dequant_error_flag(ctypes.byref(v), 1 if reset else 0), "nf4b_dequant_error_flag")
     return int(v.value)
 
 

@@ -17,8 +17,8 @@
 //   The 16-entry code sits in shared memory (16 distinct words in 16 banks: a
 //   warp's lookups never conflict); the 256-entry second-level code is read
 //   through the read-only cache.
-// The main fp16 path is the chunk kernel further down; its batched variant runs many
-// tensors in one launch from a device-side plan.
+// The main fp16 path is the bulk-async kernel further down (nf4_dequant_tma_kernel), for one
+// tensor or, from a device-side plan, for many tensors in one launch.
 #include <mutex>
 #include <vector>
 
@@ -153,20 +153,10 @@ __global__ void __launch_bounds__(DQ_THREADS) nf4_dequant_kernel(const DqParams 
   dequant_chunk<ALIGNED>(p, blockIdx.x, s_code);
 }
 
-// ---------------------------------------------------------------- chunk kernel
-// Main path (fp16 out, 16-byte aligned buffers, numel a multiple of 64): one lane owns one
-// 64-value chunk (32 packed bytes, one scale for blocksize >= 64, two for 32), builds the
-// block's 16-entry fp16 table in registers (nf4_decode.cuh: T[i] = fp16(code[i] * scale),
-// bit-identical to the reference's per-value multiply-then-round) and decodes 8 words with
-// byte permutes.  The warp's 32 chunks (4 KB of fp16) go through a per-warp shared buffer,
-// written with the 16-byte slot XOR-swizzled by (lane & 7) and read back transposed, so both
-// sides are bank-conflict free and every global store instruction writes 512 contiguous
-// bytes.  Persistent grid: warps stride over 32-chunk iterations; in the batched kernel a
-// warp's iterations ascend, so its job index only moves forward.
-constexpr int DQ2_THREADS = 256;
-constexpr int DQ2_WARPS = DQ2_THREADS / 32;
-constexpr int DQ2_CHUNKS_PER_ITER = 32;  // one per lane
-constexpr int DQ2_CTAS_PER_SM = 3;       // persistent grid: 24 resident warps per SM
+// ---------------------------------------------------------------- main path
+// Work unit of the main path: 32 chunks of 64 values (one per lane of a warp), i.e. 1 KB of
+// packed bytes and 4 KB of fp16 output.
+constexpr int DQ_CHUNKS_PER_ITER = 32;
 
 __device__ __forceinline__ void load_code16(const float* code, float (&c)[16]) {
   const float4* c4 = reinterpret_cast<const float4*>(code);
@@ -177,91 +167,301 @@ __device__ __forceinline__ void load_code16(const float* code, float (&c)[16]) {
   }
 }
 
-// One warp iteration: chunks [iter*32, iter*32+32) of job p.
-__device__ __forceinline__ void dequant_iter_v2(const DqParams& p, int64_t nchunks, int64_t iter,
-                                                const float (&code)[16], uint8_t* wbuf) {
-  const int lane = threadIdx.x & 31;
-  const int64_t ch = iter * DQ2_CHUNKS_PER_ITER + lane;
-  const bool valid = ch < nchunks;
-  uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
-  float s0 = 0.f, s1 = 0.f;
-  if (valid) {
-    const uint4* src = reinterpret_cast<const uint4*>(p.packed + ch * 32);
-    w0 = __ldg(src);
-    w1 = __ldg(src + 1);
-    if (p.log2_bs >= 6) {
-      const int64_t blk = (ch << 6) >> p.log2_bs;
-      s0 = s1 = block_scale(p, blk);
-    } else {  // 32-value blocks: two per chunk
-      s0 = block_scale(p, 2 * ch);
-      s1 = block_scale(p, 2 * ch + 1);
+// ------------------------------------------------------------ bulk-async kernel
+// Main path for blocksizes >= 64 (one scale per 64-value chunk), fp16 out, aligned buffers.
+// Each warp runs its own pipeline over a contiguous range of 32-chunk iterations (1 KB packed
+// in, 4 KB fp16 out each):
+//   * lane 0 streams the packed bytes of the next DQ3_IN iterations into a ring of 1 KB
+//     shared-memory slots with cp.async.bulk (completion counted on one mbarrier per slot), so
+//     the next iteration's reads are in flight while the warp decodes;
+//   * the block scales (absmax8 -> code2 * absmax2 + offset, or the fp32 absmax) of the next
+//     iteration are loaded into registers one iteration ahead, which takes the dependent
+//     absmax8 -> code2 load chain off the critical path;
+//   * each lane decodes its 64-value chunk into a linear 4 KB output stage -- at step j it
+//     handles word j ^ (lane & 7), read straight from the shared slot, so the 16-byte stores of
+//     the 8 lanes of a shared-memory wavefront hit 8 different bank groups -- and lane 0 writes
+//     the stage back with one cp.async.bulk store; two stages alternate, a stage being reused
+//     only after its previous store has been read out (cp.async.bulk.wait_group.read).
+// Warps take runs of 8 consecutive iterations in turn (blocked-cyclic), which keeps the grid
+// inside one window of the sweep and keeps job changes (a new table, new pointers) rare.
+// All loads and stores carry an L2 evict-first policy (streaming data, touched once).
+// Every mbarrier wait is bounded; on expiry the warp records g_dequant_error, waits (bounded)
+// for the loads it has in flight and returns.
+constexpr int DQ3_WARPS = 4;
+constexpr int DQ3_THREADS = 32 * DQ3_WARPS;
+// Pipeline depth and residency, measured on the whole-model sweep (B200): more resident warps
+// beat deeper per-warp pipelines -- 2 packed slots x 5 CTAs (20 warps) 5,756 GB/s, 3 x 5
+// 5,674, 4 x 4 5,634, 5 x 4 5,583; single output stages with 6-7 CTAs (registers spill)
+// 5,381-5,478.
+constexpr int DQ3_IN = 2;    // packed slots per warp, 1 KB each
+constexpr int DQ3_OUT = 2;   // output stages per warp, 4 KB each
+constexpr int DQ3_WARP_BYTES = DQ3_OUT * 4096 + DQ3_IN * 1024;
+constexpr int DQ3_SMEM = DQ3_WARPS * DQ3_WARP_BYTES + DQ3_WARPS * DQ3_IN * 8;
+// Resident CTAs per SM: 5 (20 warps; 5 x 41 KB of shared memory, <= 102 registers a thread)
+// for blocksizes >= 64, 4 for plans with blocksize 32 (two tables per chunk need more
+// registers).
+template <bool TWO>
+constexpr int dq3_ctas_per_sm() { return TWO ? 4 : 5; }
+// Run length of the blocked-cyclic walk: iterations (4 KB of output each) a warp takes in a
+// row.  Measured: 1 -> 4,802 GB/s, 2 -> 5,213, 4 -> 5,470, 8 -> 5,564, 16 -> 5,573, 64 -> 5,317,
+// one contiguous range per warp -> 5,404 (3 packed slots, no L2 hint); 8 with the hint: 5,636.
+constexpr int DQ3_RUN = 8;
+constexpr long long DQ3_WAIT_CYCLES = 4000000000ll;  // ~2 s
+
+__device__ int g_dequant_error;
+
+// Streaming data is read and written once: both directions carry an L2 evict-first policy
+// (+1.3 % on the whole-model sweep).
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void bulk_load_1d(uint32_t smem_dst, const void* src, uint32_t bytes,
+                                             uint32_t bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+          "r"(smem_dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(pol)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_store_1d(void* dst, uint32_t smem_src, uint32_t bytes, uint64_t pol) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group.L2::cache_hint [%0], [%1], %2, %3;" ::"l"(dst),
+               "r"(smem_src), "r"(bytes), "l"(pol)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// All but the last N bulk stores have finished reading their shared-memory stages.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ bool dq3_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
+    if (clock64() - t0 > DQ3_WAIT_CYCLES) {
+      atomicExch(&g_dequant_error, 1);
+      return false;
     }
   }
-  const Nf4Table t0 = make_table(code, s0);
-  const Nf4Table t1 = (p.log2_bs >= 6) ? t0 : make_table(code, s1);
-  const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-  const uint32_t row = smem_u32(wbuf) + uint32_t(lane) * 128u;
-  const uint32_t key = uint32_t(lane & 7);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const uint4 v = decode_word_f16(j < 4 ? t0 : t1, w[j]);
-    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(row + ((uint32_t(j) ^ key) << 4)),
-                 "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-                 : "memory");
-  }
-  __syncwarp();
-  uint8_t* out = static_cast<uint8_t*>(p.out) + iter * (DQ2_CHUNKS_PER_ITER * 128);
-  const int c = lane & 7;
-#pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    const int b = 4 * r + (lane >> 3);  // chunk of this 16-byte piece
-    uint4 v;
-    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "r"(smem_u32(wbuf) + uint32_t(b) * 128u + ((uint32_t(c) ^ uint32_t(b & 7)) << 4)));
-    if (iter * DQ2_CHUNKS_PER_ITER + b < nchunks) st_cs_u128(out + r * 512 + lane * 16, v);
-  }
-  __syncwarp();
+  return true;
 }
 
-__global__ void __launch_bounds__(DQ2_THREADS, DQ2_CTAS_PER_SM) nf4_dequant_chunk_kernel(const DqParams p) {
-  __shared__ __align__(128) uint8_t stage[DQ2_WARPS][4096];
-  const int warp = threadIdx.x >> 5;
-  float code[16];
-  load_code16(p.code, code);
-  const int64_t nchunks = p.nwords >> 3;
-  const int64_t iters = (nchunks + DQ2_CHUNKS_PER_ITER - 1) / DQ2_CHUNKS_PER_ITER;
-  for (int64_t it = int64_t(blockIdx.x) * DQ2_WARPS + warp; it < iters;
-       it += int64_t(gridDim.x) * DQ2_WARPS)
-    dequant_iter_v2(p, nchunks, it, code, stage[warp]);
+// Job cursor over the prefix sums of iterations (n_jobs == 0: the single job of the launch).
+struct Dq3Jobs {
+  const DqParams* params;
+  const int64_t* start;
+  int32_t n;
+  __device__ __forceinline__ int64_t lo(int j) const { return start ? __ldg(start + j) : 0; }
+  __device__ __forceinline__ int64_t hi(int j) const {
+    return start ? __ldg(start + j + 1) : ((params->nwords >> 3) + DQ_CHUNKS_PER_ITER - 1) / DQ_CHUNKS_PER_ITER;
+  }
+  // the job holding iteration `it` (binary search over the prefix sums)
+  __device__ __forceinline__ int find(int64_t it) const {
+    int a = 0, b = n - 1;
+    while (a < b) {
+      const int m = (a + b + 1) >> 1;
+      if (lo(m) <= it) a = m; else b = m - 1;
+    }
+    return a;
+  }
+};
+
+// Scale sources of one 64-value chunk: its block (blocksize >= 64), or its two 32-value
+// blocks (blocksize 32; the second pair is the first one otherwise).
+struct Dq3Src {
+  uint32_t q0, q1;
+  float a0, a1;
+};
+
+// TWO: the launch has blocksize-32 jobs, whose chunks span two blocks; for the other jobs of
+// such a launch the second block is the first one again.
+template <bool TWO>
+__device__ __forceinline__ Dq3Src dq3_scale_src(const DqParams& p, int64_t chunk, bool valid) {
+  Dq3Src r{0u, 0u, 0.f, 0.f};
+  if (!valid) return r;
+  const int64_t blk = (chunk << 6) >> p.log2_bs;
+  if (p.nested) {
+    r.q0 = __ldg(p.absmax8 + blk);
+    r.a0 = __ldg(p.absmax2 + (blk >> p.log2_bs2));
+  } else {
+    r.a0 = __ldg(p.absmax32 + blk);
+  }
+  if (TWO) {
+    const int64_t blk1 = p.log2_bs == 5 ? blk + 1 : blk;
+    if (p.nested) {
+      r.q1 = __ldg(p.absmax8 + blk1);
+      r.a1 = __ldg(p.absmax2 + (blk1 >> p.log2_bs2));
+    } else {
+      r.a1 = __ldg(p.absmax32 + blk1);
+    }
+  }
+  return r;
 }
 
-// Batched plan in device memory: DqParams params[n_jobs]; int64_t iter_start[n_jobs + 1]
-// (prefix sums of 32-chunk iterations).
-__global__ void __launch_bounds__(DQ2_THREADS, DQ2_CTAS_PER_SM)
-    nf4_dequant_batched_kernel(const DqParams* __restrict__ params,
-                               const int64_t* __restrict__ iter_start, int32_t n_jobs) {
-  __shared__ __align__(128) uint8_t stage[DQ2_WARPS][4096];
+__device__ __forceinline__ float dq3_scale(const DqParams& p, uint32_t q, float a, float off) {
+  return p.nested ? __fadd_rn(__fmul_rn(__ldg(p.code2 + q), a), off) : a;
+}
+
+// TWO: blocksize 32 (two blocks, two tables per chunk); otherwise every job of the launch has
+// blocksize >= 64.
+template <bool TWO>
+__global__ void __launch_bounds__(DQ3_THREADS, dq3_ctas_per_sm<TWO>())
+    nf4_dequant_tma_kernel(const DqParams* __restrict__ params, const int64_t* __restrict__ iter_start,
+                           int32_t n_jobs, const __grid_constant__ DqParams single) {
+  extern __shared__ __align__(128) uint8_t dq3_smem[];
   const int warp = threadIdx.x >> 5;
-  const int64_t total = __ldg(iter_start + n_jobs);
-  int job = -1;
-  int64_t job_lo = 0, job_hi = 0, nchunks = 0;
+  const int lane = threadIdx.x & 31;
+  const uint32_t out_s = smem_u32(dq3_smem + warp * DQ3_WARP_BYTES);
+  const uint32_t in_s = out_s + DQ3_OUT * 4096;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(dq3_smem + DQ3_WARPS * DQ3_WARP_BYTES) + warp * DQ3_IN;
+  const Dq3Jobs J{n_jobs > 0 ? params : &single, n_jobs > 0 ? iter_start : nullptr, n_jobs > 0 ? n_jobs : 1};
+  const int64_t total = J.start ? J.lo(J.n) : J.hi(0);
+  // Blocked-cyclic walk: runs of DQ3_RUN consecutive iterations dealt to the warps in turn, so
+  // at any time the warps of the grid work inside one window of the sweep (DRAM pages are
+  // shared) and a warp's iterations still come in runs (few job changes, scale prefetch).
+  const int64_t nw = int64_t(gridDim.x) * DQ3_WARPS;
+  const int64_t wid = int64_t(blockIdx.x) * DQ3_WARPS + warp;
+  constexpr int64_t bl = DQ3_RUN;
+  const uint64_t pol = l2_evict_first();
+  const int64_t jump = (nw - 1) * bl;  // from the last iteration of a run to the next run
+  auto next_it = [&](int64_t it) -> int64_t { return ((it + 1) % bl) ? it + 1 : it + 1 + jump; };
+  const int64_t r0 = wid * bl;
+  if (r0 >= total) return;  // nothing issued yet
+  if (lane == 0) {
+    for (int i = 0; i < DQ3_IN; ++i) mbar_init(&bars[i], 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+
+  // producer cursor (lane 0): the next iteration to load and its job
+  int64_t pit = r0;
+  int pj = J.find(r0);
+  int64_t plo = J.lo(pj), phi = J.hi(pj);
+  auto issue = [&](int64_t k) {  // loads the warp's k-th iteration (k issued in order) into slot k % DQ3_IN
+    while (pit >= phi) {
+      ++pj;
+      plo = phi;
+      phi = J.hi(pj);
+    }
+    const uint8_t* packed = J.params[pj].packed;
+    const int64_t nch = J.params[pj].nwords >> 3;
+    const int64_t li = pit - plo;
+    const uint32_t bytes = uint32_t(min64(DQ_CHUNKS_PER_ITER, nch - li * DQ_CHUNKS_PER_ITER)) * 32u;
+    const int s = int(k % DQ3_IN);
+    mbar_arrive_expect_tx(&bars[s], bytes);
+    bulk_load_1d(in_s + uint32_t(s) * 1024u, packed + li * 1024, bytes, smem_u32(&bars[s]), pol);
+    pit = next_it(pit);
+  };
+  // the warp's iteration count
+  const int64_t runs = (total - r0 + nw * bl - 1) / (nw * bl);  // runs that start below total
+  const int64_t last_run = r0 + (runs - 1) * nw * bl;
+  const int64_t cnt = (runs - 1) * bl + min64(bl, total - last_run);
+  if (lane == 0)
+    for (int64_t k = 0; k < cnt && k < DQ3_IN; ++k) issue(k);
+  // run-time 1 << 16 and 1 << 31 for the decode's multiply-high shifts (nf4_decode.cuh)
+  const uint32_t k16 = 1u << (16 + (n_jobs < 0));
+  const uint32_t k31 = k16 << 15;
+
+  // consumer cursor (all lanes, warp-uniform)
+  int cj = -1;
+  int64_t clo = 0, chi = 0;
   DqParams p;
   float code[16];
-  for (int64_t it = int64_t(blockIdx.x) * DQ2_WARPS + warp; it < total;
-       it += int64_t(gridDim.x) * DQ2_WARPS) {
-    if (it >= job_hi) {  // warp-uniform: advance to the job holding iteration `it`
-      do {
-        ++job;
-        job_lo = __ldg(iter_start + job);
-        job_hi = __ldg(iter_start + job + 1);
-      } while (it >= job_hi && job + 1 < n_jobs);
-      p = params[job];
-      nchunks = p.nwords >> 3;
+  float off = 0.f;
+  Dq3Src pre{0u, 0u, 0.f, 0.f};
+  bool have_pre = false;
+  int64_t k = 0;
+  bool ok = true;
+  int s = 0;          // slot of iteration k (k % DQ3_IN) and the phase of its barrier
+  uint32_t ph = 0;
+  int64_t it = r0;
+  for (; k < cnt; ++k, it = next_it(it)) {
+    if (it >= chi) {
+      cj = (cj < 0) ? J.find(it) : cj + 1;
+      while (J.hi(cj) <= it) ++cj;
+      clo = J.lo(cj);
+      chi = J.hi(cj);
+      p = J.params[cj];
       load_code16(p.code, code);
+      off = p.nested ? __ldg(p.offset) : 0.f;
+      have_pre = false;
     }
-    dequant_iter_v2(p, nchunks, it - job_lo, code, stage[warp]);
+    const int64_t li = it - clo;
+    const int64_t nch = p.nwords >> 3;
+    const int nvalid = int(min64(DQ_CHUNKS_PER_ITER, nch - li * DQ_CHUNKS_PER_ITER));
+    const int64_t ch = li * DQ_CHUNKS_PER_ITER + lane;
+    const bool valid = lane < nvalid;
+    const Dq3Src cur = have_pre ? pre : dq3_scale_src<TWO>(p, ch, valid);
+    // the next iteration's scale sources, while it belongs to the same job
+    const int64_t it1 = next_it(it);
+    have_pre = it1 < chi && k + 1 < cnt;
+    if (have_pre) {
+      const int64_t li1 = it1 - clo;
+      const int nv1 = int(min64(DQ_CHUNKS_PER_ITER, nch - li1 * DQ_CHUNKS_PER_ITER));
+      pre = dq3_scale_src<TWO>(p, li1 * DQ_CHUNKS_PER_ITER + lane, lane < nv1);
+    }
+    const float sc0 = valid ? dq3_scale(p, cur.q0, cur.a0, off) : 0.f;
+    const Nf4Table t0 = make_table(code, sc0);
+    const Nf4Table t1 = TWO ? make_table(code, valid ? dq3_scale(p, cur.q1, cur.a1, off) : 0.f) : t0;
+
+    ok = __all_sync(0xffffffffu, dq3_wait(&bars[s], ph));
+    if (!ok) break;
+    // the output stage written DQ3_OUT iterations ago has been read out by its store
+    if (lane == 0 && k >= DQ3_OUT) bulk_wait_read<DQ3_OUT - 1>();
+    __syncwarp();
+    const uint32_t stage = out_s + uint32_t(k % DQ3_OUT) * 4096u;
+    const uint32_t src = in_s + uint32_t(s) * 1024u + uint32_t(lane) * 32u;
+    const uint32_t dst = stage + uint32_t(lane) * 128u;
+    const uint32_t key = uint32_t(lane & 7);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t jj = uint32_t(j) ^ key;
+      uint32_t w;
+      asm volatile("ld.shared.b32 %0, [%1];" : "=r"(w) : "r"(src + jj * 4u));
+      uint4 v;
+      if (!TWO) {
+        v = decode_word_f16_mh(t0, w, k16, k31);
+      } else {
+        // blocksize 32: words 0-3 of the chunk are the first block, 4-7 the second
+        const bool hi = jj >= 4u;
+        Nf4Table t;
+        t.l0 = hi ? t1.l0 : t0.l0; t.l1 = hi ? t1.l1 : t0.l1; t.l2 = hi ? t1.l2 : t0.l2;
+        t.l3 = hi ? t1.l3 : t0.l3; t.h0 = hi ? t1.h0 : t0.h0; t.h1 = hi ? t1.h1 : t0.h1;
+        t.h2 = hi ? t1.h2 : t0.h2; t.h3 = hi ? t1.h3 : t0.h3;
+        v = decode_word_f16_mh(t, w, k16, k31);
+      }
+      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(dst + jj * 16u), "r"(v.x), "r"(v.y),
+                   "r"(v.z), "r"(v.w)
+                   : "memory");
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      bulk_store_1d(static_cast<uint8_t*>(p.out) + li * 4096, stage, uint32_t(nvalid) * 128u, pol);
+      // slot s has been read by every lane: refill it with the iteration DQ3_IN ahead
+      if (k + DQ3_IN < cnt) issue(k + DQ3_IN);
+    }
+    if (++s == DQ3_IN) {
+      s = 0;
+      ph ^= 1u;
+    }
   }
+  if (!ok && lane == 0) {
+    // loads still in flight land in this warp's slots: wait for them (bounded) before leaving
+    for (int64_t j = k; j < cnt && j < k + DQ3_IN; ++j) {
+      if (!dq3_wait(&bars[s], ph)) break;
+      if (++s == DQ3_IN) {
+        s = 0;
+        ph ^= 1u;
+      }
+    }
+  }
+  if (lane == 0) bulk_wait_all();
+  __syncwarp();
 }
 
 static int sm_count() {
@@ -276,10 +476,45 @@ static int sm_count() {
   return cached[dev];
 }
 
-// Chunk-kernel eligibility: fp16 out, whole 64-value chunks, 16-byte aligned buffers.
+// Main-path eligibility: fp16 out, whole 64-value chunks, 16-byte aligned buffers (the bulk
+// copies move whole 16-byte units between 16-byte aligned addresses).
 static bool chunk_path_ok(const DqParams& p) {
   return !p.f32out && (p.nwords % 8) == 0 && aligned(p.packed, 16) && aligned(p.out, 16) &&
          aligned(p.code, 16);
+}
+
+// Launch descriptor bit of nf4b_dequant_plan / nf4b_dequant_batched: the plan has a job of
+// blocksize 32 and runs the two-table variant.
+constexpr int64_t kDq3TwoFlag = int64_t(1) << 32;
+
+static int64_t dq3_iters(const DqParams& p) {
+  return ((p.nwords >> 3) + DQ_CHUNKS_PER_ITER - 1) / DQ_CHUNKS_PER_ITER;
+}
+
+// CTAs of a main-path launch over `iters` iterations: enough for one iteration per warp, at
+// most the resident CTAs of the variant on every SM.
+static int64_t dq3_grid(int64_t iters, bool two) {
+  const int64_t want = (iters + DQ3_WARPS - 1) / DQ3_WARPS;
+  const int64_t cap = int64_t(sm_count()) * (two ? dq3_ctas_per_sm<true>() : dq3_ctas_per_sm<false>());
+  return want < cap ? want : cap;
+}
+
+// The main path's dynamic shared memory (above the 48 KB default) on the current device.
+static int dq3_smem_attr() {
+  static std::mutex mu;
+  static bool done[64] = {false};
+  int dev = 0;
+  NF4B_CUDA_TRY(cudaGetDevice(&dev));
+  NF4B_RETURN_IF(dev < 0 || dev >= 64, NF4B_ERR_DEVICE);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!done[dev]) {
+    NF4B_CUDA_TRY(cudaFuncSetAttribute(nf4_dequant_tma_kernel<false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, DQ3_SMEM));
+    NF4B_CUDA_TRY(cudaFuncSetAttribute(nf4_dequant_tma_kernel<true>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, DQ3_SMEM));
+    done[dev] = true;
+  }
+  return NF4B_OK;
 }
 
 // ------------------------------------------------------------------- host side
@@ -302,9 +537,17 @@ static int check_qstate(const nf4b_qstate* qs, int32_t* log2_bs, int32_t* log2_b
 
 static int make_params(const uint8_t* packed, const nf4b_qstate* qs, void* out, int32_t out_dtype,
                        int64_t numel, DqParams* p) {
-  NF4B_RETURN_IF(packed == nullptr || out == nullptr, NF4B_ERR_INVALID_ARG);
   NF4B_RETURN_IF(out_dtype != NF4B_F16 && out_dtype != NF4B_F32, NF4B_ERR_UNSUPPORTED);
   NF4B_RETURN_IF(numel < 0, NF4B_ERR_INVALID_ARG);
+  if (numel == 0) {  // an empty tensor: nothing is read or written, its pointers may be NULL
+    NF4B_RETURN_IF(qs == nullptr, NF4B_ERR_INVALID_ARG);
+    const int lb = ilog2_exact(qs->blocksize);
+    NF4B_RETURN_IF(lb < 5 || lb > 8, NF4B_ERR_UNSUPPORTED);
+    *p = DqParams{packed, out, nullptr, nullptr, nullptr, nullptr, nullptr, qs->code, 0, lb, 8,
+                  qs->nested ? 1 : 0, out_dtype == NF4B_F32};
+    return NF4B_OK;
+  }
+  NF4B_RETURN_IF(packed == nullptr || out == nullptr, NF4B_ERR_INVALID_ARG);
   int32_t lb = 0, lb2 = 0;
   int st = check_qstate(qs, &lb, &lb2);
   if (st != NF4B_OK) return st;
@@ -359,11 +602,15 @@ extern "C" int nf4b_dequant(const uint8_t* packed, const nf4b_qstate* qs, void* 
   if (st != NF4B_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (chunk_path_ok(p)) {
-    const int64_t iters = (p.nwords / 8 + DQ2_CHUNKS_PER_ITER - 1) / DQ2_CHUNKS_PER_ITER;
-    const int64_t want = (iters + DQ2_WARPS - 1) / DQ2_WARPS;
-    const int64_t cap = int64_t(sm_count()) * DQ2_CTAS_PER_SM;
-    nf4_dequant_chunk_kernel<<<unsigned(want < cap ? want : cap), DQ2_THREADS, 0, s>>>(p);
-    return launch_status("nf4_dequant_chunk_kernel launch");
+    st = dq3_smem_attr();
+    if (st != NF4B_OK) return st;
+    const bool two = p.log2_bs == 5;
+    const unsigned grid = unsigned(dq3_grid(dq3_iters(p), two));
+    if (two)
+      nf4_dequant_tma_kernel<true><<<grid, DQ3_THREADS, DQ3_SMEM, s>>>(nullptr, nullptr, 0, p);
+    else
+      nf4_dequant_tma_kernel<false><<<grid, DQ3_THREADS, DQ3_SMEM, s>>>(nullptr, nullptr, 0, p);
+    return launch_status("nf4_dequant_tma_kernel launch");
   }
   const int64_t ctas = (p.nwords + DQ_WORDS_PER_CTA - 1) / DQ_WORDS_PER_CTA;
   NF4B_RETURN_IF(ctas > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
@@ -397,12 +644,13 @@ extern "C" int nf4b_dequant_plan(const nf4b_dequant_job* jobs, int32_t n_jobs, v
     NF4B_RETURN_IF(params[i].f32out || params[i].nwords % 8 != 0, NF4B_ERR_UNSUPPORTED);
     NF4B_RETURN_IF(!chunk_path_ok(params[i]), NF4B_ERR_ALIGNMENT);
     starts[i] = total;
-    total += (params[i].nwords / 8 + DQ2_CHUNKS_PER_ITER - 1) / DQ2_CHUNKS_PER_ITER;
+    total += dq3_iters(params[i]);
   }
   starts[n_jobs] = total;
-  const int64_t want = (total + DQ2_WARPS - 1) / DQ2_WARPS;
-  const int64_t cap = int64_t(sm_count()) * DQ2_CTAS_PER_SM;
-  *n_ctas = want < cap ? want : cap;
+  // the launch descriptor: CTA count, and bit 32 for the blocksize-32 variant
+  bool two = false;
+  for (int i = 0; i < n_jobs; ++i) two = two || (params[i].nwords > 0 && params[i].log2_bs == 5);
+  *n_ctas = dq3_grid(total, two) | (two ? kDq3TwoFlag : 0);
   // A copy from pageable host memory returns once the source has been staged,
   // so the local buffer may be released right after.
   NF4B_CUDA_TRY(cudaMemcpyAsync(plan_dev, host.data(), host.size(), cudaMemcpyHostToDevice,
@@ -410,9 +658,11 @@ extern "C" int nf4b_dequant_plan(const nf4b_dequant_job* jobs, int32_t n_jobs, v
   return NF4B_OK;
 }
 
-extern "C" int nf4b_dequant_batched(const void* plan_dev, int32_t n_jobs, int64_t n_ctas,
+extern "C" int nf4b_dequant_batched(const void* plan_dev, int32_t n_jobs, int64_t launch,
                                     void* stream) {
-  NF4B_RETURN_IF(plan_dev == nullptr || n_jobs <= 0 || n_ctas < 0, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(plan_dev == nullptr || n_jobs <= 0 || launch < 0, NF4B_ERR_INVALID_ARG);
+  const bool two = (launch & kDq3TwoFlag) != 0;
+  const int64_t n_ctas = launch & ~kDq3TwoFlag;
   NF4B_RETURN_IF(n_ctas > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
   if (n_ctas == 0) return NF4B_OK;
   int st = check_device();
@@ -420,7 +670,23 @@ extern "C" int nf4b_dequant_batched(const void* plan_dev, int32_t n_jobs, int64_
   const DqParams* params = static_cast<const DqParams*>(plan_dev);
   const int64_t* starts = reinterpret_cast<const int64_t*>(
       static_cast<const uint8_t*>(plan_dev) + size_t(n_jobs) * sizeof(DqParams));
-  nf4_dequant_batched_kernel<<<unsigned(n_ctas), DQ2_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
-      params, starts, n_jobs);
-  return launch_status("nf4_dequant_batched_kernel launch");
+  st = dq3_smem_attr();
+  if (st != NF4B_OK) return st;
+  DqParams none{};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (two)
+    nf4_dequant_tma_kernel<true><<<unsigned(n_ctas), DQ3_THREADS, DQ3_SMEM, s>>>(params, starts, n_jobs, none);
+  else
+    nf4_dequant_tma_kernel<false><<<unsigned(n_ctas), DQ3_THREADS, DQ3_SMEM, s>>>(params, starts, n_jobs, none);
+  return launch_status("nf4_dequant_tma_kernel launch");
+}
+
+extern "C" int nf4b_dequant_error_flag(int* value, int reset) {
+  NF4B_RETURN_IF(value == nullptr, NF4B_ERR_INVALID_ARG);
+  NF4B_CUDA_TRY(cudaMemcpyFromSymbol(value, g_dequant_error, sizeof(int)));
+  if (reset) {
+    const int zero = 0;
+    NF4B_CUDA_TRY(cudaMemcpyToSymbol(g_dequant_error, &zero, sizeof(int)));
+  }
+  return NF4B_OK;
 }

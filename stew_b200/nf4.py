@@ -193,7 +193,7 @@ def linear_forward(A: torch.Tensor, Bv: torch.Tensor, st, bias=None) -> torch.Te
     why = _unfused_reason(A, out_f, in_f) if not _fused_ok(A, out_f, in_f) else "a non-fp16 bias"
     _warn_once("fwd:" + why, f"{why}: the forward runs the unpack kernel + F.linear (not fused)")
     weight = dequantize_nf4(Bv, st).to(A.dtype)
-    return torch.nn.functional.linear(A, weight, bias)
+    return torch.nn.functional.linear(A, weight, None if bias is None else bias.to(A.dtype))
 
 
 def linear_backward_dx(grad_output: torch.Tensor, Bv: torch.Tensor, st) -> torch.Tensor:

