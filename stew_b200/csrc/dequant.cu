@@ -259,12 +259,19 @@ struct Dq3Jobs {
   __device__ __forceinline__ int64_t hi(int j) const {
     return start ? __ldg(start + j + 1) : ((params->nwords >> 3) + DQ_CHUNKS_PER_ITER - 1) / DQ_CHUNKS_PER_ITER;
   }
-  // the job holding iteration `it` (binary search over the prefix sums)
+  // The job holding iteration `it`: the last job whose first iteration is <= it, found by the
+  // whole warp (32 probes per round, so two dependent loads for up to 1,024 jobs).  Call from
+  // all 32 lanes with the same `it`.
   __device__ __forceinline__ int find(int64_t it) const {
-    int a = 0, b = n - 1;
+    const int lane = threadIdx.x & 31;
+    int a = 0, b = n - 1;  // the answer lies in [a, b]
     while (a < b) {
-      const int m = (a + b + 1) >> 1;
-      if (lo(m) <= it) a = m; else b = m - 1;
+      const int step = (b - a + 32) / 32;  // ceil((b - a + 1) / 32)
+      const int m = min(a + lane * step, b);
+      const uint32_t le = __ballot_sync(0xffffffffu, lo(m) <= it);
+      const int last = 31 - __clz(le);  // lane 0 always qualifies (lo(a) <= it)
+      a = min(a + last * step, b);
+      b = min(b, a + step - 1);
     }
     return a;
   }
@@ -320,16 +327,27 @@ __global__ void __launch_bounds__(DQ3_THREADS, dq3_ctas_per_sm<TWO>())
   uint64_t* bars = reinterpret_cast<uint64_t*>(dq3_smem + DQ3_WARPS * DQ3_WARP_BYTES) + warp * DQ3_IN;
   const Dq3Jobs J{n_jobs > 0 ? params : &single, n_jobs > 0 ? iter_start : nullptr, n_jobs > 0 ? n_jobs : 1};
   const int64_t total = J.start ? J.lo(J.n) : J.hi(0);
-  // Blocked-cyclic walk: runs of DQ3_RUN consecutive iterations dealt to the warps in turn, so
-  // at any time the warps of the grid work inside one window of the sweep (DRAM pages are
-  // shared) and a warp's iterations still come in runs (few job changes, scale prefetch).
+  // Blocked-cyclic walk: rounds in which every warp takes a run of DQ3_RUN consecutive
+  // iterations, so at any time the grid works inside one window of the sweep (DRAM pages are
+  // shared) and a warp's iterations still come in runs (few job changes, scale prefetch).  What
+  // is left after the whole rounds is dealt in one last round of shorter runs (ceil(rest /
+  // warps) each), so no warp is left running a whole run alone at the end.
   const int64_t nw = int64_t(gridDim.x) * DQ3_WARPS;
   const int64_t wid = int64_t(blockIdx.x) * DQ3_WARPS + warp;
   constexpr int64_t bl = DQ3_RUN;
   const uint64_t pol = l2_evict_first();
-  const int64_t jump = (nw - 1) * bl;  // from the last iteration of a run to the next run
-  auto next_it = [&](int64_t it) -> int64_t { return ((it + 1) % bl) ? it + 1 : it + 1 + jump; };
-  const int64_t r0 = wid * bl;
+  const int64_t rounds = total / (nw * bl);
+  const int64_t tail0 = rounds * nw * bl;            // first iteration of the last round
+  const int64_t bl2 = (total - tail0 + nw - 1) / nw;  // run length of the last round
+  const int64_t t0 = tail0 + wid * bl2;               // this warp's run in the last round
+  const int64_t t1 = min64(t0 + bl2, total);
+  auto next_it = [&](int64_t it) -> int64_t {
+    if (it >= tail0) return it + 1 < t1 ? it + 1 : total;
+    if ((it + 1) % bl) return it + 1;
+    const int64_t nx = it + 1 + (nw - 1) * bl;
+    return nx < tail0 ? nx : (t0 < t1 ? t0 : total);
+  };
+  const int64_t r0 = rounds > 0 ? wid * bl : (t0 < t1 ? t0 : total);
   if (r0 >= total) return;  // nothing issued yet
   if (lane == 0) {
     for (int i = 0; i < DQ3_IN; ++i) mbar_init(&bars[i], 1);
@@ -357,9 +375,7 @@ __global__ void __launch_bounds__(DQ3_THREADS, dq3_ctas_per_sm<TWO>())
     pit = next_it(pit);
   };
   // the warp's iteration count
-  const int64_t runs = (total - r0 + nw * bl - 1) / (nw * bl);  // runs that start below total
-  const int64_t last_run = r0 + (runs - 1) * nw * bl;
-  const int64_t cnt = (runs - 1) * bl + min64(bl, total - last_run);
+  const int64_t cnt = rounds * bl + (t0 < t1 ? t1 - t0 : 0);
   if (lane == 0)
     for (int64_t k = 0; k < cnt && k < DQ3_IN; ++k) issue(k);
   // run-time 1 << 16 and 1 << 31 for the decode's multiply-high shifts (nf4_decode.cuh)
