@@ -221,7 +221,7 @@ class GemmPass:
                     self.lora[(li, name)] = (a, b, xa, dyb, da, db, lc)
                 self.items.append((li, name, out_f, in_f, q, qs, lc))
         wb = max(int(self.L.nf4b_lora_grads_work_bytes(n, in_f, out_f, 16)) for _, out_f, in_f in QWEN_PROJ)
-        self.work = torch.empty(wb // 4 + 4, device=dev, dtype=torch.float32)
+        self.work = torch.zeros(max(wb, 256) // 4 + 4, device=dev, dtype=torch.float32)  # ticket words zero
         # grouped forward: per layer q/k/v in one launch, o, gate/up in one launch, down
         self.yname = {name: torch.empty(n, out_f, device=dev, dtype=torch.float16)
                       for name, out_f, _ in QWEN_PROJ}

@@ -195,22 +195,25 @@ int nf4b_linear_bwd_dx_group(const nf4b_linear_bwd_item* items, int32_t n_items,
                              int64_t n, int64_t in_features, void* work, int64_t work_bytes,
                              void* stream);
 
-/* LoRA weight gradients (fp32 out, overwritten):
+/* LoRA weight gradients (fp32 out, overwritten), both in one launch:
  *   dA[rank, in]  = scale * (dY B)^T X
  *   dB[out, rank] = scale * dY^T (X A^T)
  * x fp16 [n, in], dy fp16 [n, out], xa fp16 [n, rank], dyb fp16 [n, rank], all 16-byte
  * aligned; in and out multiples of 8.
- * `work` is caller-provided fp32 scratch of nf4b_lora_grads_work_bytes() bytes.  */
+ * `work`: caller-provided scratch of nf4b_lora_grads_work_bytes() bytes, 256-byte aligned (0
+ * bytes: no token split, any pointer will do).  Its leading 4 KB are per-column-tile ticket
+ * words that must be zero before the first call; every call leaves them zero, so allocate the
+ * buffer zeroed once and reuse it (one per stream: calls that overlap on the GPU need distinct
+ * buffers).  The sums are added in a fixed order: the result does not depend on scheduling.  */
 int64_t nf4b_lora_grads_work_bytes(int64_t n, int64_t in_features, int64_t out_features, int32_t rank);
 int nf4b_lora_grads(const void* x, const void* dy, const void* xa, const void* dyb, float scale,
                     float* da, float* db, void* work, int64_t n, int64_t in_features,
                     int64_t out_features, int32_t rank, void* stream);
 
 /* The weight gradients of several adapters (e.g. q and v of one layer, whose backward runs at
- * the same time) in two launches in total: every adapter's dA and dB outer products in one,
- * all their reductions in the next.  Same math as nf4b_lora_grads per item; rank 16; at most 3
- * items.  `work`: fp32 scratch of nf4b_lora_grads_group_work_bytes(items, n_items, n) bytes
- * (the items' partial sums side by side; -1 for invalid items).  */
+ * the same time) in one launch.  Same math as nf4b_lora_grads per item; rank 16; at most 3
+ * items.  `work`: scratch of nf4b_lora_grads_group_work_bytes(items, n_items, n) bytes (-1 for
+ * invalid items) with the same ticket-word contract as nf4b_lora_grads.  */
 typedef struct nf4b_lora_grads_item {
   const void* x;        /* fp16 [n, in_features], the projection's input        */
   const void* dy;       /* fp16 [n, out_features], the gradient of its output   */
@@ -229,18 +232,19 @@ int nf4b_lora_grads_group(const nf4b_lora_grads_item* items, int32_t n_items, vo
 /* nf4b_lora_grads without the `work` argument, for callers that cannot call
  * cudaMalloc on this path (inside a framework that already holds the device's memory
  * in its own pool, or in a loop where allocating is not allowed).  It allocates
- * nothing: its split-token partial sums live in a fixed device array of
- * NF4B_NOALLOC_SCRATCH_BYTES inside the library, present on every GPU that loads the
- * library until the process exits.  Problems whose partial sums need more
- * (nf4b_lora_grads_work_bytes() > NF4B_NOALLOC_SCRATCH_BYTES) return
- * NF4B_ERR_UNSUPPORTED with a message in nf4b_last_error().  All calls share the
- * array, so calls that overlap on the GPU race; each call writes all it reads.  The
- * first call on a device looks up the array's device address; make that first call
- * before any stream capture.  The address is cached for the life of the process: after a
+ * nothing: its split-token partial sums and ticket words live in a fixed device array of
+ * NF4B_NOALLOC_SCRATCH_BYTES (4 MiB) inside the library, present on every GPU that loads the
+ * library until the process exits.  A rank-16 problem needs at most ~2.4 MB of it (two 8 KB
+ * partial tiles per SM plus 4 KB of tickets, whatever the shape and token count); a problem
+ * that needed more (nf4b_lora_grads_work_bytes() > NF4B_NOALLOC_SCRATCH_BYTES) would return
+ * NF4B_ERR_UNSUPPORTED with a message in nf4b_last_error().  All calls share the array, so
+ * calls that overlap on the GPU race; the ticket words start zero and every call leaves them
+ * zero, and each call writes every partial sum it reads.  The first call on a device looks up
+ * the array's device address; make that first call before any stream capture.  The address is cached for the life of the process: after a
  * cudaDeviceReset (or a reset of the primary context) the library's module is loaded
  * again and this entry point must not be used on that device any more.  No counterpart in
  * the reference.  */
-#define NF4B_NOALLOC_SCRATCH_BYTES (8 << 20)
+#define NF4B_NOALLOC_SCRATCH_BYTES (4 << 20)
 int nf4b_lora_grads_noalloc(const void* x, const void* dy, const void* xa, const void* dyb,
                             float scale, float* da, float* db, int64_t n, int64_t in_features,
                             int64_t out_features, int32_t rank, void* stream);

@@ -5,9 +5,10 @@
 //  lora_project16   out[t, r] = sum_k act[t, k] * W[r, k]       (X A^T forward, dY B backward)
 //                   fp32 accumulate, fp16 result (what peft's fp16 autocast linear yields).
 //                   HBM-bound on `act`; mma.sync tiles of 16 tokens, K split over 8 warps.
-//  lora_outer16     G[r, c] = sum_t P[t, r] * Q[t, c]            (the two weight gradients)
-//                   split over tokens; partial sums go to caller-provided scratch and a
-//                   second kernel adds them up and applies the scale.
+//  lora_grads16     G[r, c] = sum_t P[t, r] * Q[t, c]            (the two weight gradients)
+//                   split over columns and tokens; the token ranges' fp32 partials go to
+//                   caller-provided scratch and the last CTA of each column tile adds them up
+//                   in a fixed order and applies the scale (one launch, deterministic).
 #include <mutex>
 
 #include "common.cuh"
@@ -83,19 +84,30 @@ __global__ void __launch_bounds__(LP_THREADS)
   const uint4* x0 = reinterpret_cast<const uint4*>(act + (t0 + g) * kdim);
   const uint4* x1 = reinterpret_cast<const uint4*>(act + (t0 + g + 8) * kdim);
   float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 2
-  for (int64_t j = jb; j < je; ++j) {
-    const int64_t k = 32 * j + 8 * c;
-    const uint4 xa = v0 ? __ldg(x0 + (k >> 3)) : make_uint4(0, 0, 0, 0);
-    const uint4 xb = v1 ? __ldg(x1 + (k >> 3)) : make_uint4(0, 0, 0, 0);
-    const uint4 w0 = ld_w8<WK>(w, sr, sk, g, k);      // adapter rows 0-7  (output columns of d0)
-    const uint4 w1 = ld_w8<WK>(w, sr, sk, 8 + g, k);  // adapter rows 8-15 (d1)
-    const uint32_t s0[4] = {xa.x, xb.x, xa.y, xb.y};
-    const uint32_t s1[4] = {xa.z, xb.z, xa.w, xb.w};
-    mma16816(d0, s0, w0.x, w0.y);
-    mma16816(d1, s0, w1.x, w1.y);
-    mma16816(d0, s1, w0.z, w0.w);
-    mma16816(d1, s1, w1.z, w1.w);
+  // chunks in batches of LP_BATCH: every load of a batch is issued before its MMAs, so a warp
+  // waits for memory about once per batch instead of once per chunk (2 for a weight read with
+  // strided 2-byte loads, whose 16 values a chunk take 16 registers)
+  constexpr int LP_BATCH = WK ? 4 : 2;
+  for (int64_t j0 = jb; j0 < je; j0 += LP_BATCH) {
+    uint4 xa[LP_BATCH], xb[LP_BATCH], w0[LP_BATCH], w1[LP_BATCH];
+#pragma unroll
+    for (int u = 0; u < LP_BATCH; ++u) {
+      const int64_t k = 32 * (j0 + u) + 8 * c;
+      const bool in = j0 + u < je;
+      xa[u] = (in && v0) ? __ldg(x0 + (k >> 3)) : make_uint4(0, 0, 0, 0);
+      xb[u] = (in && v1) ? __ldg(x1 + (k >> 3)) : make_uint4(0, 0, 0, 0);
+      w0[u] = in ? ld_w8<WK>(w, sr, sk, g, k) : make_uint4(0, 0, 0, 0);      // adapter rows 0-7 (d0)
+      w1[u] = in ? ld_w8<WK>(w, sr, sk, 8 + g, k) : make_uint4(0, 0, 0, 0);  // adapter rows 8-15 (d1)
+    }
+#pragma unroll
+    for (int u = 0; u < LP_BATCH; ++u) {
+      const uint32_t s0[4] = {xa[u].x, xb[u].x, xa[u].y, xb[u].y};
+      const uint32_t s1[4] = {xa[u].z, xb[u].z, xa[u].w, xb[u].w};
+      mma16816(d0, s0, w0[u].x, w0[u].y);
+      mma16816(d1, s0, w1[u].x, w1[u].y);
+      mma16816(d0, s1, w0[u].z, w0[u].w);
+      mma16816(d1, s1, w1[u].z, w1[u].w);
+    }
   }
   red[warp][g][2 * c] = d0[0];
   red[warp][g][2 * c + 1] = d0[1];
@@ -149,24 +161,26 @@ int lora_project16(const void* act, const void* w, int64_t w_stride_r, int64_t w
 // G[r, c] = sum_t P[t, r] * Q[t, c] on the tensor cores: M = the 16 adapter rows, N = columns
 // of Q, K = tokens.  Both operands are contiguous along M/N, not K, so each 32-token chunk of
 // P and Q is staged in shared memory (cp.async, double-buffered) and the fragments are read
-// with ldmatrix .trans.  A CTA of 4 warps owns 256 columns (64 per warp) of one token range;
-// the ranges' partial sums go to caller-provided scratch and lora_reduce adds them up.
+// with ldmatrix .trans.  A CTA of 4 warps owns 128 columns (32 per warp) of one token range
+// ("split").  With one split the CTA writes its scaled result directly; otherwise it writes its
+// fp32 partial to the workspace, takes a ticket on its column tile, and the tile's last CTA
+// adds the partials up in split order (deterministic whatever the arrival order) and writes
+// the result.  Nobody waits: each CTA publishes its partial before it takes its ticket, so the
+// last ticket holder finds every partial in place.
 constexpr int LO_THREADS = 128;
-constexpr int LO_COLS = 256;                   // columns per CTA
+constexpr int LO_COLS = 128;                   // columns per CTA
 constexpr int LO_TOK = 32;                     // tokens per staged chunk (two k16 steps)
+constexpr int LO_STAGES = 4;                   // staged chunks in the ring
 constexpr int LO_QROW = LO_COLS * 2 + 16;      // staged Q row, bytes (+16: conflict-free ldmatrix)
 constexpr int LO_PROW = 48;                    // staged P row, bytes (32 of data + pad)
 constexpr int LO_QBUF = LO_TOK * LO_QROW;
 constexpr int LO_PBUF = LO_TOK * LO_PROW;
-constexpr int LO_TARGET_CTAS = 2 * 148;        // two waves' worth of CTAs on a 148-SM B200
-
-static int64_t outer_splits(int64_t n, int64_t cols) {
-  const int64_t col_ctas = (cols + LO_COLS - 1) / LO_COLS;
-  int64_t s = (LO_TARGET_CTAS + col_ctas - 1) / col_ctas;
-  const int64_t max_s = (n + LO_TOK - 1) / LO_TOK;
-  if (s > max_s) s = max_s;
-  return s < 1 ? 1 : s;
-}
+constexpr int LO_TARGET_CTAS = 2 * 148;        // two CTAs per SM of a B200, evenly
+constexpr int LO_MIN_TOK = 64;                 // tokens per split at least (two chunks)
+// Workspace: LO_CNT_BYTES of per-column-tile tickets (zero between calls; every call leaves
+// them zero), then the fp32 partials [splits][16][cols] of each job with more than one split.
+constexpr int LO_MAX_TILES = 1024;
+constexpr int64_t LO_CNT_BYTES = LO_MAX_TILES * 4;
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
@@ -184,12 +198,12 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
                : "r"(addr));
 }
 
-// One outer product of a launch: its CTAs are [cta0, cta0 + col tiles * splits); its reduce
-// blocks (32 outputs each) are [red0, red0 + ceil(16 cols / 32)).
+// One outer product of a launch: its CTAs are [cta0, cta0 + col tiles * splits), its tickets
+// [tile0, tile0 + col tiles).
 struct OuterJob {
   const __half* P;
   const __half* Q;
-  float* partial;    // [splits][16][cols]
+  float* partial;    // [splits][16][cols] (splits > 1)
   float* out;        // [16][cols], or [cols][16] when transpose
   int64_t cols;
   int64_t splits;
@@ -197,47 +211,49 @@ struct OuterJob {
   float scale;
   int32_t transpose;
   int32_t cta0;
-  int32_t red0;
+  int32_t tile0;
 };
 constexpr int LO_MAX_JOBS = 6;  // dA and dB of up to three adapters
 struct OuterJobs {
   OuterJob j[LO_MAX_JOBS];
+  int32_t* tickets;
   int32_t n;
 };
 
-__device__ __forceinline__ int find_job(const OuterJobs& js, int bid, bool reduce) {
+__device__ __forceinline__ int find_job(const OuterJobs& js, int bid) {
   int k = 0;
   for (int i = 1; i < js.n; ++i)
-    if (bid >= (reduce ? js.j[i].red0 : js.j[i].cta0)) k = i;
+    if (bid >= js.j[i].cta0) k = i;
   return k;
 }
 
 __global__ void __launch_bounds__(LO_THREADS)
-    lora_outer16_kernel(const __grid_constant__ OuterJobs jobs, int64_t n) {
+    lora_grads16_kernel(const __grid_constant__ OuterJobs jobs, int64_t n) {
   grid_dep_wait();  // programmatic launch: no global access before the wait
-  __shared__ __align__(128) uint8_t qbuf[2][LO_QBUF];
-  __shared__ __align__(128) uint8_t pbuf[2][LO_PBUF];
+  __shared__ __align__(128) uint8_t qbuf[LO_STAGES][LO_QBUF];
+  __shared__ __align__(128) uint8_t pbuf[LO_STAGES][LO_PBUF];
+  __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const OuterJob& job = jobs.j[find_job(jobs, int(blockIdx.x), false)];
+  const OuterJob& job = jobs.j[find_job(jobs, int(blockIdx.x))];
   const __half* __restrict__ P = job.P;
   const __half* __restrict__ Q = job.Q;
   const int64_t cols = job.cols;
   const int64_t col_tiles = (cols + LO_COLS - 1) / LO_COLS;
   const int64_t local = int64_t(blockIdx.x) - job.cta0;
   const int64_t split = local / col_tiles;
-  const int64_t c0 = (local - split * col_tiles) * LO_COLS;
+  const int64_t tile = local - split * col_tiles;
+  const int64_t c0 = tile * LO_COLS;
   const int64_t tb = split * job.tps;
   const int64_t te = min64(n, tb + job.tps);
-  float* __restrict__ partial = job.partial;
 
-  // stage tokens [ts, ts + 32) of P (32 B per token) and of Q's 256 columns; rows past te or
+  // stage tokens [ts, ts + 32) of P (32 B per token) and of Q's 128 columns; rows past te or
   // columns past `cols` are zero-filled
   auto stage = [&](int buf, int64_t ts) {
     const uint32_t qb = smem_u32(qbuf[buf]), pb = smem_u32(pbuf[buf]);
 #pragma unroll
     for (int i = 0; i < (LO_TOK * LO_COLS / 8) / LO_THREADS; ++i) {
-      const int e = threadIdx.x + i * LO_THREADS;  // 16-byte piece: row e / 32, piece e % 32
-      const int row = e >> 5, pc = e & 31;
+      const int e = threadIdx.x + i * LO_THREADS;  // 16-byte piece: row e / 16, piece e % 16
+      const int row = e >> 4, pc = e & 15;
       const int64_t t = ts + row, c = c0 + 8 * pc;
       const bool ok = t < te && c < cols;
       cp_async16(qb + row * LO_QROW + pc * 16, ok ? Q + t * cols + c : Q, ok);
@@ -250,19 +266,22 @@ __global__ void __launch_bounds__(LO_THREADS)
     cp_async_commit();
   };
 
-  float acc[8][4];
+  float acc[4][4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  // a ring of LO_STAGES chunk buffers: LO_STAGES - 1 chunks in flight while one is multiplied
+  // (an empty commit group keeps the group count in step past the last chunk)
   const int64_t nchunks = (te - tb + LO_TOK - 1) / LO_TOK;
-  if (nchunks > 0) stage(0, tb);
+#pragma unroll
+  for (int i = 0; i < LO_STAGES - 1; ++i) {
+    if (i < nchunks)
+      stage(i, tb + int64_t(i) * LO_TOK);
+    else
+      cp_async_commit();
+  }
   for (int64_t ch = 0; ch < nchunks; ++ch) {
-    const int buf = int(ch & 1);
-    if (ch + 1 < nchunks) {
-      stage(buf ^ 1, tb + (ch + 1) * LO_TOK);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
+    const int buf = int(ch % LO_STAGES);
+    cp_async_wait<LO_STAGES - 2>();  // chunk ch has landed
     __syncthreads();
     const uint32_t qb = smem_u32(qbuf[buf]), pb = smem_u32(pbuf[buf]);
 #pragma unroll
@@ -275,108 +294,159 @@ __global__ void __launch_bounds__(LO_THREADS)
         ldsm_x4_t(pb + t * LO_PROW + r * 2, a);
       }
 #pragma unroll
-      for (int nt = 0; nt < 8; nt += 2) {
+      for (int nt = 0; nt < 4; nt += 2) {
         // B[t][c] = Q[t][c], stored [t][c]: (t 0-7, t 8-15) for column tiles nt and nt+1
         uint32_t b[4];
         const int j = lane >> 3, row = lane & 7;
         const int t = ks * 16 + (j & 1) * 8 + row;
-        const int col = 64 * warp + 8 * (nt + (j >> 1));
+        const int col = 32 * warp + 8 * (nt + (j >> 1));
         ldsm_x4_t(qb + t * LO_QROW + col * 2, b);
         mma16816(acc[nt], a, b[0], b[1]);
         mma16816(acc[nt + 1], a, b[2], b[3]);
       }
     }
-    __syncthreads();
+    __syncthreads();  // buffer `buf` is free: refill it with the chunk LO_STAGES - 1 ahead
+    const int64_t nx = ch + LO_STAGES - 1;
+    if (nx < nchunks)
+      stage(int(nx % LO_STAGES), tb + nx * LO_TOK);
+    else
+      cp_async_commit();
   }
+  cp_async_wait<0>();
   // D fragment: d[0..1] = G[g][2c..2c+1], d[2..3] = G[g+8][2c..2c+1] of each 16 x 8 tile
   const int g = lane >> 2, cq = lane & 3;
+  const float scale = job.scale;
+  float* __restrict__ out = job.out;
+  if (job.splits == 1) {
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const int64_t c = c0 + 32 * warp + 8 * nt + 2 * cq;
+      if (c < cols) {
+        if (job.transpose) {
+          out[c * 16 + g] = acc[nt][0] * scale;
+          out[(c + 1) * 16 + g] = acc[nt][1] * scale;
+          out[c * 16 + g + 8] = acc[nt][2] * scale;
+          out[(c + 1) * 16 + g + 8] = acc[nt][3] * scale;
+        } else {
+          *reinterpret_cast<float2*>(out + int64_t(g) * cols + c) = make_float2(acc[nt][0] * scale, acc[nt][1] * scale);
+          *reinterpret_cast<float2*>(out + int64_t(g + 8) * cols + c) =
+              make_float2(acc[nt][2] * scale, acc[nt][3] * scale);
+        }
+      }
+    }
+    return;
+  }
+  float* __restrict__ partial = job.partial;
   float* dst = partial + split * 16 * cols;
 #pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
-    const int64_t c = c0 + 64 * warp + 8 * nt + 2 * cq;
+  for (int nt = 0; nt < 4; ++nt) {
+    const int64_t c = c0 + 32 * warp + 8 * nt + 2 * cq;
     if (c < cols) {
-      *reinterpret_cast<float2*>(dst + int64_t(g) * cols + c) = make_float2(acc[nt][0], acc[nt][1]);
-      *reinterpret_cast<float2*>(dst + int64_t(g + 8) * cols + c) = make_float2(acc[nt][2], acc[nt][3]);
+      __stcg(reinterpret_cast<float2*>(dst + int64_t(g) * cols + c), make_float2(acc[nt][0], acc[nt][1]));
+      __stcg(reinterpret_cast<float2*>(dst + int64_t(g + 8) * cols + c), make_float2(acc[nt][2], acc[nt][3]));
     }
   }
-}
-
-// out = scale * sum_s partial[s]; transpose_out: out[c][r] (dB [out, 16]) else out[r][c] (dA).
-// A CTA of 8 warps owns 32 consecutive outputs; warp w sums the splits s = w, w+8, ... and
-// the 8 warp sums are added in warp order (a fixed order: the result is deterministic).
-constexpr int LR_THREADS = 256;
-__global__ void __launch_bounds__(LR_THREADS)
-    lora_reduce_kernel(const __grid_constant__ OuterJobs jobs) {
-  grid_dep_wait();  // programmatic launch: no global access before the wait
-  __shared__ float ws[LR_THREADS / 32][33];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const OuterJob& job = jobs.j[find_job(jobs, int(blockIdx.x), true)];
-  const float* __restrict__ partial = job.partial;
-  const int64_t splits = job.splits, cols = job.cols;
-  const float scale = job.scale;
-  const int transpose_out = job.transpose;
-  float* __restrict__ out = job.out;
-  const int64_t e = int64_t(blockIdx.x - job.red0) * 32 + lane;  // index into [16][cols]
-  const bool ok = e < 16 * cols;
-  float sum = 0.f;
-  if (ok)
-    for (int64_t sp = warp; sp < splits; sp += LR_THREADS / 32) sum += partial[sp * 16 * cols + e];
-  ws[warp][lane] = sum;
+  // publish the partial, then take the column tile's ticket
+  __threadfence();
   __syncthreads();
-  if (warp == 0 && ok) {
-    float t = 0.f;
+  int32_t* ticket = jobs.tickets + job.tile0 + tile;
+  if (threadIdx.x == 0) s_last = atomicAdd(ticket, 1) == int(job.splits) - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // the last CTA of the tile: column c0 + threadIdx.x, all 16 rows, splits in order
+  const int64_t c = c0 + threadIdx.x;
+  if (c < cols) {
+    float sum[16];
 #pragma unroll
-    for (int w = 0; w < LR_THREADS / 32; ++w) t += ws[w][lane];
-    const int64_t r = e / cols, c = e - r * cols;
-    if (transpose_out)
-      out[c * 16 + r] = t * scale;
-    else
-      out[e] = t * scale;
+    for (int r = 0; r < 16; ++r) sum[r] = 0.f;
+    for (int64_t sp = 0; sp < job.splits; ++sp) {
+      const float* src = partial + sp * 16 * cols + c;
+#pragma unroll
+      for (int r = 0; r < 16; ++r) sum[r] += __ldcg(src + int64_t(r) * cols);
+    }
+    if (job.transpose) {
+#pragma unroll
+      for (int r = 0; r < 16; ++r) out[c * 16 + r] = sum[r] * scale;
+    } else {
+#pragma unroll
+      for (int r = 0; r < 16; ++r) out[int64_t(r) * cols + c] = sum[r] * scale;
+    }
   }
+  if (threadIdx.x == 0) *ticket = 0;  // every CTA of the tile has taken its ticket: reset for reuse
 }
 
-// Partial-sum floats of one job.
-static int64_t outer_floats(int64_t n, int64_t cols) { return outer_splits(n, cols) * 16 * cols; }
-
-// Appends one outer product (G = P^T Q over n tokens, scaled, optionally transposed) to a launch
-// table; its partial sums start at `partial`.
-static void add_job(OuterJobs* js, const __half* P, const __half* Q, int64_t n, int64_t cols,
-                    float scale, int transpose, float* out, float* partial, int64_t* ctas,
-                    int64_t* reds) {
-  OuterJob& j = js->j[js->n++];
-  j.P = P;
-  j.Q = Q;
-  j.partial = partial;
-  j.out = out;
-  j.cols = cols;
-  j.splits = outer_splits(n, cols);
-  j.tps = (n + j.splits - 1) / j.splits;
-  j.scale = scale;
-  j.transpose = transpose;
-  j.cta0 = int32_t(*ctas);
-  j.red0 = int32_t(*reds);
-  *ctas += j.splits * ((cols + LO_COLS - 1) / LO_COLS);
-  *reds += (16 * cols + 31) / 32;
+// Splits (token ranges) of the jobs of one launch: at most LO_TARGET_CTAS CTAs over all the
+// launch's column tiles (rounding down, so no SM gets a third CTA while others have two), at
+// least LO_MIN_TOK tokens a split; one split when the tickets would not fit.
+static int64_t grads_splits(int64_t n, int64_t col_tiles) {
+  if (col_tiles > LO_MAX_TILES) return 1;
+  int64_t s = LO_TARGET_CTAS / col_tiles;
+  const int64_t max_s = (n + LO_MIN_TOK - 1) / LO_MIN_TOK;
+  if (s > max_s) s = max_s;
+  return s < 1 ? 1 : s;
 }
 
-// One launch of the outer products of a table, then one launch of their reductions.
-static int run_jobs(const OuterJobs& js, int64_t n, int64_t ctas, int64_t reds, cudaStream_t s) {
-  NF4B_RETURN_IF(ctas > 0x7FFFFFFFll || reds > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
-  NF4B_CUDA_TRY(launch_pdl(lora_outer16_kernel, dim3(unsigned(ctas)), dim3(LO_THREADS), size_t(0),
-                           s, js, n));
-  int st = launch_status();
-  if (st != NF4B_OK) return st;
-  NF4B_CUDA_TRY(launch_pdl(lora_reduce_kernel, dim3(unsigned(reds)), dim3(LR_THREADS), size_t(0), s,
-                           js));
-  return launch_status();
+// The launch of a list of outer products G = P^T Q over n tokens (scaled, optionally
+// transposed): tickets and partials in `work` (LO_CNT_BYTES of zeroed tickets, then partials).
+struct GradsPlan {
+  OuterJobs js;
+  int64_t ctas;
+  int64_t bytes;  // workspace bytes the launch needs (0: no split)
+};
+
+struct GradsSpec {
+  const __half* P;
+  const __half* Q;
+  int64_t cols;
+  float scale;
+  int transpose;
+  float* out;
+};
+
+static GradsPlan plan_grads(const GradsSpec* specs, int n_specs, int64_t n, void* work) {
+  GradsPlan p{};
+  int64_t tiles = 0;
+  for (int i = 0; i < n_specs; ++i) tiles += (specs[i].cols + LO_COLS - 1) / LO_COLS;
+  const int64_t splits = grads_splits(n, tiles);
+  float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(work) + LO_CNT_BYTES);
+  int64_t floats = 0, ctas = 0, tile0 = 0;
+  for (int i = 0; i < n_specs; ++i) {
+    OuterJob& j = p.js.j[p.js.n++];
+    const int64_t ct = (specs[i].cols + LO_COLS - 1) / LO_COLS;
+    j.P = specs[i].P;
+    j.Q = specs[i].Q;
+    j.out = specs[i].out;
+    j.cols = specs[i].cols;
+    j.splits = splits;
+    j.tps = (n + splits - 1) / splits;
+    j.scale = specs[i].scale;
+    j.transpose = specs[i].transpose;
+    j.cta0 = int32_t(ctas);
+    j.tile0 = int32_t(tile0);
+    j.partial = splits > 1 && work ? part + floats : nullptr;
+    if (splits > 1) floats += splits * 16 * specs[i].cols;
+    ctas += splits * ct;
+    tile0 += ct;
+  }
+  p.js.tickets = static_cast<int32_t*>(work);
+  p.ctas = ctas;
+  p.bytes = splits > 1 ? LO_CNT_BYTES + floats * int64_t(sizeof(float)) : 0;
+  return p;
 }
 
-static int outer_and_reduce(const __half* P, const __half* Q, int64_t n, int64_t cols, float scale,
-                            int transpose_out, float* out, float* work, cudaStream_t s) {
-  OuterJobs js{};
-  int64_t ctas = 0, reds = 0;
-  add_job(&js, P, Q, n, cols, scale, transpose_out, out, work, &ctas, &reds);
-  return run_jobs(js, n, ctas, reds, s);
+static int run_grads(const GradsPlan& p, int64_t n, cudaStream_t s) {
+  NF4B_RETURN_IF(p.ctas > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
+  NF4B_CUDA_TRY(launch_pdl(lora_grads16_kernel, dim3(unsigned(p.ctas)), dim3(LO_THREADS), size_t(0), s, p.js, n));
+  return launch_status("lora_grads16_kernel launch");
+}
+
+// dA = s (dY B)^T X and dB = s dY^T (X A^T) of one adapter, as two jobs of one launch.
+static void adapter_specs(GradsSpec* sp, const __half* x, const __half* dy, const __half* xa,
+                          const __half* dyb, float scale, float* da, float* db, int64_t in_f,
+                          int64_t out_f) {
+  sp[0] = GradsSpec{dyb, x, in_f, scale, 0, da};   // dA[r, i] = s * sum_t dyb[t, r] x[t, i]
+  sp[1] = GradsSpec{xa, dy, out_f, scale, 1, db};  // dB[o, r] = s * sum_t dy[t, o] xa[t, r] (G^T)
 }
 
 }  // namespace nf4b
@@ -386,92 +456,84 @@ using namespace nf4b;
 extern "C" int64_t nf4b_lora_grads_work_bytes(int64_t n, int64_t in_features, int64_t out_features,
                                               int32_t rank) {
   if (n < 0 || in_features <= 0 || out_features <= 0 || rank != 16) return -1;
-  const int64_t a = outer_splits(n, in_features) * 16 * in_features;
-  const int64_t b = outer_splits(n, out_features) * 16 * out_features;
-  return (a > b ? a : b) * int64_t(sizeof(float));
+  GradsSpec sp[2];
+  adapter_specs(sp, nullptr, nullptr, nullptr, nullptr, 1.f, nullptr, nullptr, in_features, out_features);
+  return plan_grads(sp, 2, n, nullptr).bytes;
+}
+
+// Shared checks of one adapter's operands.
+static int check_adapter(const void* x, const void* dy, const void* xa, const void* dyb, const float* da,
+                         const float* db, int64_t in_f, int64_t out_f) {
+  NF4B_RETURN_IF(!x || !dy || !xa || !dyb || !da || !db, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(in_f <= 0 || out_f <= 0, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(in_f % 8 != 0 || out_f % 8 != 0, NF4B_ERR_UNSUPPORTED);
+  NF4B_RETURN_IF(!aligned(x, 16) || !aligned(dy, 16) || !aligned(xa, 16) || !aligned(dyb, 16),
+                 NF4B_ERR_ALIGNMENT);
+  return NF4B_OK;
+}
+
+// Launches the grads of `n_specs` jobs with workspace `work` (work_bytes bytes; its ticket words
+// zero), or zeros the outputs when there are no tokens.
+static int launch_grads(const GradsSpec* sp, int n_specs, int64_t n, void* work, int64_t work_bytes,
+                        cudaStream_t s) {
+  if (n == 0) {
+    for (int i = 0; i < n_specs; ++i)
+      NF4B_CUDA_TRY(cudaMemsetAsync(sp[i].out, 0, size_t(16 * sp[i].cols) * sizeof(float), s));
+    return NF4B_OK;
+  }
+  const GradsPlan p = plan_grads(sp, n_specs, n, work);
+  NF4B_RETURN_IF(p.bytes > 0 && (!work || work_bytes < p.bytes), NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(p.bytes > 0 && !aligned(work, 256), NF4B_ERR_ALIGNMENT);
+  return run_grads(p, n, s);
 }
 
 extern "C" int nf4b_lora_grads(const void* x, const void* dy, const void* xa, const void* dyb,
                                float scale, float* da, float* db, void* work, int64_t n,
                                int64_t in_features, int64_t out_features, int32_t rank,
                                void* stream) {
-  NF4B_RETURN_IF(!x || !dy || !xa || !dyb || !da || !db || !work, NF4B_ERR_INVALID_ARG);
-  NF4B_RETURN_IF(n < 0 || in_features <= 0 || out_features <= 0, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(n < 0, NF4B_ERR_INVALID_ARG);
   NF4B_RETURN_IF(rank != 16, NF4B_ERR_UNSUPPORTED);
-  NF4B_RETURN_IF(in_features % 8 != 0 || out_features % 8 != 0, NF4B_ERR_UNSUPPORTED);
-  NF4B_RETURN_IF(!aligned(x, 16) || !aligned(dy, 16) || !aligned(xa, 16) || !aligned(dyb, 16) ||
-                     !aligned(work, 8),
-                 NF4B_ERR_ALIGNMENT);
-  int st = check_device();
+  int st = check_adapter(x, dy, xa, dyb, da, db, in_features, out_features);
   if (st != NF4B_OK) return st;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (n == 0) {
-    NF4B_CUDA_TRY(cudaMemsetAsync(da, 0, size_t(16 * in_features) * sizeof(float), s));
-    NF4B_CUDA_TRY(cudaMemsetAsync(db, 0, size_t(16 * out_features) * sizeof(float), s));
-    return NF4B_OK;
-  }
-  // dA[r, i] = s * sum_t dyb[t, r] x[t, i]
-  st = outer_and_reduce(static_cast<const __half*>(dyb), static_cast<const __half*>(x), n,
-                        in_features, scale, 0, da, static_cast<float*>(work), s);
+  st = check_device();
   if (st != NF4B_OK) return st;
-  // dB[o, r] = s * sum_t dy[t, o] xa[t, r]  (computed as G[r, o], written transposed)
-  return outer_and_reduce(static_cast<const __half*>(xa), static_cast<const __half*>(dy), n,
-                          out_features, scale, 1, db, static_cast<float*>(work), s);
+  GradsSpec sp[2];
+  adapter_specs(sp, static_cast<const __half*>(x), static_cast<const __half*>(dy),
+                static_cast<const __half*>(xa), static_cast<const __half*>(dyb), scale, da, db, in_features,
+                out_features);
+  const int64_t need = plan_grads(sp, 2, n, nullptr).bytes;
+  return launch_grads(sp, 2, n, work, need, static_cast<cudaStream_t>(stream));
 }
 
-// ------------------------------------------------- several adapters in two launches
+// ------------------------------------------------- several adapters in one launch
 extern "C" int64_t nf4b_lora_grads_group_work_bytes(const nf4b_lora_grads_item* items, int32_t n_items,
                                                     int64_t n) {
   if (!items || n_items < 1 || n_items > LO_MAX_JOBS / 2 || n < 0) return -1;
-  int64_t floats = 0;
+  GradsSpec sp[LO_MAX_JOBS];
   for (int i = 0; i < n_items; ++i) {
     if (items[i].in_features <= 0 || items[i].out_features <= 0) return -1;
-    floats += outer_floats(n, items[i].in_features) + outer_floats(n, items[i].out_features);
+    adapter_specs(sp + 2 * i, nullptr, nullptr, nullptr, nullptr, 1.f, nullptr, nullptr, items[i].in_features,
+                  items[i].out_features);
   }
-  return floats * int64_t(sizeof(float));
+  return plan_grads(sp, 2 * n_items, n, nullptr).bytes;
 }
 
 extern "C" int nf4b_lora_grads_group(const nf4b_lora_grads_item* items, int32_t n_items, void* work,
                                      int64_t work_bytes, int64_t n, void* stream) {
   NF4B_RETURN_IF(!items || n_items < 1 || n < 0, NF4B_ERR_INVALID_ARG);
   NF4B_RETURN_IF(n_items > LO_MAX_JOBS / 2, NF4B_ERR_UNSUPPORTED);
+  GradsSpec sp[LO_MAX_JOBS];
   for (int i = 0; i < n_items; ++i) {
     const nf4b_lora_grads_item& it = items[i];
-    NF4B_RETURN_IF(!it.x || !it.dy || !it.xa || !it.dyb || !it.da || !it.db, NF4B_ERR_INVALID_ARG);
-    NF4B_RETURN_IF(it.in_features <= 0 || it.out_features <= 0, NF4B_ERR_INVALID_ARG);
-    NF4B_RETURN_IF(it.in_features % 8 != 0 || it.out_features % 8 != 0, NF4B_ERR_UNSUPPORTED);
-    NF4B_RETURN_IF(!aligned(it.x, 16) || !aligned(it.dy, 16) || !aligned(it.xa, 16) || !aligned(it.dyb, 16),
-                   NF4B_ERR_ALIGNMENT);
+    const int st = check_adapter(it.x, it.dy, it.xa, it.dyb, it.da, it.db, it.in_features, it.out_features);
+    if (st != NF4B_OK) return st;
+    adapter_specs(sp + 2 * i, static_cast<const __half*>(it.x), static_cast<const __half*>(it.dy),
+                  static_cast<const __half*>(it.xa), static_cast<const __half*>(it.dyb), it.scale, it.da, it.db,
+                  it.in_features, it.out_features);
   }
-  const int64_t need = nf4b_lora_grads_group_work_bytes(items, n_items, n);
-  NF4B_RETURN_IF(need < 0, NF4B_ERR_INVALID_ARG);
-  NF4B_RETURN_IF(need > 0 && (!work || work_bytes < need), NF4B_ERR_INVALID_ARG);
-  NF4B_RETURN_IF(need > 0 && !aligned(work, 8), NF4B_ERR_ALIGNMENT);
-  int st = check_device();
+  const int st = check_device();
   if (st != NF4B_OK) return st;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (n == 0) {
-    for (int i = 0; i < n_items; ++i) {
-      NF4B_CUDA_TRY(cudaMemsetAsync(items[i].da, 0, size_t(16 * items[i].in_features) * sizeof(float), s));
-      NF4B_CUDA_TRY(cudaMemsetAsync(items[i].db, 0, size_t(16 * items[i].out_features) * sizeof(float), s));
-    }
-    return NF4B_OK;
-  }
-  OuterJobs js{};
-  int64_t ctas = 0, reds = 0;
-  float* part = static_cast<float*>(work);
-  for (int i = 0; i < n_items; ++i) {
-    const nf4b_lora_grads_item& it = items[i];
-    // dA[r, i] = s * sum_t dyb[t, r] x[t, i]
-    add_job(&js, static_cast<const __half*>(it.dyb), static_cast<const __half*>(it.x), n, it.in_features,
-            it.scale, 0, it.da, part, &ctas, &reds);
-    part += outer_floats(n, it.in_features);
-    // dB[o, r] = s * sum_t dy[t, o] xa[t, r]  (computed as G[r, o], written transposed)
-    add_job(&js, static_cast<const __half*>(it.xa), static_cast<const __half*>(it.dy), n, it.out_features,
-            it.scale, 1, it.db, part, &ctas, &reds);
-    part += outer_floats(n, it.out_features);
-  }
-  return run_jobs(js, n, ctas, reds, s);
+  return launch_grads(sp, 2 * n_items, n, work, work_bytes, static_cast<cudaStream_t>(stream));
 }
 
 // ------------------------------------------------- entry point without allocation
@@ -481,8 +543,9 @@ extern "C" int nf4b_lora_grads_group(const nf4b_lora_grads_item* items, int32_t 
 // nf4b_lora_grads_noalloc keeps its split-token partial sums in this fixed file-scope device
 // array instead of a caller-provided buffer.  Every GPU that loads the library holds these
 // NF4B_NOALLOC_SCRATCH_BYTES until the process exits.  All calls share it: calls that overlap on
-// the GPU (other streams, other host threads) race on it.  Each call writes every partial sum it
-// later reads, so nothing has to start at zero and no clearing is needed.
+// the GPU (other streams, other host threads) race on it.  Its leading ticket words are zero when
+// the library is loaded (a __device__ array starts zeroed) and every call leaves them zero; each
+// call writes every partial sum it later reads, so nothing else has to start at zero.
 namespace nf4b {
 
 static __device__ __align__(256) float g_lora_noalloc_scratch[NF4B_NOALLOC_SCRATCH_BYTES / sizeof(float)];
@@ -514,32 +577,24 @@ extern "C" int nf4b_lora_grads_noalloc(const void* x, const void* dy, const void
                                        const void* dyb, float scale, float* da, float* db,
                                        int64_t n, int64_t in_features, int64_t out_features,
                                        int32_t rank, void* stream) {
-  NF4B_RETURN_IF(!x || !dy || !xa || !dyb || !da || !db, NF4B_ERR_INVALID_ARG);
-  NF4B_RETURN_IF(n < 0 || in_features <= 0 || out_features <= 0, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(n < 0, NF4B_ERR_INVALID_ARG);
   NF4B_RETURN_IF(rank != 16, NF4B_ERR_UNSUPPORTED);
-  NF4B_RETURN_IF(in_features % 8 != 0 || out_features % 8 != 0, NF4B_ERR_UNSUPPORTED);
-  NF4B_RETURN_IF(!aligned(x, 16) || !aligned(dy, 16) || !aligned(xa, 16) || !aligned(dyb, 16),
-                 NF4B_ERR_ALIGNMENT);
+  int st = check_adapter(x, dy, xa, dyb, da, db, in_features, out_features);
+  if (st != NF4B_OK) return st;
   const int64_t need = nf4b_lora_grads_work_bytes(n, in_features, out_features, rank);
   if (need > int64_t(NF4B_NOALLOC_SCRATCH_BYTES)) {
     record_message("nf4b_lora_grads_noalloc: the split-token partial sums need more than "
                    "NF4B_NOALLOC_SCRATCH_BYTES; use nf4b_lora_grads with a caller buffer");
     return NF4B_ERR_UNSUPPORTED;
   }
-  int st = check_device();
+  st = check_device();
   if (st != NF4B_OK) return st;
   float* work = nullptr;
   st = noalloc_scratch(&work);
   if (st != NF4B_OK) return st;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (n == 0) {
-    NF4B_CUDA_TRY(cudaMemsetAsync(da, 0, size_t(16 * in_features) * sizeof(float), s));
-    NF4B_CUDA_TRY(cudaMemsetAsync(db, 0, size_t(16 * out_features) * sizeof(float), s));
-    return NF4B_OK;
-  }
-  st = outer_and_reduce(static_cast<const __half*>(dyb), static_cast<const __half*>(x), n,
-                        in_features, scale, 0, da, work, s);
-  if (st != NF4B_OK) return st;
-  return outer_and_reduce(static_cast<const __half*>(xa), static_cast<const __half*>(dy), n,
-                          out_features, scale, 1, db, work, s);
+  GradsSpec sp[2];
+  adapter_specs(sp, static_cast<const __half*>(x), static_cast<const __half*>(dy),
+                static_cast<const __half*>(xa), static_cast<const __half*>(dyb), scale, da, db, in_features,
+                out_features);
+  return launch_grads(sp, 2, n, work, NF4B_NOALLOC_SCRATCH_BYTES, static_cast<cudaStream_t>(stream));
 }

@@ -5,9 +5,9 @@ q/v projections of the reference run the base layer is a bitsandbytes Linear4bit
 (r = 16, lora_alpha = 32 -> scaling 2; the reference only touches peft's input cast,
 solution/rmsnorm.py:137-150, and its dropout modules, solution/unpad.py:77-138).
 
-Here the whole thing is three launches forward (x A^T, then one tensor-core GEMM that
-unpacks W and adds the adapter as an extra K=16 slab) and four backward (dY B, the
-fused dX GEMM with the adapter slab, and the two weight-gradient reductions).
+Here the whole thing is two launches forward (x A^T, then one tensor-core GEMM that
+unpacks W and adds the adapter as an extra K=16 slab) and three backward (dY B, the
+fused dX GEMM with the adapter slab, and one launch for both weight gradients).
 Dropout must be 0 (the configuration this path serves); other adapters use peft's own path.
 """
 from __future__ import annotations
@@ -99,11 +99,12 @@ class NF4LoraFunction(torch.autograd.Function):
             if need_a or need_b:
                 da32 = torch.empty(LORA_RANK, in_f, dtype=torch.float32, device=dev)
                 db32 = torch.empty(out_f, LORA_RANK, dtype=torch.float32, device=dev)
-                wb = int(L.nf4b_lora_grads_work_bytes(n, in_f, out_f, LORA_RANK))
-                work = torch.empty(max(wb, 16) // 4 + 4, dtype=torch.float32, device=dev)
+                # the stream's zeroed workspace (its ticket words are left zero by every call)
+                work, _ = _workspace_bytes(dev, max(int(L.nf4b_lora_grads_work_bytes(n, in_f, out_f,
+                                                                                    LORA_RANK)), 256))
                 _lib.check(L.nf4b_lora_grads(x2.data_ptr(), dy.data_ptr(), xa.data_ptr(), dyb.data_ptr(),
                                              ctx.scaling, da32.data_ptr(), db32.data_ptr(),
-                                             work.data_ptr(), n, in_f, out_f, LORA_RANK, _stream(dev)),
+                                             work, n, in_f, out_f, LORA_RANK, _stream(dev)),
                            "nf4b_lora_grads")
                 da = da32.to(ctx.param_dtypes[0]) if need_a else None
                 db = db32.to(ctx.param_dtypes[1]) if need_b else None
@@ -230,10 +231,10 @@ class GroupedNF4Function(torch.autograd.Function):
                 pgrads += [da32, db32]
             if gitems:
                 arr = (_lib.LoraGradsItemC * len(gitems))(*gitems)
-                wb = int(L.nf4b_lora_grads_group_work_bytes(arr, len(gitems), n))
-                work = torch.empty(max(wb, 16) // 4 + 4, dtype=torch.float32, device=dev)
-                _lib.check(L.nf4b_lora_grads_group(arr, len(gitems), work.data_ptr(), work.numel() * 4, n,
-                                                   _stream(dev)), "nf4b_lora_grads_group")
+                wb = max(int(L.nf4b_lora_grads_group_work_bytes(arr, len(gitems), n)), 256)
+                work, wbytes = _workspace_bytes(dev, wb)
+                _lib.check(L.nf4b_lora_grads_group(arr, len(gitems), work, wbytes, n, _stream(dev)),
+                           "nf4b_lora_grads_group")
         pgrads = [None if gr is None else gr.to(dt) for gr, dt in zip(pgrads, ctx.param_dtypes)]
         return (None if dx is None else dx.reshape(ctx.x_shape), None, *pgrads)
 

@@ -134,7 +134,11 @@ def dequantize_nf4(A: torch.Tensor, st) -> torch.Tensor:
     return out
 
 
-_WORK = {}  # (device index, stream handle) -> split-K workspace (uint8, zeroed once)
+# (device index, stream handle) -> the stream's workspace (uint8, zeroed once): the split-K
+# partials of the fused GEMMs and the token-range partials of the LoRA weight gradients, behind
+# leading counter / ticket words that every call leaves zero.  Calls on one stream never overlap,
+# so one buffer per stream serves both.
+_WORK = {}
 
 
 def _workspace(device, n: int, in_f: int, out_f: int, backward: bool):

@@ -88,10 +88,10 @@ def test_lora_module_trains(cuda_lib):
 
 @pytest.mark.parametrize("n", [1, 77, 1311])
 def test_grouped_lora_grads_match_per_adapter_calls(cuda_lib, n):
-    """nf4b_lora_grads_group (q and v adapters of one layer: dA, dB of both in one outer-product
-    launch and one reduction launch) gives the same dA / dB, bit for bit, as one
-    nf4b_lora_grads call per adapter (same token splits, same reduction order), and matches
-    the fp64 products."""
+    """nf4b_lora_grads_group (q and v adapters of one layer: dA, dB of both in one launch) gives
+    the dA / dB of one nf4b_lora_grads call per adapter up to fp32 summation order (the group
+    splits the tokens differently), repeats bit for bit (fixed reduction order), and matches the
+    fp64 products."""
     import ctypes
     from stew_b200 import _lib
     L = _lib.lib()
@@ -113,17 +113,23 @@ def test_grouped_lora_grads_match_per_adapter_calls(cuda_lib, n):
         keep.append((dy, xa, dyb, da, db, out_f, s))
     arr = (_lib.LoraGradsItemC * 2)(*items)
     wb = int(L.nf4b_lora_grads_group_work_bytes(arr, 2, n))
-    assert wb > 0
-    work = torch.empty(wb // 4 + 4, device="cuda")
+    assert (wb > 0) == (n > 64), "tokens are split in ranges of at least 64"
+    work = torch.zeros(wb // 4 + 4, device="cuda")  # ticket words zero before the first call
     assert L.nf4b_lora_grads_group(arr, 2, work.data_ptr(), wb, n, stream) == 0, L.nf4b_last_error()
-    assert L.nf4b_lora_grads_group(arr, 2, work.data_ptr(), wb - 4, n, stream) == _lib.NF4B_ERR_INVALID_ARG
-    for dy, xa, dyb, da, db, out_f, s in keep:
+    if wb > 0:
+        assert L.nf4b_lora_grads_group(arr, 2, work.data_ptr(), wb - 4, n, stream) == _lib.NF4B_ERR_INVALID_ARG
+    first = [(da.clone(), db.clone()) for _, _, _, da, db, _, _ in keep]
+    assert L.nf4b_lora_grads_group(arr, 2, work.data_ptr(), wb, n, stream) == 0, L.nf4b_last_error()
+    assert int(work[:1024].view(torch.int32).count_nonzero()) == 0, "ticket words must be left zero"
+    for (da0, db0), (dy, xa, dyb, da, db, out_f, s) in zip(first, keep):
+        torch.cuda.synchronize()
+        assert torch.equal(da0, da) and torch.equal(db0, db), "a repeated call differs"
         da1 = torch.empty(16, 1536, device="cuda")
         db1 = torch.empty(out_f, 16, device="cuda")
-        w1 = torch.empty(int(L.nf4b_lora_grads_work_bytes(n, 1536, out_f, 16)) // 4 + 4, device="cuda")
+        w1 = torch.zeros(max(int(L.nf4b_lora_grads_work_bytes(n, 1536, out_f, 16)), 16) // 4 + 4, device="cuda")
         assert L.nf4b_lora_grads(x.data_ptr(), dy.data_ptr(), xa.data_ptr(), dyb.data_ptr(), s, da1.data_ptr(),
                                  db1.data_ptr(), w1.data_ptr(), n, 1536, out_f, 16, stream) == 0
         torch.cuda.synchronize()
-        assert torch.equal(da, da1) and torch.equal(db, db1)
+        assert max_rel_err(da, da1) <= 1e-5 and max_rel_err(db, db1) <= 1e-5
         assert max_rel_err(da, s * dyb.double().T @ x.double()) <= 1e-3
         assert max_rel_err(db, s * dy.double().T @ xa.double()) <= 1e-3

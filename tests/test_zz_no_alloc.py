@@ -2,8 +2,9 @@
 allocate device memory (their framework already holds the GPU's memory in its own pool, or
 they run where allocating is not allowed), gives the same dA / dB as nf4b_lora_grads with a
 caller-provided scratch buffer -- called through the C ABI, twice in a row, so the second
-call runs on the scratch array the first one left behind.  Oversized problems are refused
-before anything is launched.
+call runs on the scratch array the first one left behind (its ticket words must have been left
+zero).  Its fixed array covers the scratch of every rank-16 problem, so it refuses none; the
+size check that would refuse one stays as a guard.
 
 This file is named to be collected last."""
 import ctypes
@@ -38,7 +39,7 @@ def test_noalloc_lora_grads_match_caller_scratch_version(cuda_lib):
         db_ref = torch.empty(out_f, 16, device="cuda")
         wb = int(L.nf4b_lora_grads_work_bytes(n, in_f, out_f, 16))
         assert 0 < wb <= L.nf4b_lora_grads_work_bytes(n, in_f, out_f, 16)
-        work = torch.empty(wb // 4 + 4, device="cuda")
+        work = torch.zeros(wb // 4 + 4, device="cuda")  # ticket words zero before the first call
         rc = L.nf4b_lora_grads(x.data_ptr(), dy.data_ptr(), xa.data_ptr(), dyb.data_ptr(), 2.0,
                                da_ref.data_ptr(), db_ref.data_ptr(), work.data_ptr(), n, in_f, out_f,
                                16, stream)
@@ -58,12 +59,19 @@ def test_noalloc_lora_grads_match_caller_scratch_version(cuda_lib):
     assert _lib.NF4B_OK == 0
 
 
-def test_noalloc_refuses_problems_larger_than_its_scratch(cuda_lib):
+def test_noalloc_scratch_covers_every_rank16_problem(cuda_lib):
+    """The scratch of a rank-16 problem is at most ~2.4 MB (two token-range partials of 8 KB per
+    SM plus 4 KB of ticket words), below the fixed 4 MiB array for every shape and token count;
+    wrong ranks are refused before anything is launched."""
     from stew_b200 import _lib
     L = cuda_lib
-    big_in = 1 << 20  # 16 x 2^20 fp32 partial sums = 64 MiB > the fixed scratch
-    assert L.nf4b_lora_grads_work_bytes(4096, big_in, 64, 16) > (8 << 20)
-    p = ctypes.c_void_p(256)  # never dereferenced: the size check comes first
-    rc = L.nf4b_lora_grads_noalloc(p, p, p, p, 2.0, p, p, 4096, big_in, 64, 16, None)
+    limit = 4 << 20
+    worst = 0
+    for n in (1, 64, 65, 1170, 2048, 8192, 1 << 20):
+        for in_f in (8, 256, 1536, 8960, 8192, 12800, 18816, 1 << 20):
+            for out_f in (8, 256, 1536, 8960):
+                worst = max(worst, int(L.nf4b_lora_grads_work_bytes(n, in_f, out_f, 16)))
+    assert 0 < worst <= limit
+    p = ctypes.c_void_p(256)  # never dereferenced: the rank check comes before any launch
+    rc = L.nf4b_lora_grads_noalloc(p, p, p, p, 2.0, p, p, 4096, 1536, 1536, 8, None)
     assert rc == _lib.NF4B_ERR_UNSUPPORTED
-    assert b"NF4B_NOALLOC_SCRATCH_BYTES" in L.nf4b_last_error()
