@@ -490,7 +490,7 @@ def run_reference(args):
 
 
 def profile_case():
-    """Launches, in order: nf4_dequant_batched_kernel (2 layers = 14 matrices, 235.7 MB of
+    """Launches, in order: nf4_dequant_tma_kernel (2 layers = 14 matrices, 235.7 MB of
     algorithmic traffic, larger than L2), nf4_gemm_kernel<fwd> and nf4_gemm_kernel<bwd> on the
     gate projection (8960 x 1536) at N = 2048 tokens."""
     import torch
@@ -701,7 +701,7 @@ def main():
                        "algorithmic_bytes_per_step": algo,
                        "l2": "inputs larger than L2: 3.30 GB moved per step, no flush needed",
                        "parallelism": f"replicas x{world} (no collective on this path)"},
-            "roofline": {"bound": "hbm", "kernel": "nf4_dequant_batched_kernel",
+            "roofline": {"bound": "hbm", "kernel": "nf4_dequant_tma_kernel",
                          "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 3), "peak_source": f"{peak_src} hbm_gbs",
                          "traffic": traffic,
@@ -711,7 +711,7 @@ def main():
             "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clk,
-            # headline timed region: one nf4_dequant_batched_kernel launch per step
+            # headline timed region: one nf4_dequant_tma_kernel launch per step
             "gpu_launches": args.steps,
         }
         print(json.dumps(line), flush=True)

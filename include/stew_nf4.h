@@ -195,6 +195,22 @@ int nf4b_linear_bwd_dx_group(const nf4b_linear_bwd_item* items, int32_t n_items,
                              int64_t n, int64_t in_features, void* work, int64_t work_bytes,
                              void* stream);
 
+/* The gate/up projections of a SwiGLU MLP and the SwiGLU itself in ONE launch:
+ *   gate_out[n, out] = X . Wg^T,  up_out[n, out] = X . Wu^T           (fp16, kept for the backward)
+ *   m_out[n, out]    = fp16(gate_out * sigmoid(gate_out) * up_out)    (the input of down)
+ * on the fp16 gate and up values, fp32 inside with one rounding and a fast exp and divide: the
+ * rounding points of the reference's SwiGLU kernel (solution/swiglu.py:16-23, which its
+ * unpad path calls, solution/unpad.py:60-63), and bit for bit what nf4b_swiglu_fwd gives.  Gate and up share the shape [out, in] (out a multiple of 64),
+ * no bias, no adapter.  Each 128-row tile holds 64 features of both weights, so the epilogue
+ * has gate and up of a feature side by side.  `work`: split-K workspace of
+ * nf4b_linear_swiglu_work_bytes(n, in, out) bytes, same contract as nf4b_linear_fwd_ws.
+ * No counterpart in the reference (there: two F.linear calls, then the SwiGLU kernel).  */
+int64_t nf4b_linear_swiglu_work_bytes(int64_t n, int64_t in_features, int64_t out_features);
+int nf4b_linear_fwd_swiglu(const void* x, int64_t n, int64_t in_features, const uint8_t* gate_packed,
+                           const nf4b_qstate* gate_qs, const uint8_t* up_packed, const nf4b_qstate* up_qs,
+                           void* gate_out, void* up_out, void* m_out, int64_t out_features, void* work,
+                           int64_t work_bytes, void* stream);
+
 /* LoRA weight gradients (fp32 out, overwritten), both in one launch:
  *   dA[rank, in]  = scale * (dY B)^T X
  *   dB[out, rank] = scale * dY^T (X A^T)

@@ -44,10 +44,12 @@ int nf4b_rope_qk(const void* q, const void* k, const float* cos_t, const float* 
                  void* k_out, int64_t tokens, int32_t q_heads, int32_t k_heads, int32_t head_dim,
                  int32_t inverse, void* stream);
 
-/* m = fp16(fp16(silu(gate)) * up), n elements (a multiple of 8).  */
+/* m = fp16(gate * sigmoid(gate) * up), fp32 inside (the reference's SwiGLU kernel,
+ * solution/swiglu.py:16-23), n elements (a multiple of 8).  */
 int nf4b_swiglu_fwd(const void* gate, const void* up, void* out, int64_t n, void* stream);
 
-/* dgate = fp16(fp16(dout*up) * silu'(gate)), dup = fp16(dout * fp16(silu(gate))).  */
+/* dup = fp16(dout * gate * sig), dgate = fp16(dout * up * sig * (1 + gate * (1 - sig))),
+ * sig = sigmoid(gate), fp32 inside (solution/swiglu.py:26-37).  */
 int nf4b_swiglu_bwd(const void* dout, const void* gate, const void* up, void* dgate, void* dup,
                     int64_t n, void* stream);
 

@@ -134,6 +134,7 @@ struct GemmArgs {
   int32_t* ws_cnt;        // split-K: per-tile counters [2][G_SPLIT_MAX_TILES] + exit count, zero
                           // between launches
   int32_t drop_ticket_unit;  // test hook: this work unit skips its ticket (-1: none)
+  __half* glu_out;        // SwiGLU launches: m = fp16(gate * sigmoid(gate) * up) [n, out]
 };
 
 __device__ int g_gemm_error;
@@ -206,6 +207,13 @@ __device__ __forceinline__ uint32_t slab_off(int r, int kc) {
   return uint32_t((r >> 3) * 256 + kc * 128 + (r & 7) * 16);
 }
 
+// sigmoid of the SwiGLU epilogue: fast exp and divide, the expression of the standalone SwiGLU
+// kernel (step_ops.cu) -- m = fp16(g * sigmoid(g) * u) with fp32 inside, the rounding points
+// of the reference's SwiGLU kernel (solution/swiglu.py:16-23).  (The IEEE-exact exp and divide
+// cost the epilogue enough issue slots to slow the decode: 96.4 vs 76.7 us on gate/up at 1,170
+// tokens.)
+__device__ __forceinline__ float glu_sigmoid(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+
 __device__ __forceinline__ uint4 scale_pack8(uint4 v, float s) {
   const __half2* h = reinterpret_cast<const __half2*>(&v);
   uint4 o;
@@ -246,13 +254,16 @@ struct TileCoord {
 // MULTI: the launch carries more than one weight (a grouped forward).  Single-weight launches
 // compile with the weight index fixed at 0, so its fields stay direct constant-bank operands.
 // PAIR: tiles are 256 weight rows, of which CTA `rank` of the pair owns rows 128 rank ..
-template <bool MULTI, bool PAIR>
+// GLU: a SwiGLU launch over gate (weight 0) and up (weight 1): a CTA's 128 rows are 64 features
+// of both, so m0 is the first of the CTA's 64 features.
+template <bool MULTI, bool PAIR, bool GLU>
 __device__ __forceinline__ TileCoord tile_coord(const GemmArgs& g, int tile, uint32_t rank) {
   TileCoord c;
   const int mt = tile / g.n_tiles;
   const int nt = tile - mt * g.n_tiles;
   c.seg = MULTI ? (mt >= g.m_end[0]) + (mt >= g.m_end[1]) : 0;
-  c.m0 = int64_t(mt - (c.seg ? g.m_end[c.seg - 1] : 0)) * (PAIR ? 2 * G_M : G_M) + int64_t(rank) * G_M;
+  c.m0 = GLU ? int64_t(mt) * (PAIR ? G_M : G_M / 2) + int64_t(rank) * (G_M / 2)
+             : int64_t(mt - (c.seg ? g.m_end[c.seg - 1] : 0)) * (PAIR ? 2 * G_M : G_M) + int64_t(rank) * G_M;
   c.t0 = int64_t(nt) * g.tile_n;
   c.tn_real = int(min64(g.tile_n, g.n - c.t0));
   c.tn = (c.tn_real + 15) & ~15;
@@ -268,12 +279,12 @@ struct WorkUnit {
   int kb, ke;   // stage range [kb, ke)
 };
 
-template <bool MULTI, bool PAIR>
+template <bool MULTI, bool PAIR, bool GLU>
 __device__ __forceinline__ WorkUnit work_unit(const GemmArgs& g, int u, uint32_t rank) {
   WorkUnit w;
   w.tile = u / g.splits;
   w.split = u - w.tile * g.splits;
-  w.tc = tile_coord<MULTI, PAIR>(g, w.tile, rank);
+  w.tc = tile_coord<MULTI, PAIR, GLU>(g, w.tile, rank);
   w.kb = int((int64_t(w.split) * g.nk) / g.splits);
   w.ke = int((int64_t(w.split + 1) * g.nk) / g.splits);
   return w;
@@ -332,7 +343,9 @@ __device__ __forceinline__ bool wait_count(const int32_t* p, int want) {
 
 // SPLIT: compiled with the split-K epilogue (launches with g.splits > 1).
 // PAIR: launched as 2-CTA clusters; CTA rank 0 issues cta_group::2 MMAs over both CTAs' tiles.
-template <bool BWD, bool SPLIT, bool MULTI, bool PAIR>
+// GLU: the SwiGLU forward of an MLP: gate and up in one tile, epilogue writes gate, up and
+// m = fp16(gate * sigmoid(gate) * up).
+template <bool BWD, bool SPLIT, bool MULTI, bool PAIR, bool GLU>
 __global__ void __launch_bounds__(G_THREADS, 1)
     nf4_gemm_kernel(const __grid_constant__ CUtensorMap tm_act0, const __grid_constant__ CUtensorMap tm_act1,
                     const __grid_constant__ CUtensorMap tm_act2, const __grid_constant__ CUtensorMap tm_w0,
@@ -341,6 +354,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   // BWD && MULTI: several weights along K (dX = sum_i dY_i W_i); !BWD && MULTI: several
   // weights along M (Y_i = X W_i^T).
   constexpr bool KCAT = BWD && MULTI;
+  static_assert(!GLU || (!BWD && !MULTI), "SwiGLU launches are forward, over one gate/up pair");
   using L = Smem<PAIR>;
   constexpr int NS = L::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -444,7 +458,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int u = unit0; ok && u < nunits; u += ustride) {
-        const WorkUnit wu = work_unit<MULTI, PAIR>(g, u, rank);
+        const WorkUnit wu = work_unit<MULTI, PAIR, GLU>(g, u, rank);
         const TileCoord& tc = wu.tc;
         // A pair tile's MMA h (h = 0, 1) covers tokens [256 h, 256 h + n_h) of the tile, n_h =
         // min(tn - 256 h, 256); it reads the first n_h / 2 of them from rank 0 and the rest
@@ -469,7 +483,12 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           for (int h = 0; h < nh; ++h)
             tma_load_2d(smem + L::X + s * L::X_BYTES + h * (G_NMAX / 2) * 128, KCAT ? tm_a : &tm_act0,
                         &full[s], kl * G_K, trow[h]);
-          if (!BWD)
+          if (GLU) {
+            // gate rows [m0, m0 + 64) in packed rows 0-63, up rows [m0, m0 + 64) in rows 64-127
+            tma_load_2d(smem + L::P + s * L::P_BYTES, &tm_w0, &full[s], kl * (G_K / 2), int(tc.m0));
+            tma_load_2d(smem + L::P + s * L::P_BYTES + L::P_BYTES / 2, &tm_w1, &full[s], kl * (G_K / 2),
+                        int(tc.m0));
+          } else if (!BWD)
             tma_load_2d(smem + L::P + s * L::P_BYTES, tm_w, &full[s], kl * (G_K / 2), int(tc.m0));
           else
             tma_load_2d(smem + L::P + s * L::P_BYTES, tm_w, &full[s], int(tc.m0 / 2), kl * G_K);
@@ -489,7 +508,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       const uint64_t ad0 = BWD ? smem_desc_sw128(sbase + L::A, 8192, 1024) : smem_desc_sw128(sbase + L::A, 16, 1024);
       const uint64_t bd0 = smem_desc_sw128(sbase + L::X, 16, 1024);
       for (int u = unit0; ok && u < nunits; u += ustride, ++lt) {
-        const WorkUnit wu = work_unit<MULTI, PAIR>(g, u, rank);
+        const WorkUnit wu = work_unit<MULTI, PAIR, GLU>(g, u, rank);
         const TileCoord& tc = wu.tc;
         // Single CTAs: one 256-column accumulator per tile, two alternating between tiles
         // (acc_full / acc_empty[b]).  Pairs: one 512-column accumulator per tile, MMA h writing
@@ -641,16 +660,22 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     const uint32_t p_off0 = BWD ? uint32_t(r * 64 + (((2 * j) ^ sw) << 4)) : uint32_t(r * 32) + (sw32 << 4);
     const uint32_t p_off1 = BWD ? uint32_t(r * 64 + (((2 * j + 1) ^ sw) << 4))
                                 : uint32_t(r * 32) + ((1u ^ sw32) << 4);
-    const uint32_t a_off = uint32_t(j * 8192 + (r >> 3) * 1024 + (r & 7) * 128);
-    const uint32_t key = uint32_t(r & 7);
+    // GLU: packed row d is row d & 63 of gate (d < 64) or of up; it goes to operand row
+    // 32 q + 16 (up) + i for feature 16 q + i, so TMEM lanes i and i + 16 of an epilogue warp
+    // hold the gate and up rows of one feature
+    const int rrow = GLU ? (d & 63) : r;  // row of its weight, from the tile's m0
+    const int arow = GLU ? 32 * ((d & 63) >> 4) + 16 * (d >> 6) + (d & 15) : r;
+    const uint32_t a_off = uint32_t(j * 8192 + (arow >> 3) * 1024 + (arow & 7) * 128);
+    const uint32_t key = uint32_t(arow & 7);
     const uint32_t k16 = g.k16, k31 = g.k16 << 15;
 
     uint32_t it = 0, lc = 0;
     bool ok = true;
     for (int u = unit0; ok && u < nunits; u += ustride) {
-      const WorkUnit wu = work_unit<MULTI, PAIR>(g, u, rank);
+      const WorkUnit wu = work_unit<MULTI, PAIR, GLU>(g, u, rank);
       const TileCoord& tc = wu.tc;
-      const int tws = MULTI ? tc.seg : 0;  // the tile's weight (forward); weight 0 backward
+      // the tile's weight (forward; GLU: this thread's row's); weight 0 backward
+      const int tws = GLU ? (d >> 6) : (MULTI ? tc.seg : 0);
       const GemmW& W = g.w[tws];
       // one slab per adapter (a K-concatenated backward may carry several), in the order the
       // MMA issuer consumes them
@@ -717,7 +742,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       if (!ok) break;
 
       const int64_t col = BWD ? (tc.m0 + 64 * j) : 0;
-      const bool lane_valid = BWD ? (col < g.in_f) : (tc.m0 + r < W.out_f);
+      const bool lane_valid = BWD ? (col < g.in_f) : (tc.m0 + rrow < W.out_f);
       // weight of stage k, and the element offset of the thread's first value in it
       struct Src {
         ScaleSrc v;
@@ -729,7 +754,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         if (KCAT) x.ws = kseg(g, k);
         const GemmW& Wk = g.w[KCAT ? x.ws : tws];
         const int kl = KCAT ? k - kbeg(g, x.ws) : k;
-        const int64_t e = BWD ? int64_t(kl * G_K + r) * g.in_f + col : (tc.m0 + r) * g.in_f + int64_t(kl) * G_K;
+        const int64_t e = BWD ? int64_t(kl * G_K + r) * g.in_f + col : (tc.m0 + rrow) * g.in_f + int64_t(kl) * G_K;
         x.v = load_scale_src(Wk, e >> Wk.log2_bs, lane_valid);
         return x;
       };
@@ -747,7 +772,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         const GemmW& Wk = g.w[x.ws];
         const int kl = KCAT ? k - kbeg(g, x.ws) : k;
         const int64_t e = BWD ? int64_t(kl * G_K + r) * g.in_f + col + 32
-                              : (tc.m0 + r) * g.in_f + int64_t(kl) * G_K + 32;
+                              : (tc.m0 + rrow) * g.in_f + int64_t(kl) * G_K + 32;
         x.v = load_scale_src(Wk, e >> Wk.log2_bs, lane_valid);
         return scale_of(x);
       };
@@ -815,11 +840,13 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     volatile int* s_ticket = reinterpret_cast<volatile int*>(smem + L::MISC + 8);  // [2]
     uint32_t lt = 0;
     for (int u = unit0; u < nunits; u += ustride, ++lt) {
-      const WorkUnit wu = work_unit<MULTI, PAIR>(g, u, rank);
+      const WorkUnit wu = work_unit<MULTI, PAIR, GLU>(g, u, rank);
       // split-K bookkeeping is per CTA: a pair's two 128-row halves are separate tiles there
       const int ctile = PAIR ? 2 * wu.tile + int(rank) : wu.tile;
       const TileCoord& tc = wu.tc;
-      const GemmW& W = g.w[MULTI ? tc.seg : 0];
+      // GLU: lanes 0-15 of a warp hold gate rows, lanes 16-31 the up rows of the same features
+      const int glu_up = GLU ? (lane >> 4) : 0;
+      const GemmW& W = g.w[GLU ? glu_up : (MULTI ? tc.seg : 0)];
       const int64_t ld_out = BWD ? g.in_f : W.out_f;
       // single CTAs: accumulator b of two; a pair: the tile's 512 columns, handed over in two
       // halves (acc_full[0] / [1]); split-K takes both halves at once
@@ -834,7 +861,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       tc_fence_after();
       if (!ok) break;
       const int prow = 32 * lq + lane;  // accumulator row = TMEM lane
-      const int64_t row = tc.m0 + prow;
+      // output column of this lane's row (GLU: the feature; lanes 2i, 2i+1 stay adjacent)
+      const int64_t row = GLU ? tc.m0 + 16 * lq + (lane & 15) : tc.m0 + prow;
       const bool row_ok = row < ld_out;  // ld_out is a multiple of 64: pairs are all in or out
       const uint32_t taddr = tmem_base + (uint32_t(32 * lq) << 16) + b * G_ACC_COLS;
       constexpr int ACC_T = acc_tokens<PAIR>();
@@ -885,6 +913,43 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         uint32_t* outp = reinterpret_cast<uint32_t*>(W.out + (tc.t0 + (odd ? 1 : 0)) * ld_out +
                                                      (row & ~int64_t(1)));
         // 16 half2 stores of one 32-token chunk; lim: the lane's stores with jj < lim land
+        // SwiGLU epilogue of one 32-token chunk: this lane's gate or up row to its output (as
+        // emit), then m = fp16(g * sigmoid(g) * u) from the fp16 g and u -- each lane trades
+        // half of its chunk with lane ^ 16, so lanes 0-15 get tokens 0-15 of their feature and
+        // lanes 16-31 tokens 16-31 -- stored with the same neighbour pairing
+        uint32_t* moutp = GLU ? reinterpret_cast<uint32_t*>(g.glu_out + (tc.t0 + (odd ? 1 : 0)) * ld_out +
+                                                            (row & ~int64_t(1)))
+                              : nullptr;
+        auto glu_emit = [&](const uint32_t (&acc)[32], int c0) {
+          uint32_t hp[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) hp[k] = pack_half2(__uint_as_float(acc[2 * k]), __uint_as_float(acc[2 * k + 1]));
+          const int lim = row_ok ? tc.tn_real - c0 - (odd ? 1 : 0) : 0;
+          uint32_t* p = outp + ((int64_t(c0) * ld_out) >> 1);
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const uint32_t h = prmt(hp[k], __shfl_xor_sync(0xffffffffu, hp[k], 1), xsel);
+            if (2 * k < lim) p[int64_t(k) * ld_out] = h;
+          }
+          uint32_t mp[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t other = __shfl_xor_sync(0xffffffffu, glu_up ? hp[k] : hp[8 + k], 16);
+            const uint32_t gg = glu_up ? other : hp[k];
+            const uint32_t uu = glu_up ? hp[8 + k] : other;
+            const float2 gf = __half22float2(*reinterpret_cast<const __half2*>(&gg));
+            const float2 uf = __half22float2(*reinterpret_cast<const __half2*>(&uu));
+            mp[k] = pack_half2(gf.x * glu_sigmoid(gf.x) * uf.x, gf.y * glu_sigmoid(gf.y) * uf.y);
+          }
+          const int base = glu_up ? 16 : 0;
+          const int limm = row_ok ? tc.tn_real - c0 - base - (odd ? 1 : 0) : 0;
+          uint32_t* pm = moutp + ((int64_t(c0 + base) * ld_out) >> 1);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t h = prmt(mp[k], __shfl_xor_sync(0xffffffffu, mp[k], 1), xsel);
+            if (2 * k < limm) pm[int64_t(k) * ld_out] = h;
+          }
+        };
         auto emit = [&](const uint32_t (&acc)[32], int c0, auto bias_c, int lim) {
           uint32_t* p = outp + ((int64_t(c0) * ld_out) >> 1);
 #pragma unroll
@@ -941,6 +1006,10 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             }
             // stores of token c0 + jj + odd land while that token is in the tile; the paths
             // below are warp-uniform (emit shuffles across the warp)
+            if (GLU) {
+              glu_emit(acc, c0);
+              continue;
+            }
             const int lim = row_ok ? tc.tn_real - c0 - (odd ? 1 : 0) : 0;
             const bool whole = __all_sync(0xffffffffu, lim >= 32);
             if (has_bias) {
@@ -1053,7 +1122,7 @@ static int sm_count_cached() {
   return cached[dev];
 }
 
-template <bool BWD, bool SPLIT, bool MULTI, bool PAIR>
+template <bool BWD, bool SPLIT, bool MULTI, bool PAIR, bool GLU = false>
 static int set_smem_attr() {
   static std::mutex mu;
   static bool done[64] = {false};
@@ -1062,7 +1131,7 @@ static int set_smem_attr() {
   if (dev < 0 || dev >= 64) return NF4B_ERR_DEVICE;
   std::lock_guard<std::mutex> lock(mu);
   if (!done[dev]) {
-    NF4B_CUDA_TRY(cudaFuncSetAttribute(nf4_gemm_kernel<BWD, SPLIT, MULTI, PAIR>,
+    NF4B_CUDA_TRY(cudaFuncSetAttribute(nf4_gemm_kernel<BWD, SPLIT, MULTI, PAIR, GLU>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, Smem<PAIR>::ALLOC));
     done[dev] = true;
   }
@@ -1102,7 +1171,7 @@ static int pair_slots_cached() {
     int n = 0;
     if (set_smem_attr<false, false, false, true>() == NF4B_OK) {
       PairLaunch pl(2u * unsigned(sm_count_cached()), nullptr, false);
-      if (cudaOccupancyMaxActiveClusters(&n, nf4_gemm_kernel<false, false, false, true>, &pl.cfg) !=
+      if (cudaOccupancyMaxActiveClusters(&n, nf4_gemm_kernel<false, false, false, true, false>, &pl.cfg) !=
           cudaSuccess)
         n = 0;
     }
@@ -1239,17 +1308,17 @@ static int64_t plan_work_bytes(const GemmPlan& p) {
 // Token rows of the activation tile one CTA loads per stage.
 static uint32_t act_box_rows(const GemmPlan& p) { return p.pair ? G_NMAX / 2 : uint32_t(p.tile_n); }
 
-template <bool BWD, bool SPLIT, bool MULTI, bool PAIR>
+template <bool BWD, bool SPLIT, bool MULTI, bool PAIR, bool GLU = false>
 static int launch_variant(unsigned grid, const CUtensorMap (&ta)[G_MAX_W], const CUtensorMap (&tw)[G_MAX_W],
                           const GemmArgs& g, cudaStream_t s) {
-  int st = set_smem_attr<BWD, SPLIT, MULTI, PAIR>();
+  int st = set_smem_attr<BWD, SPLIT, MULTI, PAIR, GLU>();
   if (st != NF4B_OK) return st;
   if (!PAIR) {
-    NF4B_CUDA_TRY(launch_pdl(nf4_gemm_kernel<BWD, SPLIT, MULTI, PAIR>, dim3(grid), dim3(G_THREADS),
+    NF4B_CUDA_TRY(launch_pdl(nf4_gemm_kernel<BWD, SPLIT, MULTI, PAIR, GLU>, dim3(grid), dim3(G_THREADS),
                              size_t(Smem<PAIR>::ALLOC), s, ta[0], ta[1], ta[2], tw[0], tw[1], tw[2], g));
   } else {
     PairLaunch pl(grid, s, pdl_enabled(s));
-    NF4B_CUDA_TRY(cudaLaunchKernelEx(&pl.cfg, nf4_gemm_kernel<BWD, SPLIT, MULTI, PAIR>, ta[0], ta[1],
+    NF4B_CUDA_TRY(cudaLaunchKernelEx(&pl.cfg, nf4_gemm_kernel<BWD, SPLIT, MULTI, PAIR, GLU>, ta[0], ta[1],
                                      ta[2], tw[0], tw[1], tw[2], g));
   }
   return NF4B_OK;
@@ -1260,9 +1329,10 @@ static int launch_variant(unsigned grid, const CUtensorMap (&ta)[G_MAX_W], const
 static std::atomic<int> g_drop_ticket_unit{-1};
 
 // One persistent CTA per SM, or one 2-CTA cluster per pair slot (at most one per work unit).
+// glu: a SwiGLU forward (gate and up as weights 0 and 1, one tile holding both).
 template <bool BWD>
 static int launch_gemm(const GemmPlan& p, const CUtensorMap (&ta)[G_MAX_W], const CUtensorMap (&tw)[G_MAX_W],
-                       GemmArgs g, void* work, int64_t work_bytes, cudaStream_t s) {
+                       GemmArgs g, void* work, int64_t work_bytes, cudaStream_t s, bool glu = false) {
   GemmPlan q = p;
   if (work == nullptr) q.splits = 1;
   NF4B_RETURN_IF(q.tiles * q.splits > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
@@ -1283,9 +1353,16 @@ static int launch_gemm(const GemmPlan& p, const CUtensorMap (&ta)[G_MAX_W], cons
   const int64_t slots = units < q.slots ? units : q.slots;
   const unsigned grid = unsigned(q.pair ? 2 * slots : slots);
   const bool split = q.splits > 1;
-  const bool multi = g.nw > 1;
+  const bool multi = g.nw > 1 && !glu;
   int st;
-  if (q.pair) {
+  if (!BWD && glu) {
+    if (q.pair)
+      st = split ? launch_variant<false, true, false, true, true>(grid, ta, tw, g, s)
+                 : launch_variant<false, false, false, true, true>(grid, ta, tw, g, s);
+    else
+      st = split ? launch_variant<false, true, false, false, true>(grid, ta, tw, g, s)
+                 : launch_variant<false, false, false, false, true>(grid, ta, tw, g, s);
+  } else if (q.pair) {
     if (multi)
       st = split ? launch_variant<BWD, true, true, true>(grid, ta, tw, g, s)
                  : launch_variant<BWD, false, true, true>(grid, ta, tw, g, s);
@@ -1458,6 +1535,68 @@ extern "C" int nf4b_linear_fwd(const void* x, const uint8_t* packed, const nf4b_
                                int64_t in_features, int64_t out_features, void* stream) {
   return nf4b_linear_fwd_ws(x, packed, qs, bias, lora, y, n, in_features, out_features, nullptr, 0,
                             stream);
+}
+
+// ------------------------------------------------------------ SwiGLU forward
+// Tiles of 64 features of gate and of up (128 operand rows), so the plan is that of one weight
+// of 2 x out rows.
+static GemmPlan plan_swiglu(int64_t n, int64_t in_features, int64_t out_features) {
+  const int64_t rows = 2 * out_features;
+  return plan_gemm(n, &rows, 1, in_features);
+}
+
+extern "C" int64_t nf4b_linear_swiglu_work_bytes(int64_t n, int64_t in_features, int64_t out_features) {
+  if (n <= 0 || in_features <= 0 || out_features <= 0) return 0;
+  if (check_device() != NF4B_OK) return -1;
+  return plan_work_bytes(plan_swiglu(n, in_features, out_features));
+}
+
+extern "C" int nf4b_linear_fwd_swiglu(const void* x, int64_t n, int64_t in_features, const uint8_t* gate_packed,
+                                      const nf4b_qstate* gate_qs, const uint8_t* up_packed,
+                                      const nf4b_qstate* up_qs, void* gate_out, void* up_out, void* m_out,
+                                      int64_t out_features, void* work, int64_t work_bytes, void* stream) {
+  int32_t lb[2];
+  int st = gemm_common_checks(x, gate_packed, gate_qs, gate_out, n, in_features, out_features, &lb[0]);
+  if (st != NF4B_OK) return st;
+  st = gemm_common_checks(x, up_packed, up_qs, up_out, n, in_features, out_features, &lb[1]);
+  if (st != NF4B_OK) return st;
+  NF4B_RETURN_IF(!m_out, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(!aligned(m_out, 4), NF4B_ERR_ALIGNMENT);
+  if (n == 0) return NF4B_OK;
+  st = check_device();
+  if (st != NF4B_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const GemmPlan plan = plan_swiglu(n, in_features, out_features);
+  CUtensorMap ta[G_MAX_W], tw[G_MAX_W];
+  st = make_tmap_2d(&ta[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, uint64_t(in_features), uint64_t(n),
+                    uint64_t(in_features) * 2, G_K, act_box_rows(plan), CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != NF4B_OK) return st;
+  ta[1] = ta[2] = ta[0];
+  // 64-row boxes: a stage holds 64 rows of gate, then the same 64 rows of up
+  const uint8_t* packed[2] = {gate_packed, up_packed};
+  for (int i = 0; i < 2; ++i) {
+    st = make_tmap_2d(&tw[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, packed[i], uint64_t(in_features / 2),
+                      uint64_t(out_features), uint64_t(in_features / 2), G_K / 2, G_M / 2, CU_TENSOR_MAP_SWIZZLE_32B);
+    if (st != NF4B_OK) return st;
+  }
+  tw[2] = tw[0];
+  GemmArgs g{};
+  const nf4b_qstate* qs[2] = {gate_qs, up_qs};
+  void* outs[2] = {gate_out, up_out};
+  for (int i = 0; i < 2; ++i) {
+    GemmW& w = g.w[i];
+    fill_qstate_args(&w, qs[i], lb[i]);
+    w.out = static_cast<__half*>(outs[i]);
+    w.out_f = out_features;
+  }
+  const int64_t rows = 2 * out_features;
+  set_m_end(&g, &rows, 1, plan.pair);
+  g.nw = 2;  // both weights' code tables are loaded
+  for (int i = 0; i < G_MAX_W; ++i) g.k_end[i] = 0x7FFFFFFF;
+  g.n = n;
+  g.in_f = in_features;
+  g.glu_out = static_cast<__half*>(m_out);
+  return launch_gemm<false>(plan, ta, tw, g, work, work_bytes, s, true);
 }
 
 extern "C" int64_t nf4b_linear_bwd_group_work_bytes(int64_t n, int64_t in_features,

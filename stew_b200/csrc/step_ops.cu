@@ -9,7 +9,7 @@
 //   add+RMSNorm  s = fp16(res + delta), then RMSNorm of s
 //   RoPE         out[i] = x[i] c[i] - x[i+d] s[i],  out[i+d] = x[i+d] c[i+d] + x[i] s[i+d]
 //                (the rotate-half convention of Qwen2); the backward applies the transpose
-//   SwiGLU       m = fp16(fp16(silu(g)) * u)
+//   SwiGLU       m = fp16(g * sigmoid(g) * u), fp32 inside (solution/swiglu.py)
 // All activations are fp16 row-major; one warp owns one row of a norm (16-byte loads, the
 // row kept in registers between the two passes); the elementwise kernels move 16 bytes per
 // thread and access.
@@ -197,9 +197,10 @@ __global__ void rope_qk_kernel(const __half* __restrict__ q, const __half* __res
   *reinterpret_cast<uint4*>(dst + i0 + d) = f_to_h8(ob);
 }
 
-__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
-// silu(x) = x / (1 + exp(-x)), IEEE division (the form torch's silu evaluates)
-__device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, __fadd_rn(1.f, expf(-x))); }
+// sigmoid through the fast exp and divide (the reference's SwiGLU kernel, solution/swiglu.py,
+// computes it in fp32 with Triton's fast exp as well); the fused gate/up GEMM's epilogue uses
+// the same expression, so the two SwiGLU forwards agree bit for bit
+__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
 // SwiGLU: 8 values per thread.
 __global__ void swiglu_fwd_kernel(const __half* __restrict__ g, const __half* __restrict__ u,
@@ -211,11 +212,12 @@ __global__ void swiglu_fwd_kernel(const __half* __restrict__ g, const __half* __
   h8_to_f(reinterpret_cast<const uint4*>(g)[i], gf);
   h8_to_f(reinterpret_cast<const uint4*>(u)[i], uf);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) o[j] = __fmul_rn(round_h(silu_f(gf[j])), uf[j]);
+  for (int j = 0; j < 8; ++j) o[j] = gf[j] * sigmoid_fast(gf[j]) * uf[j];
   reinterpret_cast<uint4*>(m)[i] = f_to_h8(o);
 }
 
-// dg = fp16(fp16(dm u) * silu'(g)), du = fp16(dm fp16(silu(g))).
+// du = fp16(dm g sig), dg = fp16(dm u sig (1 + g (1 - sig))), sig = sigmoid(g), all in fp32 with
+// one rounding (the reference's backward, solution/swiglu.py:26-37).
 __global__ void swiglu_bwd_kernel(const __half* __restrict__ dm, const __half* __restrict__ g,
                                   const __half* __restrict__ u, __half* __restrict__ dg,
                                   __half* __restrict__ du, int64_t n8) {
@@ -228,11 +230,9 @@ __global__ void swiglu_bwd_kernel(const __half* __restrict__ dm, const __half* _
   h8_to_f(reinterpret_cast<const uint4*>(u)[i], uf);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const float sg = sigmoid_f(gf[j]);
-    const float s16 = round_h(silu_f(gf[j]));
-    ou[j] = __fmul_rn(df[j], s16);
-    const float ds = round_h(__fmul_rn(df[j], uf[j]));
-    og[j] = ds * (sg * (1.f + gf[j] * (1.f - sg)));
+    const float sg = sigmoid_fast(gf[j]);
+    ou[j] = df[j] * gf[j] * sg;
+    og[j] = df[j] * uf[j] * sg * (1.f + gf[j] * (1.f - sg));
   }
   reinterpret_cast<uint4*>(dg)[i] = f_to_h8(og);
   reinterpret_cast<uint4*>(du)[i] = f_to_h8(ou);

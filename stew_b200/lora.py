@@ -239,6 +239,67 @@ class GroupedNF4Function(torch.autograd.Function):
         return (None if dx is None else dx.reshape(ctx.x_shape), None, *pgrads)
 
 
+class SwiGLUProjection(torch.autograd.Function):
+    """m = fp16(g * sigmoid(g) * u), g = x Wg^T, u = x Wu^T, for the NF4 gate and up weights of an MLP, in ONE
+    launch (nf4b_linear_fwd_swiglu: the GEMM's epilogue applies the SwiGLU; gate and up are
+    also written, for the backward).  Backward: the SwiGLU backward kernel gives dgate and dup,
+    then ONE dX GEMM over the concatenated gate/up out features (nf4b_linear_bwd_dx_group)."""
+
+    @staticmethod
+    def forward(ctx, x, gate, up):
+        (pg, sg), (pu, su) = gate, up
+        out_f, in_f = int(sg.shape[0]), int(sg.shape[1])
+        x2 = x.reshape(-1, in_f).contiguous()
+        n = x2.shape[0]
+        dev = x.device
+        g = torch.empty(n, out_f, dtype=torch.float16, device=dev)
+        u = torch.empty_like(g)
+        m = torch.empty_like(g)
+        with torch.cuda.device(dev):
+            L = _lib.lib()
+            qg, qu = _qstate(sg, dev), _qstate(su, dev)
+            work, wbytes = _workspace_bytes(dev, int(L.nf4b_linear_swiglu_work_bytes(n, in_f, out_f)))
+            _lib.check(L.nf4b_linear_fwd_swiglu(x2.data_ptr(), n, in_f, pg.data_ptr(), ctypes.byref(qg),
+                                                pu.data_ptr(), ctypes.byref(qu), g.data_ptr(), u.data_ptr(),
+                                                m.data_ptr(), out_f, work, wbytes, _stream(dev)),
+                       "nf4b_linear_fwd_swiglu")
+        ctx.save_for_backward(g, u)
+        ctx.weights = (gate, up)
+        ctx.x_shape = x.shape
+        return m.reshape(*x.shape[:-1], out_f)
+
+    @staticmethod
+    def backward(ctx, dm):
+        g, u = ctx.saved_tensors
+        (pg, sg), (pu, su) = ctx.weights
+        n, out_f = g.shape
+        in_f = int(sg.shape[1])
+        dev = g.device
+        dm = dm.reshape(n, out_f).to(torch.float16).contiguous()
+        dg, du = torch.empty_like(g), torch.empty_like(u)
+        with torch.cuda.device(dev):
+            L = _lib.lib()
+            _lib.check(L.nf4b_swiglu_bwd(dm.data_ptr(), g.data_ptr(), u.data_ptr(), dg.data_ptr(), du.data_ptr(),
+                                         g.numel(), _stream(dev)), "nf4b_swiglu_bwd")
+            items = (_lib.LinearBwdItemC * 2)()
+            qs = [_qstate(sg, dev), _qstate(su, dev)]
+            for j, (packed, dy, q) in enumerate(((pg, dg, qs[0]), (pu, du, qs[1]))):
+                items[j].dy, items[j].packed, items[j].qs = dy.data_ptr(), packed.data_ptr(), ctypes.pointer(q)
+                items[j].lora, items[j].dyb, items[j].out_features = None, None, out_f
+            dx = torch.empty(n, in_f, dtype=torch.float16, device=dev)
+            outs = (ctypes.c_int64 * 2)(out_f, out_f)
+            work, wbytes = _workspace_bytes(dev, int(L.nf4b_linear_bwd_group_work_bytes(n, in_f, outs, 2)))
+            _lib.check(L.nf4b_linear_bwd_dx_group(items, 2, dx.data_ptr(), n, in_f, work, wbytes, _stream(dev)),
+                       "nf4b_linear_bwd_dx_group")
+        return dx.reshape(ctx.x_shape), None, None
+
+
+def swiglu_projection(x, gate, up):
+    """fp16(g * sigmoid(g) * u) of g = gate(x), u = up(x) for two NF4Linear modules without bias (an MLP's gate
+    and up projections), fused into one launch forward."""
+    return SwiGLUProjection.apply(x, (gate.packed, gate.quant_state), (up.packed, up.quant_state))
+
+
 def grouped_projection(x, modules):
     """The outputs of several NF4Linear / NF4LoraLinear modules that read the same input x,
     computed by one grouped forward launch (up to 3 modules)."""

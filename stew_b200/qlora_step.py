@@ -24,8 +24,8 @@ import torch
 import torch.nn.functional as F
 
 from . import dp
-from .lora import LORA_RANK, NF4Linear, NF4LoraLinear, grouped_projection
-from .step_ops import add_rms_norm, head_cross_entropy, rms_norm, rope_qk, swiglu
+from .lora import LORA_RANK, NF4Linear, NF4LoraLinear, grouped_projection, swiglu_projection
+from .step_ops import add_rms_norm, head_cross_entropy, rms_norm, rope_qk
 from .sweep import QWEN_PROJ, qwen_model_weights
 
 
@@ -109,8 +109,8 @@ class Layer(torch.nn.Module):
 
     def _gate_up(self, h):
         p = self.proj
-        gate, up = grouped_projection(h, [p["gate"], p["up"]])  # one launch
-        return swiglu(gate, up)
+        # gate, up and the SwiGLU in one launch (the GEMM's epilogue applies the SwiGLU)
+        return swiglu_projection(h, p["gate"], p["up"])
 
     def mlp(self, h, recompute: bool = False):
         """down(SwiGLU(gate(h), up(h))); recompute: keep only h and recompute gate/up and the

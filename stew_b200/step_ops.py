@@ -146,7 +146,7 @@ def rope_qk(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tens
 
 
 def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
-    """fp16(fp16(silu(gate)) * up)."""
+    """fp16(gate * sigmoid(gate) * up), fp32 inside (the reference's SwiGLU kernel)."""
     return _SwiGLU.apply(gate, up)
 
 

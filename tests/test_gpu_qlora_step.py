@@ -76,7 +76,8 @@ def _ref_loss(model, tokens, lengths):
                                            v.transpose(0, 1)[None], attn_mask=mask, enable_gqa=True)
         x = x + lin(p["o"], a[0].transpose(0, 1).reshape(n, -1), "o", li)
         h = rms_norm(x, layer.ln2, cfg.rms_eps)
-        m = F.silu(lin(p["gate"], h, "gate", li).float()).to(torch.float16) * lin(p["up"], h, "up", li)
+        gg = lin(p["gate"], h, "gate", li).float()
+        m = (gg * torch.sigmoid(gg) * lin(p["up"], h, "up", li).float()).to(torch.float16)
         x = x + lin(p["down"], m, "down", li)
     h = rms_norm(x, model.ln_f, cfg.rms_eps)
     nxt = torch.roll(ids, -1)
