@@ -211,6 +211,19 @@ int nf4b_linear_fwd_swiglu(const void* x, int64_t n, int64_t in_features, const 
                            void* gate_out, void* up_out, void* m_out, int64_t out_features, void* work,
                            int64_t work_bytes, void* stream);
 
+/* The input gradient of a SwiGLU MLP's down projection with the SwiGLU backward in the same
+ * launch: dm = fp16(dY . Wd) (Wd the NF4 down weight [out, in], in = the MLP width) is not
+ * written; from it and the forward's gate and up [n, in] (fp16) the epilogue writes
+ *   dup[n, in]   = fp16(dm * gate * sig)
+ *   dgate[n, in] = fp16(dm * up * sig * (1 + gate * (1 - sig))),   sig = sigmoid(gate)
+ * (nf4b_swiglu_bwd's arithmetic, bit for bit, on the dm nf4b_linear_bwd_dx_ws would write).
+ * No adapter.  `work`: the split-K workspace of nf4b_linear_work_bytes(n, in, out, 1) bytes, same
+ * contract as nf4b_linear_bwd_dx_ws.  No counterpart in the reference (there: dX of down, then
+ * the SwiGLU backward kernel, solution/swiglu.py:26-37).  */
+int nf4b_linear_bwd_dx_swiglu(const void* dy, const uint8_t* packed, const nf4b_qstate* qs, const void* gate,
+                              const void* up, void* dgate, void* dup, int64_t n, int64_t in_features,
+                              int64_t out_features, void* work, int64_t work_bytes, void* stream);
+
 /* LoRA weight gradients (fp32 out, overwritten), both in one launch:
  *   dA[rank, in]  = scale * (dY B)^T X
  *   dB[out, rank] = scale * dY^T (X A^T)

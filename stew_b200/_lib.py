@@ -95,6 +95,9 @@ SIGNATURES = {
     "nf4b_linear_fwd_swiglu": (c_int32, [c_void_p, c_int64, c_int64, c_void_p, ctypes.POINTER(QStateC), c_void_p,
                                          ctypes.POINTER(QStateC), c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
                                          c_int64, c_void_p]),
+    "nf4b_linear_bwd_dx_swiglu": (c_int32, [c_void_p, c_void_p, ctypes.POINTER(QStateC), c_void_p, c_void_p,
+                                            c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64,
+                                            c_void_p]),
     "nf4b_lora_grads_work_bytes": (c_int64, [c_int64, c_int64, c_int64, c_int32]),
     "nf4b_lora_grads_group_work_bytes": (c_int64, [ctypes.POINTER(LoraGradsItemC), c_int32, c_int64]),
     "nf4b_lora_grads_group": (c_int32, [ctypes.POINTER(LoraGradsItemC), c_int32, c_void_p, c_int64,

@@ -135,6 +135,12 @@ struct GemmArgs {
                           // between launches
   int32_t drop_ticket_unit;  // test hook: this work unit skips its ticket (-1: none)
   __half* glu_out;        // SwiGLU launches: m = fp16(gate * sigmoid(gate) * up) [n, out]
+  // SwiGLU-backward launches (dX of down): the forward's gate and up [n, in], and the outputs
+  // dgate, dup [n, in] written instead of dX
+  const __half* glu_g;
+  const __half* glu_u;
+  __half* glu_dg;
+  __half* glu_du;
 };
 
 __device__ int g_gemm_error;
@@ -343,8 +349,10 @@ __device__ __forceinline__ bool wait_count(const int32_t* p, int want) {
 
 // SPLIT: compiled with the split-K epilogue (launches with g.splits > 1).
 // PAIR: launched as 2-CTA clusters; CTA rank 0 issues cta_group::2 MMAs over both CTAs' tiles.
-// GLU: the SwiGLU forward of an MLP: gate and up in one tile, epilogue writes gate, up and
-// m = fp16(gate * sigmoid(gate) * up).
+// GLU, forward: the SwiGLU forward of an MLP: gate and up in one tile, epilogue writes gate, up
+// and m = fp16(gate * sigmoid(gate) * up).  GLU, backward: dX of the MLP's down projection, whose
+// epilogue applies the SwiGLU backward (dgate, dup from dm = the rounded dX and the forward's
+// gate and up) instead of writing dm.
 template <bool BWD, bool SPLIT, bool MULTI, bool PAIR, bool GLU>
 __global__ void __launch_bounds__(G_THREADS, 1)
     nf4_gemm_kernel(const __grid_constant__ CUtensorMap tm_act0, const __grid_constant__ CUtensorMap tm_act1,
@@ -354,7 +362,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   // BWD && MULTI: several weights along K (dX = sum_i dY_i W_i); !BWD && MULTI: several
   // weights along M (Y_i = X W_i^T).
   constexpr bool KCAT = BWD && MULTI;
-  static_assert(!GLU || (!BWD && !MULTI), "SwiGLU launches are forward, over one gate/up pair");
+  static_assert(!GLU || !MULTI, "SwiGLU launches carry one gate/up pair (forward) or down (backward)");
+  constexpr bool GLUF = GLU && !BWD;  // SwiGLU forward tiles (gate and up rows side by side)
   using L = Smem<PAIR>;
   constexpr int NS = L::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -483,7 +492,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           for (int h = 0; h < nh; ++h)
             tma_load_2d(smem + L::X + s * L::X_BYTES + h * (G_NMAX / 2) * 128, KCAT ? tm_a : &tm_act0,
                         &full[s], kl * G_K, trow[h]);
-          if (GLU) {
+          if (GLUF) {
             // gate rows [m0, m0 + 64) in packed rows 0-63, up rows [m0, m0 + 64) in rows 64-127
             tma_load_2d(smem + L::P + s * L::P_BYTES, &tm_w0, &full[s], kl * (G_K / 2), int(tc.m0));
             tma_load_2d(smem + L::P + s * L::P_BYTES + L::P_BYTES / 2, &tm_w1, &full[s], kl * (G_K / 2),
@@ -663,8 +672,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     // GLU: packed row d is row d & 63 of gate (d < 64) or of up; it goes to operand row
     // 32 q + 16 (up) + i for feature 16 q + i, so TMEM lanes i and i + 16 of an epilogue warp
     // hold the gate and up rows of one feature
-    const int rrow = GLU ? (d & 63) : r;  // row of its weight, from the tile's m0
-    const int arow = GLU ? 32 * ((d & 63) >> 4) + 16 * (d >> 6) + (d & 15) : r;
+    const int rrow = GLUF ? (d & 63) : r;  // row of its weight, from the tile's m0
+    const int arow = GLUF ? 32 * ((d & 63) >> 4) + 16 * (d >> 6) + (d & 15) : r;
     const uint32_t a_off = uint32_t(j * 8192 + (arow >> 3) * 1024 + (arow & 7) * 128);
     const uint32_t key = uint32_t(arow & 7);
     const uint32_t k16 = g.k16, k31 = g.k16 << 15;
@@ -675,7 +684,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       const WorkUnit wu = work_unit<MULTI, PAIR, GLU>(g, u, rank);
       const TileCoord& tc = wu.tc;
       // the tile's weight (forward; GLU: this thread's row's); weight 0 backward
-      const int tws = GLU ? (d >> 6) : (MULTI ? tc.seg : 0);
+      const int tws = GLUF ? (d >> 6) : (MULTI ? tc.seg : 0);
       const GemmW& W = g.w[tws];
       // one slab per adapter (a K-concatenated backward may carry several), in the order the
       // MMA issuer consumes them
@@ -845,8 +854,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       const int ctile = PAIR ? 2 * wu.tile + int(rank) : wu.tile;
       const TileCoord& tc = wu.tc;
       // GLU: lanes 0-15 of a warp hold gate rows, lanes 16-31 the up rows of the same features
-      const int glu_up = GLU ? (lane >> 4) : 0;
-      const GemmW& W = g.w[GLU ? glu_up : (MULTI ? tc.seg : 0)];
+      const int glu_up = GLUF ? (lane >> 4) : 0;
+      const GemmW& W = g.w[GLUF ? glu_up : (MULTI ? tc.seg : 0)];
       const int64_t ld_out = BWD ? g.in_f : W.out_f;
       // single CTAs: accumulator b of two; a pair: the tile's 512 columns, handed over in two
       // halves (acc_full[0] / [1]); split-K takes both halves at once
@@ -862,7 +871,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       if (!ok) break;
       const int prow = 32 * lq + lane;  // accumulator row = TMEM lane
       // output column of this lane's row (GLU: the feature; lanes 2i, 2i+1 stay adjacent)
-      const int64_t row = GLU ? tc.m0 + 16 * lq + (lane & 15) : tc.m0 + prow;
+      const int64_t row = GLUF ? tc.m0 + 16 * lq + (lane & 15) : tc.m0 + prow;
       const bool row_ok = row < ld_out;  // ld_out is a multiple of 64: pairs are all in or out
       const uint32_t taddr = tmem_base + (uint32_t(32 * lq) << 16) + b * G_ACC_COLS;
       constexpr int ACC_T = acc_tokens<PAIR>();
@@ -917,9 +926,9 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         // emit), then m = fp16(g * sigmoid(g) * u) from the fp16 g and u -- each lane trades
         // half of its chunk with lane ^ 16, so lanes 0-15 get tokens 0-15 of their feature and
         // lanes 16-31 tokens 16-31 -- stored with the same neighbour pairing
-        uint32_t* moutp = GLU ? reinterpret_cast<uint32_t*>(g.glu_out + (tc.t0 + (odd ? 1 : 0)) * ld_out +
-                                                            (row & ~int64_t(1)))
-                              : nullptr;
+        uint32_t* moutp = GLUF ? reinterpret_cast<uint32_t*>(g.glu_out + (tc.t0 + (odd ? 1 : 0)) * ld_out +
+                                                             (row & ~int64_t(1)))
+                               : nullptr;
         auto glu_emit = [&](const uint32_t (&acc)[32], int c0) {
           uint32_t hp[16];
 #pragma unroll
@@ -948,6 +957,49 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           for (int k = 0; k < 8; ++k) {
             const uint32_t h = prmt(mp[k], __shfl_xor_sync(0xffffffffu, mp[k], 1), xsel);
             if (2 * k < limm) pm[int64_t(k) * ld_out] = h;
+          }
+        };
+        // SwiGLU backward epilogue of one 32-token chunk (dX of down = dm): for the lane's word
+        // (row, row + 1) at token c0 + jj + odd -- the word the dm store would write -- read the
+        // forward's gate and up words at the same place and write
+        //   dup = fp16(dm * g * sig), dgate = fp16(dm * u * sig * (1 + g * (1 - sig)))
+        // with dm rounded to fp16 first (nf4b_swiglu_bwd's arithmetic, bit for bit); the gate and
+        // up words of a half chunk are loaded before any is used
+        auto glub_emit = [&](const uint32_t (&acc)[32], int c0) {
+          const int lim = row_ok ? tc.tn_real - c0 - (odd ? 1 : 0) : 0;
+          const int64_t w0 = ((tc.t0 + c0 + (odd ? 1 : 0)) * ld_out + (row & ~int64_t(1))) >> 1;
+          const uint32_t* gw = reinterpret_cast<const uint32_t*>(g.glu_g) + w0;
+          const uint32_t* uw = reinterpret_cast<const uint32_t*>(g.glu_u) + w0;
+          uint32_t* dgw = reinterpret_cast<uint32_t*>(g.glu_dg) + w0;
+          uint32_t* duw = reinterpret_cast<uint32_t*>(g.glu_du) + w0;
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t gv[8], uv[8], dmw[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const int jj = 16 * hh + 2 * q;
+              const int64_t o = int64_t(jj >> 1) * ld_out;
+              gv[q] = jj < lim ? __ldcs(gw + o) : 0u;
+              uv[q] = jj < lim ? __ldcs(uw + o) : 0u;
+              const uint32_t own = pack_half2(__uint_as_float(acc[jj]), __uint_as_float(acc[jj + 1]));
+              dmw[q] = prmt(own, __shfl_xor_sync(0xffffffffu, own, 1), xsel);
+            }
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const int jj = 16 * hh + 2 * q;
+              const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&dmw[q]));
+              const float2 gg = __half22float2(*reinterpret_cast<const __half2*>(&gv[q]));
+              const float2 uu = __half22float2(*reinterpret_cast<const __half2*>(&uv[q]));
+              const float s0 = glu_sigmoid(gg.x), s1 = glu_sigmoid(gg.y);
+              const uint32_t du = pack_half2(dm.x * gg.x * s0, dm.y * gg.y * s1);
+              const uint32_t dg = pack_half2(dm.x * uu.x * s0 * (1.f + gg.x * (1.f - s0)),
+                                             dm.y * uu.y * s1 * (1.f + gg.y * (1.f - s1)));
+              if (jj < lim) {
+                const int64_t o = int64_t(jj >> 1) * ld_out;
+                duw[o] = du;
+                dgw[o] = dg;
+              }
+            }
           }
         };
         auto emit = [&](const uint32_t (&acc)[32], int c0, auto bias_c, int lim) {
@@ -1006,8 +1058,12 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             }
             // stores of token c0 + jj + odd land while that token is in the tile; the paths
             // below are warp-uniform (emit shuffles across the warp)
-            if (GLU) {
+            if (GLUF) {
               glu_emit(acc, c0);
+              continue;
+            }
+            if (GLU && BWD) {
+              glub_emit(acc, c0);
               continue;
             }
             const int lim = row_ok ? tc.tn_real - c0 - (odd ? 1 : 0) : 0;
@@ -1329,7 +1385,8 @@ static int launch_variant(unsigned grid, const CUtensorMap (&ta)[G_MAX_W], const
 static std::atomic<int> g_drop_ticket_unit{-1};
 
 // One persistent CTA per SM, or one 2-CTA cluster per pair slot (at most one per work unit).
-// glu: a SwiGLU forward (gate and up as weights 0 and 1, one tile holding both).
+// glu: forward, a SwiGLU forward (gate and up as weights 0 and 1, one tile holding both);
+// backward, the dX of down with the SwiGLU backward in its epilogue.
 template <bool BWD>
 static int launch_gemm(const GemmPlan& p, const CUtensorMap (&ta)[G_MAX_W], const CUtensorMap (&tw)[G_MAX_W],
                        GemmArgs g, void* work, int64_t work_bytes, cudaStream_t s, bool glu = false) {
@@ -1355,13 +1412,13 @@ static int launch_gemm(const GemmPlan& p, const CUtensorMap (&ta)[G_MAX_W], cons
   const bool split = q.splits > 1;
   const bool multi = g.nw > 1 && !glu;
   int st;
-  if (!BWD && glu) {
+  if (glu) {
     if (q.pair)
-      st = split ? launch_variant<false, true, false, true, true>(grid, ta, tw, g, s)
-                 : launch_variant<false, false, false, true, true>(grid, ta, tw, g, s);
+      st = split ? launch_variant<BWD, true, false, true, true>(grid, ta, tw, g, s)
+                 : launch_variant<BWD, false, false, true, true>(grid, ta, tw, g, s);
     else
-      st = split ? launch_variant<false, true, false, false, true>(grid, ta, tw, g, s)
-                 : launch_variant<false, false, false, false, true>(grid, ta, tw, g, s);
+      st = split ? launch_variant<BWD, true, false, false, true>(grid, ta, tw, g, s)
+                 : launch_variant<BWD, false, false, false, true>(grid, ta, tw, g, s);
   } else if (q.pair) {
     if (multi)
       st = split ? launch_variant<BWD, true, true, true>(grid, ta, tw, g, s)
@@ -1686,6 +1743,46 @@ extern "C" int nf4b_linear_bwd_dx_group(const nf4b_linear_bwd_item* items, int32
   g.n = n;
   g.in_f = in_features;
   return launch_gemm<true>(plan, ta, tw, g, work, work_bytes, s);
+}
+
+extern "C" int nf4b_linear_bwd_dx_swiglu(const void* dy, const uint8_t* packed, const nf4b_qstate* qs,
+                                         const void* gate, const void* up, void* dgate, void* dup, int64_t n,
+                                         int64_t in_features, int64_t out_features, void* work,
+                                         int64_t work_bytes, void* stream) {
+  int32_t lb = 0;
+  int st = gemm_common_checks(dy, packed, qs, dgate, n, in_features, out_features, &lb);
+  if (st != NF4B_OK) return st;
+  NF4B_RETURN_IF(!gate || !up || !dup, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(!aligned(gate, 4) || !aligned(up, 4) || !aligned(dup, 4), NF4B_ERR_ALIGNMENT);
+  if (n == 0) return NF4B_OK;
+  st = check_device();
+  if (st != NF4B_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the plan of the plain dX launch of this weight (same tiles, same K ranges)
+  const GemmPlan plan = plan_gemm(n, &in_features, 1, out_features);
+  CUtensorMap ta[G_MAX_W], tw[G_MAX_W];
+  st = make_tmap_2d(&ta[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, dy, uint64_t(out_features), uint64_t(n),
+                    uint64_t(out_features) * 2, G_K, act_box_rows(plan), CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != NF4B_OK) return st;
+  st = make_tmap_2d(&tw[0], CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, uint64_t(in_features / 2), uint64_t(out_features),
+                    uint64_t(in_features / 2), G_M / 2, G_K, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (st != NF4B_OK) return st;
+  ta[1] = ta[2] = ta[0];
+  tw[1] = tw[2] = tw[0];
+  GemmArgs g{};
+  fill_qstate_args(&g.w[0], qs, lb);
+  g.w[0].out = static_cast<__half*>(dgate);  // not written: the epilogue writes dgate / dup
+  g.w[0].out_f = out_features;
+  g.k_end[0] = int32_t(out_features / G_K);
+  for (int i = 1; i < G_MAX_W; ++i) g.k_end[i] = 0x7FFFFFFF;
+  set_m_end(&g, &in_features, 1, plan.pair);
+  g.n = n;
+  g.in_f = in_features;
+  g.glu_g = static_cast<const __half*>(gate);
+  g.glu_u = static_cast<const __half*>(up);
+  g.glu_dg = static_cast<__half*>(dgate);
+  g.glu_du = static_cast<__half*>(dup);
+  return launch_gemm<true>(plan, ta, tw, g, work, work_bytes, s, true);
 }
 
 extern "C" int nf4b_linear_bwd_dx_ws(const void* dy, const uint8_t* packed, const nf4b_qstate* qs,

@@ -240,58 +240,138 @@ class GroupedNF4Function(torch.autograd.Function):
 
 
 class SwiGLUProjection(torch.autograd.Function):
-    """m = fp16(g * sigmoid(g) * u), g = x Wg^T, u = x Wu^T, for the NF4 gate and up weights of an MLP, in ONE
-    launch (nf4b_linear_fwd_swiglu: the GEMM's epilogue applies the SwiGLU; gate and up are
-    also written, for the backward).  Backward: the SwiGLU backward kernel gives dgate and dup,
-    then ONE dX GEMM over the concatenated gate/up out features (nf4b_linear_bwd_dx_group)."""
+    """m = fp16(g * sigmoid(g) * u), g = x Wg^T, u = x Wu^T, for the NF4 gate and up weights of an
+    MLP, in ONE launch (nf4b_linear_fwd_swiglu: the GEMM's epilogue applies the SwiGLU; gate and up
+    are also written, for the backward).  Backward: the SwiGLU backward kernel gives dgate and
+    dup, then ONE dX GEMM over the concatenated gate/up out features (nf4b_linear_bwd_dx_group)."""
 
     @staticmethod
     def forward(ctx, x, gate, up):
-        (pg, sg), (pu, su) = gate, up
-        out_f, in_f = int(sg.shape[0]), int(sg.shape[1])
+        in_f = int(gate[1].shape[1])
         x2 = x.reshape(-1, in_f).contiguous()
-        n = x2.shape[0]
-        dev = x.device
-        g = torch.empty(n, out_f, dtype=torch.float16, device=dev)
-        u = torch.empty_like(g)
-        m = torch.empty_like(g)
-        with torch.cuda.device(dev):
-            L = _lib.lib()
-            qg, qu = _qstate(sg, dev), _qstate(su, dev)
-            work, wbytes = _workspace_bytes(dev, int(L.nf4b_linear_swiglu_work_bytes(n, in_f, out_f)))
-            _lib.check(L.nf4b_linear_fwd_swiglu(x2.data_ptr(), n, in_f, pg.data_ptr(), ctypes.byref(qg),
-                                                pu.data_ptr(), ctypes.byref(qu), g.data_ptr(), u.data_ptr(),
-                                                m.data_ptr(), out_f, work, wbytes, _stream(dev)),
-                       "nf4b_linear_fwd_swiglu")
+        with torch.cuda.device(x.device):
+            g, u, m = _swiglu_launch(x2, gate, up)
         ctx.save_for_backward(g, u)
         ctx.weights = (gate, up)
         ctx.x_shape = x.shape
-        return m.reshape(*x.shape[:-1], out_f)
+        return m.reshape(*x.shape[:-1], m.shape[1])
 
     @staticmethod
     def backward(ctx, dm):
         g, u = ctx.saved_tensors
-        (pg, sg), (pu, su) = ctx.weights
+        gate, up = ctx.weights
         n, out_f = g.shape
-        in_f = int(sg.shape[1])
         dev = g.device
         dm = dm.reshape(n, out_f).to(torch.float16).contiguous()
         dg, du = torch.empty_like(g), torch.empty_like(u)
         with torch.cuda.device(dev):
-            L = _lib.lib()
-            _lib.check(L.nf4b_swiglu_bwd(dm.data_ptr(), g.data_ptr(), u.data_ptr(), dg.data_ptr(), du.data_ptr(),
-                                         g.numel(), _stream(dev)), "nf4b_swiglu_bwd")
-            items = (_lib.LinearBwdItemC * 2)()
-            qs = [_qstate(sg, dev), _qstate(su, dev)]
-            for j, (packed, dy, q) in enumerate(((pg, dg, qs[0]), (pu, du, qs[1]))):
-                items[j].dy, items[j].packed, items[j].qs = dy.data_ptr(), packed.data_ptr(), ctypes.pointer(q)
-                items[j].lora, items[j].dyb, items[j].out_features = None, None, out_f
-            dx = torch.empty(n, in_f, dtype=torch.float16, device=dev)
-            outs = (ctypes.c_int64 * 2)(out_f, out_f)
-            work, wbytes = _workspace_bytes(dev, int(L.nf4b_linear_bwd_group_work_bytes(n, in_f, outs, 2)))
-            _lib.check(L.nf4b_linear_bwd_dx_group(items, 2, dx.data_ptr(), n, in_f, work, wbytes, _stream(dev)),
-                       "nf4b_linear_bwd_dx_group")
+            _lib.check(_lib.lib().nf4b_swiglu_bwd(dm.data_ptr(), g.data_ptr(), u.data_ptr(), dg.data_ptr(),
+                                                  du.data_ptr(), g.numel(), _stream(dev)), "nf4b_swiglu_bwd")
+            dx = _gate_up_bwd(dg, du, gate, up, int(gate[1].shape[1]))
         return dx.reshape(ctx.x_shape), None, None
+
+
+class MLPFunction(torch.autograd.Function):
+    """down(fp16(g * sigmoid(g) * u)), g = x Wg^T, u = x Wu^T, of a SwiGLU MLP with NF4 gate, up
+    and down weights (no bias, no adapter), in two launches each way:
+      forward : nf4b_linear_fwd_swiglu (gate, up and the SwiGLU), then the down projection;
+      backward: nf4b_linear_bwd_dx_swiglu (dm of down with the SwiGLU backward in its epilogue:
+                dgate, dup), then ONE dX GEMM over the concatenated gate/up out features.
+    recompute=True keeps only x: the backward runs the forward's gate/up launch again for g and u
+    (the reference's MLP memory cap, solution/unpad.py:48-57) -- no torch checkpoint, so the step
+    stays capturable in a CUDA graph."""
+
+    @staticmethod
+    def forward(ctx, x, gate, up, down, recompute):
+        (pg, sg), (pu, su), (pd, sd) = gate, up, down
+        inter, hidden = int(sg.shape[0]), int(sg.shape[1])
+        x2 = x.reshape(-1, hidden).contiguous()
+        n = x2.shape[0]
+        dev = x.device
+        with torch.cuda.device(dev):
+            g, u, m = _swiglu_launch(x2, gate, up)
+            y = torch.empty(n, hidden, dtype=torch.float16, device=dev)
+            qd = _qstate(sd, dev)
+            work, wbytes = _workspace(dev, n, inter, hidden, False)
+            _lib.check(_lib.lib().nf4b_linear_fwd_ws(x2.data_ptr(), pd.view(-1, 1).data_ptr(), ctypes.byref(qd),
+                                                     None, None, y.data_ptr(), n, inter, hidden, work, wbytes,
+                                                     _stream(dev)), "nf4b_linear_fwd_ws")
+        if recompute:
+            ctx.save_for_backward(x2)
+        else:
+            ctx.save_for_backward(x2, g, u)
+        ctx.weights = (gate, up, down)
+        ctx.x_shape = x.shape
+        return y.reshape(*x.shape[:-1], hidden)
+
+    @staticmethod
+    def backward(ctx, dy):
+        saved = ctx.saved_tensors
+        (pg, sg), (pu, su), (pd, sd) = ctx.weights
+        x2 = saved[0]
+        inter, hidden = int(sg.shape[0]), int(sg.shape[1])
+        n = x2.shape[0]
+        dev = x2.device
+        dy = dy.reshape(n, hidden).to(torch.float16).contiguous()
+        with torch.cuda.device(dev):
+            L = _lib.lib()
+            if len(saved) == 3:
+                g, u = saved[1], saved[2]
+            else:
+                g, u, _ = _swiglu_launch(x2, (pg, sg), (pu, su))
+            dg, du = torch.empty_like(g), torch.empty_like(u)
+            qd = _qstate(sd, dev)
+            work, wbytes = _workspace(dev, n, inter, hidden, True)
+            _lib.check(L.nf4b_linear_bwd_dx_swiglu(dy.data_ptr(), pd.view(-1, 1).data_ptr(), ctypes.byref(qd),
+                                                   g.data_ptr(), u.data_ptr(), dg.data_ptr(), du.data_ptr(), n,
+                                                   inter, hidden, work, wbytes, _stream(dev)),
+                       "nf4b_linear_bwd_dx_swiglu")
+            dx = _gate_up_bwd(dg, du, (pg, sg), (pu, su), hidden)
+        return dx.reshape(ctx.x_shape), None, None, None, None
+
+
+def _swiglu_launch(x2, gate, up):
+    """(g, u, m) of one nf4b_linear_fwd_swiglu launch."""
+    (pg, sg), (pu, su) = gate, up
+    out_f, in_f = int(sg.shape[0]), int(sg.shape[1])
+    n = x2.shape[0]
+    dev = x2.device
+    g = torch.empty(n, out_f, dtype=torch.float16, device=dev)
+    u = torch.empty_like(g)
+    m = torch.empty_like(g)
+    L = _lib.lib()
+    qg, qu = _qstate(sg, dev), _qstate(su, dev)
+    work, wbytes = _workspace_bytes(dev, int(L.nf4b_linear_swiglu_work_bytes(n, in_f, out_f)))
+    _lib.check(L.nf4b_linear_fwd_swiglu(x2.data_ptr(), n, in_f, pg.data_ptr(), ctypes.byref(qg), pu.data_ptr(),
+                                        ctypes.byref(qu), g.data_ptr(), u.data_ptr(), m.data_ptr(), out_f, work,
+                                        wbytes, _stream(dev)), "nf4b_linear_fwd_swiglu")
+    return g, u, m
+
+
+def _gate_up_bwd(dg, du, gate, up, in_f):
+    """dX = dg Wg + du Wu as one K-concatenated dX GEMM."""
+    (pg, sg), (pu, su) = gate, up
+    n, out_f = dg.shape
+    dev = dg.device
+    L = _lib.lib()
+    items = (_lib.LinearBwdItemC * 2)()
+    qs = [_qstate(sg, dev), _qstate(su, dev)]
+    for j, (packed, dy, q) in enumerate(((pg, dg, qs[0]), (pu, du, qs[1]))):
+        items[j].dy, items[j].packed, items[j].qs = dy.data_ptr(), packed.data_ptr(), ctypes.pointer(q)
+        items[j].lora, items[j].dyb, items[j].out_features = None, None, out_f
+    dx = torch.empty(n, in_f, dtype=torch.float16, device=dev)
+    outs = (ctypes.c_int64 * 2)(out_f, out_f)
+    work, wbytes = _workspace_bytes(dev, int(L.nf4b_linear_bwd_group_work_bytes(n, in_f, outs, 2)))
+    _lib.check(L.nf4b_linear_bwd_dx_group(items, 2, dx.data_ptr(), n, in_f, work, wbytes, _stream(dev)),
+               "nf4b_linear_bwd_dx_group")
+    return dx
+
+
+def nf4_mlp(x, gate, up, down, recompute: bool = False):
+    """down(SwiGLU(gate(x), up(x))) for three NF4Linear modules without bias, two launches each
+    way (MLPFunction); recompute=True keeps only x for the backward."""
+    return MLPFunction.apply(x, (gate.packed, gate.quant_state), (up.packed, up.quant_state),
+                             (down.packed, down.quant_state), bool(recompute))
 
 
 def swiglu_projection(x, gate, up):

@@ -24,7 +24,7 @@ import torch
 import torch.nn.functional as F
 
 from . import dp
-from .lora import LORA_RANK, NF4Linear, NF4LoraLinear, grouped_projection, swiglu_projection
+from .lora import LORA_RANK, NF4Linear, NF4LoraLinear, grouped_projection, nf4_mlp
 from .step_ops import add_rms_norm, head_cross_entropy, rms_norm, rope_qk
 from .sweep import QWEN_PROJ, qwen_model_weights
 
@@ -42,8 +42,8 @@ class QwenConfig:
     rms_eps: float = 1e-6
     lora_alpha: float = 32.0
     # MLP memory cap (the reference's unpad path, solution/unpad.py:48-57): with more than this
-    # many real tokens, the first layers recompute gate/up + SwiGLU in the backward instead of
-    # keeping them.  None: never (a B200's 180 GB holds every layer's activations).
+    # many real tokens, the first layers keep only the MLP input and run their gate/up + SwiGLU
+    # launch again in the backward.  None: never (a B200's 180 GB holds every layer's activations).
     mlp_token_budget: int | None = None
 
 
@@ -107,22 +107,12 @@ class Layer(torch.nn.Module):
         a = packed_causal_attention(q, k, v, rows)
         return p["o"](a.reshape(n, c.heads * c.head_dim))
 
-    def _gate_up(self, h):
-        p = self.proj
-        # gate, up and the SwiGLU in one launch (the GEMM's epilogue applies the SwiGLU)
-        return swiglu_projection(h, p["gate"], p["up"])
-
     def mlp(self, h, recompute: bool = False):
-        """down(SwiGLU(gate(h), up(h))); recompute: keep only h and recompute gate/up and the
-        SwiGLU in the backward (activation checkpointing of the block)."""
-        if recompute and torch.is_grad_enabled():
-            from torch.utils.checkpoint import checkpoint
-            # no RNG in the block (dropout 0): skipping the RNG-state save/restore keeps the
-            # recompute capturable in the step's CUDA graph
-            m = checkpoint(self._gate_up, h, use_reentrant=False, preserve_rng_state=False)
-        else:
-            m = self._gate_up(h)
-        return self.proj["down"](m)
+        """down(SwiGLU(gate(h), up(h))) in two launches each way (lora.MLPFunction: the SwiGLU runs
+        in the gate/up GEMM's epilogue forward and in down's dX epilogue backward); recompute:
+        keep only h and run the gate/up launch again in the backward."""
+        p = self.proj
+        return nf4_mlp(h, p["gate"], p["up"], p["down"], recompute=recompute and torch.is_grad_enabled())
 
 
 @dataclass
@@ -358,15 +348,12 @@ class QLoRATrainer:
 
     def step(self, tokens, lengths):
         """Returns (mean loss of this rank's labelled tokens as a 0-d device tensor,
-        labelled tokens of this rank, labelled tokens over all ranks).  With cuda_graph=True,
-        a batch large enough for the MLP memory cap to recompute activations runs eagerly."""
+        labelled tokens of this rank, labelled tokens over all ranks).  Steps whose MLP memory
+        cap recomputes activations are captured as well (the recompute is the MLP op's own
+        launch, not torch's checkpoint)."""
         pb = self.model.pack(tokens, lengths)
         n_lab = pb.n_labels
-        # steps that recompute MLP activations (the memory cap) run eagerly: torch's checkpoint
-        # recomputation does not capture into a CUDA graph
-        recompute = mlp_recompute_layers(int(pb.ids.numel()), len(self.model.layers),
-                                         self.model.cfg.mlp_token_budget) > 0
-        if not self.cuda_graph or recompute:
+        if not self.cuda_graph:
             loss_sum, total = self._eager(pb)
             return loss_sum / max(n_lab, 1), n_lab, total
         if self._graph is None or self._key != pb.shape_key():

@@ -162,8 +162,8 @@ def test_mlp_recompute_matches_kept_activations(cuda_lib):
     """The MLP memory cap (gate/up + SwiGLU recomputed in the backward for the first layers,
     the reference's solution/unpad.py:48-57 rule) changes no result: the same loss, and LoRA
     gradients equal up to the run-to-run spread of the flash-attention backward (relative L2
-    <= 1e-2); and a graph trainer runs such a step eagerly (checkpoint recomputation is not
-    captured)."""
+    <= 1e-2); and a graph trainer captures such a step too (the recompute is the MLP op's own
+    gate/up launch, not torch's checkpoint), with the eager step's loss."""
     import dataclasses
     from stew_b200.qlora_step import QLoRATrainer, mlp_recompute_layers, synthetic_batch
     tokens, lengths = synthetic_batch(batch=2, seq=96, vocab=4096, seed=6)
@@ -179,8 +179,12 @@ def test_mlp_recompute_matches_kept_activations(cuda_lib):
     for pa, pb in zip(kept.lora_parameters(), rec.lora_parameters()):
         d = (pa.grad.double() - pb.grad.double()).norm() / pa.grad.double().norm()
         assert float(d) <= 1e-2
+    rec2 = _small_model()
+    rec2.cfg = dataclasses.replace(rec2.cfg, mlp_token_budget=n // 2)
+    eager = QLoRATrainer(rec2, lr=1e-3)
     tr = QLoRATrainer(rec, lr=1e-3, cuda_graph=True)
-    for _ in range(2):
-        loss, _, _ = tr.step(tokens, lengths)
-    assert torch.isfinite(loss) and tr._graph is None
+    le, _, _ = eager.step(tokens, lengths)
+    lg, _, _ = tr.step(tokens, lengths)
+    assert tr._graph is not None, "the recompute step is captured"
+    assert torch.isfinite(lg) and abs(float(lg) - float(le)) <= 1e-5 * abs(float(le))
     tr.release()

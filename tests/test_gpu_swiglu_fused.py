@@ -117,3 +117,62 @@ def test_swiglu_projection_autograd_matches_composition(cuda_lib):
     torch.cuda.synchronize()
     assert torch.equal(ma, mb)
     assert torch.equal(xa.grad, xb.grad)
+
+
+@pytest.mark.parametrize("pair", ["auto", "0", "1"])
+@pytest.mark.parametrize("n", [1, 77, 1170, 2048, 8192])
+def test_down_dx_with_swiglu_backward_equals_two_step(cuda_lib, monkeypatch, n, pair):
+    """nf4b_linear_bwd_dx_swiglu (down's dX with the SwiGLU backward in its epilogue) gives, bit for
+    bit, dX of down (nf4b_linear_bwd_dx_ws) followed by nf4b_swiglu_bwd -- single-CTA, pair and
+    split-K plans of the Qwen2.5-1.5B down projection (1536 x 8960)."""
+    from stew_b200 import _lib
+    from stew_b200.nf4 import _qstate, _stream
+    if pair != "auto":
+        monkeypatch.setenv("STEW_NF4_PAIR", pair)
+    L = _lib.lib()
+    pd, sd = _weight((1536, 8960), 31)
+    dy = _x(n, 1536, 32, std=0.01)
+    gate = _x(n, 8960, 33, std=2.0)
+    up = _x(n, 8960, 34)
+    qd = _qstate(sd, dy.device)
+    wb = max(int(L.nf4b_linear_work_bytes(n, 8960, 1536, 1)), 256)
+    ws = torch.zeros(wb, dtype=torch.uint8, device="cuda")
+    st = _stream(dy.device)
+    dm = torch.empty(n, 8960, dtype=torch.float16, device="cuda")
+    _lib.check(L.nf4b_linear_bwd_dx_ws(dy.data_ptr(), pd.data_ptr(), ctypes.byref(qd), None, None, dm.data_ptr(),
+                                       n, 8960, 1536, ws.data_ptr(), wb, st), "bwd")
+    dg0, du0 = torch.empty_like(dm), torch.empty_like(dm)
+    _lib.check(L.nf4b_swiglu_bwd(dm.data_ptr(), gate.data_ptr(), up.data_ptr(), dg0.data_ptr(), du0.data_ptr(),
+                                 dm.numel(), st), "swiglu bwd")
+    dg1 = torch.full_like(dm, float("nan"))
+    du1 = torch.full_like(dm, float("nan"))
+    _lib.check(L.nf4b_linear_bwd_dx_swiglu(dy.data_ptr(), pd.data_ptr(), ctypes.byref(qd), gate.data_ptr(),
+                                           up.data_ptr(), dg1.data_ptr(), du1.data_ptr(), n, 8960, 1536,
+                                           ws.data_ptr(), wb, st), "bwd swiglu")
+    torch.cuda.synchronize()
+    assert torch.equal(dg0, dg1) and torch.equal(du0, du1)
+    assert int(ws[:4100].count_nonzero()) == 0
+    assert _lib.gemm_error_flag(reset=True) == 0
+
+
+@pytest.mark.parametrize("recompute", [False, True])
+def test_mlp_op_matches_composition(cuda_lib, recompute):
+    """lora.MLPFunction (two launches each way) against the composition it replaces -- grouped
+    gate/up projection, SwiGLU kernel, down projection -- output and dX bit for bit; with
+    recompute the backward's second gate/up launch gives the same."""
+    from stew_b200.lora import NF4Linear, grouped_projection, nf4_mlp
+    from stew_b200.step_ops import swiglu
+    (pg, sg), (pu, su), (pd, sd) = _weight((8960, 1536), 41), _weight((8960, 1536), 42), _weight((1536, 8960), 43)
+    gate, up, down = NF4Linear(pg, sg), NF4Linear(pu, su), NF4Linear(pd, sd)
+    x0 = _x(1170, 1536, 44)
+    dy = _x(1170, 1536, 45, std=0.01)
+    xa = x0.clone().requires_grad_(True)
+    ya = nf4_mlp(xa, gate, up, down, recompute=recompute)
+    ya.backward(dy)
+    xb = x0.clone().requires_grad_(True)
+    gb, ub = grouped_projection(xb, [gate, up])
+    yb = down(swiglu(gb, ub))
+    yb.backward(dy)
+    torch.cuda.synchronize()
+    assert torch.equal(ya, yb)
+    assert torch.equal(xa.grad, xb.grad)
