@@ -260,7 +260,7 @@ struct TileCoord {
 // MULTI: the launch carries more than one weight (a grouped forward).  Single-weight launches
 // compile with the weight index fixed at 0, so its fields stay direct constant-bank operands.
 // PAIR: tiles are 256 weight rows, of which CTA `rank` of the pair owns rows 128 rank ..
-// GLU: a SwiGLU launch over gate (weight 0) and up (weight 1): a CTA's 128 rows are 64 features
+// GLU: a SwiGLU forward launch over gate (weight 0) and up (weight 1): a CTA's 128 rows are 64 features
 // of both, so m0 is the first of the CTA's 64 features.
 template <bool MULTI, bool PAIR, bool GLU>
 __device__ __forceinline__ TileCoord tile_coord(const GemmArgs& g, int tile, uint32_t rank) {
@@ -467,7 +467,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int u = unit0; ok && u < nunits; u += ustride) {
-        const WorkUnit wu = work_unit<MULTI, PAIR, GLU>(g, u, rank);
+        const WorkUnit wu = work_unit<MULTI, PAIR, GLUF>(g, u, rank);
         const TileCoord& tc = wu.tc;
         // A pair tile's MMA h (h = 0, 1) covers tokens [256 h, 256 h + n_h) of the tile, n_h =
         // min(tn - 256 h, 256); it reads the first n_h / 2 of them from rank 0 and the rest
@@ -517,7 +517,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       const uint64_t ad0 = BWD ? smem_desc_sw128(sbase + L::A, 8192, 1024) : smem_desc_sw128(sbase + L::A, 16, 1024);
       const uint64_t bd0 = smem_desc_sw128(sbase + L::X, 16, 1024);
       for (int u = unit0; ok && u < nunits; u += ustride, ++lt) {
-        const WorkUnit wu = work_unit<MULTI, PAIR, GLU>(g, u, rank);
+        const WorkUnit wu = work_unit<MULTI, PAIR, GLUF>(g, u, rank);
         const TileCoord& tc = wu.tc;
         // Single CTAs: one 256-column accumulator per tile, two alternating between tiles
         // (acc_full / acc_empty[b]).  Pairs: one 512-column accumulator per tile, MMA h writing
@@ -681,7 +681,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     uint32_t it = 0, lc = 0;
     bool ok = true;
     for (int u = unit0; ok && u < nunits; u += ustride) {
-      const WorkUnit wu = work_unit<MULTI, PAIR, GLU>(g, u, rank);
+      const WorkUnit wu = work_unit<MULTI, PAIR, GLUF>(g, u, rank);
       const TileCoord& tc = wu.tc;
       // the tile's weight (forward; GLU: this thread's row's); weight 0 backward
       const int tws = GLUF ? (d >> 6) : (MULTI ? tc.seg : 0);
@@ -849,7 +849,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     volatile int* s_ticket = reinterpret_cast<volatile int*>(smem + L::MISC + 8);  // [2]
     uint32_t lt = 0;
     for (int u = unit0; u < nunits; u += ustride, ++lt) {
-      const WorkUnit wu = work_unit<MULTI, PAIR, GLU>(g, u, rank);
+      const WorkUnit wu = work_unit<MULTI, PAIR, GLUF>(g, u, rank);
       // split-K bookkeeping is per CTA: a pair's two 128-row halves are separate tiles there
       const int ctile = PAIR ? 2 * wu.tile + int(rank) : wu.tile;
       const TileCoord& tc = wu.tc;

@@ -293,7 +293,7 @@ class MLPFunction(torch.autograd.Function):
             y = torch.empty(n, hidden, dtype=torch.float16, device=dev)
             qd = _qstate(sd, dev)
             work, wbytes = _workspace(dev, n, inter, hidden, False)
-            _lib.check(_lib.lib().nf4b_linear_fwd_ws(x2.data_ptr(), pd.view(-1, 1).data_ptr(), ctypes.byref(qd),
+            _lib.check(_lib.lib().nf4b_linear_fwd_ws(m.data_ptr(), pd.view(-1, 1).data_ptr(), ctypes.byref(qd),
                                                      None, None, y.data_ptr(), n, inter, hidden, work, wbytes,
                                                      _stream(dev)), "nf4b_linear_fwd_ws")
         if recompute:

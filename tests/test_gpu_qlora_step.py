@@ -179,10 +179,14 @@ def test_mlp_recompute_matches_kept_activations(cuda_lib):
     for pa, pb in zip(kept.lora_parameters(), rec.lora_parameters()):
         d = (pa.grad.double() - pb.grad.double()).norm() / pa.grad.double().norm()
         assert float(d) <= 1e-2
-    rec2 = _small_model()
-    rec2.cfg = dataclasses.replace(rec2.cfg, mlp_token_budget=n // 2)
+    # the eager losses keep their autograd graphs -- and the AccumulateGrad nodes, bound to the
+    # stream they ran on -- alive; the graph trainer gets models those graphs never touched
+    del l0, l1
+    rec2, rec3 = _small_model(), _small_model()
+    for m in (rec2, rec3):
+        m.cfg = dataclasses.replace(m.cfg, mlp_token_budget=n // 2)
     eager = QLoRATrainer(rec2, lr=1e-3)
-    tr = QLoRATrainer(rec, lr=1e-3, cuda_graph=True)
+    tr = QLoRATrainer(rec3, lr=1e-3, cuda_graph=True)
     le, _, _ = eager.step(tokens, lengths)
     lg, _, _ = tr.step(tokens, lengths)
     assert tr._graph is not None, "the recompute step is captured"
