@@ -510,6 +510,36 @@ def profile_case():
     print("profile case done")
 
 
+def profile_shape(name: str, n: int):
+    """Launches, in order, for one projection of the model at n tokens: the fused forward
+    (q and v with their r=16 adapter, through nf4_lora_linear), then its backward (dX GEMM,
+    with the adapter's dX term in the accumulator, and for q/v the LoRA weight gradients).
+    Inputs as in the per-shape measurement: X ~ N(0, 1), dY ~ N(0, 1e-2)."""
+    import math
+    import torch
+    from stew_b200.lora import nf4_lora_linear
+    from stew_b200.nf4 import matmul_4bit
+    from stew_b200.sweep import QWEN_PROJ, qwen_model_weights
+    shapes = dict(QWEN_PROJ)
+    if name not in shapes:
+        raise SystemExit(f"unknown projection {name!r}: one of {sorted(shapes)}")
+    out_f, in_f = shapes[name]
+    (q, st), = qwen_model_weights(layers=1, device="cuda", seed=0, projections=((name, (out_f, in_f)),))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(n, in_f, generator=g, device="cuda").half().requires_grad_(True)
+    dy = (torch.randn(n, out_f, generator=g, device="cuda") * 0.01).half()
+    if name in LORA_ON:
+        bound = 1.0 / math.sqrt(in_f)
+        a = ((torch.rand(16, in_f, generator=g, device="cuda") * 2 - 1) * bound).half().requires_grad_(True)
+        b = (torch.randn(out_f, 16, generator=g, device="cuda") * 0.01).half().requires_grad_(True)
+        y = nf4_lora_linear(x, q, st, a, b, 2.0)
+    else:
+        y = matmul_4bit(x, q.t(), st)
+    y.backward(dy)
+    torch.cuda.synchronize()
+    print("profile shape done", flush=True)
+
+
 def profile_step(full: bool = False):
     import torch
     from stew_b200.qlora_step import QLoRATrainer, QwenConfig, QwenQLoRA, synthetic_batch
@@ -555,6 +585,10 @@ def main():
                          "cudaProfilerStart/Stop (use ncu --profile-from-start off)")
     ap.add_argument("--profile-full", action="store_true",
                     help="with --profile-step: the full 28-layer model and vocabulary")
+    ap.add_argument("--profile-shape", type=str, default=None,
+                    help="small single-GPU case for ncu captures: one projection (q, k, v, o, gate, up, "
+                         "down) forward then backward at --profile-n tokens, with the adapter on q/v")
+    ap.add_argument("--profile-n", type=int, default=1170)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -563,6 +597,8 @@ def main():
         return profile_case()
     if args.profile_step:
         return profile_step(full=args.profile_full)
+    if args.profile_shape:
+        return profile_shape(args.profile_shape, args.profile_n)
 
     import torch
     world, rank, local = _dist()
