@@ -963,8 +963,9 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         // (row, row + 1) at token c0 + jj + odd -- the word the dm store would write -- read the
         // forward's gate and up words at the same place and write
         //   dup = fp16(dm * g * sig), dgate = fp16(dm * u * sig * (1 + g * (1 - sig)))
-        // with dm rounded to fp16 first (nf4b_swiglu_bwd's arithmetic, bit for bit); the gate and
-        // up words of a half chunk are loaded before any is used
+        // with dm rounded to fp16 first (nf4b_swiglu_bwd's arithmetic, bit for bit); all 32
+        // gate and up words of the chunk are loaded before any is used (one DRAM round trip per
+        // chunk: the drain is bound by the loads' latency)
         auto glub_emit = [&](const uint32_t (&acc)[32], int c0) {
           const int lim = row_ok ? tc.tn_real - c0 - (odd ? 1 : 0) : 0;
           const int64_t w0 = ((tc.t0 + c0 + (odd ? 1 : 0)) * ld_out + (row & ~int64_t(1))) >> 1;
@@ -972,15 +973,20 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           const uint32_t* uw = reinterpret_cast<const uint32_t*>(g.glu_u) + w0;
           uint32_t* dgw = reinterpret_cast<uint32_t*>(g.glu_dg) + w0;
           uint32_t* duw = reinterpret_cast<uint32_t*>(g.glu_du) + w0;
+          uint32_t gv[16], uv[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const int jj = 2 * q;
+            const int64_t o = int64_t(q) * ld_out;
+            gv[q] = jj < lim ? __ldcs(gw + o) : 0u;
+            uv[q] = jj < lim ? __ldcs(uw + o) : 0u;
+          }
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
-            uint32_t gv[8], uv[8], dmw[8];
+            uint32_t dmw[8];
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
               const int jj = 16 * hh + 2 * q;
-              const int64_t o = int64_t(jj >> 1) * ld_out;
-              gv[q] = jj < lim ? __ldcs(gw + o) : 0u;
-              uv[q] = jj < lim ? __ldcs(uw + o) : 0u;
               const uint32_t own = pack_half2(__uint_as_float(acc[jj]), __uint_as_float(acc[jj + 1]));
               dmw[q] = prmt(own, __shfl_xor_sync(0xffffffffu, own, 1), xsel);
             }
@@ -988,8 +994,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             for (int q = 0; q < 8; ++q) {
               const int jj = 16 * hh + 2 * q;
               const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&dmw[q]));
-              const float2 gg = __half22float2(*reinterpret_cast<const __half2*>(&gv[q]));
-              const float2 uu = __half22float2(*reinterpret_cast<const __half2*>(&uv[q]));
+              const float2 gg = __half22float2(*reinterpret_cast<const __half2*>(&gv[8 * hh + q]));
+              const float2 uu = __half22float2(*reinterpret_cast<const __half2*>(&uv[8 * hh + q]));
               const float s0 = glu_sigmoid(gg.x), s1 = glu_sigmoid(gg.y);
               const uint32_t du = pack_half2(dm.x * gg.x * s0, dm.y * gg.y * s1);
               const uint32_t dg = pack_half2(dm.x * uu.x * s0 * (1.f + gg.x * (1.f - s0)),

@@ -273,16 +273,22 @@ class SwiGLUProjection(torch.autograd.Function):
 
 class MLPFunction(torch.autograd.Function):
     """down(fp16(g * sigmoid(g) * u)), g = x Wg^T, u = x Wu^T, of a SwiGLU MLP with NF4 gate, up
-    and down weights (no bias, no adapter), in two launches each way:
-      forward : nf4b_linear_fwd_swiglu (gate, up and the SwiGLU), then the down projection;
-      backward: nf4b_linear_bwd_dx_swiglu (dm of down with the SwiGLU backward in its epilogue:
-                dgate, dup), then ONE dX GEMM over the concatenated gate/up out features.
+    and down weights (no bias, no adapter):
+      forward : nf4b_linear_fwd_swiglu (gate, up and the SwiGLU in one launch), then the down
+                projection;
+      backward: dm = dX of down (nf4b_linear_bwd_dx_ws), dgate/dup from the SwiGLU backward
+                kernel (nf4b_swiglu_bwd), then ONE dX GEMM over the concatenated gate/up out
+                features.  fused_backward=True applies the SwiGLU backward in down's dX epilogue
+                instead (nf4b_linear_bwd_dx_swiglu, bit-identical): one launch and no dm in HBM,
+                but on B200 its epilogue -- two loads and two stores per output, bound by load
+                latency -- outlasts the tile's MMAs (66 vs 60 us at 1,170 tokens), so it is off
+                by default.
     recompute=True keeps only x: the backward runs the forward's gate/up launch again for g and u
     (the reference's MLP memory cap, solution/unpad.py:48-57) -- no torch checkpoint, so the step
     stays capturable in a CUDA graph."""
 
     @staticmethod
-    def forward(ctx, x, gate, up, down, recompute):
+    def forward(ctx, x, gate, up, down, recompute, fused_backward=False):
         (pg, sg), (pu, su), (pd, sd) = gate, up, down
         inter, hidden = int(sg.shape[0]), int(sg.shape[1])
         x2 = x.reshape(-1, hidden).contiguous()
@@ -302,6 +308,7 @@ class MLPFunction(torch.autograd.Function):
             ctx.save_for_backward(x2, g, u)
         ctx.weights = (gate, up, down)
         ctx.x_shape = x.shape
+        ctx.fused_backward = fused_backward
         return y.reshape(*x.shape[:-1], hidden)
 
     @staticmethod
@@ -322,12 +329,21 @@ class MLPFunction(torch.autograd.Function):
             dg, du = torch.empty_like(g), torch.empty_like(u)
             qd = _qstate(sd, dev)
             work, wbytes = _workspace(dev, n, inter, hidden, True)
-            _lib.check(L.nf4b_linear_bwd_dx_swiglu(dy.data_ptr(), pd.view(-1, 1).data_ptr(), ctypes.byref(qd),
-                                                   g.data_ptr(), u.data_ptr(), dg.data_ptr(), du.data_ptr(), n,
-                                                   inter, hidden, work, wbytes, _stream(dev)),
-                       "nf4b_linear_bwd_dx_swiglu")
+            st = _stream(dev)
+            if ctx.fused_backward:
+                _lib.check(L.nf4b_linear_bwd_dx_swiglu(dy.data_ptr(), pd.view(-1, 1).data_ptr(), ctypes.byref(qd),
+                                                       g.data_ptr(), u.data_ptr(), dg.data_ptr(), du.data_ptr(), n,
+                                                       inter, hidden, work, wbytes, st),
+                           "nf4b_linear_bwd_dx_swiglu")
+            else:
+                dm = torch.empty_like(g)
+                _lib.check(L.nf4b_linear_bwd_dx_ws(dy.data_ptr(), pd.view(-1, 1).data_ptr(), ctypes.byref(qd),
+                                                   None, None, dm.data_ptr(), n, inter, hidden, work, wbytes, st),
+                           "nf4b_linear_bwd_dx_ws")
+                _lib.check(L.nf4b_swiglu_bwd(dm.data_ptr(), g.data_ptr(), u.data_ptr(), dg.data_ptr(),
+                                             du.data_ptr(), g.numel(), st), "nf4b_swiglu_bwd")
             dx = _gate_up_bwd(dg, du, (pg, sg), (pu, su), hidden)
-        return dx.reshape(ctx.x_shape), None, None, None, None
+        return dx.reshape(ctx.x_shape), None, None, None, None, None
 
 
 def _swiglu_launch(x2, gate, up):
@@ -367,11 +383,12 @@ def _gate_up_bwd(dg, du, gate, up, in_f):
     return dx
 
 
-def nf4_mlp(x, gate, up, down, recompute: bool = False):
-    """down(SwiGLU(gate(x), up(x))) for three NF4Linear modules without bias, two launches each
-    way (MLPFunction); recompute=True keeps only x for the backward."""
+def nf4_mlp(x, gate, up, down, recompute: bool = False, fused_backward: bool = False):
+    """down(SwiGLU(gate(x), up(x))) for three NF4Linear modules without bias (MLPFunction): two
+    launches forward, three backward (four with recompute=True, which keeps only x);
+    fused_backward=True puts the SwiGLU backward in down's dX epilogue (one launch fewer)."""
     return MLPFunction.apply(x, (gate.packed, gate.quant_state), (up.packed, up.quant_state),
-                             (down.packed, down.quant_state), bool(recompute))
+                             (down.packed, down.quant_state), bool(recompute), bool(fused_backward))
 
 
 def swiglu_projection(x, gate, up):

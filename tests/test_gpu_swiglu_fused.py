@@ -155,11 +155,13 @@ def test_down_dx_with_swiglu_backward_equals_two_step(cuda_lib, monkeypatch, n, 
     assert _lib.gemm_error_flag(reset=True) == 0
 
 
+@pytest.mark.parametrize("fused_backward", [False, True])
 @pytest.mark.parametrize("recompute", [False, True])
-def test_mlp_op_matches_composition(cuda_lib, recompute):
-    """lora.MLPFunction (two launches each way) against the composition it replaces -- grouped
-    gate/up projection, SwiGLU kernel, down projection -- output and dX bit for bit; with
-    recompute the backward's second gate/up launch gives the same."""
+def test_mlp_op_matches_composition(cuda_lib, recompute, fused_backward):
+    """lora.MLPFunction against the composition it replaces -- grouped gate/up projection, SwiGLU
+    kernel, down projection -- output and dX bit for bit, with the SwiGLU backward as its own
+    kernel or in down's dX epilogue; with recompute the backward's second gate/up launch gives
+    the same."""
     from stew_b200.lora import NF4Linear, grouped_projection, nf4_mlp
     from stew_b200.step_ops import swiglu
     (pg, sg), (pu, su), (pd, sd) = _weight((8960, 1536), 41), _weight((8960, 1536), 42), _weight((1536, 8960), 43)
@@ -167,7 +169,7 @@ def test_mlp_op_matches_composition(cuda_lib, recompute):
     x0 = _x(1170, 1536, 44)
     dy = _x(1170, 1536, 45, std=0.01)
     xa = x0.clone().requires_grad_(True)
-    ya = nf4_mlp(xa, gate, up, down, recompute=recompute)
+    ya = nf4_mlp(xa, gate, up, down, recompute=recompute, fused_backward=fused_backward)
     ya.backward(dy)
     xb = x0.clone().requires_grad_(True)
     gb, ub = grouped_projection(xb, [gate, up])
