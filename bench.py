@@ -569,7 +569,7 @@ def main():
     ap.add_argument("--gemm-n", type=str, default="1170,2048,8192")
     ap.add_argument("--gemm-steps", type=int, default=5)
     ap.add_argument("--e2e-steps", type=int, default=5)
-    ap.add_argument("--e2e-chunks", type=int, default=14,
+    ap.add_argument("--e2e-chunks", type=int, default=28,
                     help="groups of matrices the end-to-end sweep pipelines over (copies overlap)")
     ap.add_argument("--step-steps", type=int, default=5)
     ap.add_argument("--no-step", action="store_true")
