@@ -130,6 +130,11 @@ class BucketedGradAllReduce:
 
     def _hook(self, p):
         i = self._where[p]
+        if self._launched[i]:
+            # the bucket was exchanged already: a second backward before finish() would
+            # accumulate gradients that no all-reduce carries
+            raise RuntimeError("BucketedGradAllReduce: a second backward before finish(); call finish() "
+                               "after each backward")
         self._ready[i] += 1
         if self._ready[i] == len(self.buckets[i]):
             self._launch(i)

@@ -212,6 +212,21 @@ def _bucket_worker(rank, world, port, q, n_buckets):
         dist.destroy_process_group()
 
 
+def test_bucketed_allreduce_refuses_a_second_backward_before_finish():
+    """Buckets are exchanged as the backward completes them; a second backward before finish()
+    would add gradients that no exchange carries, so it raises (single process, no group)."""
+    x, labels = _rows(0)
+    m = LayeredLoRA()
+    red = dp.BucketedGradAllReduce(m.layer_params(), n_buckets=2)
+    loss, n = m(x, labels)
+    red.count = torch.tensor([float(n)])
+    loss.backward()
+    loss2, _ = m(x, labels)
+    with pytest.raises(RuntimeError, match="second backward before finish"):
+        loss2.backward()
+    red.remove()
+
+
 @pytest.mark.parametrize("n_buckets", [1, 2, 5])
 def test_bucketed_allreduce_equals_one_flat_allreduce(n_buckets):
     """dp.BucketedGradAllReduce (buckets launched from post-accumulate-grad hooks as the
