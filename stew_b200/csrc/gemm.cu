@@ -134,6 +134,8 @@ struct GemmArgs {
   int32_t* ws_cnt;        // split-K: per-tile counters [2][G_SPLIT_MAX_TILES] + exit count, zero
                           // between launches
   int32_t drop_ticket_unit;  // test hook: this work unit skips its ticket (-1: none)
+  int32_t epi_decode;     // every CTA (pair) has at most one work unit: the epilogue warps decode
+                          // stages too until their accumulator is ready (four decode groups)
   __half* glu_out;        // SwiGLU launches: m = fp16(gate * sigmoid(gate) * up) [n, out]
   // SwiGLU-backward launches (dX of down): the forward's gate and up [n, in], and the outputs
   // dgate, dup [n, in] written instead of dX
@@ -645,11 +647,17 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     } else if (PAIR && lane == 0) {
       drain_wait(mma_done, 0);
     }
-  } else if (warp < G_EPI_WARP0) {
+  } else {
+   const bool epi = warp >= G_EPI_WARP0;
+   if (!epi || g.epi_decode) {
     // ------------------------------------------------------------ decode warps
-    // Two groups of four warps; group g decodes the stages whose global index has parity g
-    // (so every ring slot has one owner), each thread one whole 64-value block row per stage:
-    // one scale and one 16-entry table per 64 values.
+    // Two groups of four warps (warps 2-5, 6-9); group g decodes the stages whose global index
+    // is g modulo the group count (so every ring slot has one owner), each thread one whole
+    // 64-value block row per stage: one scale and one 16-entry table per 64 values.  When
+    // every CTA has at most one work unit (`epi_decode`), the epilogue warps have nothing to do
+    // until that unit's accumulator is ready, so they decode as groups 2 and 3 (warps 10-13,
+    // 14-17) first: each group then has four stage-times for its stage, which hides the lag of
+    // the decode warp that shares the MMA issuer's SM sub-partition.
     //  forward : row d of the K-major tile = weight row m0 + d, K columns 64 kl .. +63 of the
     //            stage; packed row d of the stage is 32 B in the 32B swizzle (16-byte chunk c
     //            at c ^ ((d >> 2) & 1)), so a warp's 16-byte loads hit all 32 banks.
@@ -657,8 +665,9 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     //            64 j .. +63 with j = d >> 6 (one 128-byte row of M chunk j); packed row r has
     //            64 B in the 64B swizzle (16-byte chunk c at c ^ ((r >> 1) & 3)), the thread's
     //            two chunks are 2j and 2j + 1.
-    const int dq = threadIdx.x - 32 * G_DQ_WARP0;  // 0..255
-    const int grp = dq >> 7;
+    const int dq = threadIdx.x - 32 * (epi ? G_EPI_WARP0 : G_DQ_WARP0);  // 0..255
+    const int ngrp = g.epi_decode ? 4 : 2;
+    const int grp = (dq >> 7) + (epi ? 2 : 0);
     const int d = dq & 127;
     float code[16];  // NF4 code of the current weight (reloaded when the weight changes)
     int code_seg = -1;
@@ -688,7 +697,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       const GemmW& W = g.w[tws];
       // one slab per adapter (a K-concatenated backward may carry several), in the order the
       // MMA issuer consumes them
-      for (int li = 0; wu.split == 0 && li < (KCAT ? g.nw : 1); ++li) {
+      for (int li = 0; !epi && wu.split == 0 && li < (KCAT ? g.nw : 1); ++li) {
         const GemmW& WL = KCAT ? g.w[li] : W;
         if (!WL.has_lora) continue;
         if (!pwait(lora_empty, (lc & 1) ^ 1)) {
@@ -785,11 +794,11 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         x.v = load_scale_src(Wk, e >> Wk.log2_bs, lane_valid);
         return scale_of(x);
       };
-      // this group's stages of the unit: k0, k0 + 2, ...; scales of the next two in flight
-      const int k0 = wu.kb + ((int(it & 1u) == grp) ? 0 : 1);
+      // this group's stages of the unit: k0, k0 + ngrp, ...; scales of the next two in flight
+      const int k0 = wu.kb + int((uint32_t(grp) - it) & uint32_t(ngrp - 1));
       float sc = scale_of(src(k0));
-      Src raw1 = src(k0 + 2);
-      for (int k = k0; k < wu.ke; k += 2) {
+      Src raw1 = src(k0 + ngrp);
+      for (int k = k0; k < wu.ke; k += ngrp) {
         const int ws = KCAT ? kseg(g, k) : tws;
         if (ws != code_seg) {
           code_seg = ws;
@@ -800,7 +809,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         const int s = its % NS;
         const uint32_t ph = (its / NS) & 1;
         const Nf4Table tab = make_table(code, sc);
-        const Src raw2 = src(k + 4);
+        const Src raw2 = src(k + 2 * ngrp);
         const float sc1 = scale_of(raw1);
         if (!pwait(&full[s], ph)) {
           ok = false;
@@ -832,7 +841,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       }
       it += uint32_t(wu.ke - wu.kb);
     }
-  } else {
+   }
+   if (epi) {
     // --------------------------------------------------------------- epilogue
     // Warp w may only read TMEM lanes 32*(w%4)..+31 (the tile's weight rows); the two
     // groups of four warps take alternate 32-column chunks.  Lanes 2i and 2i+1 hold
@@ -1100,6 +1110,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       }
       if (fail) break;
     }
+   }
   }
 
   tc_fence_before();
@@ -1415,6 +1426,7 @@ static int launch_gemm(const GemmPlan& p, const CUtensorMap (&ta)[G_MAX_W], cons
   const int64_t units = q.tiles * q.splits;
   const int64_t slots = units < q.slots ? units : q.slots;
   const unsigned grid = unsigned(q.pair ? 2 * slots : slots);
+  g.epi_decode = units <= q.slots ? 1 : 0;  // one unit per CTA (pair) at most
   const bool split = q.splits > 1;
   const bool multi = g.nw > 1 && !glu;
   int st;
