@@ -134,8 +134,8 @@ struct GemmArgs {
   int32_t* ws_cnt;        // split-K: per-tile counters [2][G_SPLIT_MAX_TILES] + exit count, zero
                           // between launches
   int32_t drop_ticket_unit;  // test hook: this work unit skips its ticket (-1: none)
-  int32_t epi_decode;     // every CTA (pair) has at most one work unit: the epilogue warps decode
-                          // stages too until their accumulator is ready (four decode groups)
+  int32_t epi_decode;     // a backward launch whose CTAs (pairs) have at most one work unit: the
+                          // epilogue warps decode stages too until their accumulator is ready
   __half* glu_out;        // SwiGLU launches: m = fp16(gate * sigmoid(gate) * up) [n, out]
   // SwiGLU-backward launches (dX of down): the forward's gate and up [n, in], and the outputs
   // dgate, dup [n, in] written instead of dX
@@ -653,11 +653,11 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     // ------------------------------------------------------------ decode warps
     // Two groups of four warps (warps 2-5, 6-9); group g decodes the stages whose global index
     // is g modulo the group count (so every ring slot has one owner), each thread one whole
-    // 64-value block row per stage: one scale and one 16-entry table per 64 values.  When
-    // every CTA has at most one work unit (`epi_decode`), the epilogue warps have nothing to do
-    // until that unit's accumulator is ready, so they decode as groups 2 and 3 (warps 10-13,
-    // 14-17) first: each group then has four stage-times for its stage, which hides the lag of
-    // the decode warp that shares the MMA issuer's SM sub-partition.
+    // 64-value block row per stage: one scale and one 16-entry table per 64 values.  In a
+    // backward launch where every CTA has at most one work unit (`epi_decode`), the epilogue
+    // warps have nothing to do until that unit's accumulator is ready, so they decode as groups
+    // 2 and 3 (warps 10-13, 14-17) first: each group then has four stage-times for its stage,
+    // which hides the lag of the decode warp that shares the MMA issuer's SM sub-partition.
     //  forward : row d of the K-major tile = weight row m0 + d, K columns 64 kl .. +63 of the
     //            stage; packed row d of the stage is 32 B in the 32B swizzle (16-byte chunk c
     //            at c ^ ((d >> 2) & 1)), so a warp's 16-byte loads hit all 32 banks.
@@ -1426,7 +1426,8 @@ static int launch_gemm(const GemmPlan& p, const CUtensorMap (&ta)[G_MAX_W], cons
   const int64_t units = q.tiles * q.splits;
   const int64_t slots = units < q.slots ? units : q.slots;
   const unsigned grid = unsigned(q.pair ? 2 * slots : slots);
-  g.epi_decode = units <= q.slots ? 1 : 0;  // one unit per CTA (pair) at most
+  // backward launches with one unit per CTA (pair) at most (forward ones measured no faster)
+  g.epi_decode = (BWD && units <= q.slots) ? 1 : 0;
   const bool split = q.splits > 1;
   const bool multi = g.nw > 1 && !glu;
   int st;
