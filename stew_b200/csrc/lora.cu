@@ -152,10 +152,6 @@ int lora_project16_multi(const void* const* act, const void* const* w, int64_t w
   return launch_status("lora_project16_kernel launch");
 }
 
-int lora_project16(const void* act, const void* w, int64_t w_stride_r, int64_t w_stride_k,
-                   void* out, int64_t n, int64_t kdim, cudaStream_t s) {
-  return lora_project16_multi(&act, &w, w_stride_r, w_stride_k, &out, &kdim, 1, n, s);
-}
 
 // ---------------------------------------------------------------- weight grads
 // G[r, c] = sum_t P[t, r] * Q[t, c] on the tensor cores: M = the 16 adapter rows, N = columns
