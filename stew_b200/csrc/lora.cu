@@ -32,24 +32,41 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// W(r, k .. k+7) as 8 halves (k a multiple of 8): one 16-byte load when W is K-contiguous
-// (forward: lora A [16, in]), else eight strided loads (backward: lora B [out, 16], which is
-// small and stays in L1/L2).
-template <bool WK>
-__device__ __forceinline__ uint4 ld_w8(const __half* w, int64_t sr, int64_t sk, int r, int64_t k) {
-  if (WK) return __ldg(reinterpret_cast<const uint4*>(w + r * sr + k));
-  uint32_t h[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) h[i] = __ldg(reinterpret_cast<const unsigned short*>(w + r * sr + (k + i) * sk));
-  return make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
 }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// W(r, k .. k+7) as 8 halves (k a multiple of 8) of a K-contiguous weight (forward: lora A
+// [16, in]): one 16-byte load.
+__device__ __forceinline__ uint4 ld_w8(const __half* w, int64_t sr, int r, int64_t k) {
+  return __ldg(reinterpret_cast<const uint4*>(w + r * sr + k));
+}
+
+// Strided weight (backward: lora B [out, 16], K = out, one 32-byte row per k): a warp stages the
+// rows of up to LP_STAGE_CHUNKS chunks of its K slice in shared memory with cp.async (the two
+// 16-byte halves of row k swapped when bit 3 of k is set, so the eight rows an ldmatrix reads
+// fall in four bank groups) and reads each chunk's fragments with two ldmatrix .trans.
+constexpr int LP_STAGE_CHUNKS = 8;
+constexpr int LP_STAGE_BYTES = LP_STAGE_CHUNKS * 32 * 32;  // per warp
 
 // Thread (g, c) of a warp reads, per 32-wide K chunk j, the 8 consecutive values
 // [32 j + 8 c, +8) of token rows g and g+8 (two 16-byte loads) and feeds them to two k16 MMA
 // steps: fragment position 2c(+1) takes values 0-1 (step 0) / 4-5 (step 1), position
 // 2c+8(+9) values 2-3 / 6-7.  The adapter weight is read with the same assignment, so both
 // operands see one permutation of K and the dot products are those of the natural order.
-// WK: the weight is K-contiguous (sk == 1).
+// WK: the weight is K-contiguous (sk == 1); otherwise it is [kdim][16] (sr == 1, sk == 16).
 // One projection of a launch (blockIdx.y picks it; all of a launch's share n and WK).
 struct ProjJob {
   const __half* act;
@@ -84,29 +101,79 @@ __global__ void __launch_bounds__(LP_THREADS)
   const uint4* x0 = reinterpret_cast<const uint4*>(act + (t0 + g) * kdim);
   const uint4* x1 = reinterpret_cast<const uint4*>(act + (t0 + g + 8) * kdim);
   float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-  // chunks in batches of LP_BATCH: every load of a batch is issued before its MMAs, so a warp
-  // waits for memory about once per batch instead of once per chunk (2 for a weight read with
-  // strided 2-byte loads, whose 16 values a chunk take 16 registers)
-  constexpr int LP_BATCH = WK ? 4 : 2;
-  for (int64_t j0 = jb; j0 < je; j0 += LP_BATCH) {
-    uint4 xa[LP_BATCH], xb[LP_BATCH], w0[LP_BATCH], w1[LP_BATCH];
+  auto mma_chunk = [&](const uint4& xa, const uint4& xb, uint32_t w0x, uint32_t w0y, uint32_t w0z,
+                       uint32_t w0w, uint32_t w1x, uint32_t w1y, uint32_t w1z, uint32_t w1w) {
+    const uint32_t s0[4] = {xa.x, xb.x, xa.y, xb.y};
+    const uint32_t s1[4] = {xa.z, xb.z, xa.w, xb.w};
+    mma16816(d0, s0, w0x, w0y);
+    mma16816(d1, s0, w1x, w1y);
+    mma16816(d0, s1, w0z, w0w);
+    mma16816(d1, s1, w1z, w1w);
+  };
+  // chunks in batches of 4: every activation load of a batch is issued before its MMAs, so a
+  // warp waits for memory about once per batch instead of once per chunk
+  constexpr int LP_BATCH = 4;
+  if (WK) {
+    for (int64_t j0 = jb; j0 < je; j0 += LP_BATCH) {
+      uint4 xa[LP_BATCH], xb[LP_BATCH], w0[LP_BATCH], w1[LP_BATCH];
 #pragma unroll
-    for (int u = 0; u < LP_BATCH; ++u) {
-      const int64_t k = 32 * (j0 + u) + 8 * c;
-      const bool in = j0 + u < je;
-      xa[u] = (in && v0) ? __ldg(x0 + (k >> 3)) : make_uint4(0, 0, 0, 0);
-      xb[u] = (in && v1) ? __ldg(x1 + (k >> 3)) : make_uint4(0, 0, 0, 0);
-      w0[u] = in ? ld_w8<WK>(w, sr, sk, g, k) : make_uint4(0, 0, 0, 0);      // adapter rows 0-7 (d0)
-      w1[u] = in ? ld_w8<WK>(w, sr, sk, 8 + g, k) : make_uint4(0, 0, 0, 0);  // adapter rows 8-15 (d1)
+      for (int u = 0; u < LP_BATCH; ++u) {
+        const int64_t k = 32 * (j0 + u) + 8 * c;
+        const bool in = j0 + u < je;
+        xa[u] = (in && v0) ? __ldg(x0 + (k >> 3)) : make_uint4(0, 0, 0, 0);
+        xb[u] = (in && v1) ? __ldg(x1 + (k >> 3)) : make_uint4(0, 0, 0, 0);
+        w0[u] = in ? ld_w8(w, sr, g, k) : make_uint4(0, 0, 0, 0);      // adapter rows 0-7 (d0)
+        w1[u] = in ? ld_w8(w, sr, 8 + g, k) : make_uint4(0, 0, 0, 0);  // adapter rows 8-15 (d1)
+      }
+#pragma unroll
+      for (int u = 0; u < LP_BATCH; ++u)
+        mma_chunk(xa[u], xb[u], w0[u].x, w0[u].y, w0[u].z, w0[u].w, w1[u].x, w1[u].y, w1[u].z, w1[u].w);
     }
+  } else {
+    // the launch holds LP_WARPS regions of min(per, LP_STAGE_CHUNKS) KB for the job with the
+    // longest K; this job's per is at most that job's
+    extern __shared__ __align__(128) uint8_t lp_stage[];
+    const int64_t stage_chunks = per < LP_STAGE_CHUNKS ? per : LP_STAGE_CHUNKS;
+    const uint32_t wb = smem_u32(lp_stage) + uint32_t(warp) * uint32_t(stage_chunks) * 1024u;
+    // ldmatrix x4: lane l gives row l % 8 of matrix l / 8; matrix m holds, for fragment rows
+    // 2c and 2c+1, the weight rows 8 c + 2 m and 8 c + 2 m + 1 of the chunk (values 2m, 2m+1 of
+    // each lane's 8), i.e. row 8 (i / 2) + (i % 2) + 2 m for i = l % 8
+    const int lrow = 8 * ((lane & 7) >> 1) + (lane & 1) + 2 * (lane >> 3);
+    for (int64_t r0 = jb; r0 < je; r0 += stage_chunks) {
+      const int64_t r1 = min64(je, r0 + stage_chunks);
+      const int pieces = int(r1 - r0) * 64;  // 32 rows a chunk, two 16-byte halves a row
+      __syncwarp();  // the previous round's ldmatrix reads are done
+      for (int p = lane; p < pieces; p += 32) {
+        const int row = p >> 1, half = p & 1;
+        cp_async16(wb + uint32_t(row * 32 + ((half ^ ((row >> 3) & 1)) << 4)),
+                   w + (32 * r0 + row) * 16 + 8 * half, true);
+      }
+      cp_async_commit();
+      for (int64_t j0 = r0; j0 < r1; j0 += LP_BATCH) {
+        uint4 xa[LP_BATCH], xb[LP_BATCH];
 #pragma unroll
-    for (int u = 0; u < LP_BATCH; ++u) {
-      const uint32_t s0[4] = {xa[u].x, xb[u].x, xa[u].y, xb[u].y};
-      const uint32_t s1[4] = {xa[u].z, xb[u].z, xa[u].w, xb[u].w};
-      mma16816(d0, s0, w0[u].x, w0[u].y);
-      mma16816(d1, s0, w1[u].x, w1[u].y);
-      mma16816(d0, s1, w0[u].z, w0[u].w);
-      mma16816(d1, s1, w1[u].z, w1[u].w);
+        for (int u = 0; u < LP_BATCH; ++u) {
+          const int64_t k = 32 * (j0 + u) + 8 * c;
+          const bool in = j0 + u < r1;
+          xa[u] = (in && v0) ? __ldg(x0 + (k >> 3)) : make_uint4(0, 0, 0, 0);
+          xb[u] = (in && v1) ? __ldg(x1 + (k >> 3)) : make_uint4(0, 0, 0, 0);
+        }
+        if (j0 == r0) {
+          cp_async_wait<0>();
+          __syncwarp();
+        }
+#pragma unroll
+        for (int u = 0; u < LP_BATCH; ++u) {
+          if (j0 + u >= r1) break;
+          const int row = int(j0 + u - r0) * 32 + lrow;
+          const uint32_t rb = wb + uint32_t(row * 32);
+          const uint32_t sw = uint32_t((row >> 3) & 1) << 4;
+          uint32_t b0[4], b1[4];
+          ldsm_x4_t(rb + sw, b0);          // adapter rows (ranks) 0-7
+          ldsm_x4_t(rb + (sw ^ 16u), b1);  // ranks 8-15
+          mma_chunk(xa[u], xb[u], b0[0], b0[1], b0[2], b0[3], b1[0], b1[1], b1[2], b1[3]);
+        }
+      }
     }
   }
   red[warp][g][2 * c] = d0[0];
@@ -132,23 +199,44 @@ int lora_project16_multi(const void* const* act, const void* const* w, int64_t w
                          int64_t w_stride_k, void* const* out, const int64_t* kdim, int n_jobs,
                          int64_t n, cudaStream_t s) {
   NF4B_RETURN_IF(n_jobs < 1 || n_jobs > LP_MAX_JOBS, NF4B_ERR_UNSUPPORTED);
+  // the two weight layouts the kernels take: K-contiguous [16][kdim] or [kdim][16]
+  const bool wk = w_stride_k == 1;
+  NF4B_RETURN_IF(!wk && (w_stride_r != 1 || w_stride_k != 16), NF4B_ERR_UNSUPPORTED);
   ProjJobs js{};
+  int64_t kmax = 0;
   for (int i = 0; i < n_jobs; ++i) {
     NF4B_RETURN_IF(kdim[i] % 32 != 0, NF4B_ERR_UNSUPPORTED);
-    NF4B_RETURN_IF(!aligned(act[i], 16) || !aligned(w[i], w_stride_k == 1 ? 16 : 2), NF4B_ERR_ALIGNMENT);
+    NF4B_RETURN_IF(!aligned(act[i], 16) || !aligned(w[i], 16), NF4B_ERR_ALIGNMENT);
     js.j[i] = ProjJob{static_cast<const __half*>(act[i]), static_cast<const __half*>(w[i]), w_stride_r,
                       w_stride_k, static_cast<__half*>(out[i]), kdim[i]};
+    kmax = kdim[i] > kmax ? kdim[i] : kmax;
   }
   if (n == 0) return NF4B_OK;
   const int64_t ctas = (n + LP_TOK - 1) / LP_TOK;
   NF4B_RETURN_IF(ctas > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);
   const dim3 grid{unsigned(ctas), unsigned(n_jobs), 1u};
-  if (w_stride_k == 1)
+  if (wk) {
     NF4B_CUDA_TRY(launch_pdl(lora_project16_kernel<true>, dim3(grid), dim3(LP_THREADS), size_t(0),
                              s, js, n));
-  else
-    NF4B_CUDA_TRY(launch_pdl(lora_project16_kernel<false>, dim3(grid), dim3(LP_THREADS), size_t(0),
-                             s, js, n));
+  } else {
+    // each warp stages up to LP_STAGE_CHUNKS chunks of its K slice at a time
+    const int64_t per = (kmax / 32 + LP_WARPS - 1) / LP_WARPS;
+    const size_t smem = size_t(LP_WARPS) * size_t(per < LP_STAGE_CHUNKS ? per : LP_STAGE_CHUNKS) * 1024;
+    {
+      static std::mutex mu;
+      static bool done[64] = {false};
+      int dev = 0;
+      NF4B_CUDA_TRY(cudaGetDevice(&dev));
+      NF4B_RETURN_IF(dev < 0 || dev >= 64, NF4B_ERR_DEVICE);
+      std::lock_guard<std::mutex> lock(mu);
+      if (!done[dev]) {
+        NF4B_CUDA_TRY(cudaFuncSetAttribute(lora_project16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           LP_WARPS * LP_STAGE_BYTES));
+        done[dev] = true;
+      }
+    }
+    NF4B_CUDA_TRY(launch_pdl(lora_project16_kernel<false>, dim3(grid), dim3(LP_THREADS), smem, s, js, n));
+  }
   return launch_status("lora_project16_kernel launch");
 }
 
@@ -177,22 +265,6 @@ constexpr int LO_MIN_TOK = 64;                 // tokens per split at least (two
 // them zero), then the fp32 partials [splits][16][cols] of each job with more than one split.
 constexpr int LO_MAX_TILES = 1024;
 constexpr int64_t LO_CNT_BYTES = LO_MAX_TILES * 4;
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
-               "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
 
 // One outer product of a launch: its CTAs are [cta0, cta0 + col tiles * splits), its tickets
 // [tile0, tile0 + col tiles).
