@@ -51,6 +51,33 @@ def test_fused_lora_forward_backward(cuda_lib, proj, n):
     _check_flag()
 
 
+@pytest.mark.parametrize("n", [77, 1170])
+@pytest.mark.parametrize("shape", [(8960, 1536), (1536, 8960)])
+def test_fused_lora_on_wide_projections(cuda_lib, shape, n):
+    """An adapter on the MLP shapes: with 8960 output features the backward's dY B runs over
+    K = 8960, so each warp stages its slice of B in several rounds (eight 32-wide chunks a round);
+    with 8960 input features the forward's X A^T does.  Same checks as above."""
+    from stew_b200 import nf4_lora_linear
+    out_f, in_f = shape
+    q, st = _weight((out_f, in_f), 400 + n)
+    a, b = _lora(in_f, out_f, 19)
+    x = _x(n, in_f, 7).requires_grad_(True)
+    dy = _x(n, out_f, 8, std=0.01)
+    y = nf4_lora_linear(x, q, st, a, b, 2.0)
+    y.backward(dy)
+    W = _ref_weight(q, st)
+    xd = x.detach().double().requires_grad_(True)
+    ad = a.detach().double().requires_grad_(True)
+    bd = b.detach().double().requires_grad_(True)
+    ref = xd @ W.T + (xd @ ad.T) @ bd.T * 2.0
+    ref.backward(dy.double())
+    assert_gemm_close(y, ref.detach(), f"{shape} y N={n}")
+    assert_gemm_close(x.grad, xd.grad, f"{shape} dX N={n}")
+    assert max_rel_err(a.grad, ad.grad) <= 1e-3
+    assert max_rel_err(b.grad, bd.grad) <= 1e-3
+    _check_flag()
+
+
 def test_lora_term_is_applied(cuda_lib):
     """With B != 0 the adapter changes the output by exactly its own contribution."""
     from stew_b200 import nf4_lora_linear
