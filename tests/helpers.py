@@ -82,7 +82,7 @@ def to_oracle_state(st, packed: torch.Tensor):
 
 
 def seeded_weight(shape, seed, device="cpu"):
-    """fp16 weight drawn N(0, 0.02) from a seed (the BASELINE workload's weights)."""
+    """fp16 weight drawn N(0, 0.02) from a seed (the whole-model sweep's weight distribution)."""
     g = torch.Generator().manual_seed(seed)
     return (torch.randn(shape, generator=g) * 0.02).to(torch.float16).to(device)
 
