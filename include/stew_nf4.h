@@ -104,9 +104,11 @@ int nf4b_dequant_error_flag(int* value, int reset);
 /* LoRA adapter operands of a fused linear (peft lora.Linear, r = rank).
  * A is [rank, in] fp16 (lora_A.weight), B is [out, rank] fp16 (lora_B.weight),
  * scale = lora_alpha / r.  */
+/* Adapter matrices and activations are read with 16-byte loads: a, b, xa and the dyb buffer
+ * must be 16-byte aligned (NF4B_ERR_ALIGNMENT otherwise).  */
 typedef struct nf4b_lora {
-  const void* a;            /* fp16 [rank, in]                                */
-  const void* b;            /* fp16 [out, rank]                               */
+  const void* a;            /* fp16 [rank, in], contiguous                    */
+  const void* b;            /* fp16 [out, rank], contiguous                   */
   float scale;
   int32_t rank;             /* 16                                             */
   void* xa;                 /* fwd: optional fp16 [n, rank] output of x A^T (saved for the backward) */
