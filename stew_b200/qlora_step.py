@@ -261,14 +261,16 @@ class QLoRATrainer:
     call is exactly one optimizer step."""
 
     def __init__(self, model: QwenQLoRA, lr: float = 2e-4, group=None, cuda_graph: bool = False,
-                 buckets: int = 4):
+                 buckets: int = 4, buckets_on_one_rank: bool = False):
         self.model = model
         self.params = model.lora_parameters()
         self.cuda_graph = cuda_graph
         # data parallel: the LoRA-grad all-reduce in `buckets` groups of layers, each launched
-        # from the backward as soon as its layers' gradients are complete (dp.BucketedGradAllReduce)
+        # from the backward as soon as its layers' gradients are complete (dp.BucketedGradAllReduce);
+        # buckets_on_one_rank runs that machinery (hooks, side stream, normalisation) with no
+        # collective on a single rank
         self._reducer = None
-        if dp._world(group) > 1 and buckets > 0:
+        if buckets > 0 and (dp._world(group) > 1 or buckets_on_one_rank):
             layer_params = [[p for p in layer.parameters() if p.requires_grad] for layer in model.layers]
             self._reducer = dp.BucketedGradAllReduce(layer_params, group, n_buckets=buckets)
         self.buckets = len(self._reducer) if self._reducer is not None else 0
