@@ -514,13 +514,26 @@ def profile_shape(name: str, n: int):
     """Launches, in order, for one projection of the model at n tokens: the fused forward
     (q and v with their r=16 adapter, through nf4_lora_linear), then its backward (dX GEMM,
     with the adapter's dX term in the accumulator, and for q/v the LoRA weight gradients).
-    Inputs as in the per-shape measurement: X ~ N(0, 1), dY ~ N(0, 1e-2)."""
+    name "mlp": the layer's MLP op instead (lora.nf4_mlp): gate/up with the SwiGLU in the
+    epilogue, down; backward dX of down, the SwiGLU backward kernel, the K-concatenated gate/up
+    dX.  Inputs as in the per-shape measurement: X ~ N(0, 1), dY ~ N(0, 1e-2)."""
     import math
     import torch
-    from stew_b200.lora import nf4_lora_linear
+    from stew_b200.lora import NF4Linear, nf4_lora_linear, nf4_mlp
     from stew_b200.nf4 import matmul_4bit
     from stew_b200.sweep import QWEN_PROJ, qwen_model_weights
     shapes = dict(QWEN_PROJ)
+    if name == "mlp":
+        mats = qwen_model_weights(layers=1, device="cuda", seed=0,
+                                  projections=tuple((p, shapes[p]) for p in ("gate", "up", "down")))
+        gate, up, down = (NF4Linear(q, st) for q, st in mats)
+        g = torch.Generator(device="cuda").manual_seed(0)
+        x = torch.randn(n, 1536, generator=g, device="cuda").half().requires_grad_(True)
+        dy = (torch.randn(n, 1536, generator=g, device="cuda") * 0.01).half()
+        nf4_mlp(x, gate, up, down).backward(dy)
+        torch.cuda.synchronize()
+        print("profile shape done", flush=True)
+        return
     if name not in shapes:
         raise SystemExit(f"unknown projection {name!r}: one of {sorted(shapes)}")
     out_f, in_f = shapes[name]
@@ -587,7 +600,8 @@ def main():
                     help="with --profile-step: the full 28-layer model and vocabulary")
     ap.add_argument("--profile-shape", type=str, default=None,
                     help="small single-GPU case for ncu captures: one projection (q, k, v, o, gate, up, "
-                         "down) forward then backward at --profile-n tokens, with the adapter on q/v")
+                         "down) forward then backward at --profile-n tokens, with the adapter on q/v; "
+                         "'mlp': the MLP op forward then backward")
     ap.add_argument("--profile-n", type=int, default=1170)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
