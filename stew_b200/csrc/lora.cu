@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(LP_THREADS)
   const ProjJob& job = jobs.j[blockIdx.y];
   const __half* __restrict__ act = job.act;
   const __half* __restrict__ w = job.w;
-  const int64_t sr = job.sr, sk = job.sk, kdim = job.kdim;
+  const int64_t sr = job.sr, kdim = job.kdim;  // sk is 1 (WK) or 16, fixed by the layout
   __half* __restrict__ out = job.out;
   __shared__ float red[LP_WARPS][LP_TOK][17];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
