@@ -58,7 +58,13 @@ typedef struct nf4b_qstate {
   const float* code;        /* 16-entry fp32 NF4 code                        */
   int32_t blocksize;        /* 32, 64, 128 or 256                            */
   int32_t blocksize2;       /* nested: 256                                   */
-  int32_t nested;           /* 1 = nested (double-quantized), 0 = plain      */
+  int32_t nested;           /* 1 = nested (double-quantized), 0 = plain;
+                             * 2 = nested with the scale computed as ONE fused
+                             * multiply-add, fmaf(code2[q], absmax2, offset): the
+                             * contracted form a GPU build of nf4.py:36-39 may emit
+                             * (solution/test_nf4_unpack.py:29-30 tolerates it), a
+                             * debug form for the unpack only -- the fused GEMMs
+                             * return NF4B_ERR_UNSUPPORTED for it */
   int32_t reserved;
 } nf4b_qstate;
 

@@ -14,6 +14,10 @@ What it restates (reference = evilandangry/stew):
     out[r*bs + 2j+1] = code[b & 15] * scale[r]                   (nf4.py:46)
   all in fp32 with one rounding per operation (multiply, then add -- no FMA),
   then ONE rounding to the output dtype (nf4.py:49-50).
+  ``fma=True`` gives the contracted variant -- the nested scale as one fused
+  multiply-add, rounded once (``fma_f32``) -- which a GPU compiler may emit for
+  nf4.py:36-39; the reference's own test allows for it with a mismatch
+  fraction below 1e-4 (solution/test_nf4_unpack.py:29-30).
 * ``linear_fwd_ref`` / ``linear_bwd_ref`` -- the patched MatMul4Bit forward
   (nf4.py:142-159: unpack, then F.linear) and bitsandbytes' unchanged
   MatMul4Bit backward (grad_A = dY . W), evaluated in fp32/fp64 on the
@@ -154,26 +158,51 @@ def quantize_nf4(w: np.ndarray, blocksize: int = 64, nested: bool = True,
     return packed, st
 
 
-def block_scales(st: QState) -> np.ndarray:
+def fma_f32(a, b, c) -> np.ndarray:
+    """fp32 a*b + c rounded ONCE (round to nearest even), elementwise.  The float64 product
+    of two fp32 values is exact; TwoSum gives the float64 sum s and its exact error e
+    (a*b + c = s + e).  s rounds to fp32 as the exact sum does unless s lies exactly halfway
+    between two fp32 values, where the sign of e decides the side."""
+    p = np.asarray(a, np.float32).astype(np.float64) * np.asarray(b, np.float32).astype(np.float64)
+    c = np.broadcast_to(np.asarray(c, np.float32).astype(np.float64), p.shape)
+    s = p + c
+    bv = s - p
+    e = (p - (s - bv)) + (c - bv)
+    with np.errstate(over="ignore"):
+        r = s.astype(np.float32)
+    r64 = r.astype(np.float64)
+    toward = np.where(s > r64, np.float32(np.inf), np.float32(-np.inf)).astype(np.float32)
+    n = np.nextafter(r, toward)
+    n64 = n.astype(np.float64)
+    tie = (s != r64) & (s == (r64 + n64) * 0.5) & (e != 0)
+    return np.where(tie & (np.sign(e) == np.sign(n64 - s)), n, r).astype(np.float32)
+
+
+def block_scales(st: QState, fma: bool = False) -> np.ndarray:
     """Per-block fp32 scale, nf4.py:36-41: code2[q] * absmax2[r // bs2], then + offset,
-    each an IEEE fp32 operation rounded on its own."""
+    each an IEEE fp32 operation rounded on its own (fma: one fused multiply-add)."""
     if not st.nested:
         return np.asarray(st.absmax, dtype=np.float32)
     q = np.asarray(st.absmax).astype(np.int64)
     r = np.arange(q.size)
     outer = np.asarray(st.state2.absmax, np.float32)[r // st.state2.blocksize]
-    prod = (np.asarray(st.state2.code, np.float32)[q] * outer).astype(np.float32)
+    c2 = np.asarray(st.state2.code, np.float32)[q]
+    if fma:
+        return fma_f32(c2, outer, np.float32(st.offset))
+    prod = (c2 * outer).astype(np.float32)
     return (prod + np.float32(st.offset)).astype(np.float32)
 
 
-def dequant_nf4(packed: np.ndarray, st: QState, code: np.ndarray | None = None) -> np.ndarray:
+def dequant_nf4(packed: np.ndarray, st: QState, code: np.ndarray | None = None,
+                fma: bool = False) -> np.ndarray:
     """Restates `_nf4_unpack` (nf4.py:30-50) for the whole tensor; returns st.shape
-    in st.dtype.  `code` defaults to the NF4 table (the reference's `_code()`)."""
+    in st.dtype.  `code` defaults to the NF4 table (the reference's `_code()`); fma: the
+    nested scale as one fused multiply-add (the contracted variant)."""
     code = nf4_codebook() if code is None else np.asarray(code, np.float32)
     b = np.asarray(packed, np.uint8).reshape(-1)
     n = int(np.prod(st.shape))
     assert n == 2 * b.size and n % st.blocksize == 0
-    scale = block_scales(st)
+    scale = block_scales(st, fma=fma)
     hb = st.blocksize // 2
     bb = b.reshape(-1, hb)
     hi = (code[(bb >> 4).astype(np.int64)] * scale[:, None]).astype(np.float32)

@@ -7,6 +7,11 @@
 //   out[2j] = code[b >> 4] * scale, out[2j+1] = code[b & 15] * scale    (nf4.py:45-47)
 // fp32 math with one rounding per operation (explicit __fmul_rn / __fadd_rn, so
 // no FMA contraction can change a bit), one rounding to the output dtype.
+// nf4b_qstate.nested == 2 selects the contracted form of the nested scale instead,
+// fmaf(code2[absmax8[blk]], absmax2[blk / bs2], offset) rounded once: what a GPU compiler may
+// emit for nf4.py:36-39, and what the reference's own test tolerates with a mismatch
+// fraction below 1e-4 (solution/test_nf4_unpack.py:29-30) -- a debug form for diffing
+// against such a build.
 //
 // General path (fp32 out, unaligned buffers, numel not a multiple of 64), HBM-bound:
 //   one CTA = one chunk of 1024 packed 32-bit words (8192 values); thread t of
@@ -45,9 +50,13 @@ struct DqParams {
   int64_t nwords;   // numel / 8
   int32_t log2_bs;  // log2(blocksize)
   int32_t log2_bs2; // log2(blocksize2)
-  int32_t nested;
+  int32_t nested;   // 0 plain, 1 nested (multiply, then add), 2 nested (one fused multiply-add)
   int32_t f32out;
 };
+
+__device__ __forceinline__ float nested_scale(int32_t mode, float c2, float a2, float off) {
+  return mode == 2 ? __fmaf_rn(c2, a2, off) : __fadd_rn(__fmul_rn(c2, a2), off);
+}
 
 static_assert(sizeof(nf4b_dequant_job) % 8 == 0, "job struct layout");
 
@@ -56,7 +65,7 @@ __device__ __forceinline__ float block_scale(const DqParams& p, int64_t blk) {
     const uint32_t q = __ldg(p.absmax8 + blk);
     const float c2 = __ldg(p.code2 + q);
     const float a2 = __ldg(p.absmax2 + (blk >> p.log2_bs2));
-    return __fadd_rn(__fmul_rn(c2, a2), __ldg(p.offset));
+    return nested_scale(p.nested, c2, a2, __ldg(p.offset));
   }
   return __ldg(p.absmax32 + blk);
 }
@@ -310,7 +319,7 @@ __device__ __forceinline__ Dq3Src dq3_scale_src(const DqParams& p, int64_t chunk
 }
 
 __device__ __forceinline__ float dq3_scale(const DqParams& p, uint32_t q, float a, float off) {
-  return p.nested ? __fadd_rn(__fmul_rn(__ldg(p.code2 + q), a), off) : a;
+  return p.nested ? nested_scale(p.nested, __ldg(p.code2 + q), a, off) : a;
 }
 
 // TWO: blocksize 32 (two blocks, two tables per chunk); otherwise every job of the launch has
@@ -540,6 +549,7 @@ static int check_qstate(const nf4b_qstate* qs, int32_t* log2_bs, int32_t* log2_b
   NF4B_RETURN_IF(lb < 5 || lb > 8, NF4B_ERR_UNSUPPORTED);  // 32, 64, 128, 256 (nf4.py:66)
   *log2_bs = lb;
   *log2_bs2 = 0;
+  NF4B_RETURN_IF(qs->nested < 0 || qs->nested > 2, NF4B_ERR_INVALID_ARG);
   if (qs->nested) {
     NF4B_RETURN_IF(!qs->absmax8 || !qs->code2 || !qs->absmax2 || !qs->offset,
                    NF4B_ERR_INVALID_ARG);
@@ -560,7 +570,7 @@ static int make_params(const uint8_t* packed, const nf4b_qstate* qs, void* out, 
     const int lb = ilog2_exact(qs->blocksize);
     NF4B_RETURN_IF(lb < 5 || lb > 8, NF4B_ERR_UNSUPPORTED);
     *p = DqParams{packed, out, nullptr, nullptr, nullptr, nullptr, nullptr, qs->code, 0, lb, 8,
-                  qs->nested ? 1 : 0, out_dtype == NF4B_F32};
+                  qs->nested, out_dtype == NF4B_F32};
     return NF4B_OK;
   }
   NF4B_RETURN_IF(packed == nullptr || out == nullptr, NF4B_ERR_INVALID_ARG);
@@ -569,7 +579,7 @@ static int make_params(const uint8_t* packed, const nf4b_qstate* qs, void* out, 
   if (st != NF4B_OK) return st;
   NF4B_RETURN_IF(numel % qs->blocksize != 0, NF4B_ERR_UNSUPPORTED);  // nf4.py:69
   *p = DqParams{packed, out, qs->absmax8, qs->absmax32, qs->code2, qs->absmax2, qs->offset,
-                qs->code, numel >> 3, lb, lb2, qs->nested ? 1 : 0, out_dtype == NF4B_F32};
+                qs->code, numel >> 3, lb, lb2, qs->nested, out_dtype == NF4B_F32};
   return NF4B_OK;
 }
 

@@ -1476,6 +1476,9 @@ static int gemm_common_checks(const void* act, const uint8_t* packed, const nf4b
                  NF4B_ERR_UNSUPPORTED);
   const int lb = ilog2_exact(qs->blocksize);
   NF4B_RETURN_IF(lb < 5 || lb > 8, NF4B_ERR_UNSUPPORTED);
+  // nested == 2 (the unpack's contracted-scale debug form) has no fused-GEMM counterpart
+  NF4B_RETURN_IF(qs->nested < 0 || qs->nested > 2, NF4B_ERR_INVALID_ARG);
+  NF4B_RETURN_IF(qs->nested == 2, NF4B_ERR_UNSUPPORTED);
   if (qs->nested) {
     NF4B_RETURN_IF(!qs->absmax8 || !qs->code2 || !qs->absmax2 || !qs->offset, NF4B_ERR_INVALID_ARG);
     NF4B_RETURN_IF(qs->blocksize2 != 256, NF4B_ERR_UNSUPPORTED);

@@ -120,14 +120,23 @@ def _qstate(st, device) -> QStateC:
     return c
 
 
-def dequantize_nf4(A: torch.Tensor, st) -> torch.Tensor:
-    """Unpacked weight of shape st.shape and dtype st.dtype (callers check _supported)."""
+def dequantize_nf4(A: torch.Tensor, st, *, fma_scale: bool = False) -> torch.Tensor:
+    """Unpacked weight of shape st.shape and dtype st.dtype (callers check _supported).
+
+    fma_scale: compute a nested state's block scale as one fused multiply-add,
+    fmaf(code2[q], absmax2, offset) rounded once, instead of the multiply then the add
+    (nf4.py:36-39) -- the contracted form a GPU build of the reference may emit, which its
+    test tolerates (solution/test_nf4_unpack.py:29-30).  A debug form for diffing against
+    such a build; no effect on plain states."""
     flat = A.reshape(-1)
     out = torch.empty(st.shape, dtype=st.dtype, device=A.device)
     if out.numel() == 0:
         return out
     with torch.cuda.device(A.device):
         qs = _qstate(st, A.device)
+        if fma_scale and qs.nested:
+            qs = QStateC.from_buffer_copy(qs)
+            qs.nested = 2
         dt = _lib.NF4B_F16 if st.dtype == torch.float16 else _lib.NF4B_F32
         _lib.check(_lib.lib().nf4b_dequant(flat.data_ptr(), ctypes.byref(qs), out.data_ptr(), dt,
                                            out.numel(), _stream(A.device)), "nf4b_dequant")

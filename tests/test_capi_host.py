@@ -66,6 +66,15 @@ def test_host_validation_rejects_before_launch():
     qs.blocksize2 = 256
     assert L.nf4b_dequant(ctypes.c_void_p(16), ctypes.byref(qs), ctypes.c_void_p(16), 0, 64, None) == \
         _lib.NF4B_ERR_INVALID_ARG  # nested without absmax8/code2/absmax2/offset
+    # nested outside {0, 1, 2}; the contracted-scale form (2) has no fused-GEMM counterpart
+    qs.nested = 3
+    assert L.nf4b_dequant(ctypes.c_void_p(16), ctypes.byref(qs), ctypes.c_void_p(16), 0, 64, None) == \
+        _lib.NF4B_ERR_INVALID_ARG
+    qs.nested = 2
+    qs.absmax8 = qs.code2 = qs.absmax2 = qs.offset = 16
+    assert L.nf4b_linear_fwd(ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.byref(qs), None, None,
+                             ctypes.c_void_p(16), 4, 64, 64, None) == _lib.NF4B_ERR_UNSUPPORTED
+    qs.absmax8 = qs.code2 = qs.absmax2 = qs.offset = None
     # GEMM: K or N not a multiple of 64 -> unsupported, nothing launched
     qs.nested = 0
     assert L.nf4b_linear_fwd(ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.byref(qs), None, None,

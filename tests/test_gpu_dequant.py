@@ -57,6 +57,32 @@ def test_dequant_bit_exact_qwen_shapes(cuda_lib, nested, shape, blocksize):
     assert np.array_equal(_bits(out.cpu().numpy()), _bits(ref))
 
 
+@pytest.mark.parametrize("blocksize", [32, 64, 128])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_contracted_scale_variant_against_oracle(cuda_lib, blocksize, dtype):
+    """fma_scale (nf4b_qstate.nested == 2): the nested scale as one fused multiply-add, the form
+    a GPU build of nf4.py:36-39 may take -- bit-exact against the oracle's restatement of it
+    on the bulk-copy path (fp16; blocksize 32 in its two-table variant) and the general path
+    (fp32).  The default stays the two-rounding form, and in fp16 the two differ in fewer than
+    1e-4 of the outputs, the mismatch fraction solution/test_nf4_unpack.py:29-30 allows."""
+    from stew_b200 import dequantize_nf4, quantize_4bit
+    g = torch.Generator(device="cuda").manual_seed(11)
+    W = (torch.randn(1536, 1536, generator=g, device="cuda") * 0.02).to(dtype)
+    q, st = quantize_4bit(W, blocksize=blocksize, compress_statistics=True)
+    ost = to_oracle_state(st, q)
+    assert np.any(O.block_scales(ost) != O.block_scales(ost, fma=True))  # the variant matters here
+    packed = q.cpu().numpy()
+    fused = dequantize_nf4(q, st, fma_scale=True).cpu().numpy()
+    plain = dequantize_nf4(q, st).cpu().numpy()
+    assert np.array_equal(_bits(fused), _bits(O.dequant_nf4(packed, ost, fma=True)))
+    assert np.array_equal(_bits(plain), _bits(O.dequant_nf4(packed, ost)))
+    if dtype == torch.float16:  # fp32 outputs keep the scale's last bit
+        assert np.mean(_bits(fused) != _bits(plain)) < 1e-4
+    # plain (not nested) states have no offset to contract: the option changes nothing
+    q2, st2 = quantize_4bit(W, blocksize=blocksize, compress_statistics=False)
+    assert torch.equal(dequantize_nf4(q2, st2, fma_scale=True), dequantize_nf4(q2, st2))
+
+
 def test_dequant_transposed_view(cuda_lib):
     """test_nf4_unpack.py:34-42: a (1, n) view of the packed tensor unpacks identically."""
     from stew_b200 import dequantize_nf4, quantize_4bit
