@@ -205,7 +205,8 @@ constexpr int DQ3_THREADS = 32 * DQ3_WARPS;
 constexpr int DQ3_IN = 2;    // packed slots per warp, 1 KB each
 constexpr int DQ3_OUT = 2;   // output stages per warp, 4 KB each
 constexpr int DQ3_WARP_BYTES = DQ3_OUT * 4096 + DQ3_IN * 1024;
-constexpr int DQ3_SMEM = DQ3_WARPS * DQ3_WARP_BYTES + DQ3_WARPS * DQ3_IN * 8;
+constexpr int DQ3_RING = 8;  // tickets a warp's producer may hold ahead (dynamic walk)
+constexpr int DQ3_SMEM = DQ3_WARPS * DQ3_WARP_BYTES + DQ3_WARPS * DQ3_IN * 8 + DQ3_WARPS * DQ3_RING * 4;
 // Resident CTAs per SM: 5 (20 warps; 5 x 41 KB of shared memory, <= 102 registers a thread)
 // for blocksizes >= 64, 4 for plans with blocksize 32 (two tables per chunk need more
 // registers).
@@ -327,48 +328,79 @@ __device__ __forceinline__ float dq3_scale(const DqParams& p, uint32_t q, float 
 template <bool TWO>
 __global__ void __launch_bounds__(DQ3_THREADS, dq3_ctas_per_sm<TWO>())
     nf4_dequant_tma_kernel(const DqParams* __restrict__ params, const int64_t* __restrict__ iter_start,
-                           int32_t n_jobs, const __grid_constant__ DqParams single) {
+                           int32_t n_jobs, uint32_t* __restrict__ work,
+                           const __grid_constant__ DqParams single) {
   extern __shared__ __align__(128) uint8_t dq3_smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t out_s = smem_u32(dq3_smem + warp * DQ3_WARP_BYTES);
   const uint32_t in_s = out_s + DQ3_OUT * 4096;
   uint64_t* bars = reinterpret_cast<uint64_t*>(dq3_smem + DQ3_WARPS * DQ3_WARP_BYTES) + warp * DQ3_IN;
+  volatile int32_t* ring = reinterpret_cast<volatile int32_t*>(
+                               dq3_smem + DQ3_WARPS * DQ3_WARP_BYTES + DQ3_WARPS * DQ3_IN * 8) +
+                           warp * DQ3_RING;
   const Dq3Jobs J{n_jobs > 0 ? params : &single, n_jobs > 0 ? iter_start : nullptr, n_jobs > 0 ? n_jobs : 1};
   const int64_t total = J.start ? J.lo(J.n) : J.hi(0);
-  // Blocked-cyclic walk: rounds in which every warp takes a run of DQ3_RUN consecutive
-  // iterations, so at any time the grid works inside one window of the sweep (DRAM pages are
-  // shared) and a warp's iterations still come in runs (few job changes, scale prefetch).  What
-  // is left after the whole rounds is dealt in one last round of shorter runs (ceil(rest /
-  // warps) each), so no warp is left running a whole run alone at the end.
   const int64_t nw = int64_t(gridDim.x) * DQ3_WARPS;
   const int64_t wid = int64_t(blockIdx.x) * DQ3_WARPS + warp;
   constexpr int64_t bl = DQ3_RUN;
   const uint64_t pol = l2_evict_first();
+  // Static walk (a launch without a work counter): blocked-cyclic rounds in which every warp
+  // takes a run of DQ3_RUN consecutive iterations, so at any time the grid works inside one
+  // window of the sweep (DRAM pages are shared) and a warp's iterations still come in runs (few
+  // job changes, scale prefetch); what is left after the whole rounds is dealt in one last
+  // round of shorter runs (ceil(rest / warps) each).  -1 ends a warp's walk.
   const int64_t rounds = total / (nw * bl);
   const int64_t tail0 = rounds * nw * bl;            // first iteration of the last round
   const int64_t bl2 = (total - tail0 + nw - 1) / nw;  // run length of the last round
   const int64_t t0 = tail0 + wid * bl2;               // this warp's run in the last round
   const int64_t t1 = min64(t0 + bl2, total);
-  auto next_it = [&](int64_t it) -> int64_t {
-    if (it >= tail0) return it + 1 < t1 ? it + 1 : total;
+  auto next_static = [&](int64_t it) -> int64_t {
+    if (it >= tail0) return it + 1 < t1 ? it + 1 : -1;
     if ((it + 1) % bl) return it + 1;
     const int64_t nx = it + 1 + (nw - 1) * bl;
-    return nx < tail0 ? nx : (t0 < t1 ? t0 : total);
+    return nx < tail0 ? nx : (t0 < t1 ? t0 : -1);
   };
-  const int64_t r0 = rounds > 0 ? wid * bl : (t0 < t1 ? t0 : total);
-  if (r0 >= total) return;  // nothing issued yet
+  // Dynamic walk (a batched plan's work counter): a warp takes the next ticket when it needs
+  // one -- runs of DQ3_RUN iterations in sweep order, then single iterations for the last
+  // ~2 per warp -- so warps that the SM's scheduler favours take more of the work instead of
+  // finishing early and leaving the last CTAs of every SM to run alone.  Lane 0 (the producer,
+  // which runs DQ3_IN iterations ahead) takes the tickets and keeps them in a per-warp ring in
+  // shared memory, where the consumer lanes read them after a __syncwarp.
+  const int64_t tail_n = min64(total, 2 * nw);
+  const int64_t n_runs = (total - tail_n) / bl;
+  const int64_t dyn0 = n_runs * bl;                   // first single-iteration ticket
+  const int64_t n_tickets = n_runs + (total - dyn0);
+  auto t_lo = [&](int32_t t) -> int64_t { return t < n_runs ? int64_t(t) * bl : dyn0 + (t - n_runs); };
+  auto t_hi = [&](int32_t t) -> int64_t { return t < n_runs ? int64_t(t) * bl + bl : dyn0 + (t - n_runs) + 1; };
+  auto grab = [&]() -> int32_t {  // lane 0
+    const uint32_t t = atomicAdd(work, 1u);
+    return int64_t(t) < n_tickets ? int32_t(t) : -1;
+  };
+
   if (lane == 0) {
     for (int i = 0; i < DQ3_IN; ++i) mbar_init(&bars[i], 1);
     fence_barrier_init();
+    if (work != nullptr) ring[0] = grab();
   }
   __syncwarp();
+  // the warp's first iteration (-1: none) -- both cursors start there
+  int64_t first;
+  if (work != nullptr) {
+    const int32_t t = ring[0];
+    first = t >= 0 ? t_lo(t) : -1;
+  } else {
+    first = rounds > 0 ? wid * bl : (t0 < t1 ? t0 : -1);
+  }
 
-  // producer cursor (lane 0): the next iteration to load and its job
-  int64_t pit = r0;
-  int pj = J.find(r0);
+  // producer cursor (lane 0): the next iteration to load (-1: none), its ticket's end and ring
+  // position, and its job
+  int64_t pit = first, pend = (work != nullptr && first >= 0) ? t_hi(ring[0]) : 0;
+  uint32_t pr = 0;
+  int pj = first >= 0 ? J.find(first) : 0;
   int64_t plo = J.lo(pj), phi = J.hi(pj);
-  auto issue = [&](int64_t k) {  // loads the warp's k-th iteration (k issued in order) into slot k % DQ3_IN
+  int64_t issued = 0;
+  auto issue = [&]() {  // lane 0: loads iteration pit into slot issued % DQ3_IN, then advances
     while (pit >= phi) {
       ++pj;
       plo = phi;
@@ -378,20 +410,37 @@ __global__ void __launch_bounds__(DQ3_THREADS, dq3_ctas_per_sm<TWO>())
     const int64_t nch = J.params[pj].nwords >> 3;
     const int64_t li = pit - plo;
     const uint32_t bytes = uint32_t(min64(DQ_CHUNKS_PER_ITER, nch - li * DQ_CHUNKS_PER_ITER)) * 32u;
-    const int s = int(k % DQ3_IN);
+    const int s = int(issued % DQ3_IN);
     mbar_arrive_expect_tx(&bars[s], bytes);
     bulk_load_1d(in_s + uint32_t(s) * 1024u, packed + li * 1024, bytes, smem_u32(&bars[s]), pol);
-    pit = next_it(pit);
+    ++issued;
+    if (work == nullptr) {
+      pit = next_static(pit);
+    } else if (++pit == pend) {
+      const int32_t t = grab();
+      ring[++pr & (DQ3_RING - 1)] = t;
+      pit = t >= 0 ? t_lo(t) : -1;
+      pend = t >= 0 ? t_hi(t) : 0;
+    }
   };
-  // the warp's iteration count
-  const int64_t cnt = rounds * bl + (t0 < t1 ? t1 - t0 : 0);
   if (lane == 0)
-    for (int64_t k = 0; k < cnt && k < DQ3_IN; ++k) issue(k);
+    while (issued < DQ3_IN && pit >= 0) issue();
+  __syncwarp();
   // run-time 1 << 16 and 1 << 31 for the decode's multiply-high shifts (nf4_decode.cuh)
   const uint32_t k16 = 1u << (16 + (n_jobs < 0));
   const uint32_t k31 = k16 << 15;
 
-  // consumer cursor (all lanes, warp-uniform)
+  // consumer cursor (all lanes, warp-uniform): the iteration, its ticket's end and ring position
+  int64_t it = first;
+  int64_t cend = pend;
+  uint32_t cr = 0;
+  if (work != nullptr && first >= 0) cend = t_hi(ring[0]);
+  auto peek = [&](int64_t i) -> int64_t {  // the iteration after i in this warp's walk
+    if (work == nullptr) return next_static(i);
+    if (i + 1 < cend) return i + 1;
+    const int32_t t = ring[(cr + 1) & (DQ3_RING - 1)];
+    return t >= 0 ? t_lo(t) : -1;
+  };
   int cj = -1;
   int64_t clo = 0, chi = 0;
   DqParams p;
@@ -403,8 +452,7 @@ __global__ void __launch_bounds__(DQ3_THREADS, dq3_ctas_per_sm<TWO>())
   bool ok = true;
   int s = 0;          // slot of iteration k (k % DQ3_IN) and the phase of its barrier
   uint32_t ph = 0;
-  int64_t it = r0;
-  for (; k < cnt; ++k, it = next_it(it)) {
+  for (; it >= 0; ++k) {
     if (it >= chi) {
       cj = (cj < 0) ? J.find(it) : cj + 1;
       while (J.hi(cj) <= it) ++cj;
@@ -422,8 +470,8 @@ __global__ void __launch_bounds__(DQ3_THREADS, dq3_ctas_per_sm<TWO>())
     const bool valid = lane < nvalid;
     const Dq3Src cur = have_pre ? pre : dq3_scale_src<TWO>(p, ch, valid);
     // the next iteration's scale sources, while it belongs to the same job
-    const int64_t it1 = next_it(it);
-    have_pre = it1 < chi && k + 1 < cnt;
+    const int64_t it1 = peek(it);
+    have_pre = it1 >= 0 && it1 < chi;
     if (have_pre) {
       const int64_t li1 = it1 - clo;
       const int nv1 = int(min64(DQ_CHUNKS_PER_ITER, nch - li1 * DQ_CHUNKS_PER_ITER));
@@ -467,17 +515,26 @@ __global__ void __launch_bounds__(DQ3_THREADS, dq3_ctas_per_sm<TWO>())
     __syncwarp();
     if (lane == 0) {
       bulk_store_1d(static_cast<uint8_t*>(p.out) + li * 4096, stage, uint32_t(nvalid) * 128u, pol);
-      // slot s has been read by every lane: refill it with the iteration DQ3_IN ahead
-      if (k + DQ3_IN < cnt) issue(k + DQ3_IN);
+      // slot s has been read by every lane: refill it with the walk's next unloaded iteration
+      if (pit >= 0) issue();
     }
     if (++s == DQ3_IN) {
       s = 0;
       ph ^= 1u;
     }
+    // advance the consumer cursor (a new ticket's ring entry was written when the producer
+    // loaded the iteration before it, at least one __syncwarp ago)
+    if (work == nullptr) {
+      it = next_static(it);
+    } else if (++it == cend) {
+      const int32_t t = ring[++cr & (DQ3_RING - 1)];
+      it = t >= 0 ? t_lo(t) : -1;
+      cend = t >= 0 ? t_hi(t) : 0;
+    }
   }
   if (!ok && lane == 0) {
     // loads still in flight land in this warp's slots: wait for them (bounded) before leaving
-    for (int64_t j = k; j < cnt && j < k + DQ3_IN; ++j) {
+    for (int64_t j = k; j < issued; ++j) {
       if (!dq3_wait(&bars[s], ph)) break;
       if (++s == DQ3_IN) {
         s = 0;
@@ -487,6 +544,15 @@ __global__ void __launch_bounds__(DQ3_THREADS, dq3_ctas_per_sm<TWO>())
   }
   if (lane == 0) bulk_wait_all();
   __syncwarp();
+  if (work != nullptr && lane == 0) {
+    // the last warp of the launch leaves the plan's work counter at zero for its next launch
+    __threadfence();
+    if (atomicAdd(work + 1, 1u) == uint32_t(nw) - 1u) {
+      work[0] = 0u;
+      work[1] = 0u;
+      __threadfence();
+    }
+  }
 }
 
 static int sm_count() {
@@ -633,9 +699,9 @@ extern "C" int nf4b_dequant(const uint8_t* packed, const nf4b_qstate* qs, void* 
     const bool two = p.log2_bs == 5;
     const unsigned grid = unsigned(dq3_grid(dq3_iters(p), two));
     if (two)
-      nf4_dequant_tma_kernel<true><<<grid, DQ3_THREADS, DQ3_SMEM, s>>>(nullptr, nullptr, 0, p);
+      nf4_dequant_tma_kernel<true><<<grid, DQ3_THREADS, DQ3_SMEM, s>>>(nullptr, nullptr, 0, nullptr, p);
     else
-      nf4_dequant_tma_kernel<false><<<grid, DQ3_THREADS, DQ3_SMEM, s>>>(nullptr, nullptr, 0, p);
+      nf4_dequant_tma_kernel<false><<<grid, DQ3_THREADS, DQ3_SMEM, s>>>(nullptr, nullptr, 0, nullptr, p);
     return launch_status("nf4_dequant_tma_kernel launch");
   }
   const int64_t ctas = (p.nwords + DQ_WORDS_PER_CTA - 1) / DQ_WORDS_PER_CTA;
@@ -648,9 +714,15 @@ extern "C" int nf4b_dequant(const uint8_t* packed, const nf4b_qstate* qs, void* 
   return launch_status();
 }
 
+// Plan layout: the jobs' parameters, the prefix sums of their iterations (n_jobs + 1), then
+// the launch's work counter (next ticket, finished warps; zero between launches).
+static int64_t plan_work_offset(int32_t n_jobs) {
+  return int64_t(n_jobs) * int64_t(sizeof(DqParams)) + int64_t(n_jobs + 1) * 8;
+}
+
 extern "C" int64_t nf4b_dequant_plan_bytes(int32_t n_jobs) {
   if (n_jobs <= 0) return 0;
-  return int64_t(n_jobs) * int64_t(sizeof(DqParams)) + int64_t(n_jobs + 1) * 8;
+  return plan_work_offset(n_jobs) + 16;
 }
 
 extern "C" int nf4b_dequant_plan(const nf4b_dequant_job* jobs, int32_t n_jobs, void* plan_dev,
@@ -673,6 +745,7 @@ extern "C" int nf4b_dequant_plan(const nf4b_dequant_job* jobs, int32_t n_jobs, v
     total += dq3_iters(params[i]);
   }
   starts[n_jobs] = total;
+  NF4B_RETURN_IF(total > 0x7FFFFFFFll, NF4B_ERR_UNSUPPORTED);  // tickets are 32-bit
   // the launch descriptor: CTA count, and bit 32 for the blocksize-32 variant
   bool two = false;
   for (int i = 0; i < n_jobs; ++i) two = two || (params[i].nwords > 0 && params[i].log2_bs == 5);
@@ -698,12 +771,14 @@ extern "C" int nf4b_dequant_batched(const void* plan_dev, int32_t n_jobs, int64_
       static_cast<const uint8_t*>(plan_dev) + size_t(n_jobs) * sizeof(DqParams));
   st = dq3_smem_attr();
   if (st != NF4B_OK) return st;
+  uint32_t* work = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(const_cast<void*>(plan_dev)) +
+                                               plan_work_offset(n_jobs));
   DqParams none{};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (two)
-    nf4_dequant_tma_kernel<true><<<unsigned(n_ctas), DQ3_THREADS, DQ3_SMEM, s>>>(params, starts, n_jobs, none);
+    nf4_dequant_tma_kernel<true><<<unsigned(n_ctas), DQ3_THREADS, DQ3_SMEM, s>>>(params, starts, n_jobs, work, none);
   else
-    nf4_dequant_tma_kernel<false><<<unsigned(n_ctas), DQ3_THREADS, DQ3_SMEM, s>>>(params, starts, n_jobs, none);
+    nf4_dequant_tma_kernel<false><<<unsigned(n_ctas), DQ3_THREADS, DQ3_SMEM, s>>>(params, starts, n_jobs, work, none);
   return launch_status("nf4_dequant_tma_kernel launch");
 }
 
