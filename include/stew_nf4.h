@@ -92,7 +92,10 @@ int64_t nf4b_dequant_plan_bytes(int32_t n_jobs);
  * `plan_dev` (nf4b_dequant_plan_bytes(n_jobs) bytes of 16-byte aligned device memory owned
  * by the caller) with one cudaMemcpyAsync on `stream`, and returns the launch descriptor in
  * *launch (the CTA count in the low 32 bits, the kernel variant above them): pass it to
- * nf4b_dequant_batched unchanged.  The plan stays valid while the buffers it names do.  */
+ * nf4b_dequant_batched unchanged.  The plan stays valid while the buffers it names do.
+ * The plan also holds its launch's work counter (left zero by every launch), so launches of
+ * one plan must not overlap: issue them on one stream.  At most 2^31 - 1 iterations of 2,048
+ * values (NF4B_ERR_UNSUPPORTED beyond).  */
 int nf4b_dequant_plan(const nf4b_dequant_job* jobs, int32_t n_jobs, void* plan_dev,
                       int64_t* launch, void* stream);
 
