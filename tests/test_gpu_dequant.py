@@ -147,6 +147,31 @@ def test_batched_sweep_equals_single_calls(cuda_lib):
         assert torch.equal(o, dequantize_nf4(q, st))
 
 
+def test_plan_work_counter_is_reset_between_launches(cuda_lib):
+    """Batched launches take their work from a counter held in the plan, which the last warp
+    of each launch sets back to zero: the same plan launched again and again, and two plans
+    launched in turn on one stream, give the single-call outputs every time."""
+    from stew_b200 import _lib, dequantize_nf4, quantize_4bit
+    from stew_b200.sweep import DequantSweep
+    sets = []
+    for base, shapes in ((0, [(1536, 1536), (256, 1536), (8960, 1536)]), (10, [(1536, 8960), (100, 64)])):
+        ws = []
+        for i, s in enumerate(shapes):
+            g = torch.Generator(device="cuda").manual_seed(base + i)
+            ws.append(quantize_4bit((torch.randn(s, generator=g, device="cuda") * 0.02).half(),
+                                    blocksize=64, compress_statistics=(i % 2 == 0)))
+        sets.append((ws, DequantSweep(ws), [dequantize_nf4(q, st) for q, st in ws]))
+    for rep in range(3):
+        for ws, sweep, want in sets:
+            for o in sweep.outputs:  # a launch that did no work would leave the zeros
+                o.zero_()
+            outs = sweep.run()
+            for o, w in zip(outs, want):
+                assert torch.equal(o, w), rep
+    torch.cuda.synchronize()
+    assert _lib.dequant_error_flag(reset=True) == 0
+
+
 def test_whole_model_sweep_properties(cuda_lib):
     """Full config-1 size (28 layers x 7 projections, 1.31 B weights): batched sweep ==
     single calls (digest of digests), and random blocks of every matrix bit-exact against
