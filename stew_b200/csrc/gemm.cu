@@ -659,12 +659,12 @@ __global__ void __launch_bounds__(G_THREADS, 1)
    const bool epi = warp >= G_EPI_WARP0;
    if (!epi || g.epi_decode) {
     // ------------------------------------------------------------ decode warps
-    // Two groups of four warps (warps 2-5, 6-9); group g decodes the stages whose global index
+    // Two groups of four warps (below); group g decodes the stages whose global index
     // is g modulo the group count (so every ring slot has one owner), each thread one whole
     // 64-value block row per stage: one scale and one 16-entry table per 64 values.  In a
     // backward launch where every CTA has at most one work unit (`epi_decode`), the epilogue
     // warps have nothing to do until that unit's accumulator is ready, so they decode as groups
-    // 2 and 3 (warps 10-13, 14-17) first: each group then has four stage-times for its stage,
+    // 2 and 3 first: each group then has four stage-times for its stage,
     // which hides the lag of the decode warp that shares the MMA issuer's SM sub-partition.
     //  forward : row d of the K-major tile = weight row m0 + d, K columns 64 kl .. +63 of the
     //            stage; packed row d of the stage is 32 B in the 32B swizzle (16-byte chunk c
@@ -673,7 +673,12 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     //            64 j .. +63 with j = d >> 6 (one 128-byte row of M chunk j); packed row r has
     //            64 B in the 64B swizzle (16-byte chunk c at c ^ ((r >> 1) & 3)), the thread's
     //            two chunks are 2j and 2j + 1.
-    const int dq = threadIdx.x - 32 * (epi ? G_EPI_WARP0 : G_DQ_WARP0);  // 0..255
+    // Each group takes the two oldest and the two youngest warps of its role (decode: warps
+    // 2, 3, 8, 9 and 4-7; epilogue: 10, 11, 16, 17 and 12-15), one on every SM sub-partition
+    // either way.  A sub-partition's scheduler favours its older warps, so with warps 2-5 and
+    // 6-9 one group decoded every stage behind the other.
+    const int wrel = warp - (epi ? G_EPI_WARP0 : G_DQ_WARP0);  // 0..7
+    const int dq = (((((wrel + 2) >> 2) & 1) << 2) + ((wrel + 2) & 3)) * 32 + lane;  // 0..255
     const int ngrp = g.epi_decode ? 4 : 2;
     const int grp = (dq >> 7) + (epi ? 2 : 0);
     const int d = dq & 127;
