@@ -76,12 +76,19 @@ struct Smem {
   static constexpr int CODE = LB + LB_BYTES;         // per weight: 16 fp32 NF4 code
   static constexpr int CODE2 = CODE + 64 * G_MAX_W;  // per weight: 256 fp32 second-level code
   static constexpr int BAR = CODE2 + 1024 * G_MAX_W;
-  // full[S], afull[S], empty[S], acc_full[2], acc_empty[2], lora_full, lora_empty, mma_done
-  static constexpr int NUM_BARS = 3 * STAGES + 7;
+  // full[S], afull[S], empty[S], acc_full[2], acc_empty[2], lora_full, lora_empty, mma_done,
+  // red_full[2] (split-K partials staged into the idle ring, RED_* below)
+  static constexpr int NUM_BARS = 3 * STAGES + 9;
   static constexpr int MISC = BAR + NUM_BARS * 8;
   static constexpr int WU0 = MISC + 16;  // the CTA's first work unit, computed in the prologue
   static constexpr int TOTAL = WU0 + 64;
   static constexpr int ALLOC = TOTAL + 1024;  // slack to align the base to 1024 B
+  // Split-K reduction of a CTA's last work unit: the activation and decoded-weight stages
+  // (contiguous from offset 0) are idle once that unit's accumulator is complete, and hold
+  // two rounds x RED_PARTS slices of 64 tokens x 128 rows fp32 (32 KB) of the other ranges'
+  // partial tiles.
+  static constexpr int RED_SLICE = 64 * G_M * 4;
+  static constexpr int RED_PARTS = (X + STAGES * (X_BYTES + A_BYTES)) / (2 * RED_SLICE);
 };
 static_assert(Smem<false>::ALLOC <= 232448 && Smem<true>::ALLOC <= 232448, "shared memory budget");
 
@@ -138,6 +145,8 @@ struct GemmArgs {
   int32_t epi_decode;     // a backward launch whose CTAs (pairs) have at most one work unit: the
                           // epilogue warps decode stages too until their accumulator is ready
   __half* glu_out;        // SwiGLU launches: m = fp16(gate * sigmoid(gate) * up) [n, out]
+  int32_t red_staged;     // split-K: the last range of a tile reads the other ranges' partials
+                          // through bulk copies into the idle ring (its CTA's last unit only)
   // SwiGLU-backward launches (dX of down): the forward's gate and up [n, in], and the outputs
   // dgate, dup [n, in] written instead of dX
   const __half* glu_g;
@@ -352,6 +361,20 @@ __device__ __forceinline__ bool wait_count(const int32_t* p, int want) {
   }
 }
 
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from global memory
+// into this CTA's shared memory, completing on mbarrier `bar` (no multicast).
+__device__ __forceinline__ void bulk_load_g2s(uint32_t smem_dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+// Orders this thread's earlier generic-proxy accesses of global memory (here: an acquire of
+// the partial tiles' arrival count) before its later async-proxy ones (the bulk copies).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // SPLIT: compiled with the split-K epilogue (launches with g.splits > 1).
 // PAIR: launched as 2-CTA clusters; CTA rank 0 issues cta_group::2 MMAs over both CTAs' tiles.
 // GLU, forward: the SwiGLU forward of an MLP: gate and up in one tile, epilogue writes gate, up
@@ -386,6 +409,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   uint64_t* lora_full = acc_empty + 2;
   uint64_t* lora_empty = lora_full + 1;
   uint64_t* mma_done = lora_empty + 1;
+  uint64_t* red_full = mma_done + 1;      // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC + 4);
   float* s_code = reinterpret_cast<float*>(smem + L::CODE);
@@ -434,6 +458,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     mbar_init(lora_full, kPeers * G_DQ_WARPS);
     mbar_init(lora_empty, 1);
     mbar_init(mma_done, 1);
+    mbar_init(&red_full[0], 1);
+    mbar_init(&red_full[1], 1);
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tma_desc(&tm_act0);
@@ -914,7 +940,31 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       }
       // partial tiles are column-major [tokens][128 rows]: for one token the 32 lanes of a
       // warp (32 consecutive rows) touch one 128-byte line
-      const float* part0 = g.ws_part + int64_t(ctile) * (nparts + 1) * (G_M * ACC_T) + prow;
+      const float* tile_part = g.ws_part + int64_t(ctile) * (nparts + 1) * (G_M * ACC_T);
+      const float* part0 = tile_part + prow;
+      // The last range of a tile on its CTA's last unit reads the other ranges' partials
+      // through bulk copies into the ring, which that unit's completed accumulator leaves idle
+      // (every stage it loaded or decoded has been consumed by its MMAs): rounds of 64 tokens,
+      // two rounds in flight, each round one 32 KB slice [64 tokens][128 rows] per range.
+      // Per-thread L2 loads of the same slices are bound by their latency (the bytes one
+      // thread can keep in flight); the bulk copies are not.
+      const bool staged = SPLIT && g.red_staged != 0 && ticket == nparts && nparts >= 1 &&
+                          nparts <= L::RED_PARTS && u + ustride >= nunits;
+      const int nrounds = staged ? (tc.tn + 63) >> 6 : 0;
+      int red_issued = 0;  // rounds the leader has issued
+      auto issue_round = [&](int r) {
+        ++red_issued;
+        const int bsl = r & 1;
+        mbar_arrive_expect_tx(&red_full[bsl], uint32_t(nparts) * uint32_t(L::RED_SLICE));
+        int j = 0;
+        for (int sp = 0; sp <= nparts; ++sp) {
+          if (sp == wu.split) continue;
+          bulk_load_g2s(sbase + uint32_t((L::RED_PARTS * bsl + j) * L::RED_SLICE),
+                        tile_part + int64_t(sp) * (G_M * ACC_T) + int64_t(64 * r) * G_M,
+                        uint32_t(L::RED_SLICE), smem_u32(&red_full[bsl]));
+          ++j;
+        }
+      };
       if (ticket < 0) {
         if (leader) atomicExch(&g_gemm_error, 4);
       } else if (ticket < nparts) {
@@ -932,10 +982,18 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       } else {
         if (split) {
           if (leader) {
-            if (!wait_count(g.ws_cnt + G_SPLIT_MAX_TILES + ctile, nparts)) *abort_flag = 1;
+            const bool arrived = wait_count(g.ws_cnt + G_SPLIT_MAX_TILES + ctile, nparts);
+            if (!arrived) *abort_flag = 1;
             g.ws_cnt[ctile] = 0;  // every range of the tile has arrived: reset for reuse
             g.ws_cnt[G_SPLIT_MAX_TILES + ctile] = 0;
             __threadfence();
+            if (staged && arrived) {
+              // the partials were published by other CTAs' generic stores and the count's
+              // acquire; the bulk copies read them through the async proxy
+              fence_proxy_async_global();
+              issue_round(0);
+              if (nrounds > 1) issue_round(1);
+            }
           }
           epi_bar_sync();
         }
@@ -1060,7 +1118,24 @@ __global__ void __launch_bounds__(G_THREADS, 1)
               break;
             }
           }
-          for (int c0 = cb + 32 * grp; c0 < ce; c0 += 64) {
+          // staged: every epilogue thread takes every round (they meet at a named barrier per
+          // round), a group whose chunk c0 lies past the tile only waits
+          for (int c0 = cb + 32 * grp, r = 0; staged ? r < nrounds : c0 < ce; c0 += 64, ++r) {
+            if (staged) {
+              // every thread is past round r - 1, whose buffer the leader refills with round r + 1
+              // (generic reads of it ordered before those async-proxy writes)
+              if (r > 0) fence_proxy_async_smem();
+              const bool okr = epi_bar_and(pwait(&red_full[r & 1], uint32_t(r >> 1) & 1u));
+              if (!okr) {
+                // no bulk copy may still be landing in the ring at exit
+                if (leader)
+                  for (int rr = r; rr < red_issued; ++rr) drain_wait(&red_full[rr & 1], uint32_t(rr >> 1) & 1u);
+                fail = true;
+                break;
+              }
+              if (leader && r >= 1 && r + 1 < nrounds) issue_round(r + 1);
+              if (c0 >= ce) continue;
+            }
             uint32_t acc[32];
             if (!SPLIT) {
               tmem_ld_32x32b_x32(taddr + uint32_t(c0), acc);
@@ -1076,6 +1151,12 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                 if (sp == wu.split) {
                   tmem_ld_32x32b_x32(taddr + uint32_t(c0), v);
                   tmem_ld_wait();
+                } else if (staged) {
+                  const float* src = reinterpret_cast<const float*>(
+                                         smem + (L::RED_PARTS * (r & 1) + sp - (sp > wu.split ? 1 : 0)) * L::RED_SLICE) +
+                                     (c0 - 64 * r) * G_M + prow;
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(src[j * G_M]);
                 } else {
                   const float* src = part0 + int64_t(sp) * (G_M * ACC_T) + c0 * G_M;
 #pragma unroll
@@ -1332,6 +1413,13 @@ static int pair_mode_env() {
   return v[0] == '0' ? 0 : 1;
 }
 
+// Split-K reduction through bulk copies into the idle ring (STEW_NF4_SPLIT_STAGED: "0" reads
+// the partials with per-thread L2 loads instead; both sum in the same order, bit for bit).
+static int red_staged_env() {
+  const char* v = std::getenv("STEW_NF4_SPLIT_STAGED");
+  return (v != nullptr && v[0] == '0') ? 0 : 1;
+}
+
 // rows: the M-side rows of each weight of the launch (forward: out features of each grouped
 // weight; backward: the in features, once).  kdim: the reduction length.
 static GemmPlan plan_gemm(int64_t n, const int64_t* rows, int nrows, int64_t kdim) {
@@ -1441,6 +1529,7 @@ static int launch_gemm(const GemmPlan& p, const CUtensorMap (&ta)[G_MAX_W], cons
   const unsigned grid = unsigned(q.pair ? 2 * slots : slots);
   // backward launches with one unit per CTA (pair) at most (forward ones measured no faster)
   g.epi_decode = (BWD && units <= q.slots) ? 1 : 0;
+  g.red_staged = red_staged_env();
   const bool split = q.splits > 1;
   const bool multi = g.nw > 1 && !glu;
   int st;

@@ -286,3 +286,88 @@ def test_counters_recover_after_a_range_gives_up(cuda_lib, monkeypatch, pair):
     assert torch.equal(ys[0], ys[1])
     assert int(_counters(ws).count_nonzero()) == 0
     _flag_clear()
+
+
+# (direction, out, in, n, STEW_NF4_PAIR): the last K range of a tile reads the other ranges'
+# partials either through bulk copies into its idle ring (the default) or with per-thread L2
+# loads (STEW_NF4_SPLIT_STAGED=0).  Both add the ranges in range order, so the outputs must be
+# bit-identical.  down at 1,170 tokens (60 tiles x 2 ranges; as pairs 512-token partials, eight
+# 64-token rounds), a 3-tile shape with 4 ranges (three staged partials), gate backward at
+# 1,170 tokens on single CTAs and on pairs.
+STAGED_CASES = [("fwd", 1536, 8960, 1170, "0"), ("fwd", 384, 4096, 77, "0"), ("fwd", 1536, 8960, 1170, "1"),
+                ("bwd", 8960, 1536, 1170, "0"), ("bwd", 8960, 1536, 1170, "1")]
+
+
+@pytest.mark.parametrize("kind,out_f,in_f,n,pair", STAGED_CASES)
+def test_staged_reduction_bit_identical_to_l2_loads(cuda_lib, monkeypatch, kind, out_f, in_f, n, pair):
+    from stew_b200 import _lib
+    from stew_b200.nf4 import _qstate
+    monkeypatch.setenv("STEW_NF4_PAIR", pair)
+    L = _lib.lib()
+    bwd = kind == "bwd"
+    need = int(L.nf4b_linear_work_bytes(n, in_f, out_f, 1 if bwd else 0))
+    assert need > 0, "this shape is expected to split"
+    q, st = _weight((out_f, in_f), 3 * out_f + in_f)
+    qs = _qstate(st, q.device)
+    a = _rand(n, out_f if bwd else in_f, 5, std=0.01 if bwd else 1.0)
+    ws = _ws(need)
+    outs = {}
+    for staged in ("1", "0"):
+        monkeypatch.setenv("STEW_NF4_SPLIT_STAGED", staged)
+        o = torch.full((n, in_f if bwd else out_f), float("nan"), dtype=torch.float16, device="cuda")
+        if bwd:
+            _bwd(L, a, q, qs, None, None, o, n, in_f, out_f, ws)
+        else:
+            _fwd(L, a, q, qs, None, None, o, n, in_f, out_f, ws)
+        outs[staged] = o
+    torch.cuda.synchronize()
+    W = _ref_weight(q, st)
+    ref = a.double() @ W if bwd else a.double() @ W.T
+    assert not torch.isnan(outs["1"]).any()
+    assert max_rel_err(outs["1"], ref) <= GEMM_MAX_REL_ERR
+    assert torch.equal(outs["1"], outs["0"])
+    assert int(_counters(ws).count_nonzero()) == 0
+    _flag_clear()
+
+
+def test_staged_reduction_grouped_gate_up_backward(cuda_lib, monkeypatch):
+    """The step's gate/up dX (one K-concatenated launch, split pairs at 1,170 tokens): staged and
+    L2-load reductions bit-identical, and both within the GEMM bound of the fp64 product."""
+    from stew_b200 import _lib
+    from stew_b200.nf4 import _qstate, _stream
+    monkeypatch.delenv("STEW_NF4_TILE_N")  # the planner's own choice, as in the step
+    L = _lib.lib()
+    n, in_f = 1170, 1536
+    specs = [(8960, 61), (8960, 62)]
+    items = (_lib.LinearBwdItemC * len(specs))()
+    keep = []
+    ref = torch.zeros(n, in_f, dtype=torch.float64, device="cuda")
+    for i, (out_f, seed) in enumerate(specs):
+        q, st = _weight((out_f, in_f), seed)
+        qs = _qstate(st, q.device)
+        dy = _rand(n, out_f, seed + 5, std=0.01)
+        ref += dy.double() @ _ref_weight(q, st)
+        items[i].dy = dy.data_ptr()
+        items[i].packed = q.data_ptr()
+        items[i].qs = ctypes.pointer(qs)
+        items[i].lora = None
+        items[i].dyb = None
+        items[i].out_features = out_f
+        keep.append((q, st, qs, dy))
+    outs_c = (ctypes.c_int64 * len(specs))(*[s[0] for s in specs])
+    need = int(L.nf4b_linear_bwd_group_work_bytes(n, in_f, outs_c, len(specs)))
+    assert need > 0, "expected a split plan"
+    ws = _ws(need)
+    outs = {}
+    for staged in ("1", "0"):
+        monkeypatch.setenv("STEW_NF4_SPLIT_STAGED", staged)
+        dx = torch.full((n, in_f), float("nan"), dtype=torch.float16, device="cuda")
+        _lib.check(L.nf4b_linear_bwd_dx_group(items, len(specs), dx.data_ptr(), n, in_f, ws.data_ptr(),
+                                              ws.numel(), _stream(dx.device)), "bwd group")
+        outs[staged] = dx
+    torch.cuda.synchronize()
+    assert not torch.isnan(outs["1"]).any()
+    assert max_rel_err(outs["1"], ref) <= GEMM_MAX_REL_ERR
+    assert torch.equal(outs["1"], outs["0"])
+    assert int(_counters(ws).count_nonzero()) == 0
+    _flag_clear()
