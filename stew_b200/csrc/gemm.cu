@@ -1405,6 +1405,16 @@ static int tile_n_env() {
   return std::atoi(v) == 128 ? 128 : 256;
 }
 
+// K ranges per tile from STEW_NF4_SPLITS ("1" to "8"; 0 = the cost model's choice): applied to
+// the chosen tiling when it may split (fewer tiles than the workspace's counters, at least two
+// stages a range).
+static int splits_env() {
+  const char* v = std::getenv("STEW_NF4_SPLITS");
+  if (v == nullptr || v[0] == '\0') return 0;
+  const int k = std::atoi(v);
+  return (k >= 1 && k <= G_MAX_SPLITS) ? k : 0;
+}
+
 // Pair mode from STEW_NF4_PAIR: "0" never, "1" whenever the device runs pairs, otherwise
 // automatic.
 static int pair_mode_env() {
@@ -1418,6 +1428,13 @@ static int pair_mode_env() {
 static int red_staged_env() {
   const char* v = std::getenv("STEW_NF4_SPLIT_STAGED");
   return (v != nullptr && v[0] == '0') ? 0 : 1;
+}
+
+static GemmPlan force_splits(GemmPlan p) {
+  const int k = splits_env();
+  const int64_t max_tiles = p.pair ? G_SPLIT_MAX_TILES / 2 : G_SPLIT_MAX_TILES;
+  if (k > 0 && p.tiles > 0 && p.tiles <= max_tiles && p.nk / k >= 2) p.splits = k;
+  return p;
 }
 
 // rows: the M-side rows of each weight of the launch (forward: out features of each grouped
@@ -1447,7 +1464,7 @@ static GemmPlan plan_gemm(int64_t n, const int64_t* rows, int nrows, int64_t kdi
   // a forced token tile width (STEW_NF4_TILE_N) also keeps automatic plans on single CTAs
   const int mode = tn_env != 0 && pair_mode_env() != 1 ? 0 : pair_mode_env();
   const int64_t pslots = mode == 0 ? 0 : pair_slots_cached();
-  if (pslots <= 0) return single;
+  if (pslots <= 0) return force_splits(single);
   // Pair tiles are near MMA-bound, so the tokens are dealt evenly over the fewest 512-token
   // tiles (a multiple of 32 each; e.g. 1311 tokens: 448 + 448 + 415, not 512 + 512 + 287):
   // the longest unit of a wave is what the launch waits for.
@@ -1464,9 +1481,9 @@ static GemmPlan plan_gemm(int64_t n, const int64_t* rows, int nrows, int64_t kdi
     const int64_t even = ((n + pair.n_tiles - 1) / pair.n_tiles + 31) / 32 * 32;
     pair.tile_n = int32_t(even < G_PAIR_TILE_N ? even : G_PAIR_TILE_N);
   }
-  if (mode == 1) return pair;
   // automatic: pairs when the model puts them 5 % ahead of single CTAs
-  return c_pair < 0.95 * c_single ? pair : single;
+  GemmPlan chosen = (mode == 1 || c_pair < 0.95 * c_single) ? pair : single;
+  return force_splits(chosen);
 }
 
 // Workspace of a split launch: the counter region, then one fp32 partial tile per K range
