@@ -371,3 +371,34 @@ def test_staged_reduction_grouped_gate_up_backward(cuda_lib, monkeypatch):
     assert torch.equal(outs["1"], outs["0"])
     assert int(_counters(ws).count_nonzero()) == 0
     _flag_clear()
+
+
+@pytest.mark.parametrize("splits,pair", [("1", "0"), ("3", "0"), ("4", "0"), ("2", "1"), ("3", "1")])
+def test_forced_split_count(cuda_lib, monkeypatch, splits, pair):
+    """STEW_NF4_SPLITS sets the K ranges of the chosen tiling (down projection at 1,170 tokens,
+    140 stages): the workspace follows it, the output stays within the GEMM bound of the fp64
+    product and within the split-vs-unsplit bound of the unsplit launch, counters left zero."""
+    from stew_b200 import _lib
+    from stew_b200.nf4 import _qstate
+    monkeypatch.setenv("STEW_NF4_PAIR", pair)
+    L = _lib.lib()
+    out_f, in_f, n = 1536, 8960, 1170
+    q, st = _weight((out_f, in_f), 101)
+    qs = _qstate(st, q.device)
+    x = _rand(n, in_f, 102)
+    monkeypatch.setenv("STEW_NF4_SPLITS", "1")
+    assert int(L.nf4b_linear_work_bytes(n, in_f, out_f, 0)) == 0, "one range: no workspace"
+    y1 = torch.empty(n, out_f, dtype=torch.float16, device="cuda")
+    _fwd(L, x, q, qs, None, None, y1, n, in_f, out_f, None)
+    monkeypatch.setenv("STEW_NF4_SPLITS", splits)
+    need = int(L.nf4b_linear_work_bytes(n, in_f, out_f, 0))
+    assert (need > 0) == (splits != "1")
+    ws = _ws(need)
+    y = torch.full((n, out_f), float("nan"), dtype=torch.float16, device="cuda")
+    _fwd(L, x, q, qs, None, None, y, n, in_f, out_f, ws if need > 0 else None)
+    torch.cuda.synchronize()
+    assert not torch.isnan(y).any()
+    assert max_rel_err(y, x.double() @ _ref_weight(q, st).T) <= GEMM_MAX_REL_ERR
+    assert max_rel_err(y, y1.double()) <= SPLIT_VS_UNSPLIT
+    assert int(_counters(ws).count_nonzero()) == 0
+    _flag_clear()
