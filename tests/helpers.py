@@ -88,8 +88,8 @@ def seeded_weight(shape, seed, device="cpu"):
 
 
 def max_rel_err(y: torch.Tensor, ref: torch.Tensor) -> float:
-    ref = ref.double()
-    return float((y.double() - ref).abs().max() / ref.abs().max().clamp_min(1e-30))
+    ref = ref.detach().double()
+    return float((y.detach().double() - ref).abs().max() / ref.abs().max().clamp_min(1e-30))
 
 
 def elem_rel_err(y: torch.Tensor, ref: torch.Tensor, floor: float = ELEM_FLOOR) -> float:
